@@ -1,0 +1,360 @@
+"""Benchmark of the GRPO step (the north-star path) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload per GPU ("grpo_step_cfg4"): Qwen3-0.6B-shaped random-init bf16 model (hidden
+1024, 28 layers, 16 q / 8 kv heads, head_dim 128, SwiGLU 3072, vocab 151936 tied,
+rope theta 1e6, weights N(0, 0.02)); 64 prompts x G=8 completions, prompt length
+U[64, 512], ids U[0, 151643); 512 new tokens (no EOS), temperature 1.0, no top-k,
+paged KV pages of 256; then log-prob recompute of the policy and a frozen reference
+copy, group advantages, clipped surrogate + 0.04 * k3 KL, backward, AdamW lr 1e-6.
+Rewards are Bernoulli(0.5).  Under torchrun each rank runs its own 64 prompt groups
+(weak scaling), sums the response-token count and the bf16 gradients with NCCL, and
+steps AdamW on the global loss.  Inputs are synthetic (no dataset exists for this path).
+
+metric: GRPO step tokens/s = (prompt + completion tokens of all ranks) / step time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GRPO step tokens/s"
+UNIT = "tokens/s"
+WORKLOAD = "grpo_step_cfg4: 64 prompts x G=8 per GPU, prompt U[64,512], 512 new tokens, Qwen3-0.6B shape"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompts", type=int, default=64, help="prompt groups per GPU")
+    ap.add_argument("--group", type=int, default=8)
+    ap.add_argument("--new-tokens", type=int, default=512)
+    ap.add_argument("--prompt-min", type=int, default=64)
+    ap.add_argument("--prompt-max", type=int, default=512)
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--microbatch-tokens", type=int, default=32768)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_gpu{index}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------ workload
+def make_prompts(args, rank, step, device=None):
+    import torch
+    g = torch.Generator().manual_seed(1 + 1000 * rank + step)
+    lens = torch.randint(args.prompt_min, args.prompt_max + 1, (args.prompts,), generator=g)
+    prompts = [torch.randint(0, 151643, (1, int(L)), generator=g) for L in lens]
+    if device is not None:
+        prompts = [p.to(device) for p in prompts]
+    return prompts
+
+
+def decode_microbench(torch, ops, device, n_iter=20):
+    """Config 3: paged decode attention, batch 256, context U[1k, 8k], 16q/8kv, head_dim 128,
+    bf16 K/V ~ N(0,1) in 256-token pages randomly permuted in a pool 1.25x the need.
+    Returns (kernel ms per launch, algorithmic bytes per launch)."""
+    g = torch.Generator().manual_seed(3)
+    B, hq, hkv, D = 256, 16, 8, 128
+    ctx = torch.randint(1024, 8193, (B,), generator=g)
+    pages = [(int(c) + 255) // 256 for c in ctx]
+    pool = int(sum(pages) * 1.25)
+    perm = torch.randperm(pool, generator=g)
+    width = max(pages)
+    bt = torch.full((B, width), -1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(pages):
+        bt[i, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    kc = torch.randn(pool, 256, hkv, D, device=device, dtype=torch.bfloat16)
+    vc = torch.randn(pool, 256, hkv, D, device=device, dtype=torch.bfloat16)
+    q = torch.randn(B, hq, D, device=device, dtype=torch.bfloat16)
+    btd = bt.to(device)
+    cl = (ctx - 1).to(torch.int32).to(device)  # context_lens; the kernel attends context + 1 keys
+    split_tokens, max_splits = ops.decode_split_plan(B, hkv, int(ctx.max()))
+    ws_bytes = ops.lib().qb_paged_decode_workspace_bytes(B, hq, D, max_splits)
+    ws = torch.empty(max(ws_bytes // 4, 1), device=device, dtype=torch.float32)
+    run = lambda: ops.paged_decode_attention(q, kc, vc, btd, cl, D ** -0.5, split_tokens=split_tokens,
+                                             max_splits=max_splits, workspace=ws)
+    for _ in range(3):
+        run()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2 between launches
+    st = torch.cuda.current_stream()
+    times = []
+    for _ in range(n_iter):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        run()
+        b.record(st)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    nbytes = int(ctx.sum()) * hkv * D * 2 * 2 + B * hq * D * 2 * 2 + B * width * 4 + B * 4
+    ops.check_device_errors()
+    del kc, vc
+    return sum(times) / len(times), nbytes
+
+
+def cpu_baseline_sample(steps=1, threads=None):
+    """The oracle (CPU restatement of the reference) on a bounded sample of the GRPO step:
+    1 prompt x G=2 completions at the full Qwen3-0.6B shape, prompt 48 tokens, 4 new
+    tokens sampled by full recompute (the reference rollout's scheme), then reference-policy
+    and policy log-probs, the loss and its backward.  Returns (tokens/s, sample text, threads)."""
+    import torch
+    from oracle import ref_model
+    from oracle import ref_ops as R
+    from qwen3_naive_inference_b200.qwen3_naive import Qwen3Config
+    if threads:
+        torch.set_num_threads(threads)
+    cfg = Qwen3Config()
+    params = ref_model.init_params(cfg, seed=0)
+    g = torch.Generator().manual_seed(11)
+    P, G, new = 48, 2, 4
+    cs = R.rope_cache(cfg.head_dim, P + new + 1, cfg.rope_theta)
+    tok_total, t_total = 0, 0.0
+    for _ in range(steps):
+        prompt = torch.randint(0, 151643, (1, P), generator=g)
+        t0 = time.perf_counter()
+        ids = prompt.repeat(G, 1)
+        old = []
+        with torch.no_grad():
+            for _t in range(new):
+                lg = ref_model.logits(params, cfg, ids, cos_sin=cs)[:, -1].float()
+                probs, logp = R.sample_distribution(lg, 1.0, None)
+                nxt = torch.multinomial(probs, 1, generator=g)
+                old.append(logp.gather(-1, nxt))
+                ids = torch.cat([ids, nxt], 1)
+            ref_lp = ref_model.forward_logprob(params, cfg, ids, shift=True, cos_sin=cs)
+        p = {k: v.clone().requires_grad_(True) for k, v in params.items()}
+        lp = ref_model.forward_logprob(p, cfg, ids, shift=True, cos_sin=cs)
+        mask = torch.zeros_like(lp)
+        mask[:, P:] = 1
+        oldp = torch.zeros_like(lp)
+        oldp[:, P:] = torch.cat(old, 1)
+        rewards = torch.bernoulli(torch.full((G,), 0.5), generator=g)
+        adv = R.grpo_advantage(rewards, torch.zeros(G, dtype=torch.long))
+        loss = R.ppo_loss(oldp, lp, adv[:, None] * mask, mask, 0.2, ref_lp, 0.04)
+        loss.backward()
+        t_total += time.perf_counter() - t0
+        tok_total += G * (P + new)
+    sample = (f"oracle GRPO step on 1 prompt x G={G}, prompt {P} + {new} new tokens, Qwen3-0.6B shape "
+              f"(rollout by full recompute, ref + policy log-probs, clipped+KL loss, backward)")
+    return tok_total / t_total, sample, torch.get_num_threads()
+
+
+# ------------------------------------------------------------------------------ arms
+def run_reference(args):
+    """CPU baseline arm: the oracle port of the reference's GRPO step on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    for _ in range(args.warmup):
+        cpu_baseline_sample(1)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, sample, th = cpu_baseline_sample(1)
+        vals.append(v)
+    elapsed = time.perf_counter() - t0
+    value = sum(vals) / len(vals)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "sample": sample, "cores": threads},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": th, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from qwen3_naive_inference_b200 import _lib, ops
+    from qwen3_naive_inference_b200 import qwen3_grpo_train as G
+    from qwen3_naive_inference_b200.qwen3_naive import Qwen3Config, build_model
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    cfg = Qwen3Config(num_hidden_layers=args.layers)
+    policy = build_model(cfg, device=dev, seed=0)
+    ref = G.make_reference_copy(policy)
+    max_ctx = args.prompt_max + args.new_tokens
+    # pages for every sequence of the step at once (64*8 seqs x 4 pages) plus slack
+    policy._num_blocks = args.prompts * args.group * math.ceil(max_ctx / 256) + 64
+    policy.max_model_len = max_ctx
+    opt = torch.optim.AdamW(policy.parameters(), lr=1e-6)
+    reward_gen = torch.Generator().manual_seed(2 + rank)
+    torch.manual_seed(1234 + rank)
+
+    def step(i, prompts):
+        return G.grpo_step(policy, opt, prompts, ref_model=ref, group_size=args.group,
+                           max_new_tokens=args.new_tokens, temperature=1.0, top_k=None, eos_token_ids=None,
+                           reward_gen=reward_gen, beta=0.04, shift=True,
+                           microbatch_tokens=args.microbatch_tokens)
+
+    for i in range(args.warmup):
+        step(i, make_prompts(args, rank, i, dev))
+
+    def timed(n, host_inputs):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tokens = 0
+        h2d = d2h = 0
+        launches0 = _lib.LAUNCHES[0]
+        host = [make_prompts(args, rank, 100 + j) for j in range(n)]
+        if host_inputs:
+            host = [[p.pin_memory() for p in ps] for ps in host]
+        else:
+            host = [[p.to(dev) for p in ps] for ps in host]
+            torch.cuda.synchronize()
+        a.record(st)
+        wall0 = time.perf_counter()
+        for j in range(n):
+            prompts = host[j]
+            if host_inputs:  # the step's inputs cross PCIe inside the timed region
+                prompts = [p.to(dev, non_blocking=True) for p in prompts]
+                h2d += sum(p.numel() * p.element_size() for p in host[j])
+            out = step(j, prompts)
+            tokens += out["tokens"]
+            d2h += 3 * 4 + out["completion_tokens"] * 12  # loss[3] + sampled tokens/log-probs read back
+        b.record(st)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        wall = time.perf_counter() - wall0
+        launches = _lib.LAUNCHES[0] - launches0
+        if world > 1:
+            t = torch.tensor([ms, float(tokens)], device=dev, dtype=torch.float64)
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            ms, tokens = float(mx[0]), int(t[1])
+        return ms, tokens, wall, launches, h2d, d2h, out
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms, tokens, wall, launches, _, _, last = timed(args.steps, host_inputs=False)
+    clocks = sampler.stop()
+    value = tokens / (ms / 1000.0)
+    e2e = None
+    if not args.no_e2e:
+        ems, etok, _, _, h2d, d2h, _ = timed(args.steps, host_inputs=True)
+        e2e = {"value": etok / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.steps),
+               "d2h_bytes_per_step": d2h // max(1, args.steps)}
+    # roofline of the dominant kernel (paged decode attention), config-3 shapes, timed alone
+    dec_ms, dec_bytes = decode_microbench(torch, ops, dev)
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    achieved = dec_bytes / (dec_ms / 1000.0) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": None, "kernel": "paged_decode_kernel",
+                "case": "config 3: batch 256, ctx U[1k,8k], 16q/8kv, d128; L2 flushed between launches",
+                "ms_per_launch": dec_ms, "algorithmic_bytes": dec_bytes,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if pk.exists() else "fallback"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, sample, th = cpu_baseline_sample(1)
+        cpu = {"value": v, "unit": UNIT, "cores": th, "kind": "port", "sample": sample}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "prompts_per_gpu": args.prompts, "group": args.group,
+                           "new_tokens": args.new_tokens, "prompt_len": [args.prompt_min, args.prompt_max],
+                           "layers": args.layers, "parallelism": f"dp{world}", "beta_kl": 0.04,
+                           "l2": "inputs far larger than L2 (weights + 60+ GB KV cache per step)",
+                           "tokens_per_step": tokens // max(1, args.steps)},
+                "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"]},
+                "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
+                "cpu_baseline": cpu, "decode_attn_gbs": achieved}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,240 @@
+/*
+ * qwen3b200.h — C ABI of the B200 (sm_100a) kernels behind the GRPO step of
+ * qwen3-naive-inference.
+ *
+ * The reference has no C ABI of its own: its hot path is Python calling
+ * Triton kernels, flash-attn and cuBLAS.  Each entry point below replaces one
+ * of those call sites; the comment above it cites the reference line it
+ * stands in for (paths are relative to the reference project root).
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are device pointers unless documented otherwise;
+ *   - `bf16` tensors are passed as void* and hold IEEE bfloat16;
+ *   - row-major layouts, explicit element strides where a view may be strided;
+ *   - `stream` is a cudaStream_t (passed as void*); nothing synchronises the
+ *     host, nothing allocates, so every call can be captured in a CUDA graph;
+ *   - `err` (nullable) is a device int that kernels OR error bits into when a
+ *     data-dependent index is out of range; the access is skipped, never made;
+ *   - the return value is QB_OK (0) or an error code; argument errors are
+ *     detected on the host before any launch.
+ */
+#ifndef QWEN3B200_H
+#define QWEN3B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QB_OK 0
+#define QB_ERR_INVALID 1       /* bad argument (null pointer, size, alignment) */
+#define QB_ERR_UNSUPPORTED 2   /* shape outside what the kernels are built for */
+#define QB_ERR_CUDA_BASE 1000  /* QB_ERR_CUDA_BASE + cudaError_t of a failed launch */
+
+/* Device error bits written to *err. */
+#define QB_DEVERR_PAGE 1
+#define QB_DEVERR_SLOT 2
+#define QB_DEVERR_TOKEN 4
+#define QB_DEVERR_SHAPE 8
+#define QB_DEVERR_TIMEOUT 16
+
+typedef void* qb_stream_t;
+
+/* Version of this ABI (bumped on any signature change). */
+int qb_abi_version(void);
+/* Static description of a status code. */
+const char* qb_status_string(int status);
+
+/* ---------------------------------------------------------------- embedding
+ * Replaces nn.Embedding forward used by Qwen3Model.forward / forward_prefill /
+ * forward_decode (qwen3_naive.py:772, :788, :800).
+ * out[i, :] = table[ids[i], :]                          (bf16, [n, hidden]) */
+int qb_embedding_fwd(const int64_t* ids, int64_t n, const void* table, int64_t vocab,
+                     int64_t hidden, void* out, int* err, qb_stream_t stream);
+/* Backward of the lookup: dtable[ids[i], :] += dout[i, :] (fp32 accumulator). */
+int qb_embedding_bwd(const int64_t* ids, int64_t n, const void* dout, int64_t vocab,
+                     int64_t hidden, float* dtable, int* err, qb_stream_t stream);
+
+/* ---------------------------------------------------------------- RMSNorm
+ * Replaces RMSNorm._rms_norm (qwen3_naive.py:156-161):
+ *   y = bf16( (x * rsqrt(mean(x^2) + eps)) * w )  in fp32.
+ * rstd (nullable, [rows] fp32) receives rsqrt(mean(x^2)+eps) for the backward.
+ * cols must be a multiple of 256 and at most 2048. */
+int qb_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows,
+                   int64_t cols, float eps, qb_stream_t stream);
+/* Replaces RMSNorm._add_rms_norm (qwen3_naive.py:163-169):
+ *   s = x + residual (fp32); residual <- bf16(s); y = bf16((s*rsqrt(mean(s^2)+eps))*w). */
+int qb_add_rmsnorm_fwd(const void* x, void* residual, const void* w, void* y, int64_t rows,
+                       int64_t cols, float eps, qb_stream_t stream);
+/* Backward of qb_rmsnorm_fwd: dx (bf16) and dw += sum_rows(dy * x * rstd) (fp32). */
+int qb_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx,
+                   float* dw, int64_t rows, int64_t cols, qb_stream_t stream);
+
+/* ---------------------------------------------------------------- QK-Norm + RoPE (+ KV store)
+ * Replaces, for one token row of the fused qkv projection, the sequence
+ *   q_norm/k_norm (qwen3_naive.py:610-611), RotaryEmbedding.forward with the
+ *   Triton _apply_rope_kernel (:389-405, :44-80) and store_kvcache (:20-41, :626).
+ * qkv:  [T, ld_in] bf16, q heads at column 0, k heads at hq*D, v heads at (hq+hkv)*D.
+ * out:  [T, ld_out] bf16 in the same column layout: rotated q, rotated k, copied v
+ *       (nullable when only the cache and q_out are wanted).
+ * q_out: nullable [T, hq, D] contiguous rotated q (used by the paged paths).
+ * k_cache/v_cache: nullable [num_slots, hkv, D]; row slot_mapping[t] receives the
+ *       rotated k and raw v of token t; slot -1 skips the write (qwen3_naive.py:26).
+ * cos_sin: [max_pos, D] fp32, first D/2 columns cos, last D/2 sin (qwen3_naive.py:383-387).
+ * q_rstd/k_rstd: nullable [T, hq] / [T, hkv] fp32 saved for the backward.
+ * D must be 128. */
+int qb_qk_norm_rope_fwd(const void* qkv, int64_t T, int64_t ld_in, int hq, int hkv, int D,
+                        const int64_t* positions, const float* cos_sin, int64_t max_pos,
+                        const void* q_norm_w, const void* k_norm_w, float eps, void* out,
+                        int64_t ld_out, void* q_out, void* k_cache, void* v_cache,
+                        const int32_t* slot_mapping, int64_t num_slots, float* q_rstd,
+                        float* k_rstd, int* err, qb_stream_t stream);
+/* Backward of qb_qk_norm_rope_fwd (no cache).  dout: [T, ld] grads w.r.t. the
+ * rotated q, rotated k and v; dqkv: [T, ld] grads w.r.t. the raw projection.
+ * rope_grad = 0 reproduces the reference, whose Triton RoPE writes outside
+ * autograd (qwen3_naive.py:74-80): q/k grads are zero and dq_norm_w/dk_norm_w
+ * are left untouched.  dq_norm_w/dk_norm_w are fp32 [D] accumulators. */
+int qb_qk_norm_rope_bwd(const void* dout, const void* qkv, int64_t T, int64_t ld, int hq,
+                        int hkv, int D, const int64_t* positions, const float* cos_sin,
+                        int64_t max_pos, const void* q_norm_w, const void* k_norm_w,
+                        const float* q_rstd, const float* k_rstd, int rope_grad, void* dqkv,
+                        float* dq_norm_w, float* dk_norm_w, int* err, qb_stream_t stream);
+
+/* ---------------------------------------------------------------- SwiGLU, residual add
+ * Replaces Qwen3MLP.forward's silu(gate)*up (qwen3_naive.py:695-701):
+ *   gate_up [T, 2I] (gate = columns [0,I)), out [T, I] = bf16(silu(gate)*up). I % 8 == 0. */
+int qb_silu_mul_fwd(const void* gate_up, int64_t T, int64_t I, void* out, qb_stream_t stream);
+int qb_silu_mul_bwd(const void* dout, const void* gate_up, int64_t T, int64_t I,
+                    void* dgate_up, qb_stream_t stream);
+/* out = bf16(a + b), n elements (the bf16 residual adds of Qwen3DecoderLayer.forward, :715-719). */
+int qb_add_bf16(const void* a, const void* b, void* out, int64_t n, qb_stream_t stream);
+
+/* ---------------------------------------------------------------- attention
+ * Causal GQA attention over variable-length sequences; replaces
+ * flash_attn_varlen_func in Qwen3Attention.forward_prefill (qwen3_naive.py:631-637,
+ * paged, block_table=) and in the varlen branch of Qwen3Attention.forward (:540-548,
+ * dense).  Query row i of sequence b sits at absolute position Lk_b - Lq_b + i
+ * and attends keys 0..Lk_b-Lq_b+i (flash-attn's bottom-right causal alignment).
+ *   q:  row (cu_q[b] + i) at q + row*q_stride + h*D
+ *   dense K/V (block_tables == NULL): row (cu_k[b] + j) at k/v + row*kv_stride + kvh*D
+ *   paged K/V: k/v are caches [num_blocks, page_size, hkv, D]; token j of sequence b
+ *       lives in page block_tables[b*bt_stride + j/page_size].
+ * tile_info: [n_tiles, 2] int32 pairs (b, first query row of a 64-row tile); when
+ *       NULL, tile t maps to b = t / tiles_per_seq, first row 64*(t % tiles_per_seq)
+ *       (tiles past a sequence's end exit at once) and n_tiles = batch*tiles_per_seq.
+ * out: row (cu_q[b]+i) at out + row*o_stride + h*D (bf16).
+ * lse: nullable [hq, total_q] fp32 natural-log softmax normaliser (for the backward).
+ * D = 128, page_size = 256, hq % hkv == 0. */
+int qb_attn_varlen_fwd(const void* q, int64_t q_stride, const void* k, const void* v,
+                       int64_t kv_stride, const int32_t* block_tables, int64_t bt_stride,
+                       int64_t num_blocks, int page_size, const int32_t* cu_seqlens_q,
+                       const int32_t* cu_seqlens_k, int batch, const int32_t* tile_info,
+                       int n_tiles, int tiles_per_seq, int hq, int hkv, int D, float scale,
+                       void* out, int64_t o_stride, float* lse, int64_t total_q, int* err,
+                       qb_stream_t stream);
+/* Backward of the dense form of qb_attn_varlen_fwd (Lq == Lk per sequence, i.e.
+ * training on packed sequences).  q/k/v/dq/dk/dv share the row stride `stride`;
+ * o/do share `o_stride`.  delta: scratch [hq, total] fp32.  dq/dk/dv are bf16 and
+ * fully overwritten.  kv_tile_info: [n_tiles,2] (b, first key row of a 64-row tile);
+ * q_tile_info: [n_tiles,2] as in the forward (the two lists are identical for
+ * Lq == Lk and may alias). */
+int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, int64_t stride,
+                       const void* o, const void* dout, int64_t o_stride, const float* lse,
+                       const int32_t* cu_seqlens, int batch, const int32_t* tile_info,
+                       int n_tiles, int hq, int hkv, int D, float scale, int64_t total,
+                       float* delta, void* dq, void* dk, void* dv, int* err,
+                       qb_stream_t stream);
+
+/* Paged single-token decode attention; replaces flash_attn_with_kvcache in
+ * Qwen3Attention.forward_decode (qwen3_naive.py:672-680).
+ *   q: [batch, hq, D] bf16; caches [num_blocks, page_size, hkv, D];
+ *   kv length of sequence b = seqlens[b] + seqlen_add (the reference passes
+ *   cache_seqlens = context_lens + 1, i.e. seqlen_add = 1 on context_lens);
+ *   the key range is split into chunks of split_tokens (multiple of 64) processed by
+ *   separate CTAs; with max_splits > 1 partial results go to `workspace`
+ *   (qb_paged_decode_workspace_bytes) and a second kernel merges them.
+ *   out: [batch, hq, D] bf16.  D = 128, page_size = 256, hq == 2*hkv. */
+int qb_paged_decode_attn(const void* q, const void* k_cache, const void* v_cache,
+                         int64_t num_blocks, int page_size, const int32_t* block_tables,
+                         int64_t bt_stride, const int32_t* seqlens, int seqlen_add, int batch,
+                         int hq, int hkv, int D, float scale, int split_tokens, int max_splits,
+                         float* workspace, void* out, int* err, qb_stream_t stream);
+size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits);
+
+/* ---------------------------------------------------------------- lm_head log-prob / sampling
+ * Token log-probability from bf16 logits rows; replaces the fp32
+ * log_softmax + gather of forward_logprob (qwen3_grpo_train.py:48-52).
+ *   logits: [n, ld] bf16 (first V columns used); targets [n] int64 (< V).
+ *   logp[dest[i]] = logits[i, t_i] - lse_i, lse[i] = logsumexp(logits[i, :V]) (fp32).
+ *   dest nullable (identity); dest[i] < 0 skips row i. */
+int qb_logprob_fwd(const void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
+                   const int64_t* dest, float* logp, float* lse, int* err, qb_stream_t stream);
+/* Backward: logits[i, v] <- bf16( g_i * (1[v == t_i] - exp(logits[i,v] - lse_i)) ), in place,
+ * with g_i = grad_logp[dest[i]] (0 for skipped rows). */
+int qb_logprob_bwd(void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
+                   const int64_t* dest, const float* lse, const float* grad_logp, int* err,
+                   qb_stream_t stream);
+/* Sampling with the sampled token's log-prob; replaces the temperature / top-k /
+ * softmax / multinomial / log_softmax.gather block of
+ * generate_continuous_with_logprobs (qwen3_naive.py:1632-1650).
+ *   x = float(logits)/temperature; top_k = 0 keeps all V entries, otherwise the k
+ *   largest (ties broken toward the lower index); token ~ softmax(x over kept) by
+ *   the Gumbel-max rule on a counter-based Philox4x32-10 stream keyed by
+ *   (seed ^ rng_state[1], rng_state[0], row, column); logp = log_softmax(x over kept)[token].
+ *   top_k = 1 is greedy argmax with logp = 0.  rng_state (nullable): device uint64[2]
+ *   {counter, seed mix}, read at run time so a captured graph draws new noise per replay. */
+int qb_sample(const void* logits, int64_t n, int64_t V, int64_t ld, float temperature,
+              int top_k, uint64_t seed, const uint64_t* rng_state, int64_t* tokens, float* logp,
+              int* err, qb_stream_t stream);
+
+/* ---------------------------------------------------------------- GRPO
+ * Group-relative advantages; replaces compute_grpo_advantage (qwen3_grpo_train.py:162-173):
+ * adv[i] = (r[i] - mean_g) / (std_g + 1e-8), std unbiased over the members of i's group
+ * (group = equal group_ids).  n <= 65536. */
+int qb_grpo_advantage(const float* rewards, const int64_t* group_ids, int64_t n, float* adv,
+                      qb_stream_t stream);
+/* Fused GRPO loss and its gradient; replaces compute_grpo_advantage + token advantage +
+ * ppo_clipped_loss (qwen3_grpo_train.py:266-269, :184-199) and adds the k3 KL term
+ * kl = exp(ref - new) - (ref - new) - 1 weighted by beta.
+ * Rows [row_begin, row_end) of the [n_rows, S] (row stride S) fp32 tensors are processed;
+ * advantages use all n_rows rewards.  denom = mask_total ? *mask_total : sum(mask rows),
+ * loss = sum(mask*(-min(r*A, clip(r)*A) + beta*kl)) / (denom + 1e-8), r = exp(new-old),
+ * A = adv*mask.  grad_new (nullable) receives dloss/dnew times (*grad_scale or 1).
+ * loss_out[3] (nullable): loss, surrogate part, kl part — accumulated (+=), so callers
+ * zero it once and microbatches add up.  adv_out (nullable) [n_rows].
+ * workspace: qb_grpo_workspace_bytes(); its first 16 bytes must be zero before the
+ * first call and are left zero by every call. */
+int qb_grpo_loss(const float* rewards, const int64_t* group_ids, int64_t n_rows, int64_t S,
+                 int64_t row_begin, int64_t row_end, const float* new_lp, const float* old_lp,
+                 const float* ref_lp, const float* mask, const float* mask_total, float clip_eps,
+                 float beta, const float* grad_scale, float* grad_new, float* loss_out,
+                 float* adv_out, void* workspace, qb_stream_t stream);
+size_t qb_grpo_workspace_bytes(int64_t n_rows);
+/* The same fused loss and gradient with caller-supplied per-token advantages
+ * (token_adv [n_rows, S], already multiplied by the mask as in grpo_train_step);
+ * replaces ppo_clipped_loss(old_log_probs, new_log_probs, advantages, response_mask)
+ * (qwen3_grpo_train.py:184-199).  ref_lp nullable (beta ignored then). */
+int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, const float* token_adv,
+                        const float* mask, const float* ref_lp, int64_t n_rows, int64_t S,
+                        const float* mask_total, float clip_eps, float beta,
+                        const float* grad_scale, float* grad_new, float* loss_out,
+                        void* workspace, qb_stream_t stream);
+/* mask_total[0] = sum of the [n] fp32 mask (the reference's response_mask.sum(),
+ * qwen3_grpo_train.py:198); workspace as above. */
+int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace,
+                qb_stream_t stream);
+
+/* ---------------------------------------------------------------- optimizer helpers
+ * dst (bf16) = bf16(src fp32); used to hand fp32-accumulated gradients to the
+ * reference's torch AdamW (qwen3_grpo_train.py:327) as bf16 .grad tensors. */
+int qb_f32_to_bf16(const float* src, void* dst, int64_t n, qb_stream_t stream);
+/* acc (fp32) += bf16 src. */
+int qb_accumulate_bf16(const void* src, float* acc, int64_t n, qb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN3B200_H */

@@ -1,0 +1,124 @@
+// Shared device helpers for the sm_100a kernels of the GRPO step.
+//
+// Every kernel in this library is launched through an extern "C" entry point
+// declared in include/qwen3b200.h.  Entry points take raw device pointers,
+// explicit sizes and a cudaStream_t, never allocate, and return a status code
+// (QB_OK == 0).  Data-dependent indices (page ids, slots, token ids) are
+// bounds-checked on the device: a bad index skips the access and ORs a bit
+// into the caller's `err` word instead of faulting.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/qwen3b200.h"
+
+typedef __nv_bfloat16 bf16;
+
+#define QB_DEVICE __device__ __forceinline__
+
+// ---------------------------------------------------------------- launch glue
+static inline int qb_launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? QB_OK : (QB_ERR_CUDA_BASE + (int)e);
+}
+
+#define QB_CHECK_ARG(cond)            \
+  do {                                \
+    if (!(cond)) return QB_ERR_INVALID; \
+  } while (0)
+
+// Device-side error flag bits (ORed into *err by kernels).
+#define QB_DEVERR_PAGE 1      // block_table entry outside [0, num_blocks)
+#define QB_DEVERR_SLOT 2      // slot_mapping entry outside the cache
+#define QB_DEVERR_TOKEN 4     // token id outside [0, vocab)
+#define QB_DEVERR_SHAPE 8     // per-row length inconsistent with the buffers
+#define QB_DEVERR_TIMEOUT 16  // a bounded wait gave up
+
+QB_DEVICE void qb_set_err(int* err, int bit) {
+  if (err) atomicOr(err, bit);
+}
+
+// ---------------------------------------------------------------- numerics
+QB_DEVICE float bf2f(bf16 x) { return __bfloat162float(x); }
+QB_DEVICE bf16 f2bf(float x) { return __float2bfloat16_rn(x); }
+QB_DEVICE float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+QB_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+QB_DEVICE float2 unpack_bf16x2(uint32_t u) {
+  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
+  return __bfloat1622float2(v);
+}
+
+QB_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+QB_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum for blockDim.x a multiple of 32 (<= 1024). `red` holds >= 32 floats.
+QB_DEVICE float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = (threadIdx.x < (unsigned)nw) ? red[threadIdx.x] : 0.f;
+  if (wid == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------- PTX wrappers
+QB_DEVICE uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte async global->shared copy; src_bytes == 0 zero-fills the destination.
+QB_DEVICE void cp_async_16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+QB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+QB_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+QB_DEVICE void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+QB_DEVICE void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16, row) * B(16x8, col) + D, bf16 inputs, fp32 accumulate.
+QB_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Tiles of 128 bf16 per row (256 B = 16 chunks of 16 B) are stored with the
+// 16-byte chunk index XORed by (row & 7): the eight rows read by one
+// ldmatrix phase then fall into eight distinct bank groups.
+QB_DEVICE uint32_t swz128(int row, int chunk) {
+  return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4));
+}

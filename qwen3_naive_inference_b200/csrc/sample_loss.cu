@@ -1,0 +1,665 @@
+// Sampling, token log-probabilities and the fused GRPO loss.
+//
+//   qb_sample        temperature / top-k / Gumbel-max sampling with the sampled
+//                    token's log-prob (qwen3_naive.py:1632-1650)
+//   qb_logprob_fwd   log_softmax + gather from bf16 logits (qwen3_grpo_train.py:48-52)
+//   qb_logprob_bwd   its gradient w.r.t. the logits, in place
+//   qb_grpo_*        advantages, clipped surrogate, k3 KL, masked token mean and
+//                    the gradient w.r.t. the new log-probs (qwen3_grpo_train.py:162-199)
+//
+// Row kernels use one CTA per row and 16-byte loads.  Reductions that span CTAs
+// write per-CTA partials to a caller workspace; the last CTA to finish (ticket
+// counter, no spinning) folds them in a fixed order, so results are
+// deterministic run to run.
+#include "common.cuh"
+
+namespace {
+
+struct alignas(16) bf16x8 {
+  uint32_t u[4];
+};
+
+QB_DEVICE void unpack8(const bf16x8& r, float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = unpack_bf16x2(r.u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Order-preserving 16-bit key of a bf16 value (larger value -> larger key).
+QB_DEVICE uint32_t bf16_key(uint32_t bits16) {
+  return (bits16 & 0x8000u) ? (~bits16 & 0xFFFFu) : (bits16 | 0x8000u);
+}
+
+// ---------------------------------------------------------------- Philox4x32-10
+// Counter-based generator of Salmon, Moraes, Dror & Shaw, "Parallel random
+// numbers: as easy as 1, 2, 3" (SC'11): ten rounds of two 32x32->64 multiplies
+// with the published multipliers and Weyl key increments.
+struct U4 {
+  uint32_t x, y, z, w;
+};
+QB_DEVICE U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = M0 * c.x, hi0 = __umulhi(M0, c.x);
+    const uint32_t lo1 = M1 * c.z, hi1 = __umulhi(M1, c.z);
+    c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    k0 += W0;
+    k1 += W1;
+  }
+  return c;
+}
+// Uniform in the open interval (0, 1) from the top 24 bits.
+QB_DEVICE float u01(uint32_t v) { return ((float)(v >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+QB_DEVICE float gumbel(uint32_t v) { return -logf(-logf(u01(v))); }
+
+// Gumbel noise for columns [c8, c8+8) of one row.
+QB_DEVICE void gumbel8(uint64_t seed, uint64_t offset, int64_t row, int64_t c8, float (&g)[8]) {
+  const uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint64_t q = (uint64_t)(c8 / 4 + h);
+    U4 r = philox4x32_10(U4{(uint32_t)q, (uint32_t)row, (uint32_t)offset, (uint32_t)(offset >> 32)}, k0, k1);
+    g[4 * h + 0] = gumbel(r.x);
+    g[4 * h + 1] = gumbel(r.y);
+    g[4 * h + 2] = gumbel(r.z);
+    g[4 * h + 3] = gumbel(r.w);
+  }
+}
+
+// ---------------------------------------------------------------- block reductions
+struct MS {  // online log-sum-exp state
+  float m, s;
+};
+QB_DEVICE MS ms_merge(MS a, MS b) {
+  const float m = fmaxf(a.m, b.m);
+  if (m == -INFINITY) return MS{m, 0.f};
+  return MS{m, a.s * expf(a.m - m) + b.s * expf(b.m - m)};
+}
+QB_DEVICE void ms_add(MS& a, float x) {
+  if (x > a.m) {
+    a.s = (a.m == -INFINITY) ? 1.f : a.s * expf(a.m - x) + 1.f;
+    a.m = x;
+  } else if (x != -INFINITY) {
+    a.s += expf(x - a.m);
+  }
+}
+struct AM {  // argmax with lowest-index tie break
+  float v;
+  int64_t i;
+};
+QB_DEVICE AM am_merge(AM a, AM b) {
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+
+template <int NT>
+QB_DEVICE MS block_ms(MS v, MS* sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MS other{__shfl_xor_sync(0xffffffffu, v.m, o), __shfl_xor_sync(0xffffffffu, v.s, o)};
+    v = ms_merge(v, other);
+  }
+  __syncthreads();
+  if (lane == 0) sh[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    v = (lane < NT / 32) ? sh[lane] : MS{-INFINITY, 0.f};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      MS other{__shfl_xor_sync(0xffffffffu, v.m, o), __shfl_xor_sync(0xffffffffu, v.s, o)};
+      v = ms_merge(v, other);
+    }
+    if (lane == 0) sh[0] = v;
+  }
+  __syncthreads();
+  MS r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+template <int NT>
+QB_DEVICE AM block_am(AM v, AM* sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    AM other{__shfl_xor_sync(0xffffffffu, v.v, o), (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v.i, o)};
+    v = am_merge(v, other);
+  }
+  __syncthreads();
+  if (lane == 0) sh[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    v = (lane < NT / 32) ? sh[lane] : AM{-INFINITY, INT64_MAX};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      AM other{__shfl_xor_sync(0xffffffffu, v.v, o), (int64_t)__shfl_xor_sync(0xffffffffu, (long long)v.i, o)};
+      v = am_merge(v, other);
+    }
+    if (lane == 0) sh[0] = v;
+  }
+  __syncthreads();
+  AM r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+// Exclusive prefix sum over the block (NT threads) of a small int; returns the block total in *total.
+template <int NT>
+QB_DEVICE int block_excl_scan(int v, int* sh, int* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) sh[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int w = (lane < NT / 32) ? sh[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < NT / 32) sh[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const int before = (wid == 0) ? 0 : sh[wid - 1];
+  *total = sh[NT / 32 - 1];
+  __syncthreads();
+  return before + x - v;
+}
+
+// ---------------------------------------------------------------- sampling
+constexpr int SNT = 512;
+
+struct SampleParams {
+  const bf16* logits;
+  int64_t V, ld;
+  float temperature;
+  int top_k;
+  uint64_t seed;
+  const uint64_t* offset;
+  int64_t* tokens;
+  float* logp;
+  int* err;
+};
+
+__global__ void __launch_bounds__(SNT) sample_kernel(SampleParams p) {
+  __shared__ MS sh_ms[32];
+  __shared__ AM sh_am[32];
+  __shared__ int hist[256];
+  __shared__ int sh_scan[32];
+  __shared__ int sh_sel[4];
+  const int64_t row = blockIdx.x;
+  const bf16* lrow = p.logits + row * p.ld;
+  const int64_t nvec = p.V / 8;
+  // rng_state = {counter, seed mix}, read at run time so graph replays draw fresh noise.
+  const uint64_t off = p.offset ? p.offset[0] : 0ull;
+  const uint64_t seed = p.seed ^ (p.offset ? p.offset[1] : 0ull);
+  const int k = p.top_k;
+
+  // --------------------------------------------------------- greedy (top_k == 1)
+  if (k == 1) {
+    AM best{-INFINITY, INT64_MAX};
+    for (int64_t v = threadIdx.x; v < nvec; v += SNT) {
+      bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+      float x[8];
+      unpack8(r, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) best = am_merge(best, AM{x[i], v * 8 + i});
+    }
+    best = block_am<SNT>(best, sh_am);
+    if (threadIdx.x == 0) {
+      const bool ok = best.i >= 0 && best.i < p.V;  // false only for an all-NaN row
+      if (!ok) qb_set_err(p.err, QB_DEVERR_TOKEN);
+      p.tokens[row] = ok ? best.i : 0;
+      p.logp[row] = 0.f;
+    }
+    return;
+  }
+
+  // --------------------------------------------------------- top-k threshold (radix select on bf16 keys)
+  uint32_t thr_key = 0;  // keep keys > thr_key, plus the first need_eq keys == thr_key
+  int need_eq = 0;
+  const bool use_topk = k > 1 && k < p.V;
+  if (use_topk) {
+    for (int i = threadIdx.x; i < 256; i += SNT) hist[i] = 0;
+    __syncthreads();
+    for (int64_t v = threadIdx.x; v < nvec; v += SNT) {
+      bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        atomicAdd(&hist[bf16_key(r.u[i] & 0xFFFFu) >> 8], 1);
+        atomicAdd(&hist[bf16_key(r.u[i] >> 16) >> 8], 1);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0, bin = 255;
+      for (; bin > 0; --bin) {
+        if (cum + hist[bin] >= k) break;
+        cum += hist[bin];
+      }
+      sh_sel[0] = bin;
+      sh_sel[1] = cum;  // count of keys with a larger high byte
+    }
+    __syncthreads();
+    const int hb = sh_sel[0], above = sh_sel[1];
+    for (int i = threadIdx.x; i < 256; i += SNT) hist[i] = 0;
+    __syncthreads();
+    for (int64_t v = threadIdx.x; v < nvec; v += SNT) {
+      bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t key = bf16_key((i & 1) ? (r.u[i >> 1] >> 16) : (r.u[i >> 1] & 0xFFFFu));
+        if ((int)(key >> 8) == hb) atomicAdd(&hist[key & 0xFF], 1);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = above, lb = 255;
+      for (; lb > 0; --lb) {
+        if (cum + hist[lb] >= k) break;
+        cum += hist[lb];
+      }
+      sh_sel[2] = (hb << 8) | lb;
+      sh_sel[3] = k - cum;  // how many keys equal to the threshold are kept
+    }
+    __syncthreads();
+    thr_key = (uint32_t)sh_sel[2];
+    need_eq = sh_sel[3];
+  }
+
+  // --------------------------------------------------------- LSE over kept entries + Gumbel argmax
+  MS ms{-INFINITY, 0.f};
+  AM best{-INFINITY, INT64_MAX};
+  int eq_carry = 0;
+  for (int64_t base = 0; base < nvec; base += SNT) {
+    const int64_t v = base + threadIdx.x;
+    bf16x8 r{};
+    const bool live = v < nvec;
+    if (live) r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+    float x[8];
+    unpack8(r, x);
+    uint32_t keys[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) keys[i] = bf16_key((i & 1) ? (r.u[i >> 1] >> 16) : (r.u[i >> 1] & 0xFFFFu));
+    int my_eq = 0;
+    if (use_topk && live) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) my_eq += (keys[i] == thr_key);
+    }
+    int rank = 0;
+    if (use_topk) {
+      int tot = 0;
+      rank = eq_carry + block_excl_scan<SNT>(my_eq, sh_scan, &tot);
+      eq_carry += tot;
+    }
+    if (!live) continue;
+    float gn[8];
+    gumbel8(seed, off, row, v * 8, gn);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      bool keep = true;
+      if (use_topk) {
+        if (keys[i] > thr_key) keep = true;
+        else if (keys[i] == thr_key) keep = (rank++ < need_eq);
+        else keep = false;
+      }
+      if (!keep) continue;
+      const float xs = __fdiv_rn(x[i], p.temperature);
+      ms_add(ms, xs);
+      best = am_merge(best, AM{xs + gn[i], v * 8 + i});
+    }
+  }
+  ms = block_ms<SNT>(ms, sh_ms);
+  best = block_am<SNT>(best, sh_am);
+  if (threadIdx.x == 0) {
+    const bool ok = best.i >= 0 && best.i < p.V;  // false only when no finite candidate exists
+    if (!ok) qb_set_err(p.err, QB_DEVERR_TOKEN);
+    const int64_t tok = ok ? best.i : 0;
+    p.tokens[row] = tok;
+    const float xt = __fdiv_rn(bf2f(lrow[tok]), p.temperature);
+    p.logp[row] = (xt - ms.m) - logf(ms.s);
+  }
+}
+
+// ---------------------------------------------------------------- log-prob fwd / bwd
+constexpr int LNT = 256;
+
+__global__ void __launch_bounds__(LNT)
+logprob_fwd_kernel(const bf16* __restrict__ logits, int64_t V, int64_t ld, const int64_t* __restrict__ targets,
+                   const int64_t* __restrict__ dest, float* __restrict__ logp, float* __restrict__ lse, int* err) {
+  __shared__ MS sh[32];
+  const int64_t row = blockIdx.x;
+  const bf16* lrow = logits + row * ld;
+  const int64_t nvec = V / 8;
+  MS ms{-INFINITY, 0.f};
+  for (int64_t v = threadIdx.x; v < nvec; v += LNT) {
+    bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+    float x[8];
+    unpack8(r, x);
+    float mx = x[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, x[i]);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += expf(x[i] - mx);
+    ms = ms_merge(ms, MS{mx, s});
+  }
+  ms = block_ms<LNT>(ms, sh);
+  if (threadIdx.x == 0) {
+    const float l = ms.m + logf(ms.s);
+    lse[row] = l;
+    const int64_t d = dest ? dest[row] : row;
+    if (d >= 0) {
+      int64_t t = targets[row];
+      if (t < 0 || t >= V) {
+        qb_set_err(err, QB_DEVERR_TOKEN);
+        logp[d] = 0.f;
+      } else {
+        logp[d] = (bf2f(lrow[t]) - ms.m) - logf(ms.s);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(LNT)
+logprob_bwd_kernel(bf16* __restrict__ logits, int64_t V, int64_t ld, const int64_t* __restrict__ targets,
+                   const int64_t* __restrict__ dest, const float* __restrict__ lse, const float* __restrict__ gl) {
+  const int64_t row = blockIdx.x;
+  bf16* lrow = logits + row * ld;
+  const int64_t d = dest ? dest[row] : row;
+  const float g = (d >= 0) ? gl[d] : 0.f;
+  const float l = lse[row];
+  const int64_t t = targets[row];
+  const int64_t nvec = V / 8;
+  for (int64_t v = threadIdx.x; v < nvec; v += LNT) {
+    bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+    float x[8];
+    unpack8(r, x);
+    bf16x8 o;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t c = v * 8 + 2 * i;
+      const float a = (c == t ? g : 0.f) - expf(x[2 * i] - l) * g;
+      const float b = (c + 1 == t ? g : 0.f) - expf(x[2 * i + 1] - l) * g;
+      o.u[i] = pack_bf16x2(a, b);
+    }
+    *reinterpret_cast<bf16x8*>(lrow + v * 8) = o;
+  }
+}
+
+// ---------------------------------------------------------------- GRPO
+// Workspace layout: [0] u32 mask ticket, [1] u32 loss ticket, [2] f32 denominator,
+// [3] pad, then f32 partials.
+constexpr int WS_HDR = 4;
+constexpr int MS_BLOCKS = 256;
+
+__global__ void mask_sum_kernel(const float* __restrict__ mask, int64_t n, float* __restrict__ out,
+                                uint32_t* __restrict__ ws) {
+  __shared__ float red[32];
+  __shared__ bool last;
+  float s = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    s += mask[i];
+  s = block_sum(s, red);
+  float* part = reinterpret_cast<float*>(ws + WS_HDR);
+  if (threadIdx.x == 0) {
+    part[blockIdx.x] = s;
+    __threadfence();
+    last = atomicAdd(&ws[0], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    float t = 0.f;
+    for (unsigned b = 0; b < gridDim.x; ++b) t += reinterpret_cast<volatile float*>(part)[b];
+    *out = t;
+    ws[0] = 0u;
+  }
+}
+
+// Group statistics of row r's group: mean and unbiased std over rows with equal id.
+QB_DEVICE float group_advantage(const float* rewards, const int64_t* gids, int64_t n, int64_t r, float* red) {
+  const int64_t gid = gids[r];
+  float cnt = 0.f, sum = 0.f;
+  for (int64_t j = threadIdx.x; j < n; j += blockDim.x)
+    if (gids[j] == gid) {
+      cnt += 1.f;
+      sum += rewards[j];
+    }
+  cnt = block_sum(cnt, red);
+  sum = block_sum(sum, red);
+  const float mean = sum / cnt;
+  float sq = 0.f;
+  for (int64_t j = threadIdx.x; j < n; j += blockDim.x)
+    if (gids[j] == gid) {
+      const float d = rewards[j] - mean;
+      sq += d * d;
+    }
+  sq = block_sum(sq, red);
+  const float stdv = sqrtf(sq / (cnt - 1.f));
+  return (rewards[r] - mean) / (stdv + 1e-8f);
+}
+
+__global__ void advantage_kernel(const float* __restrict__ rewards, const int64_t* __restrict__ gids, int64_t n,
+                                 float* __restrict__ adv) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  const float a = group_advantage(rewards, gids, n, r, red);
+  if (threadIdx.x == 0) adv[r] = a;
+}
+
+struct LossParams {
+  const float* rewards;
+  const int64_t* gids;
+  const float* token_adv;  // [n_rows, S] per-token advantages (ppo_clipped_loss form)
+  int64_t n_rows, S, row_begin;
+  const float* new_lp;
+  const float* old_lp;
+  const float* ref_lp;
+  const float* mask;
+  const float* mask_total;  // resolved denominator (user's or the workspace slot)
+  float lo, hi, beta;
+  const float* grad_scale;
+  float* grad_new;
+  float* loss_out;
+  float* adv_out;
+  uint32_t* ws;
+};
+
+// FROM_REWARDS: A = group advantage of row r times mask (compute_grpo_advantage +
+// token_advantages, qwen3_grpo_train.py:266-269); otherwise A = token_adv[i] as given
+// to ppo_clipped_loss (:184-199).
+template <bool FROM_REWARDS>
+__global__ void grpo_loss_kernel(LossParams p) {
+  __shared__ float red[32];
+  __shared__ bool last;
+  const int64_t r = p.row_begin + blockIdx.x;
+  float adv = 0.f;
+  if (FROM_REWARDS) {
+    adv = group_advantage(p.rewards, p.gids, p.n_rows, r, red);
+    if (p.adv_out && threadIdx.x == 0) p.adv_out[r] = adv;
+  }
+  const float denom = *p.mask_total + 1e-8f;
+  const float gs = p.grad_scale ? *p.grad_scale : 1.f;
+  const float u = gs / denom;  // d loss / d sum(loss_token * mask)
+  float surr = 0.f, klsum = 0.f;
+  for (int64_t s = threadIdx.x; s < p.S; s += blockDim.x) {
+    const int64_t i = r * p.S + s;
+    const float m = p.mask[i];
+    const float A = FROM_REWARDS ? adv * m : p.token_adv[i];
+    const float nw = p.new_lp[i];
+    const float ratio = expf(nw - p.old_lp[i]);
+    const float cr = fminf(fmaxf(ratio, p.lo), p.hi);
+    const float s1 = ratio * A, s2 = cr * A;
+    const float lt = -fminf(s1, s2);
+    surr += lt * m;
+    float kl = 0.f, dkl = 0.f;
+    if (p.ref_lp) {
+      const float d = p.ref_lp[i] - nw;
+      const float e = expf(d);
+      kl = e - d - 1.f;
+      dkl = 1.f - e;
+      klsum += kl * m;
+    }
+    if (p.grad_new) {
+      const float gl = u * m;     // grad of loss_token * mask w.r.t. loss_token
+      const float gmin = -gl;     // loss_token = -min(s1, s2)
+      const bool eq = s1 == s2;
+      const float g1 = eq ? gmin * 0.5f : (s1 < s2 ? gmin : 0.f);
+      const float g2 = eq ? gmin * 0.5f : (s2 < s1 ? gmin : 0.f);
+      const float inr = (ratio >= p.lo && ratio <= p.hi) ? 1.f : 0.f;
+      const float gratio = g1 * A + (g2 * A) * inr;
+      float gnew = gratio * ratio;
+      if (p.ref_lp) gnew += p.beta * gl * dkl;
+      p.grad_new[i] = gnew;
+    }
+  }
+  surr = block_sum(surr, red);
+  klsum = block_sum(klsum, red);
+  float* part = reinterpret_cast<float*>(p.ws + WS_HDR);
+  if (threadIdx.x == 0) {
+    part[2 * blockIdx.x] = surr;
+    part[2 * blockIdx.x + 1] = klsum;
+    __threadfence();
+    last = atomicAdd(&p.ws[1], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    volatile float* vp = part;
+    float ts = 0.f, tk = 0.f;
+    for (unsigned b = 0; b < gridDim.x; ++b) {
+      ts += vp[2 * b];
+      tk += vp[2 * b + 1];
+    }
+    if (p.loss_out) {
+      const float ls = ts / denom, lk = tk / denom;
+      p.loss_out[0] += ls + p.beta * lk;
+      p.loss_out[1] += ls;
+      p.loss_out[2] += lk;
+    }
+    p.ws[1] = 0u;
+  }
+}
+
+inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" int qb_sample(const void* logits, int64_t n, int64_t V, int64_t ld, float temperature, int top_k,
+                         uint64_t seed, const uint64_t* offset, int64_t* tokens, float* logp, int* err,
+                         qb_stream_t stream) {
+  QB_CHECK_ARG(n >= 0 && V > 0 && ld >= V && top_k >= 0 && temperature > 0.f);
+  if (n == 0) return QB_OK;
+  QB_CHECK_ARG(logits && tokens && logp && al16(logits) && ld % 8 == 0);
+  if (V % 8 != 0) return QB_ERR_UNSUPPORTED;
+  SampleParams p{(const bf16*)logits, V, ld, temperature, top_k, seed, offset, tokens, logp, err};
+  sample_kernel<<<(unsigned)n, SNT, 0, (cudaStream_t)stream>>>(p);
+  return qb_launch_status();
+}
+
+extern "C" int qb_logprob_fwd(const void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
+                              const int64_t* dest, float* logp, float* lse, int* err, qb_stream_t stream) {
+  QB_CHECK_ARG(n >= 0 && V > 0 && ld >= V);
+  if (n == 0) return QB_OK;
+  QB_CHECK_ARG(logits && targets && logp && lse && al16(logits) && ld % 8 == 0);
+  if (V % 8 != 0) return QB_ERR_UNSUPPORTED;
+  logprob_fwd_kernel<<<(unsigned)n, LNT, 0, (cudaStream_t)stream>>>((const bf16*)logits, V, ld, targets, dest,
+                                                                    logp, lse, err);
+  return qb_launch_status();
+}
+
+extern "C" int qb_logprob_bwd(void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
+                              const int64_t* dest, const float* lse, const float* grad_logp, int* err,
+                              qb_stream_t stream) {
+  (void)err;
+  QB_CHECK_ARG(n >= 0 && V > 0 && ld >= V);
+  if (n == 0) return QB_OK;
+  QB_CHECK_ARG(logits && targets && lse && grad_logp && al16(logits) && ld % 8 == 0);
+  if (V % 8 != 0) return QB_ERR_UNSUPPORTED;
+  logprob_bwd_kernel<<<(unsigned)n, LNT, 0, (cudaStream_t)stream>>>((bf16*)logits, V, ld, targets, dest, lse,
+                                                                    grad_logp);
+  return qb_launch_status();
+}
+
+extern "C" int qb_grpo_advantage(const float* rewards, const int64_t* group_ids, int64_t n, float* adv,
+                                 qb_stream_t stream) {
+  QB_CHECK_ARG(n >= 0 && n <= 65536);
+  if (n == 0) return QB_OK;
+  QB_CHECK_ARG(rewards && group_ids && adv);
+  advantage_kernel<<<(unsigned)n, 256, 0, (cudaStream_t)stream>>>(rewards, group_ids, n, adv);
+  return qb_launch_status();
+}
+
+extern "C" size_t qb_grpo_workspace_bytes(int64_t n_rows) {
+  const int64_t parts = (2 * n_rows > MS_BLOCKS) ? 2 * n_rows : MS_BLOCKS;
+  return (size_t)(WS_HDR + parts) * sizeof(float);
+}
+
+extern "C" int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace, qb_stream_t stream) {
+  QB_CHECK_ARG(n >= 0 && mask_total && workspace);
+  QB_CHECK_ARG(n == 0 || mask);
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > MS_BLOCKS) blocks = MS_BLOCKS;
+  if (blocks < 1) blocks = 1;
+  mask_sum_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(mask, n, mask_total, (uint32_t*)workspace);
+  return qb_launch_status();
+}
+
+extern "C" int qb_grpo_loss(const float* rewards, const int64_t* group_ids, int64_t n_rows, int64_t S,
+                            int64_t row_begin, int64_t row_end, const float* new_lp, const float* old_lp,
+                            const float* ref_lp, const float* mask, const float* mask_total, float clip_eps,
+                            float beta, const float* grad_scale, float* grad_new, float* loss_out,
+                            float* adv_out, void* workspace, qb_stream_t stream) {
+  QB_CHECK_ARG(n_rows >= 0 && n_rows <= 65536 && S >= 0 && row_begin >= 0 && row_end <= n_rows &&
+               row_begin <= row_end);
+  if (row_end == row_begin) return QB_OK;
+  QB_CHECK_ARG(rewards && group_ids && new_lp && old_lp && mask && workspace);
+  uint32_t* ws = (uint32_t*)workspace;
+  const float* denom = mask_total;
+  if (!denom) {
+    float* slot = reinterpret_cast<float*>(ws + 2);
+    int st = qb_mask_sum(mask, n_rows * S, slot, workspace, stream);
+    if (st != QB_OK) return st;
+    denom = slot;
+  }
+  LossParams p{rewards, group_ids, nullptr, n_rows, S, row_begin, new_lp, old_lp, ref_lp, mask, denom,
+               (float)(1.0 - (double)clip_eps), (float)(1.0 + (double)clip_eps), beta, grad_scale, grad_new,
+               loss_out, adv_out, ws};
+  grpo_loss_kernel<true><<<(unsigned)(row_end - row_begin), 256, 0, (cudaStream_t)stream>>>(p);
+  return qb_launch_status();
+}
+
+extern "C" int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, const float* token_adv,
+                                   const float* mask, const float* ref_lp, int64_t n_rows, int64_t S,
+                                   const float* mask_total, float clip_eps, float beta, const float* grad_scale,
+                                   float* grad_new, float* loss_out, void* workspace, qb_stream_t stream) {
+  QB_CHECK_ARG(n_rows >= 0 && n_rows <= 65536 && S >= 0);
+  if (n_rows == 0) return QB_OK;
+  QB_CHECK_ARG(old_lp && new_lp && token_adv && mask && workspace);
+  uint32_t* ws = (uint32_t*)workspace;
+  const float* denom = mask_total;
+  if (!denom) {
+    float* slot = reinterpret_cast<float*>(ws + 2);
+    int st = qb_mask_sum(mask, n_rows * S, slot, workspace, stream);
+    if (st != QB_OK) return st;
+    denom = slot;
+  }
+  LossParams p{nullptr, nullptr, token_adv, n_rows, S, 0, new_lp, old_lp, ref_lp, mask, denom,
+               (float)(1.0 - (double)clip_eps), (float)(1.0 + (double)clip_eps), beta, grad_scale, grad_new,
+               loss_out, nullptr, ws};
+  grpo_loss_kernel<false><<<(unsigned)n_rows, 256, 0, (cudaStream_t)stream>>>(p);
+  return qb_launch_status();
+}

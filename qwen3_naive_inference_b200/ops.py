@@ -1,0 +1,563 @@
+"""Torch-facing wrappers over the C ABI in ``include/qwen3b200.h``.
+
+Each function validates dtype/shape/contiguity/device, then calls one
+``qb_*`` entry point on the current CUDA stream with raw pointers.  Tensors
+must live on a CUDA device: there is no CPU fallback, and a missing shared
+library raises :class:`NativeError`.
+
+Training-path ops are ``torch.autograd.Function``s whose backward is a CUDA
+kernel of this library as well (RMSNorm, QK-Norm+RoPE, attention, SwiGLU,
+embedding).  Dense projections go through :func:`linear`.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from ._lib import NativeError, check
+
+__all__ = [
+    "NativeError", "lib", "stream_ptr", "err_flag", "check_device_errors", "embedding", "rmsnorm",
+    "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "attention_packed", "attention_paged_prefill",
+    "paged_decode_attention", "silu_mul", "add", "linear", "logprob", "sample", "grpo_advantage",
+    "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan",
+]
+
+BF16 = torch.bfloat16
+
+
+def lib():
+    return _lib.load()
+
+
+def stream_ptr() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise NativeError("qwen3_naive_inference_b200 ops need CUDA tensors (no CPU fallback)")
+
+
+_ERR: dict[int, torch.Tensor] = {}
+
+
+def err_flag(device=None) -> torch.Tensor:
+    """Device int32 error word shared by all launches on ``device``."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
+    t = _ERR.get(dev.index)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        _ERR[dev.index] = t
+    return t
+
+
+_DEVERR_NAMES = {1: "page id out of range", 2: "slot out of range", 4: "token id out of range",
+                 8: "inconsistent sequence lengths / positions", 16: "bounded wait timed out"}
+
+
+def check_device_errors(device=None) -> None:
+    """Reads (synchronously) and clears the device error word; raises if set."""
+    f = err_flag(device)
+    v = int(f.item())
+    if v:
+        f.zero_()
+        names = [n for b, n in _DEVERR_NAMES.items() if v & b]
+        raise NativeError(f"device-side bounds check failed: {', '.join(names)} (bits {v:#x})")
+
+
+# ---------------------------------------------------------------- embedding
+class _Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, weight):
+        n = ids.numel()
+        out = torch.empty(n, weight.shape[1], dtype=weight.dtype, device=weight.device)
+        check(lib().qb_embedding_fwd(_p(ids), n, _p(weight), weight.shape[0], weight.shape[1], _p(out),
+                                     _p(err_flag()), stream_ptr()), "qb_embedding_fwd")
+        ctx.save_for_backward(ids)
+        ctx.shape = weight.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        (ids,) = ctx.saved_tensors
+        g = g.contiguous()
+        acc = torch.zeros(ctx.shape, dtype=torch.float32, device=g.device)
+        check(lib().qb_embedding_bwd(_p(ids), ids.numel(), _p(g), ctx.shape[0], ctx.shape[1], _p(acc),
+                                     _p(err_flag()), stream_ptr()), "qb_embedding_bwd")
+        return None, _to_bf16(acc)
+
+
+def embedding(ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """``weight[ids]`` for int64 ``ids`` (any shape, flattened) -> [n, hidden] bf16."""
+    _cuda(ids, weight)
+    ids = ids.reshape(-1)
+    if ids.dtype != torch.long:
+        ids = ids.long()
+    return _Embedding.apply(ids.contiguous(), weight)
+
+
+def _to_bf16(acc: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(acc.shape, dtype=BF16, device=acc.device)
+    check(lib().qb_f32_to_bf16(_p(acc), _p(out), acc.numel(), stream_ptr()), "qb_f32_to_bf16")
+    return out
+
+
+# ---------------------------------------------------------------- RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+        y = torch.empty_like(x)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        check(lib().qb_rmsnorm_fwd(_p(x), _p(w), _p(y), _p(rstd), rows, cols, eps, stream_ptr()),
+              "qb_rmsnorm_fwd")
+        ctx.save_for_backward(x, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dy = dy.contiguous()
+        rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+        dx = torch.empty_like(x)
+        dw = torch.zeros(cols, dtype=torch.float32, device=x.device)
+        check(lib().qb_rmsnorm_bwd(_p(dy), _p(x), _p(w), _p(rstd), _p(dx), _p(dw), rows, cols, stream_ptr()),
+              "qb_rmsnorm_bwd")
+        return dx, _to_bf16(dw).to(w.dtype), None
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    _cuda(x, w)
+    x = x.contiguous()
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
+        return _RMSNorm.apply(x, w, eps)
+    rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+    y = torch.empty_like(x)
+    check(lib().qb_rmsnorm_fwd(_p(x), _p(w), _p(y), 0, rows, cols, eps, stream_ptr()), "qb_rmsnorm_fwd")
+    return y
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float):
+    """Fused ``residual += x; y = rmsnorm(residual)`` (inference); returns (y, residual)."""
+    _cuda(x, residual, w)
+    x = x.contiguous()
+    residual = residual.contiguous().clone() if not residual.is_contiguous() else residual
+    rows, cols = x.numel() // x.shape[-1], x.shape[-1]
+    y = torch.empty_like(x)
+    check(lib().qb_add_rmsnorm_fwd(_p(x), _p(residual), _p(w), _p(y), rows, cols, eps, stream_ptr()),
+          "qb_add_rmsnorm_fwd")
+    return y, residual
+
+
+# ---------------------------------------------------------------- QK-Norm + RoPE
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, positions, cos_sin, qw, kw, eps, hq, hkv, rope_grad):
+        T, ld = qkv.shape
+        out = torch.empty_like(qkv)
+        q_rstd = torch.empty(T, hq, dtype=torch.float32, device=qkv.device)
+        k_rstd = torch.empty(T, hkv, dtype=torch.float32, device=qkv.device)
+        check(lib().qb_qk_norm_rope_fwd(_p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin),
+                                        cos_sin.shape[0], _p(qw), _p(kw), eps, _p(out), ld, 0, 0, 0, 0, 0,
+                                        _p(q_rstd), _p(k_rstd), _p(err_flag()), stream_ptr()),
+              "qb_qk_norm_rope_fwd")
+        ctx.save_for_backward(qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd)
+        ctx.cfg = (hq, hkv, rope_grad)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd = ctx.saved_tensors
+        hq, hkv, rope_grad = ctx.cfg
+        dout = dout.contiguous()
+        T, ld = qkv.shape
+        dqkv = torch.empty_like(qkv)
+        dqw = torch.zeros(128, dtype=torch.float32, device=qkv.device)
+        dkw = torch.zeros(128, dtype=torch.float32, device=qkv.device)
+        check(lib().qb_qk_norm_rope_bwd(_p(dout), _p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin),
+                                        cos_sin.shape[0], _p(qw), _p(kw), _p(q_rstd), _p(k_rstd),
+                                        1 if rope_grad else 0, _p(dqkv), _p(dqw), _p(dkw), _p(err_flag()),
+                                        stream_ptr()), "qb_qk_norm_rope_bwd")
+        if not rope_grad:  # the reference's Triton RoPE leaves q_norm/k_norm without a grad
+            return dqkv, None, None, None, None, None, None, None, None
+        return dqkv, None, None, _to_bf16(dqw).to(qw.dtype), _to_bf16(dkw).to(kw.dtype), None, None, None, None
+
+
+def qk_norm_rope(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, rope_grad=True):
+    """[T, (hq+2hkv)*128] projection -> same layout with normed+rotated q, k and copied v."""
+    _cuda(qkv, positions, cos_sin)
+    qkv = qkv.contiguous()
+    if torch.is_grad_enabled() and (qkv.requires_grad or q_norm_w.requires_grad):
+        return _QKNormRope.apply(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, rope_grad)
+    T, ld = qkv.shape
+    out = torch.empty_like(qkv)
+    check(lib().qb_qk_norm_rope_fwd(_p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin), cos_sin.shape[0],
+                                    _p(q_norm_w), _p(k_norm_w), eps, _p(out), ld, 0, 0, 0, 0, 0, 0, 0,
+                                    _p(err_flag()), stream_ptr()), "qb_qk_norm_rope_fwd")
+    return out
+
+
+def qk_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, k_cache, v_cache,
+                       slot_mapping):
+    """Paged path: returns rotated q [T, hq, 128]; rotated k and v go to the cache rows slot_mapping."""
+    _cuda(qkv, positions, cos_sin, k_cache, v_cache, slot_mapping)
+    T, ld = qkv.shape
+    q = torch.empty(T, hq, 128, dtype=qkv.dtype, device=qkv.device)
+    num_slots = k_cache.numel() // (hkv * 128)
+    check(lib().qb_qk_norm_rope_fwd(_p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin), cos_sin.shape[0],
+                                    _p(q_norm_w), _p(k_norm_w), eps, 0, 0, _p(q), _p(k_cache), _p(v_cache),
+                                    _p(slot_mapping), num_slots, 0, 0, _p(err_flag()), stream_ptr()),
+          "qb_qk_norm_rope_fwd")
+    return q
+
+
+# ---------------------------------------------------------------- attention
+def build_tiles(lengths, block: int = 64) -> np.ndarray:
+    """Host list of (sequence, first row) pairs covering each sequence in 64-row tiles."""
+    lens = np.asarray(lengths, dtype=np.int64)
+    n = (lens + block - 1) // block
+    seq = np.repeat(np.arange(len(lens), dtype=np.int32), n)
+    start = (np.arange(int(n.sum()), dtype=np.int64) - np.repeat(np.cumsum(n) - n, n)) * block
+    return np.stack([seq, start.astype(np.int32)], axis=1).astype(np.int32).reshape(-1)
+
+
+class _AttnPacked(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cu, tiles, hq, hkv, scale):
+        T, ld = qkv.shape
+        out = torch.empty(T, hq * 128, dtype=qkv.dtype, device=qkv.device)
+        lse = torch.empty(hq, T, dtype=torch.float32, device=qkv.device)
+        batch = cu.numel() - 1
+        n_tiles = tiles.numel() // 2
+        base = qkv.data_ptr()
+        k_ptr = base + hq * 128 * 2
+        v_ptr = base + (hq + hkv) * 128 * 2
+        check(lib().qb_attn_varlen_fwd(base, ld, k_ptr, v_ptr, ld, 0, 0, 0, 256, _p(cu), _p(cu), batch,
+                                       _p(tiles), n_tiles, 0, hq, hkv, 128, scale, _p(out), hq * 128, _p(lse), T,
+                                       _p(err_flag()), stream_ptr()), "qb_attn_varlen_fwd")
+        ctx.save_for_backward(qkv, cu, tiles, out, lse)
+        ctx.cfg = (hq, hkv, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, cu, tiles, out, lse = ctx.saved_tensors
+        hq, hkv, scale = ctx.cfg
+        dout = dout.contiguous()
+        T, ld = qkv.shape
+        dqkv = torch.empty_like(qkv)
+        delta = torch.empty(hq, T, dtype=torch.float32, device=qkv.device)
+        b = qkv.data_ptr()
+        db = dqkv.data_ptr()
+        koff, voff = hq * 128 * 2, (hq + hkv) * 128 * 2
+        check(lib().qb_attn_varlen_bwd(b, b + koff, b + voff, ld, _p(out), _p(dout), hq * 128, _p(lse), _p(cu),
+                                       cu.numel() - 1, _p(tiles), tiles.numel() // 2, hq, hkv, 128, scale, T,
+                                       _p(delta), db, db + koff, db + voff, _p(err_flag()), stream_ptr()),
+              "qb_attn_varlen_bwd")
+        return dqkv, None, None, None, None, None
+
+
+def attention_packed(qkv_rot, cu_seqlens, tiles, hq, hkv, scale):
+    """Causal attention over packed sequences (training path).
+
+    qkv_rot: [T, (hq+2hkv)*128] with rotated q/k and v; cu_seqlens int32 [B+1];
+    tiles: int32 from :func:`build_tiles` on the sequence lengths.  Returns [T, hq*128].
+    """
+    _cuda(qkv_rot, cu_seqlens, tiles)
+    return _AttnPacked.apply(qkv_rot.contiguous(), cu_seqlens, tiles, hq, hkv, scale)
+
+
+def attention_paged_prefill(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, block_tables,
+                            scale, tiles=None, hkv=None):
+    """flash_attn_varlen_func(q, k_cache, v_cache, ..., causal=True, block_table=) equivalent.
+
+    q: [Tq, hq, 128]; caches [num_blocks, 256, hkv, 128]; returns [Tq, hq, 128].
+    """
+    _cuda(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables)
+    Tq, hq, D = q.shape
+    num_blocks, page, hkv_c, _ = k_cache.shape
+    out = torch.empty_like(q)
+    batch = cu_seqlens_q.numel() - 1
+    tps = (int(max_seqlen_q) + 63) // 64
+    n_tiles = 0 if tiles is None else tiles.numel() // 2
+    check(lib().qb_attn_varlen_fwd(_p(q), hq * D, _p(k_cache), _p(v_cache), 0, _p(block_tables),
+                                   block_tables.stride(0), num_blocks, page, _p(cu_seqlens_q), _p(cu_seqlens_k),
+                                   batch, _p(tiles), n_tiles, tps, hq, hkv_c, D, scale, _p(out), hq * D, 0, Tq,
+                                   _p(err_flag()), stream_ptr()), "qb_attn_varlen_fwd")
+    return out
+
+
+def decode_split_plan(batch: int, hkv: int, max_ctx: int, sm_count: int = 148) -> tuple[int, int]:
+    """(split_tokens, max_splits) for the paged decode kernel: enough CTAs to cover the GPU
+    at least twice, at most one split per 64 tokens."""
+    want = max(1, math.ceil(4 * sm_count / max(1, batch * hkv)))
+    max_splits = max(1, min(want, math.ceil(max_ctx / 64)))
+    split_tokens = math.ceil(math.ceil(max_ctx / max_splits) / 64) * 64
+    max_splits = math.ceil(max_ctx / split_tokens)
+    return split_tokens, max_splits
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_tables, seqlens, scale, seqlen_add=1,
+                           split_tokens=None, max_splits=None, workspace=None, max_ctx=None):
+    """flash_attn_with_kvcache(q[:,None], k_cache, v_cache, cache_seqlens=seqlens+seqlen_add,
+    block_table=block_tables, causal=True) equivalent; q [B, hq, 128] -> [B, hq, 128]."""
+    _cuda(q, k_cache, v_cache, block_tables, seqlens)
+    B, hq, D = q.shape
+    num_blocks, page, hkv, _ = k_cache.shape
+    if split_tokens is None:
+        if max_ctx is None:
+            max_ctx = block_tables.shape[1] * page
+        split_tokens, max_splits = decode_split_plan(B, hkv, max_ctx)
+    out = torch.empty_like(q)
+    if max_splits > 1 and workspace is None:
+        nbytes = lib().qb_paged_decode_workspace_bytes(B, hq, D, max_splits)
+        workspace = torch.empty(nbytes // 4, dtype=torch.float32, device=q.device)
+    check(lib().qb_paged_decode_attn(_p(q), _p(k_cache), _p(v_cache), num_blocks, page, _p(block_tables),
+                                     block_tables.stride(0), _p(seqlens), seqlen_add, B, hq, hkv, D, scale,
+                                     split_tokens, max_splits, _p(workspace) if max_splits > 1 else 0, _p(out),
+                                     _p(err_flag()), stream_ptr()), "qb_paged_decode_attn",
+          kernels=2 if max_splits > 1 else 1)
+    return out
+
+
+# ---------------------------------------------------------------- MLP / adds / linear
+class _SiluMul(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        T, two_i = gu.shape
+        out = torch.empty(T, two_i // 2, dtype=gu.dtype, device=gu.device)
+        check(lib().qb_silu_mul_fwd(_p(gu), T, two_i // 2, _p(out), stream_ptr()), "qb_silu_mul_fwd")
+        ctx.save_for_backward(gu)
+        return out
+
+    @staticmethod
+    def backward(ctx, d):
+        (gu,) = ctx.saved_tensors
+        d = d.contiguous()
+        dgu = torch.empty_like(gu)
+        check(lib().qb_silu_mul_bwd(_p(d), _p(gu), gu.shape[0], gu.shape[1] // 2, _p(dgu), stream_ptr()),
+              "qb_silu_mul_bwd")
+        return dgu
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    _cuda(gate_up)
+    gate_up = gate_up.contiguous()
+    if torch.is_grad_enabled() and gate_up.requires_grad:
+        return _SiluMul.apply(gate_up)
+    T, two_i = gate_up.shape
+    out = torch.empty(T, two_i // 2, dtype=gate_up.dtype, device=gate_up.device)
+    check(lib().qb_silu_mul_fwd(_p(gate_up), T, two_i // 2, _p(out), stream_ptr()), "qb_silu_mul_fwd")
+    return out
+
+
+class _Add(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b):
+        out = torch.empty_like(a)
+        check(lib().qb_add_bf16(_p(a), _p(b), _p(out), a.numel(), stream_ptr()), "qb_add_bf16")
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, g
+
+
+def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """bf16 ``a + b`` (the reference's residual adds)."""
+    _cuda(a, b)
+    a, b = a.contiguous(), b.contiguous()
+    if torch.is_grad_enabled() and (a.requires_grad or b.requires_grad):
+        return _Add.apply(a, b)
+    out = torch.empty_like(a)
+    check(lib().qb_add_bf16(_p(a), _p(b), _p(out), a.numel(), stream_ptr()), "qb_add_bf16")
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` for nn.Linear weights [out, in] (bf16)."""
+    return F.linear(x, w)
+
+
+# ---------------------------------------------------------------- log-prob / sampling
+def _logits_chunk(h, w):
+    return F.linear(h, w)
+
+
+def logprob_forward(h, weight, targets, dest=None, out=None, out_size=None, chunk_rows=4096, save_lse=True):
+    """Token log-probs of ``targets`` under ``lm_head(h)`` without materialising all logits.
+
+    Rows are processed ``chunk_rows`` at a time: a bf16 logits chunk is produced and
+    reduced by ``qb_logprob_fwd`` (fp32 log-sum-exp + gather).  ``dest`` (int64) scatters
+    row i to ``out[dest[i]]``; without it ``out`` is [n].  Returns (out, lse[n]).
+    """
+    _cuda(h, weight, targets)
+    n = h.shape[0]
+    V = weight.shape[0]
+    if out is None:
+        size = n if out_size is None else out_size
+        out = (torch.zeros if dest is not None else torch.empty)(size, dtype=torch.float32, device=h.device)
+    lse = torch.empty(n, dtype=torch.float32, device=h.device)
+    L = lib()
+    for r0 in range(0, n, chunk_rows):
+        r1 = min(n, r0 + chunk_rows)
+        logits = _logits_chunk(h[r0:r1], weight)
+        # without dest, row i of the chunk lands at out[r0 + i]
+        out_ptr = _p(out) if dest is not None else _p(out) + 4 * r0
+        check(L.qb_logprob_fwd(_p(logits), r1 - r0, V, logits.stride(0), _p(targets) + 8 * r0,
+                               0 if dest is None else _p(dest) + 8 * r0, out_ptr, _p(lse) + 4 * r0,
+                               _p(err_flag()), stream_ptr()), "qb_logprob_fwd")
+    return out, lse
+
+
+def logprob_backward(h, weight, targets, lse, grad, dest=None, chunk_rows=4096, dweight=None):
+    """Gradient of :func:`logprob_forward` w.r.t. ``h`` and ``weight`` (recomputes logits chunks).
+
+    ``grad`` is indexed like the forward's ``out`` (through ``dest``).  Returns (dh, dweight)
+    with dweight accumulated into the given fp32 tensor when provided.
+    """
+    n, V = h.shape[0], weight.shape[0]
+    dh = torch.empty_like(h)
+    if dweight is None:
+        dweight = torch.zeros(weight.shape, dtype=torch.float32, device=h.device)
+    L = lib()
+    for r0 in range(0, n, chunk_rows):
+        r1 = min(n, r0 + chunk_rows)
+        hc = h[r0:r1]
+        logits = _logits_chunk(hc, weight)
+        grad_ptr = _p(grad) if dest is not None else _p(grad) + 4 * r0
+        check(L.qb_logprob_bwd(_p(logits), r1 - r0, V, logits.stride(0), _p(targets) + 8 * r0,
+                               0 if dest is None else _p(dest) + 8 * r0, _p(lse) + 4 * r0, grad_ptr,
+                               _p(err_flag()), stream_ptr()), "qb_logprob_bwd")
+        torch.mm(logits, weight, out=dh[r0:r1])
+        # dW += dlogits^T h with fp32 output (one bf16 rounding at the very end)
+        dweight = torch.addmm(dweight, logits.t(), hc, out_dtype=torch.float32)
+    return dh, dweight
+
+
+class _LogProb(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, weight, targets, chunk_rows):
+        out, lse = logprob_forward(h, weight, targets, chunk_rows=chunk_rows)
+        ctx.save_for_backward(h, weight, targets, lse)
+        ctx.chunk_rows = chunk_rows
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        h, weight, targets, lse = ctx.saved_tensors
+        dh, dw = logprob_backward(h, weight, targets, lse, g.contiguous().float(), chunk_rows=ctx.chunk_rows)
+        return dh, dw.to(weight.dtype), None, None
+
+
+def logprob(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, chunk_rows: int = 4096):
+    """log_softmax(h @ weight.T).gather(targets) in fp32, differentiable w.r.t. h and weight."""
+    h = h.contiguous()
+    targets = targets.reshape(-1).long().contiguous()
+    if torch.is_grad_enabled() and (h.requires_grad or weight.requires_grad):
+        return _LogProb.apply(h, weight, targets, chunk_rows)
+    return logprob_forward(h, weight, targets, chunk_rows=chunk_rows)[0]
+
+
+def sample(logits: torch.Tensor, temperature: float, top_k, seed: int, rng_state: torch.Tensor,
+           tokens=None, logp=None):
+    """Sample one token per row of bf16 ``logits`` [n, V]; returns (tokens int64, logp fp32).
+
+    ``rng_state`` is a 2-element int64 device tensor {Philox counter, seed mix}, read at run
+    time so the call can sit inside a CUDA graph.  ``top_k`` None keeps the full vocabulary.
+    """
+    offset = rng_state
+    _cuda(logits, offset)
+    if offset.numel() < 2:
+        raise ValueError("rng_state must hold {counter, seed}")
+    n, V = logits.shape
+    if tokens is None:
+        tokens = torch.empty(n, dtype=torch.long, device=logits.device)
+    if logp is None:
+        logp = torch.empty(n, dtype=torch.float32, device=logits.device)
+    k = 0 if top_k is None else int(top_k)
+    check(lib().qb_sample(_p(logits), n, V, logits.stride(0), float(temperature), k, int(seed) & (2**64 - 1),
+                          _p(offset), _p(tokens), _p(logp), _p(err_flag()), stream_ptr()), "qb_sample")
+    return tokens, logp
+
+
+# ---------------------------------------------------------------- GRPO
+def grpo_advantage(rewards: torch.Tensor, group_ids: torch.Tensor) -> torch.Tensor:
+    _cuda(rewards, group_ids)
+    rewards = rewards.float().contiguous()
+    gids = group_ids.long().contiguous()
+    adv = torch.empty_like(rewards)
+    check(lib().qb_grpo_advantage(_p(rewards), _p(gids), rewards.numel(), _p(adv), stream_ptr()),
+          "qb_grpo_advantage")
+    return adv
+
+
+_WS: dict[tuple, torch.Tensor] = {}
+
+
+def grpo_workspace(n_rows: int, device) -> torch.Tensor:
+    """Zero-initialised scratch for the deterministic GRPO reductions (kept zeroed by the kernels)."""
+    nbytes = lib().qb_grpo_workspace_bytes(n_rows)
+    key = (torch.device(device).index, nbytes)
+    ws = _WS.get(key)
+    if ws is None:
+        ws = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=device)
+        _WS[key] = ws
+    return ws
+
+
+def mask_sum(mask: torch.Tensor, out=None) -> torch.Tensor:
+    _cuda(mask)
+    mask = mask.float().contiguous()
+    if out is None:
+        out = torch.empty(1, dtype=torch.float32, device=mask.device)
+    ws = grpo_workspace(1, mask.device)
+    check(lib().qb_mask_sum(_p(mask), mask.numel(), _p(out), _p(ws), stream_ptr()), "qb_mask_sum")
+    return out
+
+
+def grpo_loss_raw(rewards, group_ids, new_lp, old_lp, mask, *, ref_lp=None, mask_total=None, clip_eps=0.2,
+                  beta=0.0, row_begin=0, row_end=None, grad_new=None, loss_out=None, adv_out=None,
+                  grad_scale=None):
+    """Direct call of ``qb_grpo_loss`` on [N, S] fp32 tensors; see the header for semantics."""
+    _cuda(rewards, new_lp, old_lp, mask)
+    N, S = new_lp.shape
+    row_end = N if row_end is None else row_end
+    ws = grpo_workspace(N, new_lp.device)
+    check(lib().qb_grpo_loss(_p(rewards), _p(group_ids), N, S, row_begin, row_end, _p(new_lp), _p(old_lp),
+                             _p(ref_lp), _p(mask), _p(mask_total), float(clip_eps), float(beta), _p(grad_scale),
+                             _p(grad_new), _p(loss_out), _p(adv_out), _p(ws), stream_ptr()), "qb_grpo_loss",
+          kernels=1 if mask_total is not None else 2)
+
+
+class _GRPOLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, new_lp, old_lp, mask, rewards, group_ids, ref_lp, clip_eps, beta):
+        grad = torch.empty_like(new_lp)
+        loss = torch.zeros(3, dtype=torch.float32, device=new_lp.device)
+        grpo_loss_raw(rewards, group_ids, new_lp, old_lp, mask, ref_lp=ref_lp, clip_eps=clip_eps, beta=beta,
+                      grad_new=grad, loss_out=loss)
+        ctx.save_for_backward(grad)
+        return loss[0]
+
+    @staticmethod
+    def backward(ctx, g):
+        (grad,) = ctx.saved_tensors
+        return grad * g, None, None, None, None, None, None, None
+
+
+def grpo_loss(new_lp, old_lp, mask, rewards, group_ids, ref_lp=None, clip_eps=0.2, beta=0.0):
+    """Fused advantage + clipped surrogate (+ beta * k3 KL) masked token-mean; differentiable in new_lp."""
+    f = lambda t: None if t is None else t.float().contiguous()
+    return _GRPOLoss.apply(f(new_lp), f(old_lp), f(mask), f(rewards), group_ids.long().contiguous(), f(ref_lp),
+                           clip_eps, beta)

@@ -1,0 +1,320 @@
+"""Kernel-level parity: every CUDA entry point against the CPU oracle on seeded inputs.
+
+Tolerances: bf16 outputs within a few bf16 ulps (atol/rtol 1e-2 relative to unit-scale
+data), fp32 reductions within 1e-5..2e-3 relative as stated per test.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ref_ops as R
+from qwen3_naive_inference_b200 import ops
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def close_bf16(a, b, tol=2e-2):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs().max().item()
+    scale = b.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max abs err {err} vs scale {scale}"
+
+
+def test_embedding(cuda):
+    g = gen(0)
+    W = torch.randn(1000, 256, generator=g).to(BF)
+    ids = torch.randint(0, 1000, (77,), generator=g)
+    out = ops.embedding(ids.to(cuda), W.to(cuda))
+    assert torch.equal(out.cpu(), W[ids])
+    Wd = W.to(cuda).requires_grad_(True)
+    y = ops.embedding(ids.to(cuda), Wd)
+    gy = torch.randn(77, 256, generator=g).to(BF)
+    y.backward(gy.to(cuda))
+    ref = torch.zeros(1000, 256).index_add_(0, ids, gy.float()).to(BF)
+    close_bf16(Wd.grad, ref, 1e-2)
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1024), (37, 1024), (300, 256), (64, 2048)])
+def test_rmsnorm(cuda, rows, cols):
+    g = gen(rows)
+    x = torch.randn(rows, cols, generator=g).to(BF)
+    w = (1 + 0.1 * torch.randn(cols, generator=g)).to(BF)
+    y = ops.rmsnorm(x.to(cuda), w.to(cuda), 1e-6)
+    close_bf16(y, R.rms_norm(x, w, 1e-6), 8e-3)
+    r = torch.randn(rows, cols, generator=g).to(BF)
+    y2, r2 = ops.add_rmsnorm(x.to(cuda), r.clone().to(cuda), w.to(cuda), 1e-6)
+    ry, rr = R.add_rms_norm(x, r, w, 1e-6)
+    assert torch.equal(r2.cpu(), rr)
+    close_bf16(y2, ry, 8e-3)
+
+
+def test_rmsnorm_backward(cuda):
+    g = gen(3)
+    x = torch.randn(129, 1024, generator=g).to(BF)
+    w = (1 + 0.1 * torch.randn(1024, generator=g)).to(BF)
+    dy = torch.randn(129, 1024, generator=g).to(BF)
+    xr, wr = x.float().requires_grad_(True), w.float().requires_grad_(True)
+    yr = (xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6)) * wr
+    yr.backward(dy.float())
+    xd, wd = x.to(cuda).requires_grad_(True), w.to(cuda).requires_grad_(True)
+    ops.rmsnorm(xd, wd, 1e-6).backward(dy.to(cuda))
+    close_bf16(xd.grad, xr.grad, 1e-2)
+    close_bf16(wd.grad, wr.grad, 1e-2)
+
+
+def _qkv_case(T, seed, hq=16, hkv=8):
+    g = gen(seed)
+    qkv = torch.randn(T, (hq + 2 * hkv) * 128, generator=g).to(BF)
+    pos = torch.randint(0, 4000, (T,), generator=g)
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(BF)
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(BF)
+    return qkv, pos, qw, kw
+
+
+def test_qk_norm_rope_and_store(cuda):
+    T, hq, hkv = 45, 16, 8
+    qkv, pos, qw, kw = _qkv_case(T, 5)
+    cs = R.rope_cache(128, 4096, 1e6)
+    q_ref, k_ref, v_ref = R.qk_norm_rope(qkv, pos, cs, qw, kw, 1e-6, hq, hkv)
+    out = ops.qk_norm_rope(qkv.to(cuda), pos.to(cuda), cs.to(cuda), qw.to(cuda), kw.to(cuda), 1e-6, hq, hkv)
+    out = out.cpu()
+    close_bf16(out[:, :hq * 128].reshape(T, hq, 128), q_ref, 1e-2)
+    close_bf16(out[:, hq * 128:(hq + hkv) * 128].reshape(T, hkv, 128), k_ref, 1e-2)
+    assert torch.equal(out[:, (hq + hkv) * 128:].reshape(T, hkv, 128), v_ref)
+    # paged store: slots with a -1 hole
+    nslots = 3 * 256
+    slots = torch.randperm(nslots, generator=gen(6))[:T].to(torch.int32)
+    slots[3] = -1
+    kc = torch.zeros(3, 256, hkv, 128, dtype=BF)
+    vc = torch.zeros_like(kc)
+    kcd, vcd = kc.to(cuda), vc.to(cuda)
+    q = ops.qk_norm_rope_store(qkv.to(cuda), pos.to(cuda), cs.to(cuda), qw.to(cuda), kw.to(cuda), 1e-6, hq, hkv,
+                               kcd, vcd, slots.to(cuda))
+    close_bf16(q.cpu(), q_ref, 1e-2)
+    R.store_kvcache(k_ref, v_ref, kc.view(-1, hkv, 128), vc.view(-1, hkv, 128), slots)
+    close_bf16(kcd.cpu(), kc, 1e-2)
+    assert torch.equal(vcd.cpu(), vc)
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize("rope_grad", [True, False])
+def test_qk_norm_rope_backward(cuda, rope_grad):
+    T, hq, hkv = 33, 16, 8
+    qkv, pos, qw, kw = _qkv_case(T, 9)
+    cs = R.rope_cache(128, 4096, 1e6)
+    dout = torch.randn(T, (hq + 2 * hkv) * 128, generator=gen(10)).to(BF)
+    # fp32 autograd restatement of norm -> (bf16 round, straight-through) -> rope
+    x = qkv.float().requires_grad_(True)
+    qwf, kwf = qw.float().requires_grad_(True), kw.float().requires_grad_(True)
+    q = x[:, :hq * 128].reshape(T, hq, 128)
+    k = x[:, hq * 128:(hq + hkv) * 128].reshape(T, hkv, 128)
+    v = x[:, (hq + hkv) * 128:]
+    nq = (q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + 1e-6)) * qwf
+    nk = (k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + 1e-6)) * kwf
+    rq, rk = R.apply_rope(nq, pos, cs, torch.float32), R.apply_rope(nk, pos, cs, torch.float32)
+    if not rope_grad:
+        rq, rk = rq.detach(), rk.detach()
+    y = torch.cat([rq.reshape(T, -1), rk.reshape(T, -1), v], dim=1)
+    y.backward(dout.float())
+    xd = qkv.to(cuda).requires_grad_(True)
+    qwd, kwd = qw.to(cuda).requires_grad_(True), kw.to(cuda).requires_grad_(True)
+    yd = ops.qk_norm_rope(xd, pos.to(cuda), cs.to(cuda), qwd, kwd, 1e-6, hq, hkv, rope_grad=rope_grad)
+    yd.backward(dout.to(cuda))
+    close_bf16(xd.grad, x.grad, 1e-2)
+    if rope_grad:
+        close_bf16(qwd.grad, qwf.grad, 1e-2)
+        close_bf16(kwd.grad, kwf.grad, 1e-2)
+    else:
+        assert qwd.grad is None and kwd.grad is None
+        assert xd.grad[:, :(hq + hkv) * 128].abs().max().item() == 0.0
+
+
+def test_silu_mul(cuda):
+    g = gen(11)
+    gu = torch.randn(19, 2 * 3072, generator=g).to(BF)
+    close_bf16(ops.silu_mul(gu.to(cuda)), R.silu_mul(gu), 1e-2)
+    d = torch.randn(19, 3072, generator=g).to(BF)
+    x = gu.float().requires_grad_(True)
+    (torch.nn.functional.silu(x[:, :3072]) * x[:, 3072:]).backward(d.float())
+    xd = gu.to(cuda).requires_grad_(True)
+    ops.silu_mul(xd).backward(d.to(cuda))
+    close_bf16(xd.grad, x.grad, 1e-2)
+
+
+def _paged_case(lens, seed, hkv=8, extra_pages=3):
+    """Random caches with pages shuffled in a pool; block table per sequence."""
+    g = gen(seed)
+    pages_per = [math.ceil(L / 256) for L in lens]
+    n_pages = sum(pages_per) + extra_pages
+    perm = torch.randperm(n_pages, generator=g)
+    kc = torch.randn(n_pages, 256, hkv, 128, generator=g).to(BF)
+    vc = torch.randn(n_pages, 256, hkv, 128, generator=g).to(BF)
+    width = max(pages_per)
+    bt = torch.full((len(lens), width), -1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(pages_per):
+        bt[i, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    return kc, vc, bt
+
+
+@pytest.mark.parametrize("lens", [[1, 2, 255, 256, 257, 1000], [64] * 3 + [4097], [1], [8192, 1024, 3000]])
+def test_paged_decode(cuda, lens):
+    B, hq, hkv = len(lens), 16, 8
+    kc, vc, bt = _paged_case(lens, len(lens) + lens[-1])
+    q = torch.randn(B, hq, 128, generator=gen(1)).to(BF)
+    ctx = torch.tensor(lens, dtype=torch.int32) - 1  # context_lens; kernel adds 1
+    ref = R.paged_decode(q, kc, vc, bt, ctx + 1, 128 ** -0.5)
+    for plan in [None, (64, math.ceil(max(lens) / 64)), (8192, 1)]:
+        kw = {} if plan is None else {"split_tokens": plan[0], "max_splits": plan[1]}
+        out = ops.paged_decode_attention(q.to(cuda), kc.to(cuda), vc.to(cuda), bt.to(cuda), ctx.to(cuda),
+                                         128 ** -0.5, **kw)
+        close_bf16(out, ref, 2e-2)
+    ops.check_device_errors()
+
+
+def test_paged_decode_bad_page_sets_error(cuda):
+    kc, vc, bt = _paged_case([300], 3)
+    bt[0, 1] = 10_000  # out of range: kernel must skip and flag, not fault
+    q = torch.randn(1, 16, 128).to(BF)
+    ops.paged_decode_attention(q.to(cuda), kc.to(cuda), vc.to(cuda), bt.to(cuda),
+                               torch.tensor([299], dtype=torch.int32).to(cuda), 128 ** -0.5)
+    with pytest.raises(ops.NativeError):
+        ops.check_device_errors()
+
+
+@pytest.mark.parametrize("qk", [[(5, 5), (1, 300), (130, 700), (1, 1)], [(2048, 2048)], [(64, 64), (65, 320)]])
+def test_paged_prefill(cuda, qk):
+    hq, hkv = 16, 8
+    lq = [a for a, _ in qk]
+    lk = [b for _, b in qk]
+    kc, vc, bt = _paged_case(lk, sum(lk))
+    q = torch.randn(sum(lq), hq, 128, generator=gen(2)).to(BF)
+    cu_q = torch.tensor([0] + list(np.cumsum(lq)), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(np.cumsum(lk)), dtype=torch.int32)
+    ref = R.paged_attention(q, kc, vc, cu_q, cu_k, bt, 128 ** -0.5)
+    for tiles in [None, torch.from_numpy(ops.build_tiles(lq))]:
+        out = ops.attention_paged_prefill(q.to(cuda), kc.to(cuda), vc.to(cuda), cu_q.to(cuda), cu_k.to(cuda),
+                                          max(lq), bt.to(cuda), 128 ** -0.5,
+                                          tiles=None if tiles is None else tiles.to(cuda))
+        close_bf16(out, ref, 2e-2)
+
+
+@pytest.mark.parametrize("lens", [[1, 63, 64, 65, 200], [513]])
+def test_attention_packed_fwd_bwd(cuda, lens):
+    hq, hkv = 16, 8
+    T = sum(lens)
+    g = gen(T)
+    qkv = torch.randn(T, (hq + 2 * hkv) * 128, generator=g).to(BF)
+    dout = torch.randn(T, hq * 128, generator=g).to(BF)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    tiles = torch.from_numpy(ops.build_tiles(lens))
+    # fp32 autograd reference
+    x = qkv.float().requires_grad_(True)
+    outs = []
+    for b in range(len(lens)):
+        s0, s1 = int(cu[b]), int(cu[b + 1])
+        L = s1 - s0
+        q = x[s0:s1, :hq * 128].reshape(L, hq, 128)
+        k = x[s0:s1, hq * 128:(hq + hkv) * 128].reshape(L, hkv, 128).repeat_interleave(2, 1)
+        v = x[s0:s1, (hq + hkv) * 128:].reshape(L, hkv, 128).repeat_interleave(2, 1)
+        s = torch.einsum("qhd,khd->hqk", q, k) * 128 ** -0.5
+        s = s.masked_fill(torch.triu(torch.ones(L, L), 1).bool()[None], float("-inf"))
+        outs.append(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(L, -1))
+    y = torch.cat(outs)
+    y.backward(dout.float())
+    xd = qkv.to(cuda).requires_grad_(True)
+    yd = ops.attention_packed(xd, cu.to(cuda), tiles.to(cuda), hq, hkv, 128 ** -0.5)
+    close_bf16(yd, y.detach(), 2e-2)
+    yd.backward(dout.to(cuda))
+    close_bf16(xd.grad, x.grad, 3e-2)
+
+
+def test_logprob_fwd_bwd(cuda):
+    g = gen(21)
+    n, H, V = 300, 256, 5000
+    h = (torch.randn(n, H, generator=g)).to(BF)
+    W = (torch.randn(V, H, generator=g) * 0.1).to(BF)
+    t = torch.randint(0, V, (n,), generator=g)
+    gl = torch.randn(n, generator=g)
+    hr, Wr = h.float().requires_grad_(True), W.float().requires_grad_(True)
+    lg = (hr @ Wr.t())
+    lp = torch.log_softmax(lg, -1).gather(-1, t[:, None]).squeeze(-1)
+    lp.backward(gl)
+    hd, Wd = h.to(cuda).requires_grad_(True), W.to(cuda).requires_grad_(True)
+    lpd = ops.logprob(hd, Wd, t.to(cuda), chunk_rows=128)
+    assert lpd.dtype == torch.float32
+    err = (lpd.cpu() - lp.detach()).abs().max().item()
+    assert err < 2e-3 * lp.detach().abs().max().item() + 2e-2, err
+    lpd.backward(gl.to(cuda))
+    cos = lambda a, b: torch.nn.functional.cosine_similarity(a.float().cpu().reshape(-1), b.float().reshape(-1), 0)
+    assert 1 - cos(hd.grad, hr.grad) < 1e-2
+    assert 1 - cos(Wd.grad, Wr.grad) < 1e-2
+
+
+def test_sample_greedy_exact(cuda):
+    g = gen(31)
+    logits = torch.randn(64, 4096, generator=g).to(BF)
+    logits[5, 17] = logits[5, 99] = 50.0  # tie: lowest index wins
+    rng = torch.tensor([0, 0], dtype=torch.int64, device=cuda)
+    tok, lp = ops.sample(logits.to(cuda), 1.0, 1, 123, rng)
+    exp = logits.float().argmax(-1)
+    assert torch.equal(tok.cpu(), exp)
+    assert tok[5].item() == 17
+    assert torch.all(lp.cpu() == 0)
+
+
+@pytest.mark.parametrize("top_k,temp", [(None, 1.0), (20, 0.8), (3, 1.3)])
+def test_sample_distribution(cuda, top_k, temp):
+    V, draws = 512, 6000
+    base = torch.randn(V, generator=gen(41)).to(BF) * 2
+    logits = base[None].repeat(draws, 1)
+    rng = torch.tensor([7, 99], dtype=torch.int64, device=cuda)
+    tok, lp = ops.sample(logits.to(cuda), temp, top_k, 2024, rng)
+    probs, logps = R.sample_distribution(base[None], temp, top_k)
+    probs, logps = probs[0], logps[0]
+    tok = tok.cpu()
+    # log-prob of each sampled token equals the oracle's log_softmax at that token
+    assert torch.allclose(lp.cpu(), logps[tok], atol=2e-5, rtol=1e-5)
+    assert torch.all(probs[tok] > 0)  # never outside the top-k set
+    counts = torch.bincount(tok, minlength=V).float()
+    exp = probs * draws
+    keep = exp > 5
+    chi2 = (((counts - exp) ** 2) / exp.clamp_min(1e-9))[keep].sum().item()
+    dof = int(keep.sum().item()) - 1
+    assert chi2 < dof + 6 * math.sqrt(2 * max(dof, 1)) + 10, (chi2, dof)
+
+
+def test_grpo_advantage_and_loss(cuda):
+    g = gen(51)
+    G, n_groups, S = 4, 6, 40
+    N = G * n_groups
+    rewards = torch.bernoulli(torch.full((N,), 0.5), generator=g)
+    rewards[:G] = 1.0  # a constant group: advantage 0
+    gids = torch.arange(n_groups).repeat_interleave(G)
+    new = -torch.rand(N, S, generator=g) * 5
+    old = new + 0.05 * torch.randn(N, S, generator=g)
+    ref = new + 0.05 * torch.randn(N, S, generator=g)
+    mask = torch.zeros(N, S)
+    for i in range(N):
+        L = int(torch.randint(1, S + 1, (1,), generator=g))
+        mask[i, S - L:] = 1
+    adv = ops.grpo_advantage(rewards.to(cuda), gids.to(cuda)).cpu()
+    adv_ref = R.grpo_advantage(rewards, gids)
+    assert torch.allclose(adv, adv_ref, rtol=1e-6, atol=1e-6)
+    for beta, rp in [(0.0, None), (0.04, ref)]:
+        loss_ref, grad_ref, _ = R.grpo_loss_and_grad(rewards, gids, new, old, mask, ref=rp, beta=beta)
+        nd = new.to(cuda).requires_grad_(True)
+        loss = ops.grpo_loss(nd, old.to(cuda), mask.to(cuda), rewards.to(cuda), gids.to(cuda),
+                             None if rp is None else rp.to(cuda), 0.2, beta)
+        loss.backward()
+        assert abs(loss.item() - loss_ref.item()) <= 2e-3 * abs(loss_ref.item()) + 1e-6
+        assert torch.allclose(nd.grad.cpu(), grad_ref, rtol=1e-4, atol=1e-7)
