@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--microbatch-tokens", type=int, default=32768)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the config-3 paged-decode microbenchmark (for kernel profiling)")
+    ap.add_argument("--decode-batch", type=int, default=256, help="batch of the decode microbenchmark")
     return ap.parse_args()
 
 
@@ -109,12 +112,12 @@ def make_prompts(args, rank, step, device=None):
     return prompts
 
 
-def decode_microbench(torch, ops, device, n_iter=20):
+def decode_microbench(torch, ops, device, n_iter=20, batch=256):
     """Config 3: paged decode attention, batch 256, context U[1k, 8k], 16q/8kv, head_dim 128,
     bf16 K/V ~ N(0,1) in 256-token pages randomly permuted in a pool 1.25x the need.
     Returns (kernel ms per launch, algorithmic bytes per launch)."""
     g = torch.Generator().manual_seed(3)
-    B, hq, hkv, D = 256, 16, 8, 128
+    B, hq, hkv, D = batch, 16, 8, 128
     ctx = torch.randint(1024, 8193, (B,), generator=g)
     pages = [(int(c) + 255) // 256 for c in ctx]
     pool = int(sum(pages) * 1.25)
@@ -280,6 +283,7 @@ def run_ours(args):
         else:
             host = [[p.to(dev) for p in ps] for ps in host]
             torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("timed")  # ncu --nvtx --nvtx-include "timed/" selects this region
         a.record(st)
         wall0 = time.perf_counter()
         for j in range(n):
@@ -291,6 +295,7 @@ def run_ours(args):
             tokens += out["tokens"]
             d2h += 3 * 4 + out["completion_tokens"] * 12  # loss[3] + sampled tokens/log-probs read back
         b.record(st)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         ms = a.elapsed_time(b)
         wall = time.perf_counter() - wall0
@@ -348,9 +353,22 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_decode_only(batch):
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    ms, nbytes = decode_microbench(torch, ops, dev, n_iter=3, batch=batch)
+    print(json.dumps({"kernel": "paged_decode_kernel", "case": f"config 3 shapes, batch {batch}",
+                      "ms_per_launch": ms, "algorithmic_bytes": nbytes,
+                      "achieved_gbs": nbytes / (ms / 1000) / 1e9}), flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.decode_only:
+        run_decode_only(args.decode_batch)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -226,6 +226,16 @@ int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, const float* t
 int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace,
                 qb_stream_t stream);
 
+/* ---------------------------------------------------------------- dense projections
+ * bf16 GEMM on the sm_100a tensor cores (tcgen05.mma, TMEM accumulators, TMA loads);
+ * replaces the cuBLAS nn.Linear calls of qkv_proj, o_proj, gate_up_proj, down_proj and the
+ * tied lm_head (qwen3_naive.py:427-428, :692-693, :826):
+ *   C[M, N] = A[M, K] . B[N, K]^T       A, B bf16 row-major with K contiguous (lda, ldb >= K)
+ * mode 0: C bf16; mode 1: C fp32; mode 2: C fp32 += A.B^T.  K % 64 == 0, leading
+ * dimensions % 8 == 0, pointers 16-byte aligned. */
+int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                 int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream);
+
 /* ---------------------------------------------------------------- optimizer helpers
  * dst (bf16) = bf16(src fp32); used to hand fp32-accumulated gradients to the
  * reference's torch AdamW (qwen3_grpo_train.py:327) as bf16 .grad tensors. */

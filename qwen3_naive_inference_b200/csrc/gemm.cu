@@ -1,0 +1,393 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   C[M, N] (=|+=) A[M, K] . B[N, K]^T      A, B bf16 K-major (nn.Linear weight layout)
+//
+// Persistent kernel, one CTA per SM, 192 threads:
+//   warp 0     TMA producer: 128x64 A and BNx64 B tiles into a STAGES-deep ring of
+//              128B-swizzled shared-memory stages (mbarrier full/empty pairs);
+//   warp 1     allocates 2*BN TMEM columns; one thread issues tcgen05.mma (M=128,
+//              N=BN, K=16) into a double-buffered fp32 accumulator and commits
+//              stage releases / tile completion to mbarriers;
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (each warp owns 32 TMEM lanes =
+//              32 rows), conversion and global stores, then release of the buffer so
+//              the next tile's MMAs overlap this tile's stores.
+// Every mbarrier wait is bounded: on timeout the kernel raises QB_DEVERR_TIMEOUT, all
+// roles leave their loops, the producer waits (bounded) for its own copies, TMEM is
+// freed and the kernel returns.  No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr int THREADS = 192;
+// A wait that has not completed after this many SM clock cycles (~2 s at 1.9 GHz) is
+// declared hung.  The bound is on elapsed clock64() time, not on a poll count, because a
+// single try_wait may itself suspend for an implementation-defined interval.
+constexpr long long WAIT_CYCLES = 4000000000ll;
+
+// ---------------------------------------------------------------- PTX helpers
+QB_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+QB_DEVICE void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+QB_DEVICE void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+QB_DEVICE bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false when it gave up (or another role already aborted).
+QB_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 255) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > WAIT_CYCLES) break;
+    }
+  }
+  *abort_flag = 1;
+  qb_set_err(err, QB_DEVERR_TIMEOUT);
+  return false;
+}
+// Bounded wait used on the way out: no abort check, same time limit.
+QB_DEVICE void mbar_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity))
+    if (clock64() - t0 > WAIT_CYCLES) return;
+}
+
+QB_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+QB_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+QB_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 bytes in
+// 8-row (1024-byte) groups: start>>4 | LBO 16 B | SBO 1024 B | version 1 | layout SW128.
+QB_DEVICE uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;            // leading byte offset (16 B, unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset between 8-row groups
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+QB_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+QB_DEVICE void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: lane i receives row (lane base + i), columns [col, col+32).
+QB_DEVICE void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- kernel
+struct GemmParams {
+  void* C;
+  int64_t ldc;
+  int M, N, K;
+  int tiles_m, tiles_n;
+  int* err;
+};
+
+template <int BN, int STAGES, int MODE>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t IDESC = (1u << 4)            // D fp32
+                                    | (1u << 7)          // A bf16
+                                    | (1u << 10)         // B bf16
+                                    | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
+
+template <int BN, int STAGES, int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    GemmParams p) {
+  using Cfg = GemmCfg<BN, STAGES, MODE>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;  // SW128 atoms need 1024-byte alignment
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + STAGES * Cfg::STAGE_BYTES;
+  // barrier block: full[S], empty[S], tfull[2], tempty[2], then tmem base (u32) and abort flag
+  auto full_bar = [&](int s) { return bar0 + 8 * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8 * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8 * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8 * (2 * STAGES + 2 + a); };
+  const uint32_t done_bar = bar0 + 8 * (2 * STAGES + 4);  // completion of every MMA this CTA issued
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + STAGES * Cfg::STAGE_BYTES + 8 * (2 * STAGES + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = p.tiles_m * p.tiles_n;
+  const int kblocks = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4 * 32);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+  }
+  if (warp == 1) {  // TMEM allocation is warp-collective
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(Cfg::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0, last_parity = 0;  // per-stage bit: a load is in flight; its phase parity
+    for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+      const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
+        const uint32_t sa = base + stage * Cfg::STAGE_BYTES, sb = sa + Cfg::A_BYTES;
+        mbar_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
+        tma_load_2d(sa, &tmap_a, kb * BK, m0, full_bar(stage));
+        tma_load_2d(sb, &tmap_b, kb * BK, n0, full_bar(stage));
+        issued |= 1u << stage;
+        last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // never leave with a copy in flight into this CTA's shared memory
+    for (int s = 0; s < STAGES; ++s)
+      if (issued & (1u << s)) mbar_drain(full_bar(s), (last_parity >> s) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+      if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, abort_flag, p.err)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + acc * BN;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = base + stage * Cfg::STAGE_BYTES, sb = sa + Cfg::A_BYTES;
+#pragma unroll
+        for (int j = 0; j < BK / 16; ++j)
+          umma_bf16(d, sw128_kmajor_desc(sa + j * 32), sw128_kmajor_desc(sb + j * 32), Cfg::IDESC,
+                    (kb | j) != 0);
+        umma_commit(empty_bar(stage));  // stage reusable once these MMAs have read it
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      umma_commit(tfull_bar(acc));  // accumulator complete
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    // no MMA may still be reading shared memory or writing TMEM when the CTA leaves
+    umma_commit(done_bar);
+    mbar_drain(done_bar, 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
+      const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, p.err)) break;
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN + c, r);
+        const int col = n0 + c;
+        if (!row_ok || col >= p.N) continue;
+        const bool full = col + 32 <= p.N;
+        if (MODE == 0) {
+          bf16* dst = reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col;
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+              v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+              v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+              v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+              reinterpret_cast<uint4*>(dst)[q] = v;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col + i < p.N) dst[i] = f2bf(__uint_as_float(r[i]));
+          }
+        } else {
+          float* dst = reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc + col;
+          if (full) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                     __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+              if (MODE == 2) {
+                const float4 o = reinterpret_cast<const float4*>(dst)[q];
+                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+              }
+              reinterpret_cast<float4*>(dst)[q] = v;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col + i < p.N) dst[i] = (MODE == 2 ? dst[i] : 0.f) + __uint_as_float(r[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));  // accumulator free for the tile after next
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map: inner dim `inner` (contiguous), outer dim `outer`, row pitch ld elements,
+// box {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
+bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, int MODE>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  using Cfg = GemmCfg<BN, STAGES, MODE>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, STAGES, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM) != cudaSuccess)
+      return qb_launch_status();
+    attr = true;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  gemm_tcgen05_kernel<BN, STAGES, MODE><<<grid, THREADS, Cfg::SMEM, st>>>(ta, tb, p);
+  return qb_launch_status();
+}
+
+inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
+
+}  // namespace
+
+extern "C" int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                            int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream) {
+  QB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && mode >= 0 && mode <= 2);
+  if (M == 0 || N == 0) return QB_OK;
+  if (K % BK != 0 || K == 0) return QB_ERR_UNSUPPORTED;
+  QB_CHECK_ARG(A && B && C && al16(A) && al16(B) && al16(C));
+  QB_CHECK_ARG(lda >= K && ldb >= K && ldc >= N && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0);
+  QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
+  const bool wide = N >= 256;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM)) return QB_ERR_INVALID;
+  if (!make_tmap(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;
+  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), 0, err};
+  cudaStream_t st = (cudaStream_t)stream;
+  if (wide) {
+    p.tiles_n = (int)((N + 255) / 256);
+    if (mode == 0) return launch<256, 4, 0>(ta, tb, p, st);
+    if (mode == 1) return launch<256, 4, 1>(ta, tb, p, st);
+    return launch<256, 4, 2>(ta, tb, p, st);
+  }
+  p.tiles_n = (int)((N + 127) / 128);
+  if (mode == 0) return launch<128, 6, 0>(ta, tb, p, st);
+  if (mode == 1) return launch<128, 6, 1>(ta, tb, p, st);
+  return launch<128, 6, 2>(ta, tb, p, st);
+}

@@ -384,6 +384,22 @@ def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode: int = 0) -> torch.Tensor:
+    """tcgen05 GEMM: ``a @ b.T`` for bf16 a [M, K], b [N, K] (unit stride along K).
+
+    mode 0 -> bf16 result, 1 -> fp32 result, 2 -> ``out += a @ b.T`` in fp32."""
+    _cuda(a, b)
+    if a.dtype != BF16 or b.dtype != BF16 or a.stride(-1) != 1 or b.stride(-1) != 1:
+        raise NativeError("gemm needs bf16 operands with unit stride along K")
+    M, K = a.shape
+    N = b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=BF16 if mode == 0 else torch.float32, device=a.device)
+    check(lib().qb_gemm_bf16(_p(a), a.stride(0), _p(b), b.stride(0), _p(out), out.stride(0), M, N, K, mode,
+                             _p(err_flag()), stream_ptr()), "qb_gemm_bf16")
+    return out
+
+
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """``x @ w.T`` for nn.Linear weights [out, in] (bf16)."""
     return F.linear(x, w)

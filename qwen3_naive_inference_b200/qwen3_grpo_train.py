@@ -221,24 +221,9 @@ def policy_loss_backward(model: Qwen3ForCausalLM, batch: PackedBatch, *, ref_lp=
         dhs = torch.empty_like(hs)
         lse = torch.empty(hs.shape[0], dtype=torch.float32, device=dev)
         tok_off = np.concatenate([[0], np.cumsum(row_tok)])
-        for a, b in _row_chunks(row_tok, chunk_rows):
-            t0, t1 = int(tok_off[a]), int(tok_off[b])
-            if t1 == t0:
-                continue
-            hc = hs[t0:t1]
-            logits = ops.linear(hc, W)
-            ops.check(L.qb_logprob_fwd(logits.data_ptr(), t1 - t0, V, logits.stride(0), tgt.data_ptr() + 8 * t0,
-                                       dest.data_ptr() + 8 * t0, new_lp.data_ptr(), lse.data_ptr() + 4 * t0,
-                                       err.data_ptr(), ops.stream_ptr()), "qb_logprob_fwd")
-            ops.grpo_loss_raw(batch.rewards, batch.group_ids, new_lp, batch.old_lp, batch.mask, ref_lp=ref_lp,
-                              mask_total=mask_total, clip_eps=clip_epsilon, beta=beta, row_begin=r0 + a,
-                              row_end=r0 + b, grad_new=grad_new, loss_out=loss)
-            ops.check(L.qb_logprob_bwd(logits.data_ptr(), t1 - t0, V, logits.stride(0), tgt.data_ptr() + 8 * t0,
-                                       dest.data_ptr() + 8 * t0, lse.data_ptr() + 4 * t0, grad_new.data_ptr(),
-                                       err.data_ptr(), ops.stream_ptr()), "qb_logprob_bwd")
-            torch.mm(logits, W, out=dhs[t0:t1])
-            dW = torch.addmm(dW, logits.t(), hc, out_dtype=torch.float32)
-            del logits
+        with torch.no_grad():
+            dW = _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, loss, dW, batch, ref_lp,
+                                 beta, clip_epsilon, mask_total, r0, row_tok, tok_off, chunk_rows)
         hs_all.backward(dhs)
         del h, hs_all
     g = ops._to_bf16(dW)
@@ -247,6 +232,31 @@ def policy_loss_backward(model: Qwen3ForCausalLM, batch: PackedBatch, *, ref_lp=
     else:
         W.grad.add_(g)
     return loss, new_lp
+
+
+def _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, loss, dW, batch, ref_lp, beta,
+                    clip_epsilon, mask_total, r0, row_tok, tok_off, chunk_rows):
+    """Per row chunk: logits once -> log-prob -> fused loss/grad -> d logits in place -> dh, dW.
+    Returns the updated fp32 dW accumulator."""
+    for a, b in _row_chunks(row_tok, chunk_rows):
+        t0, t1 = int(tok_off[a]), int(tok_off[b])
+        if t1 == t0:
+            continue
+        hc = hs[t0:t1]
+        logits = ops.linear(hc, W)
+        ops.check(L.qb_logprob_fwd(logits.data_ptr(), t1 - t0, V, logits.stride(0), tgt.data_ptr() + 8 * t0,
+                                   dest.data_ptr() + 8 * t0, new_lp.data_ptr(), lse.data_ptr() + 4 * t0,
+                                   err.data_ptr(), ops.stream_ptr()), "qb_logprob_fwd")
+        ops.grpo_loss_raw(batch.rewards, batch.group_ids, new_lp, batch.old_lp, batch.mask, ref_lp=ref_lp,
+                          mask_total=mask_total, clip_eps=clip_epsilon, beta=beta, row_begin=r0 + a,
+                          row_end=r0 + b, grad_new=grad_new, loss_out=loss)
+        ops.check(L.qb_logprob_bwd(logits.data_ptr(), t1 - t0, V, logits.stride(0), tgt.data_ptr() + 8 * t0,
+                                   dest.data_ptr() + 8 * t0, lse.data_ptr() + 4 * t0, grad_new.data_ptr(),
+                                   err.data_ptr(), ops.stream_ptr()), "qb_logprob_bwd")
+        torch.mm(logits, W, out=dhs[t0:t1])
+        dW = torch.addmm(dW, logits.t(), hc, out_dtype=torch.float32)
+        del logits
+    return dW
 
 
 def grpo_train_step(model, optimizer, input_ids, old_log_probs, response_mask, rewards, prompt_ids, *,
@@ -307,14 +317,16 @@ def rollout_batch(model, prompts, *, n_rollout=N_ROLLOUT, max_new_tokens=MAX_RES
 
 # ---------------------------------------------------------------- the full step
 def make_reference_copy(model: Qwen3ForCausalLM) -> Qwen3ForCausalLM:
-    """Frozen deep copy of the policy (the KL anchor); shares no storage with it."""
-    ref = copy.deepcopy(model)
-    for p in ref.parameters():
-        p.requires_grad_(False)
-    for layer in ref.model.layers:
-        layer.self_attn.k_cache = layer.self_attn.v_cache = None
-    ref._graphs = {}
-    ref._has_cuda_graphs = False
+    """Frozen copy of the policy's weights (the KL anchor); shares no storage with it and
+    carries none of the policy's KV cache or captured graphs."""
+    from .qwen3_naive import build_model
+    w = model.lm_head.weight
+    ref = build_model(model.config, device=w.device, dtype=w.dtype, seed=None)
+    with torch.no_grad():
+        src = dict(model.named_parameters())
+        for name, p in ref.named_parameters():
+            p.copy_(src[name])
+            p.requires_grad_(False)
     return ref
 
 

@@ -174,15 +174,25 @@ def test_generate_logprobs_teacher_forced(setup, cuda, top_k, temp):
     torch.manual_seed(1)
     toks, gen, lps, plens = model.generate_continuous_with_logprobs([p.to(cuda) for p in prompts],
                                                                     max_new_tokens=20, temperature=temp, top_k=top_k)
+    checked = 0
     for t, lp, pl in zip(toks, lps, plens):
         assert len(lp) == len(t) - pl == 20
         lg, _ = _oracle_lp(params, cfg, t)
         for j, v in enumerate(lp):
             pos = pl + j
-            probs, logps = R.sample_distribution(lg[pos - 1][None].to(torch.bfloat16), temp, top_k)
+            row = lg[pos - 1]
+            if top_k is not None:
+                srt = row.sort(descending=True).values
+                # GPU and CPU logits differ at bf16 noise level; a near-tie at the k-th value
+                # can swap which token is kept, so such positions are not comparable
+                if (srt[top_k - 1] - srt[top_k]).item() < 0.01:  # ~5 bf16 ulps at this logit scale
+                    continue
+            probs, logps = R.sample_distribution(row[None].to(torch.bfloat16), temp, top_k)
             ref = logps[0, t[pos]].item()
             assert math.isfinite(ref), "sampled a token outside the oracle's support"
             assert abs(v - ref) < 2e-3 * abs(ref) + 0.05, (pos, v, ref)
+            checked += 1
+    assert checked >= 5
 
 
 def test_cuda_graph_decode_matches_eager(setup, cuda):
