@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--decode-only", action="store_true",
                     help="only the config-3 paged-decode microbenchmark (for kernel profiling)")
     ap.add_argument("--decode-batch", type=int, default=256, help="batch of the decode microbenchmark")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="only the tcgen05 GEMM microbenchmark on the model's projection shapes")
     return ap.parse_args()
 
 
@@ -364,9 +366,53 @@ def run_decode_only(batch):
                       "achieved_gbs": nbytes / (ms / 1000) / 1e9}), flush=True)
 
 
+GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
+    "qkv_proj": (8192, 4096, 1024), "o_proj": (8192, 1024, 2048), "gate_up_proj": (8192, 6144, 1024),
+    "down_proj": (8192, 1024, 3072), "lm_head": (4096, 151936, 1024), "qkv_decode512": (512, 4096, 1024),
+    "lm_head_decode512": (512, 151936, 1024),
+}
+
+
+def run_gemm_only():
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("bf16_tflops", 1590.0)
+    out = {}
+    for name, (M, N, K) in GEMM_SHAPES.items():
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        b = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        c = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        res = {}
+        for impl, fn in [("tcgen05", lambda: ops.gemm(a, b, out=c)), ("cublas", lambda: torch.mm(a, b.t(), out=c))]:
+            for _ in range(3):
+                fn()
+            st = torch.cuda.current_stream()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = 10
+            e0.record(st)
+            for _ in range(n):
+                fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            res[impl] = {"ms": ms, "tflops": 2 * M * N * K / (ms / 1000) / 1e12}
+        ref = (a.float() @ b.float().t())
+        ops.gemm(a, b, out=c)
+        res["max_rel_err"] = ((c.float() - ref).abs().max() / ref.abs().max()).item()
+        res["frac_of_peak"] = res["tcgen05"]["tflops"] / peak
+        out[name] = res
+    print(json.dumps({"gemm": out, "peak_tflops": peak}), flush=True)
+
+
 def main():
     args = parse()
-    if args.decode_only:
+    if args.gemm_only:
+        run_gemm_only()
+    elif args.decode_only:
         run_decode_only(args.decode_batch)
     elif args.impl == "reference":
         run_reference(args)

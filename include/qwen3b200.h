@@ -231,8 +231,8 @@ int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace
  * replaces the cuBLAS nn.Linear calls of qkv_proj, o_proj, gate_up_proj, down_proj and the
  * tied lm_head (qwen3_naive.py:427-428, :692-693, :826):
  *   C[M, N] = A[M, K] . B[N, K]^T       A, B bf16 row-major with K contiguous (lda, ldb >= K)
- * mode 0: C bf16; mode 1: C fp32; mode 2: C fp32 += A.B^T.  K % 64 == 0, leading
- * dimensions % 8 == 0, pointers 16-byte aligned. */
+ * mode 0: C bf16; mode 1: C fp32; mode 2: C fp32 += A.B^T.  K % 64 == 0; A and B
+ * 16-byte aligned with lda, ldb % 8 == 0 (TMA operands); any ldc >= N. */
 int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                  int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream);
 

@@ -123,6 +123,7 @@ struct GemmParams {
   int64_t ldc;
   int M, N, K;
   int tiles_m, tiles_n;
+  int vec_ok;  // every output row starts on a 16-byte boundary: 16-byte stores allowed
   int* err;
 };
 
@@ -256,7 +257,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN + c, r);
         const int col = n0 + c;
         if (!row_ok || col >= p.N) continue;
-        const bool full = col + 32 <= p.N;
+        const bool full = col + 32 <= p.N && p.vec_ok;
         if (MODE == 0) {
           bf16* dst = reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col;
           if (full) {
@@ -371,14 +372,17 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t l
   QB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && mode >= 0 && mode <= 2);
   if (M == 0 || N == 0) return QB_OK;
   if (K % BK != 0 || K == 0) return QB_ERR_UNSUPPORTED;
-  QB_CHECK_ARG(A && B && C && al16(A) && al16(B) && al16(C));
-  QB_CHECK_ARG(lda >= K && ldb >= K && ldc >= N && lda % 8 == 0 && ldb % 8 == 0 && ldc % 8 == 0);
+  // A and B feed TMA: 16-byte aligned bases and row pitches (a multiple of 8 bf16).
+  QB_CHECK_ARG(A && B && C && al16(A) && al16(B));
+  QB_CHECK_ARG(lda >= K && ldb >= K && ldc >= N && lda % 8 == 0 && ldb % 8 == 0);
   QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
+  const int64_t elem = mode == 0 ? 2 : 4;
+  const int vec_ok = al16(C) && (ldc * elem) % 16 == 0;
   const bool wide = N >= 256;
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM)) return QB_ERR_INVALID;
   if (!make_tmap(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;
-  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), 0, err};
+  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), 0, vec_ok, err};
   cudaStream_t st = (cudaStream_t)stream;
   if (wide) {
     p.tiles_n = (int)((N + 255) / 256);
