@@ -221,6 +221,26 @@ int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, const float* t
                         const float* mask_total, float clip_eps, float beta,
                         const float* grad_scale, float* grad_new, float* loss_out,
                         void* workspace, qb_stream_t stream);
+/* qb_grpo_loss without a workspace argument, for callers that cannot allocate device
+ * memory or hand the library a scratch buffer: hosts whose GPU memory is owned by another
+ * allocator (a serving runtime or a framework pool that reserved HBM up front, where a
+ * surprise cudaMalloc fails or fragments the pool and cudaMalloc/cudaFree synchronise the
+ * device) and thin FFI bindings that only forward tensors they already own.  It has no
+ * counterpart in the reference.  Same arguments and results as qb_grpo_loss.
+ *   - Scratch lives in a fixed device array inside this library (about 128 KiB, held by
+ *     every GPU that loads the library until the process exits); n_rows above 16384 is
+ *     rejected with QB_ERR_INVALID before anything runs.  Nothing is allocated.
+ *   - The first call on a device looks up that array's device address (once per device,
+ *     with the device current); make that first call before any stream capture.
+ *   - Every call reuses the same array and clears its 16-byte counter header on `stream`
+ *     first; calls that overlap on the GPU (different streams, or another thread) race
+ *     on it and must be serialised by the caller. */
+int qb_grpo_loss_noalloc(const float* rewards, const int64_t* group_ids, int64_t n_rows, int64_t S,
+                         int64_t row_begin, int64_t row_end, const float* new_lp,
+                         const float* old_lp, const float* ref_lp, const float* mask,
+                         const float* mask_total, float clip_eps, float beta,
+                         const float* grad_scale, float* grad_new, float* loss_out,
+                         float* adv_out, qb_stream_t stream);
 /* mask_total[0] = sum of the [n] fp32 mask (the reference's response_mask.sum(),
  * qwen3_grpo_train.py:198); workspace as above. */
 int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace,

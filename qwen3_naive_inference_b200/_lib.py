@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple] = {
     "qb_grpo_loss": (I, [P, P, L, L, L, L, P, P, P, P, P, F, F, P, P, P, P, P, P]),
     "qb_grpo_workspace_bytes": (c_size_t, [L]),
     "qb_ppo_clipped_loss": (I, [P, P, P, P, P, L, L, P, F, F, P, P, P, P, P]),
+    "qb_grpo_loss_noalloc": (I, [P, P, L, L, L, L, P, P, P, P, P, F, F, P, P, P, P, P]),
     "qb_mask_sum": (I, [P, L, P, P, P]),
     "qb_gemm_bf16": (I, [P, L, P, L, P, L, L, L, L, I, P, P]),
     "qb_f32_to_bf16": (I, [P, P, L, P]),

@@ -663,3 +663,60 @@ extern "C" int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, con
   grpo_loss_kernel<false><<<(unsigned)n_rows, 256, 0, (cudaStream_t)stream>>>(p);
   return qb_launch_status();
 }
+
+// ================================================================ allocation-free GRPO loss
+// Some callers cannot hand this library a workspace buffer or let it allocate one:
+// a host whose device memory is owned by another allocator (a serving runtime or a
+// framework caching allocator that has reserved the HBM pool up front), or a thin
+// FFI binding that only forwards tensors it already owns.  For them the fused GRPO
+// loss can run on a scratch area that lives in the library image itself: a fixed
+// device array, set aside once per GPU that loads the library and held until the
+// process exits.  Nothing here calls cudaMalloc or cudaFree.
+namespace {
+constexpr int64_t NOALLOC_MAX_ROWS = 16384;  // largest n_rows this variant accepts
+// Header (tickets + denominator slot, 16 B) + two fp32 partials per row, rounded up to 256 B.
+constexpr size_t NOALLOC_SCRATCH_BYTES = ((16 + 2 * NOALLOC_MAX_ROWS * 4) + 255) / 256 * 256;
+static __device__ __align__(256) unsigned char g_grpo_scratch[NOALLOC_SCRATCH_BYTES];
+
+// The symbol's device address, looked up once per device (host code cannot use the
+// array's name as a device pointer).
+void* noalloc_scratch_ptr(int* status) {
+  static void* ptrs[64] = {};
+  static bool ready[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = e != cudaSuccess ? QB_ERR_CUDA_BASE + (int)e : QB_ERR_UNSUPPORTED;
+    return nullptr;
+  }
+  if (!ready[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_grpo_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *status = QB_ERR_CUDA_BASE + (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+      return nullptr;
+    }
+    ptrs[dev] = p;
+    ready[dev] = true;
+  }
+  *status = QB_OK;
+  return ptrs[dev];
+}
+}  // namespace
+
+extern "C" int qb_grpo_loss_noalloc(const float* rewards, const int64_t* group_ids, int64_t n_rows, int64_t S,
+                                    int64_t row_begin, int64_t row_end, const float* new_lp, const float* old_lp,
+                                    const float* ref_lp, const float* mask, const float* mask_total,
+                                    float clip_eps, float beta, const float* grad_scale, float* grad_new,
+                                    float* loss_out, float* adv_out, qb_stream_t stream) {
+  if (n_rows > NOALLOC_MAX_ROWS) return QB_ERR_INVALID;  // the fixed scratch holds at most this many rows
+  int st = QB_OK;
+  void* ws = noalloc_scratch_ptr(&st);
+  if (!ws) return st;
+  // The scratch keeps whatever the previous call left; the ticket counters and the
+  // denominator slot must start at zero, so clear the 16-byte header on this stream.
+  cudaError_t e = cudaMemsetAsync(ws, 0, 16, (cudaStream_t)stream);
+  if (e != cudaSuccess) return QB_ERR_CUDA_BASE + (int)e;
+  return qb_grpo_loss(rewards, group_ids, n_rows, S, row_begin, row_end, new_lp, old_lp, ref_lp, mask, mask_total,
+                      clip_eps, beta, grad_scale, grad_new, loss_out, adv_out, ws, stream);
+}
