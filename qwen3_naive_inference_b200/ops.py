@@ -400,14 +400,47 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode
     return out
 
 
+def _gemm_operand(t: torch.Tensor) -> torch.Tensor:
+    """2-D view with unit stride along K and a 16-byte row pitch (the TMA operand rules)."""
+    if t.stride(-1) != 1 or t.stride(0) % 8 != 0 or t.data_ptr() % 16 != 0:
+        t = t.contiguous()
+    return t
+
+
+class _Linear(torch.autograd.Function):
+    """y = x w^T on the tcgen05 GEMM; the backward products (dX = g w, dW = g^T x) contract
+    over the output dimension, whose operands are MN-major, and run through torch.mm."""
+
+    @staticmethod
+    def forward(ctx, x2, w):
+        ctx.save_for_backward(x2, w)
+        return gemm(x2, w)
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, w = ctx.saved_tensors
+        g = g.contiguous()
+        dx = torch.mm(g, w) if ctx.needs_input_grad[0] else None
+        dw = torch.mm(g.t(), x2) if ctx.needs_input_grad[1] else None
+        return dx, dw
+
+
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """``x @ w.T`` for nn.Linear weights [out, in] (bf16)."""
-    return F.linear(x, w)
+    """``x @ w.T`` for nn.Linear weights [out, in] (bf16) on the tcgen05 GEMM."""
+    _cuda(x, w)
+    shape = x.shape
+    x2 = _gemm_operand(x.reshape(-1, shape[-1]))
+    w2 = _gemm_operand(w)
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
+        y = _Linear.apply(x2, w2)
+    else:
+        y = gemm(x2, w2)
+    return y.view(*shape[:-1], w.shape[0])
 
 
 # ---------------------------------------------------------------- log-prob / sampling
 def _logits_chunk(h, w):
-    return F.linear(h, w)
+    return gemm(_gemm_operand(h), _gemm_operand(w))
 
 
 def logprob_forward(h, weight, targets, dest=None, out=None, out_size=None, chunk_rows=4096, save_lse=True):
