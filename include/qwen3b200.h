@@ -162,6 +162,25 @@ int qb_paged_decode_attn(const void* q, const void* k_cache, const void* v_cache
                          int hq, int hkv, int D, float scale, int split_tokens, int max_splits,
                          float* workspace, void* out, int* err, qb_stream_t stream);
 size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits);
+/* Decode attention for groups of sequences that share a prompt (GRPO's G completions of
+ * one prompt; the reference keeps no such sharing, its siblings each hold and read their
+ * own copy of the prompt K/V).  Same result as qb_paged_decode_attn.  Every sequence
+ * belongs to exactly one group (singletons allowed): group g lists its members in
+ * group_members[g*8 .. g*8+7] (-1 padded, at most 8) and shares its first shared_len[g]
+ * keys (a multiple of page_size), stored in the pages of its first member's block_tables
+ * row.  kv_start[b] = shared_len of b's group.  The shared keys are read once per group for
+ * all members' query heads; each member's own keys [kv_start[b], len_b) separately; split-K
+ * partials (shared_splits + own_splits slots per sequence and head) are merged at the end.
+ * workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D, shared_splits + own_splits). */
+int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
+                                 int64_t num_blocks, int page_size, const int32_t* block_tables,
+                                 int64_t bt_stride, const int32_t* seqlens, int seqlen_add,
+                                 int batch, int hq, int hkv, int D, float scale,
+                                 const int32_t* group_members, const int32_t* shared_len,
+                                 int n_groups, const int32_t* kv_start, int split_tokens,
+                                 int shared_splits, int own_splits, float* workspace, void* out,
+                                 int* err, qb_stream_t stream);
+size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int D, int n_slots);
 
 /* ---------------------------------------------------------------- lm_head log-prob / sampling
  * Token log-probability from bf16 logits rows; replaces the fp32
@@ -251,10 +270,27 @@ int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace
  * replaces the cuBLAS nn.Linear calls of qkv_proj, o_proj, gate_up_proj, down_proj and the
  * tied lm_head (qwen3_naive.py:427-428, :692-693, :826):
  *   C[M, N] = A[M, K] . B[N, K]^T       A, B bf16 row-major with K contiguous (lda, ldb >= K)
- * mode 0: C bf16; mode 1: C fp32; mode 2: C fp32 += A.B^T.  K % 64 == 0; A and B
- * 16-byte aligned with lda, ldb % 8 == 0 (TMA operands); any ldc >= N. */
+ * mode 0: C bf16; mode 1: C fp32; mode 2: C fp32 += A.B^T.  Any K >= 1 (a K tail is
+ * zero-filled); A and B 16-byte aligned with lda, ldb % 8 == 0 (TMA operands); any ldc >= N. */
 int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                  int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream);
+/* The same product with either operand stored MN-major, for the backward of the projections
+ * (the reference's autograd of nn.Linear / lm_head):
+ *   a_mn_major = 0: A is [M, K] (K contiguous);  1: A is stored [K, M] (M contiguous, lda >= M)
+ *   b_mn_major = 0: B is [N, K];                 1: B is stored [K, N] (N contiguous, ldb >= N)
+ * dX = dY . W uses (0, 1); dW = dY^T . X uses (1, 1). */
+int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
+                    int b_mn_major, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int mode,
+                    int* err, qb_stream_t stream);
+
+/* Copies the first nbytes of KV page src_page into each of dst_pages[0..n_dst) in every
+ * layer of the K and V pools ([layers][num_pages][page] with the given byte strides).  Used
+ * when G completions of one prompt share its full pages and each gets its own copy of the
+ * partially filled last prompt page (the reference prefills every completion separately). */
+int qb_copy_page_prefix(void* k_pool, void* v_pool, int64_t layers, int64_t layer_bytes,
+                        int64_t page_bytes, int64_t num_pages, int src_page,
+                        const int32_t* dst_pages, int n_dst, int64_t nbytes, int* err,
+                        qb_stream_t stream);
 
 /* ---------------------------------------------------------------- optimizer helpers
  * dst (bf16) = bf16(src fp32); used to hand fp32-accumulated gradients to the

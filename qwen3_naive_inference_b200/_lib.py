@@ -40,6 +40,9 @@ SIGNATURES: dict[str, tuple] = {
     "qb_attn_varlen_bwd": (I, [P, P, P, L, P, P, L, P, P, I, P, I, I, I, I, F, L, P, P, P, P, P, P]),
     "qb_paged_decode_attn": (I, [P, P, P, L, I, P, L, P, I, I, I, I, I, F, I, I, P, P, P, P]),
     "qb_paged_decode_workspace_bytes": (c_size_t, [I, I, I, I]),
+    "qb_paged_decode_attn_grouped": (I, [P, P, P, L, I, P, L, P, I, I, I, I, I, F, P, P, I, P, I, I, I, P, P, P,
+                                         P]),
+    "qb_paged_decode_grouped_workspace_bytes": (c_size_t, [I, I, I, I]),
     "qb_logprob_fwd": (I, [P, L, L, L, P, P, P, P, P, P]),
     "qb_logprob_bwd": (I, [P, L, L, L, P, P, P, P, P, P]),
     "qb_sample": (I, [P, L, L, L, F, I, c_uint64, P, P, P, P, P]),
@@ -50,6 +53,8 @@ SIGNATURES: dict[str, tuple] = {
     "qb_grpo_loss_noalloc": (I, [P, P, L, L, L, L, P, P, P, P, P, F, F, P, P, P, P, P]),
     "qb_mask_sum": (I, [P, L, P, P, P]),
     "qb_gemm_bf16": (I, [P, L, P, L, P, L, L, L, L, I, P, P]),
+    "qb_gemm_bf16_ex": (I, [P, L, I, P, L, I, P, L, L, L, L, I, P, P]),
+    "qb_copy_page_prefix": (I, [P, P, L, L, L, L, I, P, I, L, P, P]),
     "qb_f32_to_bf16": (I, [P, P, L, P]),
     "qb_accumulate_bf16": (I, [P, P, L, P]),
 }

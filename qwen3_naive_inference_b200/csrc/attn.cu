@@ -53,7 +53,17 @@ struct DecodeParams {
   float* ws;
   bf16* out;
   int* err;
+  // Split-K partial layout: sequence b, slot s, head h at ws[((b*n_slots + s)*hq + h)*WS_ROW].
+  // This kernel's split i goes to slot slot_off + i.  kv_start (nullable) skips each
+  // sequence's first keys (they belong to a shared prefix handled elsewhere).
+  int n_slots, slot_off;
+  const int32_t* kv_start;
 };
+
+// Marks the partial of (b, slot, h) empty (log2-domain LSE = -inf) so the merge ignores it.
+QB_DEVICE void write_empty_partial(const DecodeParams& p, int b, int slot, int h) {
+  p.ws[(((int64_t)b * p.n_slots + slot) * p.hq + h) * WS_ROW + D] = NEG_INF;
+}
 
 __global__ void __launch_bounds__(DEC_WARPS * 32)
 paged_decode_kernel(DecodeParams p) {
@@ -62,8 +72,11 @@ paged_decode_kernel(DecodeParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int len = p.seqlens[b] + p.seqlen_add;
-  const int tok_begin = split * p.split_tokens;
-  if (tok_begin >= len) return;
+  const int tok_begin = (p.kv_start ? p.kv_start[b] : 0) + split * p.split_tokens;
+  if (tok_begin >= len) {
+    if (p.max_splits > 1 && threadIdx.x < 2) write_empty_partial(p, b, p.slot_off + split, kvh * 2 + threadIdx.x);
+    return;
+  }
   const int tok_end = min(len, tok_begin + p.split_tokens);
   const int n_stages = (tok_end - tok_begin + DEC_TOK - 1) / DEC_TOK;
   const int h0 = kvh * 2;
@@ -242,7 +255,7 @@ paged_decode_kernel(DecodeParams p) {
       bf16* orow = p.out + ((int64_t)b * p.hq + h0 + h) * D + d0;
       *reinterpret_cast<uint32_t*>(orow) = pack_bf16x2(acc0 * inv, acc1 * inv);
     } else {
-      float* wrow = p.ws + (((int64_t)b * p.max_splits + split) * p.hq + h0 + h) * WS_ROW;
+      float* wrow = p.ws + (((int64_t)b * p.n_slots + p.slot_off + split) * p.hq + h0 + h) * WS_ROW;
       wrow[d0] = acc0 * inv;
       wrow[d0 + 1] = acc1 * inv;
       if (d0 == 0) wrow[D] = (L > 0.f) ? M + log2f(L) : NEG_INF;  // log2-domain LSE
@@ -256,16 +269,17 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
   if (item >= batch * p.hq) return;
   const int lane = threadIdx.x & 31;
   const int b = item / p.hq, h = item % p.hq;
-  const int len = p.seqlens[b] + p.seqlen_add;
-  const int ns = min(p.max_splits, (len + p.split_tokens - 1) / p.split_tokens);
-  const float* base = p.ws + ((int64_t)b * p.max_splits * p.hq + h) * WS_ROW;
+  // every slot of (b, h) was written by some CTA, empty ones with LSE = -inf
+  const int ns = p.n_slots;
+  const float* base = p.ws + ((int64_t)b * p.n_slots * p.hq + h) * WS_ROW;
   const int64_t sstride = (int64_t)p.hq * WS_ROW;
   float M = NEG_INF;
   for (int s = 0; s < ns; ++s) M = fmaxf(M, base[s * sstride + D]);
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, W = 0.f;
   for (int s = 0; s < ns; ++s) {
     const float ls = base[s * sstride + D];
-    const float w = (ls == NEG_INF) ? 0.f : exp2f(ls - M);
+    if (ls == NEG_INF) continue;  // empty partial: its outputs were never written
+    const float w = exp2f(ls - M);
     W += w;
     const float4 v = *reinterpret_cast<const float4*>(base + s * sstride + lane * 4);
     acc[0] += w * v.x; acc[1] += w * v.y; acc[2] += w * v.z; acc[3] += w * v.w;
@@ -276,6 +290,225 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
   r.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
   r.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
   *reinterpret_cast<uint2*>(orow) = r;
+}
+
+// ============================================================================
+// Shared-prefix decode attention (GRPO groups)
+// ============================================================================
+// The G <= 8 members of a group share the K/V pages of their common prompt.  One CTA =
+// (split of the shared keys, kv head, group) reads those keys once for all 2*G query
+// heads of the kv group: 16 query rows (member i, head h0 + r) = one full M=16 MMA tile,
+// S = Q K^T, online softmax, O += P V (FlashAttention-2 rows), four warps each taking 16
+// of the 64 staged tokens, merged in shared memory.  Each member's partial (O / l and its
+// log2-domain LSE) goes to slot `split` of the split-K workspace; the members' own keys are
+// handled by paged_decode_kernel (kv_start = shared length) in later slots, and
+// paged_decode_combine_kernel merges all slots.
+constexpr int GMAX = 8;
+
+struct SharedParams {
+  DecodeParams d;             // q, caches, page tables, workspace (n_slots), scale, err
+  const int32_t* members;     // [n_groups, GMAX] sequence indices, -1 padded
+  const int32_t* shared_len;  // [n_groups] keys shared by the group (pages of members[g][0])
+};
+
+__global__ void __launch_bounds__(DEC_WARPS * 32)
+paged_decode_shared_kernel(SharedParams sp) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const DecodeParams& p = sp.d;
+  const int split = blockIdx.x, kvh = blockIdx.y, grp = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int h0 = kvh * 2;
+  const int32_t* mem = sp.members + grp * GMAX;
+  const int len = sp.shared_len[grp];
+  const int tok_begin = split * p.split_tokens;
+  const int leader = mem[0];
+  if (tok_begin >= len || leader < 0) {
+    if (tid < 2 * GMAX) {
+      const int m = mem[tid >> 1];
+      if (m >= 0) write_empty_partial(p, m, split, h0 + (tid & 1));
+    }
+    return;
+  }
+  const int tok_end = min(len, tok_begin + p.split_tokens);
+  const int n_stages = (tok_end - tok_begin + DEC_TOK - 1) / DEC_TOK;
+
+  // Q as the A operand (row r = member r/2, head h0 + r%2): a0 rows g, a1 rows g+8.
+  uint32_t qa[8][4];
+  {
+    const int r0 = g, r1 = g + 8;
+    const int m0 = mem[r0 >> 1], m1 = mem[r1 >> 1];
+    const bf16* q0 = p.q + ((int64_t)(m0 < 0 ? 0 : m0) * p.hq + h0 + (r0 & 1)) * D;
+    const bf16* q1 = p.q + ((int64_t)(m1 < 0 ? 0 : m1) * p.hq + h0 + (r1 & 1)) * D;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int c = kk * 16 + 2 * t4;
+      qa[kk][0] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+      qa[kk][1] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+      qa[kk][2] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+      qa[kk][3] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
+  }
+
+  const int32_t* btrow = p.bt + (int64_t)leader * p.bt_stride;
+  auto load_stage = [&](int s) {
+    const int buf = s % DEC_STAGES;
+    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
+    const uint32_t vbase = kbase + DEC_TOK * ROWB;
+    const int tok0 = tok_begin + s * DEC_TOK;
+    const bool col_ok = tok0 / PAGE < p.bt_stride;
+    int page = col_ok ? btrow[tok0 / PAGE] : -1;
+    bool page_ok = page >= 0 && page < p.num_blocks;
+    if (!page_ok) {
+      if (tid == 0) qb_set_err(p.err, QB_DEVERR_PAGE);
+      page = 0;
+    }
+    const int64_t row0 = ((int64_t)page * PAGE + (tok0 % PAGE)) * p.hkv + kvh;
+#pragma unroll
+    for (int i = 0; i < (DEC_TOK * 16) / (DEC_WARPS * 32); ++i) {
+      const int idx = tid + i * DEC_WARPS * 32;
+      const int r = idx >> 4, c = idx & 15;
+      const bool ok = page_ok && (tok0 + r < tok_end);
+      const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
+      cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
+      cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < DEC_STAGES - 1; ++s) {
+    if (s < n_stages) load_stage(s);
+    cp_async_commit();
+  }
+
+  float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  for (int s = 0; s < n_stages; ++s) {
+    if (s + DEC_STAGES - 1 < n_stages) load_stage(s + DEC_STAGES - 1);
+    cp_async_commit();
+    cp_async_wait<DEC_STAGES - 1>();
+    __syncthreads();
+    const int buf = s % DEC_STAGES;
+    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
+    const uint32_t vbase = kbase + DEC_TOK * ROWB;
+    const int wrow = warp * 16;
+    // S[16 q x 16 tok] = Q K^T over this warp's 16 tokens (two n-tiles of 8 tokens)
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t r0, r1, r2, r3;
+      ldmatrix_x4(kbase + swz128(wrow + (lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2,
+                  r3);
+      mma_bf16_16816(sc[0], qa[kk], r0, r1);
+      mma_bf16_16816(sc[1], qa[kk], r2, r3);
+    }
+    const int key0 = tok_begin + s * DEC_TOK + wrow;
+    float mt[2] = {NEG_INF, NEG_INF};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int kc = key0 + nt * 8 + 2 * t4;
+      sc[nt][0] = kc < tok_end ? sc[nt][0] * p.scale_log2 : NEG_INF;
+      sc[nt][1] = kc + 1 < tok_end ? sc[nt][1] * p.scale_log2 : NEG_INF;
+      sc[nt][2] = kc < tok_end ? sc[nt][2] * p.scale_log2 : NEG_INF;
+      sc[nt][3] = kc + 1 < tok_end ? sc[nt][3] * p.scale_log2 : NEG_INF;
+      mt[0] = fmaxf(mt[0], fmaxf(sc[nt][0], sc[nt][1]));
+      mt[1] = fmaxf(mt[1], fmaxf(sc[nt][2], sc[nt][3]));
+    }
+    float alpha[2], mnew[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 1));
+      mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 2));
+      mnew[r] = fmaxf(m_run[r], mt[r]);
+      alpha[r] = (mnew[r] == NEG_INF) ? 1.f : exp2f(m_run[r] - mnew[r]);
+      m_run[r] = mnew[r];
+    }
+    uint32_t pa[4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][0] - mnew[0]);
+      const float p1 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][1] - mnew[0]);
+      const float p2 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][2] - mnew[1]);
+      const float p3 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][3] - mnew[1]);
+      rs[0] += p0 + p1;
+      rs[1] += p2 + p3;
+      pa[2 * nt] = pack_bf16x2(p0, p1);
+      pa[2 * nt + 1] = pack_bf16x2(p2, p3);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      l_run[r] = l_run[r] * alpha[r] + rs[r];
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      o[dt][0] *= alpha[0];
+      o[dt][1] *= alpha[0];
+      o[dt][2] *= alpha[1];
+      o[dt][3] *= alpha[1];
+    }
+    // O[16 x 128] += P[16 x 16 tok] V[16 tok x 128]
+#pragma unroll
+    for (int dp = 0; dp < 8; ++dp) {
+      uint32_t r0, r1, r2, r3;
+      ldmatrix_x4_trans(vbase + swz128(wrow + (lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1,
+                        r2, r3);
+      mma_bf16_16816(o[2 * dp], pa, r0, r1);
+      mma_bf16_16816(o[2 * dp + 1], pa, r2, r3);
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // Merge the four warps: smem [warp][16 rows][128] floats + m, l per (warp, row).
+  float* so = reinterpret_cast<float*>(smem);
+  float* sm = so + DEC_WARPS * 16 * D;
+  float* sl = sm + DEC_WARPS * 16;
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = g + 8 * r;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      so[(warp * 16 + row) * D + dt * 8 + 2 * t4] = o[dt][2 * r];
+      so[(warp * 16 + row) * D + dt * 8 + 2 * t4 + 1] = o[dt][2 * r + 1];
+    }
+    if (t4 == 0) {
+      sm[warp * 16 + row] = m_run[r];
+      sl[warp * 16 + row] = l_run[r];
+    }
+  }
+  __syncthreads();
+  {
+    const int row = tid >> 3;          // 16 rows x 8 threads
+    const int d0 = (tid & 7) * 16;     // 16 dims per thread
+    const int member = mem[row >> 1];
+    float M = NEG_INF;
+#pragma unroll
+    for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, sm[w * 16 + row]);
+    float L = 0.f, f[DEC_WARPS];
+#pragma unroll
+    for (int w = 0; w < DEC_WARPS; ++w) {
+      const float mw = sm[w * 16 + row];
+      f[w] = (mw == NEG_INF) ? 0.f : exp2f(mw - M);
+      L += sl[w * 16 + row] * f[w];
+    }
+    if (member >= 0) {
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      float* wrow = p.ws + (((int64_t)member * p.n_slots + split) * p.hq + h0 + (row & 1)) * WS_ROW;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < DEC_WARPS; ++w) acc += so[(w * 16 + row) * D + d0 + i] * f[w];
+        wrow[d0 + i] = acc * inv;
+      }
+      if (d0 == 0) wrow[D] = (L > 0.f) ? M + log2f(L) : NEG_INF;
+    }
+  }
 }
 
 // ============================================================================
@@ -816,7 +1049,7 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
   QB_CHECK_ARG(max_splits == 1 || (workspace && al16(workspace)));
   DecodeParams p{(const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, num_blocks, block_tables,
                  bt_stride, seqlens, seqlen_add, hq, hkv, scale * LOG2E, split_tokens, max_splits,
-                 workspace, (bf16*)out, err};
+                 workspace, (bf16*)out, err, max_splits, 0, nullptr};
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
@@ -829,6 +1062,55 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
   const int wpb = 8;
   paged_decode_combine_kernel<<<(unsigned)((batch * hq + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
       p, batch);
+  return qb_launch_status();
+}
+
+extern "C" size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int Dh, int n_slots) {
+  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float);
+}
+
+extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
+                                            int64_t num_blocks, int page_size, const int32_t* block_tables,
+                                            int64_t bt_stride, const int32_t* seqlens, int seqlen_add, int batch,
+                                            int hq, int hkv, int Dh, float scale, const int32_t* group_members,
+                                            const int32_t* shared_len, int n_groups, const int32_t* kv_start,
+                                            int split_tokens, int shared_splits, int own_splits, float* workspace,
+                                            void* out, int* err, qb_stream_t stream) {
+  if (Dh != D || page_size != PAGE || hq != 2 * hkv) return QB_ERR_UNSUPPORTED;
+  QB_CHECK_ARG(batch >= 0 && batch <= 65535 && n_groups >= 0 && n_groups <= 65535 && hkv > 0 && num_blocks > 0);
+  QB_CHECK_ARG(split_tokens >= DEC_TOK && split_tokens % DEC_TOK == 0 && shared_splits >= 1 && own_splits >= 1 &&
+               shared_splits + own_splits <= 65535);
+  if (batch == 0) return QB_OK;
+  QB_CHECK_ARG(q && k_cache && v_cache && block_tables && seqlens && out && workspace && group_members &&
+               shared_len && kv_start && al16(q) && al16(k_cache) && al16(v_cache) && al16(workspace) &&
+               bt_stride > 0);
+  const int n_slots = shared_splits + own_splits;
+  DecodeParams d{(const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, num_blocks, block_tables, bt_stride,
+                 seqlens, seqlen_add, hq, hkv, scale * LOG2E, split_tokens, n_slots, workspace, (bf16*)out, err,
+                 n_slots, 0, nullptr};
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(paged_decode_shared_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    attr_set = true;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n_groups > 0) {
+    SharedParams sp{d, group_members, shared_len};
+    paged_decode_shared_kernel<<<dim3((unsigned)shared_splits, (unsigned)hkv, (unsigned)n_groups), DEC_WARPS * 32,
+                                 DEC_SMEM, st>>>(sp);
+    int s0 = qb_launch_status();
+    if (s0 != QB_OK) return s0;
+  }
+  DecodeParams own = d;
+  own.slot_off = shared_splits;
+  own.kv_start = kv_start;
+  paged_decode_kernel<<<dim3((unsigned)own_splits, (unsigned)hkv, (unsigned)batch), DEC_WARPS * 32, DEC_SMEM, st>>>(
+      own);
+  int s1 = qb_launch_status();
+  if (s1 != QB_OK) return s1;
+  const int wpb = 8;
+  paged_decode_combine_kernel<<<(unsigned)((batch * hq + wpb - 1) / wpb), wpb * 32, 0, st>>>(d, batch);
   return qb_launch_status();
 }
 

@@ -13,7 +13,7 @@
 //              the next tile's MMAs overlap this tile's stores.
 // Every mbarrier wait is bounded: on timeout the kernel raises QB_DEVERR_TIMEOUT, all
 // roles leave their loops, the producer waits (bounded) for its own copies, TMEM is
-// freed and the kernel returns.  No TMA multicast is used anywhere.
+// freed and the kernel returns.  Each CTA issues its own TMA loads from this GPU's memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -93,6 +93,26 @@ QB_DEVICE uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// MN-major operand (the matrix is stored [K rows][MN contiguous]): 64-element MN atoms of
+// 64 K-rows x 128 B (8 KB) side by side, each row 128-byte swizzled.  LBO = distance between
+// MN atoms (8 KB), SBO = distance between 8-row K groups (1024 B).
+QB_DEVICE uint64_t sw128_mnmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(8192 >> 4) << 16;  // leading byte offset: next 64-wide MN atom
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8 K-rows
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Descriptor of K-step j (16 elements) inside a 64-deep K block.
+template <bool MN_MAJOR>
+QB_DEVICE uint64_t operand_desc(uint32_t stage_addr, int j) {
+  if (MN_MAJOR) return sw128_mnmajor_desc(stage_addr + j * 16 * 128);  // 16 K-rows of 128 B
+  return sw128_kmajor_desc(stage_addr + j * 32);                       // 16 elements = 32 B along the row
+}
+
 QB_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -127,7 +147,7 @@ struct GemmParams {
   int* err;
 };
 
-template <int BN, int STAGES, int MODE>
+template <int BN, int STAGES, int MODE, bool A_MN, bool B_MN>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
@@ -137,14 +157,27 @@ struct GemmCfg {
   static constexpr uint32_t IDESC = (1u << 4)            // D fp32
                                     | (1u << 7)          // A bf16
                                     | (1u << 10)         // B bf16
+                                    | ((A_MN ? 1u : 0u) << 15) | ((B_MN ? 1u : 0u) << 16)
                                     | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 };
 
-template <int BN, int STAGES, int MODE>
+// Loads one operand tile of ROWS (M or N) x BK into a stage: one {64, ROWS} box for a K-major
+// operand, ROWS/64 {64, 64} boxes (one per 64-wide MN atom) for an MN-major operand.
+template <bool MN_MAJOR, int ROWS>
+QB_DEVICE void load_operand(uint32_t dst, const CUtensorMap* map, int k0, int mn0, uint32_t bar) {
+  if (MN_MAJOR) {
+#pragma unroll
+    for (int a = 0; a < ROWS / 64; ++a) tma_load_2d(dst + a * 64 * 128, map, mn0 + a * 64, k0, bar);
+  } else {
+    tma_load_2d(dst, map, k0, mn0, bar);
+  }
+}
+
+template <int BN, int STAGES, int MODE, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                     GemmParams p) {
-  using Cfg = GemmCfg<BN, STAGES, MODE>;
+  using Cfg = GemmCfg<BN, STAGES, MODE, A_MN, B_MN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;  // SW128 atoms need 1024-byte alignment
@@ -161,7 +194,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = p.tiles_m * p.tiles_n;
-  const int kblocks = p.K / BK;
+  const int kblocks = (p.K + BK - 1) / BK;  // a K tail is zero-filled by TMA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -199,8 +232,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
         const uint32_t sa = base + stage * Cfg::STAGE_BYTES, sb = sa + Cfg::A_BYTES;
         mbar_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
-        tma_load_2d(sa, &tmap_a, kb * BK, m0, full_bar(stage));
-        tma_load_2d(sb, &tmap_b, kb * BK, n0, full_bar(stage));
+        load_operand<A_MN, BM>(sa, &tmap_a, kb * BK, m0, full_bar(stage));
+        load_operand<B_MN, BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
         issued |= 1u << stage;
         last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -226,8 +259,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         const uint32_t sa = base + stage * Cfg::STAGE_BYTES, sb = sa + Cfg::A_BYTES;
 #pragma unroll
         for (int j = 0; j < BK / 16; ++j)
-          umma_bf16(d, sw128_kmajor_desc(sa + j * 32), sw128_kmajor_desc(sb + j * 32), Cfg::IDESC,
-                    (kb | j) != 0);
+          umma_bf16(d, operand_desc<A_MN>(sa, j), operand_desc<B_MN>(sb, j), Cfg::IDESC, (kb | j) != 0);
         umma_commit(empty_bar(stage));  // stage reusable once these MMAs have read it
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
@@ -322,18 +354,25 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D bf16 tensor map: inner dim `inner` (contiguous), outer dim `outer`, row pitch ld elements,
-// box {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
-bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_rows) {
+// box {64, box_outer}, 128-byte swizzle, zero fill out of bounds.
+bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_outer) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {BK, box_rows};
+  cuuint32_t box[2] = {64, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Operand map: K-major [rows, K] -> box {64 along K, rows_tile}; MN-major stored [K, rows] ->
+// box {64 along MN, 64 along K} (one box per 64-wide MN atom).
+bool operand_tmap(CUtensorMap* map, const void* ptr, bool mn_major, uint64_t rows, uint64_t K, uint64_t ld,
+                  uint32_t rows_tile) {
+  return mn_major ? make_tmap(map, ptr, rows, K, ld, BK) : make_tmap(map, ptr, K, rows, ld, rows_tile);
 }
 
 int sm_count() {
@@ -347,51 +386,71 @@ int sm_count() {
   return n;
 }
 
-template <int BN, int STAGES, int MODE>
+template <int BN, int STAGES, int MODE, bool A_MN, bool B_MN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
-  using Cfg = GemmCfg<BN, STAGES, MODE>;
+  using Cfg = GemmCfg<BN, STAGES, MODE, A_MN, B_MN>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, MODE, A_MN, B_MN>;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, STAGES, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) != cudaSuccess)
       return qb_launch_status();
     attr = true;
   }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  gemm_tcgen05_kernel<BN, STAGES, MODE><<<grid, THREADS, Cfg::SMEM, st>>>(ta, tb, p);
+  kern<<<grid, THREADS, Cfg::SMEM, st>>>(ta, tb, p);
   return qb_launch_status();
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+int launch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  if (mode == 0) return launch<BN, STAGES, 0, A_MN, B_MN>(ta, tb, p, st);
+  if (mode == 1) return launch<BN, STAGES, 1, A_MN, B_MN>(ta, tb, p, st);
+  return launch<BN, STAGES, 2, A_MN, B_MN>(ta, tb, p, st);
+}
+
+template <bool A_MN, bool B_MN>
+int launch_layout(bool wide, int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p,
+                  cudaStream_t st) {
+  return wide ? launch_mode<256, 4, A_MN, B_MN>(mode, ta, tb, p, st)
+              : launch_mode<128, 6, A_MN, B_MN>(mode, ta, tb, p, st);
 }
 
 inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
 
-}  // namespace
-
-extern "C" int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
-                            int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream) {
+int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, bool b_mn, void* C,
+                  int64_t ldc, int64_t M, int64_t N, int64_t K, int mode, int* err, cudaStream_t st) {
   QB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && mode >= 0 && mode <= 2);
   if (M == 0 || N == 0) return QB_OK;
-  if (K % BK != 0 || K == 0) return QB_ERR_UNSUPPORTED;
+  if (K == 0) return QB_ERR_UNSUPPORTED;
   // A and B feed TMA: 16-byte aligned bases and row pitches (a multiple of 8 bf16).
-  QB_CHECK_ARG(A && B && C && al16(A) && al16(B));
-  QB_CHECK_ARG(lda >= K && ldb >= K && ldc >= N && lda % 8 == 0 && ldb % 8 == 0);
+  QB_CHECK_ARG(A && B && C && al16(A) && al16(B) && lda % 8 == 0 && ldb % 8 == 0 && ldc >= N);
+  QB_CHECK_ARG(lda >= (a_mn ? M : K) && ldb >= (b_mn ? N : K));
   QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
   const int64_t elem = mode == 0 ? 2 : 4;
   const int vec_ok = al16(C) && (ldc * elem) % 16 == 0;
   const bool wide = N >= 256;
   CUtensorMap ta, tb;
-  if (!make_tmap(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BM)) return QB_ERR_INVALID;
-  if (!make_tmap(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;
-  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), 0, vec_ok, err};
-  cudaStream_t st = (cudaStream_t)stream;
-  if (wide) {
-    p.tiles_n = (int)((N + 255) / 256);
-    if (mode == 0) return launch<256, 4, 0>(ta, tb, p, st);
-    if (mode == 1) return launch<256, 4, 1>(ta, tb, p, st);
-    return launch<256, 4, 2>(ta, tb, p, st);
-  }
-  p.tiles_n = (int)((N + 127) / 128);
-  if (mode == 0) return launch<128, 6, 0>(ta, tb, p, st);
-  if (mode == 1) return launch<128, 6, 1>(ta, tb, p, st);
-  return launch<128, 6, 2>(ta, tb, p, st);
+  if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
+  if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;
+  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), (int)((N + (wide ? 255 : 127)) / (wide ? 256 : 128)),
+               vec_ok, err};
+  if (!a_mn && !b_mn) return launch_layout<false, false>(wide, mode, ta, tb, p, st);
+  if (!a_mn && b_mn) return launch_layout<false, true>(wide, mode, ta, tb, p, st);
+  if (a_mn && !b_mn) return launch_layout<true, false>(wide, mode, ta, tb, p, st);
+  return launch_layout<true, true>(wide, mode, ta, tb, p, st);
+}
+
+}  // namespace
+
+extern "C" int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                            int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream) {
+  return gemm_dispatch(A, lda, false, B, ldb, false, C, ldc, M, N, K, mode, err, (cudaStream_t)stream);
+}
+
+extern "C" int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
+                               int b_mn_major, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int mode,
+                               int* err, qb_stream_t stream) {
+  return gemm_dispatch(A, lda, a_mn_major != 0, B, ldb, b_mn_major != 0, C, ldc, M, N, K, mode, err,
+                       (cudaStream_t)stream);
 }

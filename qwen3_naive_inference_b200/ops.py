@@ -330,6 +330,36 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, seqlens, scale, se
     return out
 
 
+def grouped_decode_plan(batch, hkv, max_shared, max_own, sm_count=148):
+    """(split_tokens, shared_splits, own_splits) for qb_paged_decode_attn_grouped."""
+    want = max(1, math.ceil(4 * sm_count / max(1, batch * hkv)))
+    own_max = max(64, max_own)
+    split = max(64, math.ceil(math.ceil(own_max / want) / 64) * 64)
+    return split, max(1, math.ceil(max(1, max_shared) / split)), max(1, math.ceil(own_max / split))
+
+
+def paged_decode_attention_grouped(q, k_cache, v_cache, block_tables, seqlens, scale, group_members, shared_len,
+                                   kv_start, plan, workspace=None, seqlen_add=1):
+    """Decode attention where groups of sequences share their first ``shared_len`` keys
+    (same pages); equals :func:`paged_decode_attention` with the shared keys read once per group.
+    group_members int32 [n_groups, 8] (-1 padded), shared_len int32 [n_groups], kv_start int32 [B]."""
+    _cuda(q, k_cache, v_cache, block_tables, seqlens, group_members, shared_len, kv_start)
+    B, hq, D = q.shape
+    num_blocks, page, hkv, _ = k_cache.shape
+    split_tokens, s_sh, s_own = plan
+    if workspace is None:
+        nbytes = lib().qb_paged_decode_grouped_workspace_bytes(B, hq, D, s_sh + s_own)
+        workspace = torch.empty(nbytes // 4, dtype=torch.float32, device=q.device)
+    out = torch.empty_like(q)
+    check(lib().qb_paged_decode_attn_grouped(_p(q), _p(k_cache), _p(v_cache), num_blocks, page, _p(block_tables),
+                                             block_tables.stride(0), _p(seqlens), seqlen_add, B, hq, hkv, D, scale,
+                                             _p(group_members), _p(shared_len), group_members.shape[0],
+                                             _p(kv_start), split_tokens, s_sh, s_own, _p(workspace), _p(out),
+                                             _p(err_flag()), stream_ptr()), "qb_paged_decode_attn_grouped",
+          kernels=3)
+    return out
+
+
 # ---------------------------------------------------------------- MLP / adds / linear
 class _SiluMul(torch.autograd.Function):
     @staticmethod
@@ -400,6 +430,25 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode
     return out
 
 
+def gemm_ex(a: torch.Tensor, a_mn: bool, b: torch.Tensor, b_mn: bool, out: torch.Tensor | None = None,
+            mode: int = 0) -> torch.Tensor:
+    """C = op(a) @ op(b).T on the tcgen05 GEMM.  ``a`` is [M, K] (a_mn False) or stored [K, M]
+    (a_mn True); ``b`` is [N, K] (b_mn False) or stored [K, N] (b_mn True).  Unit inner stride."""
+    _cuda(a, b)
+    a, b = _gemm_operand(a), _gemm_operand(b)
+    if a.dtype != BF16 or b.dtype != BF16:
+        raise NativeError("gemm_ex needs bf16 operands")
+    M, K = (a.shape[1], a.shape[0]) if a_mn else (a.shape[0], a.shape[1])
+    N = b.shape[1] if b_mn else b.shape[0]
+    if (b.shape[0] if b_mn else b.shape[1]) != K:
+        raise NativeError("gemm_ex: inner dimensions differ")
+    if out is None:
+        out = torch.empty(M, N, dtype=BF16 if mode == 0 else torch.float32, device=a.device)
+    check(lib().qb_gemm_bf16_ex(_p(a), a.stride(0), int(a_mn), _p(b), b.stride(0), int(b_mn), _p(out),
+                                out.stride(0), M, N, K, mode, _p(err_flag()), stream_ptr()), "qb_gemm_bf16_ex")
+    return out
+
+
 def _gemm_operand(t: torch.Tensor) -> torch.Tensor:
     """2-D view with unit stride along K and a 16-byte row pitch (the TMA operand rules)."""
     if t.stride(-1) != 1 or t.stride(0) % 8 != 0 or t.data_ptr() % 16 != 0:
@@ -408,8 +457,9 @@ def _gemm_operand(t: torch.Tensor) -> torch.Tensor:
 
 
 class _Linear(torch.autograd.Function):
-    """y = x w^T on the tcgen05 GEMM; the backward products (dX = g w, dW = g^T x) contract
-    over the output dimension, whose operands are MN-major, and run through torch.mm."""
+    """y = x w^T on the tcgen05 GEMM; the backward products contract over the output
+    dimension and read w and x MN-major: dX = g . w  (B stored [out, in] = [K, N]),
+    dW = g^T . x (A stored [tokens, out] = [K, M], B stored [tokens, in] = [K, N])."""
 
     @staticmethod
     def forward(ctx, x2, w):
@@ -420,8 +470,8 @@ class _Linear(torch.autograd.Function):
     def backward(ctx, g):
         x2, w = ctx.saved_tensors
         g = g.contiguous()
-        dx = torch.mm(g, w) if ctx.needs_input_grad[0] else None
-        dw = torch.mm(g.t(), x2) if ctx.needs_input_grad[1] else None
+        dx = gemm_ex(g, False, w, True) if ctx.needs_input_grad[0] else None
+        dw = gemm_ex(g, True, x2, True) if ctx.needs_input_grad[1] else None
         return dx, dw
 
 
@@ -488,9 +538,8 @@ def logprob_backward(h, weight, targets, lse, grad, dest=None, chunk_rows=4096, 
         check(L.qb_logprob_bwd(_p(logits), r1 - r0, V, logits.stride(0), _p(targets) + 8 * r0,
                                0 if dest is None else _p(dest) + 8 * r0, _p(lse) + 4 * r0, grad_ptr,
                                _p(err_flag()), stream_ptr()), "qb_logprob_bwd")
-        torch.mm(logits, weight, out=dh[r0:r1])
-        # dW += dlogits^T h with fp32 output (one bf16 rounding at the very end)
-        dweight = torch.addmm(dweight, logits.t(), hc, out_dtype=torch.float32)
+        gemm_ex(logits, False, weight, True, out=dh[r0:r1])  # dh = dlogits . W
+        gemm_ex(logits, True, hc, True, out=dweight, mode=2)  # dW += dlogits^T . h in fp32
     return dh, dweight
 
 

@@ -253,8 +253,8 @@ def _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, los
         ops.check(L.qb_logprob_bwd(logits.data_ptr(), t1 - t0, V, logits.stride(0), tgt.data_ptr() + 8 * t0,
                                    dest.data_ptr() + 8 * t0, lse.data_ptr() + 4 * t0, grad_new.data_ptr(),
                                    err.data_ptr(), ops.stream_ptr()), "qb_logprob_bwd")
-        torch.mm(logits, W, out=dhs[t0:t1])
-        dW = torch.addmm(dW, logits.t(), hc, out_dtype=torch.float32)
+        ops.gemm_ex(logits, False, W, True, out=dhs[t0:t1])  # dh = dlogits . W
+        ops.gemm_ex(logits, True, hc, True, out=dW, mode=2)   # dW += dlogits^T . h (fp32)
         del logits
     return dW
 
@@ -353,7 +353,7 @@ def allreduce_grads(model, group=None, bucket_bytes=256 << 20):
 def grpo_step(policy: Qwen3ForCausalLM, optimizer, prompts, *, ref_model=None, group_size=8, max_new_tokens=512,
               temperature=1.0, top_k=None, eos_token_ids=None, rewards=None, reward_gen=None, beta=0.04,
               clip_epsilon=CLIP_EPSILON, shift=True, microbatch_tokens=32768, chunk_rows=4096,
-              process_group=None, return_batch=False):
+              process_group=None, return_batch=False, share_prefix=True):
     """One GRPO step (the north-star path) on this rank's prompt groups.
 
     prompts: list of [1, L] int64 tensors (this rank's share); each is sampled
@@ -367,9 +367,15 @@ def grpo_step(policy: Qwen3ForCausalLM, optimizer, prompts, *, ref_model=None, g
     t0 = time.perf_counter()
     expanded = [p for p in prompts for _ in range(group_size)]
     gids = [i for i in range(len(prompts)) for _ in range(group_size)]
-    seq_tokens, gen, lps, plens = policy.generate_continuous_with_logprobs(
-        expanded, max_new_tokens=max_new_tokens, temperature=temperature, top_k=top_k,
-        eos_token_ids=eos_token_ids)
+    if share_prefix and group_size <= 8:
+        # prompt prefilled once per group, its KV pages shared by the G completions
+        seq_tokens, gen, lps, plens = policy.generate_grouped_with_logprobs(
+            prompts, group_size, max_new_tokens=max_new_tokens, temperature=temperature, top_k=top_k,
+            eos_token_ids=eos_token_ids)
+    else:  # the reference's scheduler: every completion prefilled and stored separately
+        seq_tokens, gen, lps, plens = policy.generate_continuous_with_logprobs(
+            expanded, max_new_tokens=max_new_tokens, temperature=temperature, top_k=top_k,
+            eos_token_ids=eos_token_ids)
     t_roll = time.perf_counter()
     if rewards is None:
         rewards = torch.bernoulli(torch.full((len(expanded),), 0.5), generator=reward_gen)

@@ -328,8 +328,13 @@ class Qwen3Attention(nn.Module):
                                    self.k_cache, self.v_cache, slot_mapping)
         if decode_plan is None:
             o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale)
+        elif decode_plan[0] == "grouped":
+            # prompt pages shared by G completions: read once per group (cascade attention)
+            _, plan, ws, members, shared_len, kv_start = decode_plan
+            o = ops.paged_decode_attention_grouped(q, self.k_cache, self.v_cache, block_tables, context_lens,
+                                                   self.scale, members, shared_len, kv_start, plan, workspace=ws)
         else:
-            split_tokens, max_splits, ws = decode_plan
+            _, split_tokens, max_splits, ws = decode_plan
             o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale,
                                            split_tokens=split_tokens, max_splits=max_splits, workspace=ws)
         return ops.linear(o.view(x.shape[0], -1), self.o_proj.weight)
@@ -655,46 +660,55 @@ class Qwen3ForCausalLM(nn.Module):
         return st
 
     # ---------------------------------------------------------------- CUDA graphs
-    def _init_cuda_graphs(self, max_bs=512, max_ctx=None):
-        """Static decode buffers for batch sizes up to ``max_bs`` (the reference stops at 64)."""
+    def _init_cuda_graphs(self, max_bs=512, max_ctx=None, max_shared=0):
+        """Static decode buffers for batch sizes up to ``max_bs`` (the reference stops at 64).
+        ``max_shared``: longest prompt prefix shared by a group (grouped rollout graphs)."""
         dev = self.lm_head.weight.device
         max_ctx = max_ctx or self.config.max_position_embeddings
         self._graph_max_blocks = -(-max_ctx // self.BLOCK_SIZE)
         self._graph_max_ctx = max_ctx
+        self._graph_max_shared = max_shared
         self._graph_bs = [b for b in self.GRAPH_BATCH_SIZES if b <= max_bs]
         mb = self._graph_bs[-1]
         W = self._graph_max_blocks
-        # packed input layout: ids i64[mb] | pos i64[mb] | offset i64[2] | ctx i32[mb] | slots i32[mb] | bt i32[mb*W]
+        # packed inputs: i64 ids[mb] pos[mb] rng[2] | i32 ctx[mb] slots[mb] bt[mb*W] members[mb*8]
+        #                shared_len[mb] kv_start[mb]
         n64 = 2 * mb + 2
-        n32 = 2 * mb + mb * W
+        n32 = 2 * mb + mb * W + 8 * mb + 2 * mb
         self._gin_host = torch.zeros(n64 * 8 + n32 * 4, dtype=torch.uint8, pin_memory=True)
         self._gin_dev = torch.zeros_like(self._gin_host, device=dev)
-        i64 = self._gin_dev[:n64 * 8].view(torch.int64)
-        i32 = self._gin_dev[n64 * 8:].view(torch.int32)
-        self._graph_bufs = {
-            "input_ids": i64[:mb], "positions": i64[mb:2 * mb], "rng_state": i64[2 * mb:2 * mb + 2],
-            "context_lens": i32[:mb], "slot_mapping": i32[mb:2 * mb],
-            "block_tables": i32[2 * mb:].view(mb, W),
-            "tokens": torch.zeros(mb, dtype=torch.int64, device=dev),
-            "logp": torch.zeros(mb, dtype=torch.float32, device=dev),
-        }
-        hi64 = self._gin_host[:n64 * 8].numpy().view(np.int64)
-        hi32 = self._gin_host[n64 * 8:].numpy().view(np.int32)
-        self._graph_host = {"input_ids": hi64[:mb], "positions": hi64[mb:2 * mb], "rng_state": hi64[2 * mb:2 * mb + 2],
-                            "context_lens": hi32[:mb], "slot_mapping": hi32[mb:2 * mb],
-                            "block_tables": hi32[2 * mb:].reshape(mb, W)}
+
+        def views(i64, i32):
+            o = 2 * mb + mb * W
+            return {"input_ids": i64[:mb], "positions": i64[mb:2 * mb], "rng_state": i64[2 * mb:2 * mb + 2],
+                    "context_lens": i32[:mb], "slot_mapping": i32[mb:2 * mb],
+                    "block_tables": i32[2 * mb:o].reshape(mb, W), "members": i32[o:o + 8 * mb].reshape(mb, 8),
+                    "shared_len": i32[o + 8 * mb:o + 9 * mb], "kv_start": i32[o + 9 * mb:o + 10 * mb]}
+
+        self._graph_bufs = views(self._gin_dev[:n64 * 8].view(torch.int64), self._gin_dev[n64 * 8:].view(torch.int32))
+        self._graph_bufs["tokens"] = torch.zeros(mb, dtype=torch.int64, device=dev)
+        self._graph_bufs["logp"] = torch.zeros(mb, dtype=torch.float32, device=dev)
+        self._graph_host = views(self._gin_host[:n64 * 8].numpy().view(np.int64),
+                                 self._gin_host[n64 * 8:].numpy().view(np.int32))
         self._graphs = {}
         self._graph_pool = None
         self._has_cuda_graphs = False
 
-    def _decode_plan(self, bs):
+    def _decode_plan(self, bs, grouped=False):
         a = self.model.layers[0].self_attn
+        dev = self.lm_head.weight.device
+        if grouped:
+            b = self._graph_bufs
+            plan = ops.grouped_decode_plan(bs, a.num_kv_heads, self._graph_max_shared, self._graph_max_ctx)
+            nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(bs, a.num_heads, a.head_dim, plan[1] + plan[2])
+            ws = torch.empty(nb // 4, dtype=torch.float32, device=dev)
+            return ("grouped", plan, ws, b["members"][:bs], b["shared_len"][:bs], b["kv_start"][:bs])
         split_tokens, max_splits = ops.decode_split_plan(bs, a.num_kv_heads, self._graph_max_ctx)
         ws = None
         if max_splits > 1:
             nb = ops.lib().qb_paged_decode_workspace_bytes(bs, a.num_heads, a.head_dim, max_splits)
-            ws = torch.empty(nb // 4, dtype=torch.float32, device=self.lm_head.weight.device)
-        return split_tokens, max_splits, ws
+            ws = torch.empty(nb // 4, dtype=torch.float32, device=dev)
+        return ("split", split_tokens, max_splits, ws)
 
     def _decode_body(self, bs, plan, temperature, top_k):
         b = self._graph_bufs
@@ -703,20 +717,23 @@ class Qwen3ForCausalLM(nn.Module):
         logits = ops.linear(h, self.lm_head.weight)
         ops.sample(logits, temperature, top_k, 0, b["rng_state"], tokens=b["tokens"][:bs], logp=b["logp"][:bs])
 
-    def _capture_decode_graphs(self, temperature=1.0, top_k=None):
+    def _capture_decode_graphs(self, temperature=1.0, top_k=None, grouped=False):
         """Capture decode+lm_head+sampling graphs for every bucket (largest first, one shared pool)."""
-        key = (float(temperature), top_k)
-        self._graph_key = key
+        self._graph_key = (float(temperature), top_k, bool(grouped))
         self._graphs = {}
         self._graph_pool = None
         self._gin_dev.zero_()
         b = self._graph_bufs
-        b["block_tables"].fill_(0)
+        mb = b["members"].shape[0]
+        # warm-up inputs: every row its own group, nothing shared, writes to slot 0 skipped
+        b["slot_mapping"].fill_(-1)
+        b["members"].fill_(-1)
+        b["members"][:, 0] = torch.arange(mb, dtype=torch.int32, device=b["members"].device)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             for bs in reversed(self._graph_bs):
-                plan = self._decode_plan(bs)
+                plan = self._decode_plan(bs, grouped)
                 self._decode_body(bs, plan, temperature, top_k)  # warm-up outside capture
                 g = torch.cuda.CUDAGraph()
                 n0 = _lib.LAUNCHES[0]
@@ -729,8 +746,10 @@ class Qwen3ForCausalLM(nn.Module):
         torch.cuda.synchronize()
         self._has_cuda_graphs = True
 
-    def _run_decode_graph(self, seqs, rng_counter, rng_seed):
-        """Fill the static inputs with one H2D copy, replay, return (tokens, logp) device views."""
+    def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None):
+        """Fill the static inputs with one H2D copy, replay, return (tokens, logp) device views.
+
+        ``groups`` (grouped graphs): list of (member row indices, shared key count)."""
         bs = len(seqs)
         gbs = _round_bs(bs, self._graph_bs)
         if gbs is None:
@@ -748,6 +767,20 @@ class Qwen3ForCausalLM(nn.Module):
             hb["context_lens"][bs:gbs] = 0
             hb["slot_mapping"][bs:gbs] = -1
             hb["block_tables"][bs:gbs] = 0
+        if self._graph_key[2]:
+            mem, sl, ks = hb["members"], hb["shared_len"], hb["kv_start"]
+            mem[:gbs] = -1
+            sl[:gbs] = 0
+            ks[:gbs] = 0
+            g_i = 0
+            for rows, shared in (groups or [([i], 0) for i in range(bs)]):
+                mem[g_i, :len(rows)] = rows
+                sl[g_i] = shared
+                ks[rows] = shared
+                g_i += 1
+            for r in range(bs, gbs):  # padding rows are singleton groups
+                mem[g_i, 0] = r
+                g_i += 1
         hb["rng_state"][0] = rng_counter
         hb["rng_state"][1] = rng_seed
         self._gin_dev.copy_(self._gin_host, non_blocking=True)
@@ -777,6 +810,76 @@ class Qwen3ForCausalLM(nn.Module):
         return ([s.token_ids for s in seqs], [s.token_ids[s.num_prompt_tokens:] for s in seqs],
                 [s.response_log_probs for s in seqs], [s.num_prompt_tokens for s in seqs])
 
+    def _grouped_setup(self, max_ctx, max_shared, temperature, top_k):
+        """KV pool and grouped decode graphs for a grouped rollout; returns the step context."""
+        dev = self.lm_head.weight.device
+        self.allocate_global_kv_cache()
+        seed = int(torch.randint(0, 2**62, (1,)).item())
+        key = (float(temperature), top_k, True)
+        if (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx or getattr(self, "_graph_key", None) != key
+                or getattr(self, "_graph_max_shared", -1) < max_shared):
+            self._init_cuda_graphs(max_bs=512, max_ctx=max(max_ctx, 1024), max_shared=max(max_shared, 256))
+            self._capture_decode_graphs(temperature, top_k, grouped=True)
+        cap = 2 * self.MAX_TOKENS_PER_STEP + 512 * 8
+        return {"dev": dev, "seed": seed, "temperature": temperature, "top_k": top_k,
+                "rng": torch.tensor([0, seed], dtype=torch.int64, device=dev),
+                "tok_host": torch.empty(cap, dtype=torch.int64, pin_memory=True),
+                "lp_host": torch.empty(cap, dtype=torch.float32, pin_memory=True),
+                "err_host": torch.zeros(1, dtype=torch.int32, pin_memory=True), "err": ops.err_flag(dev)}
+
+    def _grouped_launch(self, ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples):
+        """Enqueues one grouped-rollout step: a cascade-attention decode graph when only decode
+        rows run, else a varlen paged prefill with the donors' chunks and the decode rows; the
+        partial last prompt page of each finished prefill is copied to the other members; then
+        lm_head + sampling (G draws from each finished prefill's last row) and the read-back."""
+        dev, temperature, top_k = ctx["dev"], ctx["temperature"], ctx["top_k"]
+        r = None
+        if not prefill:
+            r = self._run_decode_graph(decode_rows, step, ctx["seed"], groups=groups_rows)
+            if r is None:
+                ids, pos, cl, bt, slots = self._prepare_decode(decode_rows)
+                h = self.model.forward_decode(ids, pos, cl, bt, slots)
+                logits = ops.linear(h, self.lm_head.weight)
+                ctx["rng"][0].fill_(step)
+                r = ops.sample(logits, temperature, top_k, 0, ctx["rng"])
+        else:
+            seqs = [g.donor for g in prefill] + decode_rows
+            arrays, m_q, m_k = self._step_arrays(seqs)
+            ends = np.cumsum([s.num_scheduled_tokens for s in seqs]) - 1
+            rows_np = np.asarray([ends[prefill.index(g)] for g in done for _ in range(G)]
+                                 + [ends[len(prefill) + j] for j in range(len(decode_rows))], dtype=np.int64)
+            ids, pos, cu_q, cu_k, blk_map, bt, tiles, rows = self._staging().put(arrays + [rows_np])
+            h = self.model.forward_prefill(ids, pos, cu_q, cu_k, m_q, m_k, blk_map, bt, tiles=tiles)
+            for g in done:  # each member gets its own copy of the partial last prompt page
+                if g.partial and G > 1:
+                    dst = torch.tensor([m.block_table[g.n_full] for m in g.members[1:]], dtype=torch.int32,
+                                       device=dev)
+                    _copy_page_prefix(self, g.members[0].block_table[g.n_full], dst, g.partial)
+            logits = ops.linear(h.index_select(0, rows), self.lm_head.weight)
+            ctx["rng"][0].fill_(step)
+            r = ops.sample(logits, temperature, top_k, 0, ctx["rng"])
+        toks_dev, logp_dev = r
+        ctx["tok_host"][:n_samples].copy_(toks_dev, non_blocking=True)
+        ctx["lp_host"][:n_samples].copy_(logp_dev, non_blocking=True)
+        ctx["err_host"].copy_(ctx["err"], non_blocking=True)
+
+    @torch.no_grad()
+    def generate_grouped_with_logprobs(self, prompt_ids_list, group_size, max_new_tokens=256, temperature=0.6,
+                                       top_k=20, eos_token_ids=None):
+        """GRPO rollout: ``group_size`` (<= 8) completions of every prompt, the prompt prefilled once
+        per group and its K/V pages shared (cascade decode attention reads them once per step).
+
+        Returns the 4-tuple of :meth:`generate_continuous_with_logprobs` for the list in which each
+        prompt is repeated ``group_size`` times consecutively.  Sampling and log-probs follow the same
+        distribution; page ids and step boundaries differ from the reference's scheduler, which
+        prefills every completion separately (use generate_continuous_with_logprobs for that)."""
+        if not 1 <= group_size <= 8:
+            raise ValueError("group_size must be in [1, 8]")
+        prompts = [p[0].tolist() if isinstance(p, torch.Tensor) else list(p[0]) for p in prompt_ids_list]
+        seqs = _generate_grouped(self, prompts, group_size, max_new_tokens, temperature, top_k, eos_token_ids)
+        return ([s.token_ids for s in seqs], [s.token_ids[s.num_prompt_tokens:] for s in seqs],
+                [s.response_log_probs for s in seqs], [s.num_prompt_tokens for s in seqs])
+
     # -- device side of one generation step (kept behind two methods so the host
     #    scheduler can be exercised on its own)
     def _gen_setup(self, prompts, max_new_tokens, temperature, top_k):
@@ -786,7 +889,7 @@ class Qwen3ForCausalLM(nn.Module):
         max_ctx = self.max_model_len or (max((len(p) for p in prompts), default=1) + max_new_tokens)
         seed = int(torch.randint(0, 2**62, (1,)).item())
         if (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx
-                or getattr(self, "_graph_key", None) != (float(temperature), top_k)):
+                or getattr(self, "_graph_key", None) != (float(temperature), top_k, False)):
             if not self._has_cuda_graphs or self._graph_max_ctx < max_ctx:
                 self._init_cuda_graphs(max_bs=512, max_ctx=max(max_ctx, 1024))
             self._capture_decode_graphs(temperature, top_k)
@@ -955,6 +1058,216 @@ class Qwen3ForCausalLM(nn.Module):
             for seq in scheduled:
                 seq.num_scheduled_tokens = 0
         return all_seqs
+
+
+class _Group:
+    """G completions of one prompt: one prefill (``donor``), shared full prompt pages."""
+
+    def __init__(self, idx, prompt, G, sp):
+        self.idx = idx
+        self.prompt = list(prompt)
+        self.L = len(prompt)
+        self.G = G
+        self.sp = sp
+        self.members = [Sequence(prompt, sp) for _ in range(G)]
+        self.reset()
+
+    def reset(self):
+        self.state = "WAITING"
+        self.donor = Sequence(self.prompt, self.sp)
+        self.shared = []
+        for m in self.members:
+            m.token_ids = list(self.prompt)
+            m.last_token = self.prompt[-1]
+            m.kv_len = 0
+            m.block_table = []
+            m.response_log_probs = []
+            m.status = "WAITING"
+            m.num_scheduled_tokens = 0
+
+    @property
+    def n_full(self):
+        return self.L // Sequence.BLOCK_SIZE
+
+    @property
+    def partial(self):
+        return self.L % Sequence.BLOCK_SIZE
+
+    def pages_needed(self):
+        return self.n_full + (self.G if self.partial else 0)
+
+
+def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos_token_ids, record_logprobs=True):
+    """Continuous-batching rollout of G completions per prompt with the prompt computed once.
+
+    Scheduling follows the reference's loop (decode first, 2048-token budget, chunked prefill,
+    LIFO preemption) at the granularity of a group.  A group's full prompt pages are shared by
+    its members (reference-counted once per member); each member owns a copy of the partially
+    filled last prompt page and everything it generates.  The first token of every member is
+    sampled from the single prefill's last row (G independent draws)."""
+    BS = model.BLOCK_SIZE
+    sp = {"temperature": temperature, "max_tokens": max_new_tokens}
+    groups = [_Group(i, p, G, sp) for i, p in enumerate(prompts)]
+    max_ctx = model.max_model_len or (max((len(p) for p in prompts), default=1) + max_new_tokens)
+    max_shared = max((g.n_full * BS for g in groups), default=0)
+    ctx = model._grouped_setup(max_ctx, max_shared, temperature, top_k)
+    bm = BlockManager(model._num_blocks, BS)
+    eos = set(eos_token_ids) if eos_token_ids is not None else None
+    waiting = deque(groups)
+    running: list[_Group] = []
+    step = 0
+
+    def release(grp):
+        for m in grp.members:
+            if m.block_table:
+                bm.deallocate(m.block_table)
+                m.block_table = []
+
+    def preempt(grp):
+        release(grp)
+        grp.reset()
+        running.remove(grp)
+        waiting.appendleft(grp)
+
+    while waiting or running:
+        budget = model.MAX_TOKENS_PER_STEP
+        decode_rows: list[Sequence] = []
+        prefill: list[_Group] = []
+        # ---- running groups: decoding members first, then a group still in prefill
+        gi = 0
+        while gi < len(running) and budget > 0:
+            grp = running[gi]
+            if grp.state == "DECODE":
+                preempted = False
+                for m in grp.members:
+                    if m.status != "RUNNING" or budget <= 0:
+                        continue
+                    if m.num_completion_tokens >= m.max_tokens:
+                        m.status = "FINISHED"
+                        bm.deallocate(m.block_table)
+                        m.block_table = []
+                        continue
+                    if m.kv_len % BS == 0:
+                        while not bm.free:
+                            victim = running[-1]
+                            preempt(victim)
+                            if victim is grp:
+                                preempted = True
+                                break
+                        if preempted:
+                            break
+                        m.block_table.append(bm._take_free())
+                    m.num_scheduled_tokens = 1
+                    decode_rows.append(m)
+                    budget -= 1
+                if preempted:
+                    decode_rows = [r for r in decode_rows if r not in grp.members]
+                    continue
+                if all(m.status == "FINISHED" for m in grp.members):
+                    grp.state = "FINISHED"
+                    running.pop(gi)
+                    continue
+            elif grp.state == "PREFILL":
+                d = grp.donor
+                d.num_scheduled_tokens = min(grp.L - d.kv_len, budget)
+                budget -= d.num_scheduled_tokens
+                prefill.append(grp)
+            gi += 1
+        # ---- admit waiting groups
+        while waiting and budget > 0:
+            grp = waiting[0]
+            if grp.state == "WAITING":
+                if bm.available < grp.pages_needed():
+                    break
+                grp.shared = [bm._take_free() for _ in range(grp.n_full)]
+                for p in grp.shared:
+                    bm.ref_count[p] = G  # one reference per member
+                own = [bm._take_free() for _ in range(G)] if grp.partial else []
+                for i, m in enumerate(grp.members):
+                    m.block_table = grp.shared + ([own[i]] if own else [])
+                grp.donor.block_table = grp.members[0].block_table
+                grp.state = "PREFILL"
+            waiting.popleft()
+            running.append(grp)
+            d = grp.donor
+            remaining = grp.L - d.kv_len
+            if remaining <= budget:
+                d.num_scheduled_tokens = remaining
+            elif not decode_rows and not prefill:
+                d.num_scheduled_tokens = budget
+            else:
+                waiting.appendleft(grp)
+                running.pop()
+                break
+            budget -= d.num_scheduled_tokens
+            prefill.append(grp)
+        if not decode_rows and not prefill:
+            continue
+
+        # ---- device step (Step 4 bookkeeping below overlaps it)
+        step += 1
+        done = [g for g in prefill if g.donor.kv_len + g.donor.num_scheduled_tokens >= g.L]
+        n_samples = len(decode_rows) + G * len(done)
+        groups_rows = []
+        if not prefill:
+            pos_of = {id(m): i for i, m in enumerate(decode_rows)}
+            for grp in running:
+                rows = [pos_of[id(m)] for m in grp.members if id(m) in pos_of]
+                if rows:
+                    groups_rows.append((rows, grp.n_full * BS))
+        model._grouped_launch(ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples)
+        for g in prefill:
+            g.donor.kv_len += g.donor.num_scheduled_tokens
+            g.donor.num_scheduled_tokens = 0
+        for m in decode_rows:
+            m.kv_len += 1
+            m.num_scheduled_tokens = 0
+        toks, lps = model._finish_step(ctx, None, n_samples, True)
+        k = 0
+
+        def take(m):
+            nonlocal k
+            tok, lp = toks[k], lps[k]
+            k += 1
+            m.append_token(tok)
+            if record_logprobs:
+                m.response_log_probs.append(lp)
+            if (eos is not None and tok in eos) or m.num_completion_tokens >= m.max_tokens:
+                m.status = "FINISHED"
+                bm.deallocate(m.block_table)
+                m.block_table = []
+
+        for g in done:
+            g.state = "DECODE"
+            for m in g.members:
+                m.kv_len = g.L
+                m.status = "RUNNING"
+                take(m)
+        for m in decode_rows:
+            take(m)
+        for g in list(running):
+            if g.state == "DECODE" and all(m.status == "FINISHED" for m in g.members):
+                g.state = "FINISHED"
+                running.remove(g)
+    if bm.available != bm.num_blocks or any(bm.ref_count):
+        raise RuntimeError("grouped rollout finished with KV pages still referenced")
+    return [m for g in groups for m in g.members]
+
+
+def _copy_page_prefix(model, src_page, dst_pages, n_tokens):
+    """Copy the first n_tokens rows of KV page src_page to dst_pages in every layer."""
+    a0 = model.model.layers[0].self_attn
+    k, v = a0.k_cache, a0.v_cache  # views of the [layers, blocks, 256, hkv, D] pools
+    layers = len(model.model.layers)
+    layer_bytes = k.numel() * k.element_size()
+    if layers > 1:
+        layer_bytes = (model.model.layers[1].self_attn.k_cache.data_ptr() - k.data_ptr())
+    page_bytes = k.stride(0) * k.element_size()
+    row_bytes = k.stride(1) * k.element_size()
+    ops.check(ops.lib().qb_copy_page_prefix(k.data_ptr(), v.data_ptr(), layers, layer_bytes, page_bytes, k.shape[0],
+                                            int(src_page), dst_pages.data_ptr(), dst_pages.numel(),
+                                            n_tokens * row_bytes, ops.err_flag().data_ptr(), ops.stream_ptr()),
+              "qb_copy_page_prefix")
 
 
 def use_reference_defaults():

@@ -61,3 +61,32 @@ def test_gemm_repeated_calls_stable(cuda):
     first = ops.gemm(a, b)
     for _ in range(20):
         assert torch.equal(ops.gemm(a, b), first)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 1024, 776), (1000, 384, 4096), (64, 151936, 200)])
+def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
+    """Backward layouts: A stored [K, M] and/or B stored [K, N]; K need not be a multiple of 64
+    (row pitches stay multiples of 8 elements, the TMA rule)."""
+    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(torch.bfloat16)
+    a_st = a.t().contiguous() if a_mn else a
+    b_st = b.t().contiguous() if b_mn else b
+    c = ops.gemm_ex(a_st, a_mn, b_st, b_mn)
+    r = ref(a, b)
+    err = (c.float() - r).abs().max().item()
+    assert err <= 1e-2 * r.abs().max().item() + 1e-3, err
+    acc = torch.randn(M, N, device=cuda, generator=g)
+    out = acc.clone()
+    ops.gemm_ex(a_st, a_mn, b_st, b_mn, out=out, mode=2)
+    assert torch.allclose(out, acc + r, rtol=1e-3, atol=2e-2)
+
+
+def test_gemm_k_tail_k_major(cuda):
+    g = torch.Generator(device=cuda).manual_seed(3)
+    a = torch.randn(200, 100, device=cuda, generator=g).to(torch.bfloat16)[:, :72]
+    b = torch.randn(300, 100, device=cuda, generator=g).to(torch.bfloat16)[:, :72]
+    c = ops.gemm_ex(a.contiguous(), False, b.contiguous(), False)
+    r = ref(a, b)
+    assert (c.float() - r).abs().max().item() <= 1e-2 * r.abs().max().item()

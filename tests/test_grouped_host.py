@@ -1,0 +1,101 @@
+"""Host logic of the grouped (shared-prompt) rollout, CPU only.
+
+The device step is replaced by a deterministic stand-in: member i's first token is a
+function of the prompt and i, every later token a function of the previous token and its
+position.  Whatever the scheduling (chunked prefill, preemption), each completion must
+come out identical to a direct chain; pages must be shared exactly within a group, owned
+pages never shared, and the pool must be fully released at the end.
+"""
+import numpy as np
+import pytest
+import torch
+
+from qwen3_naive_inference_b200 import qwen3_naive as QN
+from qwen3_naive_inference_b200.qwen3_naive import Qwen3ForCausalLM
+
+V = 4096
+
+
+def nxt(tok, pos):
+    return (tok * 7 + pos * 13 + 1) % V
+
+
+class HostGrouped(Qwen3ForCausalLM):
+    def __init__(self, num_blocks):
+        torch.nn.Module.__init__(self)
+        self._num_blocks = num_blocks
+        self.max_model_len = None
+        self.checks = 0
+        self.resets = 0
+
+    def _grouped_setup(self, max_ctx, max_shared, temperature, top_k):
+        return {}
+
+    def _grouped_launch(self, ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples):
+        toks = []
+        for g in done:
+            for i in range(G):
+                toks.append((nxt(g.prompt[-1], g.L - 1) + i) % V)
+        for m in decode_rows:
+            toks.append(nxt(m.last_token, m.kv_len))
+        # structural checks on the page tables of everything that runs this step
+        own_seen = set()
+        for rows, shared in groups_rows:
+            members = [decode_rows[r] for r in rows]
+            n_full = shared // 256
+            first = members[0].block_table[:n_full]
+            for m in members:
+                assert m.block_table[:n_full] == first
+                for p in m.block_table[n_full:]:
+                    assert p not in own_seen
+                    own_seen.add(p)
+        self.checks += 1
+        ctx["toks"] = toks
+        assert len(toks) == n_samples
+
+    def _finish_step(self, ctx, pending, n, record_logprobs):
+        return ctx.get("toks", [])[:n], [0.0] * n
+
+
+def expected(prompt, i, n):
+    L = len(prompt)
+    t = (nxt(prompt[-1], L - 1) + i) % V
+    out = [t]
+    for k in range(n - 1):
+        t = nxt(t, L + k)
+        out.append(t)
+    return out
+
+
+@pytest.mark.parametrize("num_blocks,lens,G,new", [
+    (400, [5, 256, 300, 700, 2100, 512, 1], 8, 40),  # roomy pool, chunked prefill of a long prompt
+    (30, [600, 300, 200, 256], 4, 300),                # tight pool: group preemption
+    (60, [100] * 12, 8, 20),                           # many groups, all partial pages
+])
+def test_grouped_rollout_host_logic(num_blocks, lens, G, new):
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, V, L).tolist() for L in lens]
+    m = HostGrouped(num_blocks)
+    resets = [0]
+    orig = QN._Group.reset
+
+    def counting_reset(self):
+        resets[0] += 1
+        orig(self)
+
+    QN._Group.reset = counting_reset
+    try:
+        toks, gen, lps, plens = m.generate_grouped_with_logprobs([torch.tensor([p]) for p in prompts], G,
+                                                                 max_new_tokens=new, temperature=1.0, top_k=None)
+    finally:
+        QN._Group.reset = orig
+    assert plens == [len(p) for p in prompts for _ in range(G)]
+    for gi, p in enumerate(prompts):
+        for i in range(G):
+            k = gi * G + i
+            assert gen[k] == expected(p, i, new), (gi, i)
+            assert toks[k] == p + gen[k]
+            assert len(lps[k]) == new
+    assert m.checks > 0
+    if num_blocks == 30:
+        assert resets[0] > len(prompts)  # at least one group was preempted and restarted

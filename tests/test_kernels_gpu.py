@@ -318,3 +318,44 @@ def test_grpo_advantage_and_loss(cuda):
         loss.backward()
         assert abs(loss.item() - loss_ref.item()) <= 2e-3 * abs(loss_ref.item()) + 1e-6
         assert torch.allclose(nd.grad.cpu(), grad_ref, rtol=1e-4, atol=1e-7)
+
+
+@pytest.mark.parametrize("split", [64, 256])
+def test_paged_decode_grouped_shared_prefix(cuda, split):
+    """Groups sharing prompt pages: the cascade (shared keys once per group + own keys per
+    sequence + merge) equals plain paged decode attention on the same page tables."""
+    g = gen(77 + split)
+    hq, hkv = 16, 8
+    groups = [(8, 512), (3, 256), (1, 0), (5, 768), (8, 0)]  # (members, shared keys)
+    n_pages = 200
+    kc = torch.randn(n_pages, 256, hkv, 128, generator=g).to(BF)
+    vc = torch.randn(n_pages, 256, hkv, 128, generator=g).to(BF)
+    perm = torch.randperm(n_pages, generator=g).tolist()
+    tables, lens, members, shared, kv_start = [], [], [], [], []
+    for G_, sl in groups:
+        shared_pages = [perm.pop() for _ in range(sl // 256)]
+        row = []
+        for _ in range(G_):
+            L = sl + int(torch.randint(1, 700, (1,), generator=g))
+            own = [perm.pop() for _ in range((L - sl + 255) // 256)]
+            row.append(len(tables))
+            tables.append(shared_pages + own)
+            lens.append(L)
+            kv_start.append(sl)
+        members.append(row + [-1] * (8 - len(row)))
+        shared.append(sl)
+    B = len(tables)
+    width = max(len(t) for t in tables)
+    bt = torch.full((B, width), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    q = torch.randn(B, hq, 128, generator=g).to(BF)
+    ctx = torch.tensor(lens, dtype=torch.int32) - 1
+    ref = R.paged_decode(q, kc, vc, bt, ctx + 1, 128 ** -0.5)
+    plan = (split, -(-max(shared) // split) if max(shared) else 1, -(-max(L - s for L, s in zip(lens, kv_start)) // split))
+    out = ops.paged_decode_attention_grouped(q.to(cuda), kc.to(cuda), vc.to(cuda), bt.to(cuda), ctx.to(cuda),
+                                             128 ** -0.5, torch.tensor(members, dtype=torch.int32).to(cuda),
+                                             torch.tensor(shared, dtype=torch.int32).to(cuda),
+                                             torch.tensor(kv_start, dtype=torch.int32).to(cuda), plan)
+    close_bf16(out, ref, 2e-2)
+    ops.check_device_errors()

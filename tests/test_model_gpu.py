@@ -252,6 +252,53 @@ def test_fused_grpo_step_matches_autograd_path(setup, cuda):
         assert 1 - cos.item() < 1e-2, (k, cos.item())
 
 
+def test_grouped_rollout_teacher_forced(setup, cuda):
+    """Shared-prompt rollout (one prefill per group, cascade decode attention): greedy tokens and
+    full-vocabulary log-probs match the oracle teacher-forced on the produced sequences."""
+    cfg, params, model = setup
+    g = torch.Generator().manual_seed(10)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, L), generator=g) for L in (30, 260, 520)]
+    torch.manual_seed(4)
+    toks, gen, lps, plens = model.generate_grouped_with_logprobs([p.to(cuda) for p in prompts], 4,
+                                                                 max_new_tokens=16, temperature=1.0, top_k=1)
+    assert plens == [30] * 4 + [260] * 4 + [520] * 4
+    checked = 0
+    for t, pl in zip(toks, plens):
+        lg, _ = _oracle_lp(params, cfg, t)
+        for pos in range(pl, len(t)):
+            top2 = lg[pos - 1].topk(2).values
+            if (top2[0] - top2[1]).item() > 0.05:
+                assert t[pos] == lg[pos - 1].argmax().item(), (pl, pos)
+                checked += 1
+    assert checked > 60
+    torch.manual_seed(5)
+    toks, gen, lps, plens = model.generate_grouped_with_logprobs([p.to(cuda) for p in prompts], 4,
+                                                                 max_new_tokens=12, temperature=1.0, top_k=None)
+    members_differ = len({tuple(x) for x in gen[:4]}) > 1
+    assert members_differ  # independent draws per member
+    for t, lp, pl in zip(toks, lps, plens):
+        lg, _ = _oracle_lp(params, cfg, t)
+        for j, v in enumerate(lp):
+            _, logps = R.sample_distribution(lg[pl + j - 1][None].to(torch.bfloat16), 1.0, None)
+            ref = logps[0, t[pl + j]].item()
+            assert abs(v - ref) < 2e-3 * abs(ref) + 0.05, (pl, j, v, ref)
+    ops.check_device_errors()
+
+
+def test_grouped_rollout_matches_plain_greedy(setup, cuda):
+    cfg, params, model = setup
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, L), generator=g).to(cuda) for L in (77, 300)]
+    torch.manual_seed(6)
+    _, grouped, _, _ = model.generate_grouped_with_logprobs(prompts, 2, max_new_tokens=20, top_k=1, temperature=1.0)
+    torch.manual_seed(6)
+    _, plain = model.generate_continuous([p for p in prompts for _ in range(2)], max_new_tokens=20, top_k=1,
+                                         temperature=1.0)
+    a, b = sum(grouped, []), sum(plain, [])
+    assert len(a) == len(b)
+    assert np.mean([x == y for x, y in zip(a, b)]) > 0.95
+
+
 def test_grpo_step_end_to_end(setup, cuda):
     cfg, params, model = setup
     ref = G.make_reference_copy(model)
