@@ -53,6 +53,10 @@ def parse():
     ap.add_argument("--decode-batch", type=int, default=256, help="batch of the decode microbenchmark")
     ap.add_argument("--gemm-only", action="store_true",
                     help="only the tcgen05 GEMM microbenchmark on the model's projection shapes")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="eager decode launches (for launch-list profiling; ncu and graph replays do not mix)")
+    ap.add_argument("--no-share-prefix", action="store_true",
+                    help="roll out with the reference's scheduler (every completion prefilled and stored)")
     return ap.parse_args()
 
 
@@ -268,6 +272,7 @@ def run_ours(args):
     # pages for every sequence of the step at once (64*8 seqs x 4 pages) plus slack
     policy._num_blocks = args.prompts * args.group * math.ceil(max_ctx / 256) + 64
     policy.max_model_len = max_ctx
+    policy.use_cuda_graphs = not args.no_graphs
     opt = torch.optim.AdamW(policy.parameters(), lr=1e-6)
     reward_gen = torch.Generator().manual_seed(2 + rank)
     torch.manual_seed(1234 + rank)
@@ -276,7 +281,7 @@ def run_ours(args):
         return G.grpo_step(policy, opt, prompts, ref_model=ref, group_size=args.group,
                            max_new_tokens=args.new_tokens, temperature=1.0, top_k=None, eos_token_ids=None,
                            reward_gen=reward_gen, beta=0.04, shift=True,
-                           microbatch_tokens=args.microbatch_tokens)
+                           microbatch_tokens=args.microbatch_tokens, share_prefix=not args.no_share_prefix)
 
     for i in range(args.warmup):
         step(i, make_prompts(args, rank, i, dev))
@@ -356,6 +361,8 @@ def run_ours(args):
                 "config": {"workload": WORKLOAD, "prompts_per_gpu": args.prompts, "group": args.group,
                            "new_tokens": args.new_tokens, "prompt_len": [args.prompt_min, args.prompt_max],
                            "layers": args.layers, "parallelism": f"dp{world}", "beta_kl": 0.04,
+                           "rollout": "reference scheduler" if args.no_share_prefix else
+                           "grouped: prompt prefilled once per group, shared KV pages, cascade decode attention",
                            "l2": "inputs far larger than L2 (weights + 60+ GB KV cache per step)",
                            "tokens_per_step": tokens // max(1, args.steps)},
                 "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"]},

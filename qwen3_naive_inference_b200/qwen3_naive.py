@@ -544,6 +544,7 @@ class Qwen3ForCausalLM(nn.Module):
         self._num_blocks = 0
         self._graphs = {}
         self._has_cuda_graphs = False
+        self.use_cuda_graphs = True  # decode steps replay captured graphs (False: eager launches)
         self.max_model_len = None  # KV positions a sequence may reach; default = prompt + max_new_tokens
 
     def forward(self, x):
@@ -816,7 +817,9 @@ class Qwen3ForCausalLM(nn.Module):
         self.allocate_global_kv_cache()
         seed = int(torch.randint(0, 2**62, (1,)).item())
         key = (float(temperature), top_k, True)
-        if (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx or getattr(self, "_graph_key", None) != key
+        if not self.use_cuda_graphs:
+            self._has_cuda_graphs = False
+        elif (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx or getattr(self, "_graph_key", None) != key
                 or getattr(self, "_graph_max_shared", -1) < max_shared):
             self._init_cuda_graphs(max_bs=512, max_ctx=max(max_ctx, 1024), max_shared=max(max_shared, 256))
             self._capture_decode_graphs(temperature, top_k, grouped=True)
@@ -835,10 +838,25 @@ class Qwen3ForCausalLM(nn.Module):
         dev, temperature, top_k = ctx["dev"], ctx["temperature"], ctx["top_k"]
         r = None
         if not prefill:
-            r = self._run_decode_graph(decode_rows, step, ctx["seed"], groups=groups_rows)
-            if r is None:
-                ids, pos, cl, bt, slots = self._prepare_decode(decode_rows)
-                h = self.model.forward_decode(ids, pos, cl, bt, slots)
+            if self._has_cuda_graphs:
+                r = self._run_decode_graph(decode_rows, step, ctx["seed"], groups=groups_rows)
+            if r is None:  # eager decode with the same cascade attention
+                bs = len(decode_rows)
+                ids, pos, cl, bt, slots = self._decode_arrays(decode_rows)
+                mem = np.full((len(groups_rows), 8), -1, dtype=np.int32)
+                sl = np.zeros(len(groups_rows), dtype=np.int32)
+                ks = np.zeros(bs, dtype=np.int32)
+                for gi, (rows_g, shared) in enumerate(groups_rows):
+                    mem[gi, :len(rows_g)] = rows_g
+                    sl[gi] = shared
+                    ks[rows_g] = shared
+                ids, pos, cl, bt, slots, mem_d, sl_d, ks_d = self._staging().put([ids, pos, cl, bt, slots, mem, sl, ks])
+                a = self.model.layers[0].self_attn
+                plan = ops.grouped_decode_plan(bs, a.num_kv_heads, int(sl.max(initial=0)), int(cl.max(initial=0)) + 1)
+                nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(bs, a.num_heads, a.head_dim, plan[1] + plan[2])
+                ws = torch.empty(nb // 4, dtype=torch.float32, device=dev)
+                h = self.model.forward_decode(ids, pos, cl, bt, slots,
+                                              decode_plan=("grouped", plan, ws, mem_d, sl_d, ks_d))
                 logits = ops.linear(h, self.lm_head.weight)
                 ctx["rng"][0].fill_(step)
                 r = ops.sample(logits, temperature, top_k, 0, ctx["rng"])
@@ -888,7 +906,9 @@ class Qwen3ForCausalLM(nn.Module):
         self.allocate_global_kv_cache()
         max_ctx = self.max_model_len or (max((len(p) for p in prompts), default=1) + max_new_tokens)
         seed = int(torch.randint(0, 2**62, (1,)).item())
-        if (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx
+        if not self.use_cuda_graphs:
+            self._has_cuda_graphs = False
+        elif (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx
                 or getattr(self, "_graph_key", None) != (float(temperature), top_k, False)):
             if not self._has_cuda_graphs or self._graph_max_ctx < max_ctx:
                 self._init_cuda_graphs(max_bs=512, max_ctx=max(max_ctx, 1024))
