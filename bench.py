@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--decode-batch", type=int, default=256, help="batch of the decode microbenchmark")
     ap.add_argument("--gemm-only", action="store_true",
                     help="only the tcgen05 GEMM microbenchmark on the model's projection shapes")
+    ap.add_argument("--gemm-shape", default=None, help="M,N,K: run --gemm-only on this one shape")
+    ap.add_argument("--rollout-attn", action="store_true",
+                    help="only plain vs grouped decode attention on a mid-rollout batch")
     ap.add_argument("--no-graphs", action="store_true",
                     help="eager decode launches (for launch-list profiling; ncu and graph replays do not mix)")
     ap.add_argument("--no-share-prefix", action="store_true",
@@ -365,7 +368,8 @@ def run_ours(args):
                            "grouped: prompt prefilled once per group, shared KV pages, cascade decode attention",
                            "l2": "inputs far larger than L2 (weights + 60+ GB KV cache per step)",
                            "tokens_per_step": tokens // max(1, args.steps)},
-                "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"]},
+                "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"],
+                             "rollout_detail": last.get("rollout_stats")},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
                 "cpu_baseline": cpu, "decode_attn_gbs": achieved}
         print(json.dumps(line), flush=True)
@@ -385,6 +389,79 @@ def run_decode_only(batch):
                       "achieved_gbs": nbytes / (ms / 1000) / 1e9}), flush=True)
 
 
+def run_rollout_attn():
+    """Decode attention mid-rollout (config 4 shapes): 64 groups x 8 completions, prompt U[64,512],
+    256 generated tokens each.  Plain paged decode (every completion reads its prompt K/V) vs the
+    grouped cascade (the group's prompt pages read once).  Prints ms and K/V bytes read."""
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(5)
+    G, n_groups, gen, hq, hkv, D = 8, 64, 256, 16, 8, 128
+    B = G * n_groups
+    plens = torch.randint(64, 513, (n_groups,), generator=g).tolist()
+    pages_needed = sum(-(-L // 256) + G * (-(-(gen + L % 256) // 256)) for L in plens) + 16
+    kc = torch.randn(pages_needed, 256, hkv, D, device=dev, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    free = list(range(pages_needed))
+    tables, lens, members, shared, kv_start = [], [], [], [], []
+    for L in plens:
+        n_full = L // 256
+        sh = [free.pop() for _ in range(n_full)]
+        row = []
+        for _ in range(G):
+            own = [free.pop() for _ in range(-(-(L - n_full * 256 + gen) // 256))]
+            row.append(len(tables))
+            tables.append(sh + own)
+            lens.append(L + gen)
+            kv_start.append(n_full * 256)
+        members.append(row)
+        shared.append(n_full * 256)
+    W = max(len(t) for t in tables)
+    bt = torch.full((B, W), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    bt = bt.to(dev)
+    cl = (torch.tensor(lens, dtype=torch.int32) - 1).to(dev)
+    q = torch.randn(B, hq, D, device=dev, dtype=torch.bfloat16)
+    mem_d = torch.tensor(members, dtype=torch.int32, device=dev)
+    sl_d = torch.tensor(shared, dtype=torch.int32, device=dev)
+    ks_d = torch.tensor(kv_start, dtype=torch.int32, device=dev)
+    split, ms = ops.decode_split_plan(B, hkv, max(lens))
+    plan = ops.grouped_decode_plan(B, hkv, max(shared), max(L - s for L, s in zip(lens, kv_start)))
+    ws_p = torch.empty(max(1, ops.lib().qb_paged_decode_workspace_bytes(B, hq, D, ms) // 4), device=dev)
+    ws_g = torch.empty(ops.lib().qb_paged_decode_grouped_workspace_bytes(B, hq, D, plan[1] + plan[2]) // 4,
+                       device=dev)
+    runs = {
+        "plain": lambda: ops.paged_decode_attention(q, kc, vc, bt, cl, D ** -0.5, split_tokens=split, max_splits=ms,
+                                                    workspace=ws_p),
+        "grouped": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt, cl, D ** -0.5, mem_d, sl_d, ks_d, plan,
+                                                              workspace=ws_g),
+    }
+    out = {}
+    for name, fn in runs.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(20):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        out[name] = a.elapsed_time(b) / 20
+    err = (runs["plain"]().float() - runs["grouped"]().float()).abs().max().item()
+    kv_plain = sum(lens) * hkv * D * 4
+    kv_grouped = (sum(shared) + sum(L - s for L, s in zip(lens, kv_start))) * hkv * D * 4
+    print(json.dumps({"rollout_attn": {"ms": out, "kv_bytes": {"plain": kv_plain, "grouped": kv_grouped},
+                                       "gbs": {"plain": kv_plain / out["plain"] / 1e6,
+                                               "grouped_effective": kv_plain / out["grouped"] / 1e6,
+                                               "grouped_actual": kv_grouped / out["grouped"] / 1e6},
+                                       "plan": {"plain": [split, ms], "grouped": list(plan)},
+                                       "max_abs_diff": err}}), flush=True)
+
+
 GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
     "qkv_proj": (8192, 4096, 1024), "o_proj": (8192, 1024, 2048), "gate_up_proj": (8192, 6144, 1024),
     "down_proj": (8192, 1024, 3072), "lm_head": (4096, 151936, 1024), "qkv_decode512": (512, 4096, 1024),
@@ -392,7 +469,7 @@ GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
 }
 
 
-def run_gemm_only():
+def run_gemm_only(shape=None):
     import torch
 
     from qwen3_naive_inference_b200 import ops
@@ -400,7 +477,8 @@ def run_gemm_only():
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("bf16_tflops", 1590.0)
     out = {}
-    for name, (M, N, K) in GEMM_SHAPES.items():
+    shapes = GEMM_SHAPES if shape is None else {"custom": tuple(int(x) for x in shape.split(","))}
+    for name, (M, N, K) in shapes.items():
         g = torch.Generator(device=dev).manual_seed(0)
         a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         b = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
@@ -429,8 +507,10 @@ def run_gemm_only():
 
 def main():
     args = parse()
-    if args.gemm_only:
-        run_gemm_only()
+    if args.rollout_attn:
+        run_rollout_attn()
+    elif args.gemm_only:
+        run_gemm_only(args.gemm_shape)
     elif args.decode_only:
         run_decode_only(args.decode_batch)
     elif args.impl == "reference":

@@ -429,7 +429,10 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
   const int64_t elem = mode == 0 ? 2 : 4;
   const int vec_ok = al16(C) && (ldc * elem) % 16 == 0;
-  const bool wide = N >= 256;
+  // 128x256 tiles when they cover every SM at least once, else 128x128 (twice the CTAs for the
+  // skinny decode-step products)
+  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  const bool wide = N >= 256 && tiles256 >= sm_count();
   CUtensorMap ta, tb;
   if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
   if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;

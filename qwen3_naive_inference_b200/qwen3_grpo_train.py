@@ -400,7 +400,8 @@ def grpo_step(policy: Qwen3ForCausalLM, optimizer, prompts, *, ref_model=None, g
     out = {"loss": float(loss_host[0]), "surrogate": float(loss_host[1]), "kl": float(loss_host[2]),
            "tokens": batch.n_tokens, "completion_tokens": int(sum(len(g) for g in gen)),
            "prompt_tokens": int(sum(plens)), "mean_reward": float(torch.as_tensor(rewards).float().mean()),
-           "t_rollout": t_roll - t0, "t_ref": t_ref - t_roll, "t_train": t_end - t_ref}
+           "t_rollout": t_roll - t0, "t_ref": t_ref - t_roll, "t_train": t_end - t_ref,
+           "rollout_stats": dict(policy.rollout_stats)}
     if return_batch:
         out["batch"] = batch
     return out

@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import json
 import math
+import time
 from collections import deque
 from dataclasses import dataclass
 from functools import lru_cache
@@ -545,6 +546,7 @@ class Qwen3ForCausalLM(nn.Module):
         self._graphs = {}
         self._has_cuda_graphs = False
         self.use_cuda_graphs = True  # decode steps replay captured graphs (False: eager launches)
+        self.rollout_stats: dict = {}  # per generate call: steps, decode steps, host time waiting on the GPU
         self.max_model_len = None  # KV positions a sequence may reach; default = prompt + max_new_tokens
 
     def forward(self, x):
@@ -821,7 +823,9 @@ class Qwen3ForCausalLM(nn.Module):
             self._has_cuda_graphs = False
         elif (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx or getattr(self, "_graph_key", None) != key
                 or getattr(self, "_graph_max_shared", -1) < max_shared):
-            self._init_cuda_graphs(max_bs=512, max_ctx=max(max_ctx, 1024), max_shared=max(max_shared, 256))
+            # the shared-prefix bound is the whole context, so later prompts never force a recapture
+            ctx_cap = max(max_ctx, 1024)
+            self._init_cuda_graphs(max_bs=512, max_ctx=ctx_cap, max_shared=ctx_cap)
             self._capture_decode_graphs(temperature, top_k, grouped=True)
         cap = 2 * self.MAX_TOKENS_PER_STEP + 512 * 8
         return {"dev": dev, "seed": seed, "temperature": temperature, "top_k": top_k,
@@ -850,9 +854,9 @@ class Qwen3ForCausalLM(nn.Module):
                     mem[gi, :len(rows_g)] = rows_g
                     sl[gi] = shared
                     ks[rows_g] = shared
-                ids, pos, cl, bt, slots, mem_d, sl_d, ks_d = self._staging().put([ids, pos, cl, bt, slots, mem, sl, ks])
                 a = self.model.layers[0].self_attn
                 plan = ops.grouped_decode_plan(bs, a.num_kv_heads, int(sl.max(initial=0)), int(cl.max(initial=0)) + 1)
+                ids, pos, cl, bt, slots, mem_d, sl_d, ks_d = self._staging().put([ids, pos, cl, bt, slots, mem, sl, ks])
                 nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(bs, a.num_heads, a.head_dim, plan[1] + plan[2])
                 ws = torch.empty(nb // 4, dtype=torch.float32, device=dev)
                 h = self.model.forward_decode(ids, pos, cl, bt, slots,
@@ -954,7 +958,11 @@ class Qwen3ForCausalLM(nn.Module):
 
     def _finish_step(self, ctx, pending, n, record_logprobs):
         """Waits for the step, surfaces device-side bounds errors, returns host lists."""
+        t0 = time.perf_counter()
         torch.cuda.current_stream().synchronize()
+        st = self.rollout_stats
+        st["gpu_wait_s"] = st.get("gpu_wait_s", 0.0) + time.perf_counter() - t0
+        st["steps"] = st.get("steps", 0) + 1
         if int(ctx["err_host"][0]):
             ops.check_device_errors(ctx["dev"])
         if not n:
@@ -967,6 +975,7 @@ class Qwen3ForCausalLM(nn.Module):
         BS = self.BLOCK_SIZE
         budget_max = self.MAX_TOKENS_PER_STEP
         prompts = [p[0].tolist() if isinstance(p, torch.Tensor) else list(p[0]) for p in prompt_ids_list]
+        self.rollout_stats = {"t_start": time.perf_counter()}
         ctx = self._gen_setup(prompts, max_new_tokens, temperature, top_k)
         bm = BlockManager(self._num_blocks, BS)
         eos = set(eos_token_ids) if eos_token_ids is not None else None
@@ -1077,6 +1086,7 @@ class Qwen3ForCausalLM(nn.Module):
                     finish(seq)
             for seq in scheduled:
                 seq.num_scheduled_tokens = 0
+        self.rollout_stats["total_s"] = time.perf_counter() - self.rollout_stats.pop("t_start")
         return all_seqs
 
 
@@ -1130,7 +1140,9 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
     groups = [_Group(i, p, G, sp) for i, p in enumerate(prompts)]
     max_ctx = model.max_model_len or (max((len(p) for p in prompts), default=1) + max_new_tokens)
     max_shared = max((g.n_full * BS for g in groups), default=0)
+    model.rollout_stats = {"t_start": time.perf_counter()}
     ctx = model._grouped_setup(max_ctx, max_shared, temperature, top_k)
+    model.rollout_stats["setup_s"] = time.perf_counter() - model.rollout_stats["t_start"]
     bm = BlockManager(model._num_blocks, BS)
     eos = set(eos_token_ids) if eos_token_ids is not None else None
     waiting = deque(groups)
@@ -1235,6 +1247,8 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
                 rows = [pos_of[id(m)] for m in grp.members if id(m) in pos_of]
                 if rows:
                     groups_rows.append((rows, grp.n_full * BS))
+        if not prefill:
+            model.rollout_stats["decode_steps"] = model.rollout_stats.get("decode_steps", 0) + 1
         model._grouped_launch(ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples)
         for g in prefill:
             g.donor.kv_len += g.donor.num_scheduled_tokens
@@ -1271,6 +1285,8 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
                 running.remove(g)
     if bm.available != bm.num_blocks or any(bm.ref_count):
         raise RuntimeError("grouped rollout finished with KV pages still referenced")
+    st = model.rollout_stats
+    st["total_s"] = time.perf_counter() - st.pop("t_start")
     return [m for g in groups for m in g.members]
 
 
