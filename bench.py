@@ -391,8 +391,10 @@ def run_decode_only(batch):
 
 def run_rollout_attn():
     """Decode attention mid-rollout (config 4 shapes): 64 groups x 8 completions, prompt U[64,512],
-    256 generated tokens each.  Plain paged decode (every completion reads its prompt K/V) vs the
-    grouped cascade (the group's prompt pages read once).  Prints ms and K/V bytes read."""
+    256 generated tokens each.  Plain paged decode (every completion reads its own copy of the
+    prompt K/V, the reference's layout) vs the grouped cascade (all prompt pages shared and read
+    once per group; generated tokens on the members' own pages).  Both read the same K/V values.
+    Prints ms and K/V bytes read."""
     import torch
 
     from qwen3_naive_inference_b200 import ops
@@ -401,41 +403,60 @@ def run_rollout_attn():
     G, n_groups, gen, hq, hkv, D = 8, 64, 256, 16, 8, 128
     B = G * n_groups
     plens = torch.randint(64, 513, (n_groups,), generator=g).tolist()
-    pages_needed = sum(-(-L // 256) + G * (-(-(gen + L % 256) // 256)) for L in plens) + 16
-    kc = torch.randn(pages_needed, 256, hkv, D, device=dev, dtype=torch.bfloat16)
+    grouped_pages = sum(-(-L // 256) + G * (-(-gen // 256)) for L in plens)
+    plain_pages = sum(G * (-(-(L % 256 + gen) // 256)) for L in plens)
+    n_pages = grouped_pages + plain_pages
+    kc = torch.randn(n_pages, 256, hkv, D, device=dev, dtype=torch.bfloat16)
     vc = torch.randn_like(kc)
-    free = list(range(pages_needed))
-    tables, lens, members, shared, kv_start = [], [], [], [], []
+    free = list(range(n_pages))[::-1]
+    tables, ptables, lens, members, shared, kv_start = [], [], [], [], [], []
+    src, dst = [], []  # token rows copied into the plain layout
     for L in plens:
+        sh = [free.pop() for _ in range(-(-L // 256))]
         n_full = L // 256
-        sh = [free.pop() for _ in range(n_full)]
         row = []
         for _ in range(G):
-            own = [free.pop() for _ in range(-(-(L - n_full * 256 + gen) // 256))]
+            own = [free.pop() for _ in range(-(-gen // 256))]
             row.append(len(tables))
             tables.append(sh + own)
-            lens.append(L + gen)
-            kv_start.append(n_full * 256)
+            P = len(sh) * 256
+            lens.append(P + gen)
+            kv_start.append(P)
+            tail = [free.pop() for _ in range(-(-(L - n_full * 256 + gen) // 256))]
+            ptables.append(sh[:n_full] + tail)
+            for t in range(n_full * 256, L + gen):
+                s_slot = sh[t // 256] * 256 + t % 256 if t < L else own[(t - L) // 256] * 256 + (t - L) % 256
+                src.append(s_slot)
+                dst.append(ptables[-1][t // 256] * 256 + t % 256)
         members.append(row)
-        shared.append(n_full * 256)
-    W = max(len(t) for t in tables)
-    bt = torch.full((B, W), -1, dtype=torch.int32)
-    for i, t in enumerate(tables):
-        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
-    bt = bt.to(dev)
+        shared.append(L)
+    src_t, dst_t = torch.tensor(src, device=dev), torch.tensor(dst, device=dev)
+    for c in (kc, vc):
+        flat = c.view(-1, hkv, D)
+        flat[dst_t] = flat[src_t]
+
+    def table(rows):
+        W = max(len(t) for t in rows)
+        bt = torch.full((len(rows), W), -1, dtype=torch.int32)
+        for i, t in enumerate(rows):
+            bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        return bt.to(dev)
+
+    bt, bt_plain = table(tables), table(ptables)
+    plain_lens = [L for L in plens for _ in range(G)]
     cl = (torch.tensor(lens, dtype=torch.int32) - 1).to(dev)
+    cl_plain = (torch.tensor(plain_lens, dtype=torch.int32) + gen - 1).to(dev)
     q = torch.randn(B, hq, D, device=dev, dtype=torch.bfloat16)
     mem_d = torch.tensor(members, dtype=torch.int32, device=dev)
     sl_d = torch.tensor(shared, dtype=torch.int32, device=dev)
     ks_d = torch.tensor(kv_start, dtype=torch.int32, device=dev)
-    split, ms = ops.decode_split_plan(B, hkv, max(lens))
-    plan = ops.grouped_decode_plan(B, hkv, max(shared), max(L - s for L, s in zip(lens, kv_start)))
+    split, ms = ops.decode_split_plan(B, hkv, max(plain_lens) + gen)
+    plan = ops.grouped_decode_plan(B, hkv, max(shared), gen)
     ws_p = torch.empty(max(1, ops.lib().qb_paged_decode_workspace_bytes(B, hq, D, ms) // 4), device=dev)
-    ws_g = torch.empty(ops.lib().qb_paged_decode_grouped_workspace_bytes(B, hq, D, plan[1] + plan[2]) // 4,
-                       device=dev)
+    ws_g = ops.grouped_workspace(B, hq, D, plan, dev)
     runs = {
-        "plain": lambda: ops.paged_decode_attention(q, kc, vc, bt, cl, D ** -0.5, split_tokens=split, max_splits=ms,
-                                                    workspace=ws_p),
+        "plain": lambda: ops.paged_decode_attention(q, kc, vc, bt_plain, cl_plain, D ** -0.5, split_tokens=split,
+                                                    max_splits=ms, workspace=ws_p),
         "grouped": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt, cl, D ** -0.5, mem_d, sl_d, ks_d, plan,
                                                               workspace=ws_g),
     }
@@ -452,8 +473,9 @@ def run_rollout_attn():
         torch.cuda.synchronize()
         out[name] = a.elapsed_time(b) / 20
     err = (runs["plain"]().float() - runs["grouped"]().float()).abs().max().item()
-    kv_plain = sum(lens) * hkv * D * 4
-    kv_grouped = (sum(shared) + sum(L - s for L, s in zip(lens, kv_start))) * hkv * D * 4
+    ops.check_device_errors()
+    kv_plain = (sum(plain_lens) + B * gen) * hkv * D * 4
+    kv_grouped = (sum(shared) + B * gen) * hkv * D * 4
     print(json.dumps({"rollout_attn": {"ms": out, "kv_bytes": {"plain": kv_plain, "grouped": kv_grouped},
                                        "gbs": {"plain": kv_plain / out["plain"] / 1e6,
                                                "grouped_effective": kv_plain / out["grouped"] / 1e6,

@@ -167,11 +167,17 @@ size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits)
  * own copy of the prompt K/V).  Same result as qb_paged_decode_attn.  Every sequence
  * belongs to exactly one group (singletons allowed): group g lists its members in
  * group_members[g*8 .. g*8+7] (-1 padded, at most 8) and shares its first shared_len[g]
- * keys (a multiple of page_size), stored in the pages of its first member's block_tables
- * row.  kv_start[b] = shared_len of b's group.  The shared keys are read once per group for
- * all members' query heads; each member's own keys [kv_start[b], len_b) separately; split-K
- * partials (shared_splits + own_splits slots per sequence and head) are merged at the end.
- * workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D, shared_splits + own_splits). */
+ * keys, stored in the pages of its first member's block_tables row.  Sequence b attends to
+ * those shared keys and to its own keys [kv_start[b], len_b) (positions in b's block_tables
+ * row, len_b = seqlens[b] + seqlen_add); kv_start[b] >= shared_len of b's group and a
+ * multiple of 64.  Keys in [shared_len, kv_start) are never read, so a member's own tokens
+ * may start on a fresh page after a partially filled shared prompt page; with kv_start ==
+ * shared_len the result equals qb_paged_decode_attn.  The shared keys are read once per group
+ * for all members' query heads and each member's own keys separately, in one launch; split-K
+ * partials (shared_splits + own_splits slots per sequence and head) are merged inside it.
+ * workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D, shared_splits + own_splits)
+ * bytes whose last batch*hq*4 bytes (merge tickets) are zero before the first call; every
+ * call leaves them zero again. */
 int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
                                  int64_t num_blocks, int page_size, const int32_t* block_tables,
                                  int64_t bt_stride, const int32_t* seqlens, int seqlen_add,
@@ -282,15 +288,6 @@ int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
                     int b_mn_major, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int mode,
                     int* err, qb_stream_t stream);
-
-/* Copies the first nbytes of KV page src_page into each of dst_pages[0..n_dst) in every
- * layer of the K and V pools ([layers][num_pages][page] with the given byte strides).  Used
- * when G completions of one prompt share its full pages and each gets its own copy of the
- * partially filled last prompt page (the reference prefills every completion separately). */
-int qb_copy_page_prefix(void* k_pool, void* v_pool, int64_t layers, int64_t layer_bytes,
-                        int64_t page_bytes, int64_t num_pages, int src_page,
-                        const int32_t* dst_pages, int n_dst, int64_t nbytes, int* err,
-                        qb_stream_t stream);
 
 /* ---------------------------------------------------------------- optimizer helpers
  * dst (bf16) = bf16(src fp32); used to hand fp32-accumulated gradients to the

@@ -11,6 +11,8 @@
 // Layout of the paged KV cache (qwen3_naive.py:1059-1066): per layer
 // [num_blocks, 256, hkv, 128] bf16, so token j of a page for kv head h is the
 // 256-byte row at ((page*256 + j)*hkv + h)*128.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace {
@@ -54,8 +56,9 @@ struct DecodeParams {
   bf16* out;
   int* err;
   // Split-K partial layout: sequence b, slot s, head h at ws[((b*n_slots + s)*hq + h)*WS_ROW].
-  // This kernel's split i goes to slot slot_off + i.  kv_start (nullable) skips each
-  // sequence's first keys (they belong to a shared prefix handled elsewhere).
+  // This kernel's split i goes to slot slot_off + i.  kv_start (nullable): the first key
+  // read for each sequence (a multiple of 64; the keys before it belong to a shared
+  // prefix handled elsewhere).
   int n_slots, slot_off;
   const int32_t* kv_start;
 };
@@ -65,15 +68,17 @@ QB_DEVICE void write_empty_partial(const DecodeParams& p, int b, int slot, int h
   p.ws[(((int64_t)b * p.n_slots + slot) * p.hq + h) * WS_ROW + D] = NEG_INF;
 }
 
-__global__ void __launch_bounds__(DEC_WARPS * 32)
-paged_decode_kernel(DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+// One (split, kv head, sequence) work item of the per-sequence decode: keys
+// [kv_start[b] + split*split_tokens, +split_tokens) of sequence b.
+QB_DEVICE void decode_own_tile(const DecodeParams& p, uint8_t* smem, int split, int kvh, int b) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int len = p.seqlens[b] + p.seqlen_add;
   const int tok_begin = (p.kv_start ? p.kv_start[b] : 0) + split * p.split_tokens;
-  if (tok_begin >= len) {
+  // a 64-token stage must not straddle a page: the first key of a split is 64-aligned
+  const bool misaligned = (tok_begin & (DEC_TOK - 1)) != 0 || tok_begin < 0;
+  if (tok_begin >= len || misaligned) {
+    if (misaligned && tid == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
     if (p.max_splits > 1 && threadIdx.x < 2) write_empty_partial(p, b, p.slot_off + split, kvh * 2 + threadIdx.x);
     return;
   }
@@ -263,6 +268,12 @@ paged_decode_kernel(DecodeParams p) {
   }
 }
 
+__global__ void __launch_bounds__(DEC_WARPS * 32)
+paged_decode_kernel(DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  decode_own_tile(p, smem, blockIdx.x, blockIdx.y, blockIdx.z);
+}
+
 // One warp per (sequence, q head): weights w_s = 2^(lse_s - max lse).
 __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
   const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -293,222 +304,448 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 }
 
 // ============================================================================
-// Shared-prefix decode attention (GRPO groups)
+// Shared-prefix decode attention (GRPO groups): warp-independent, persistent
 // ============================================================================
-// The G <= 8 members of a group share the K/V pages of their common prompt.  One CTA =
-// (split of the shared keys, kv head, group) reads those keys once for all 2*G query
-// heads of the kv group: 16 query rows (member i, head h0 + r) = one full M=16 MMA tile,
-// S = Q K^T, online softmax, O += P V (FlashAttention-2 rows), four warps each taking 16
-// of the 64 staged tokens, merged in shared memory.  Each member's partial (O / l and its
-// log2-domain LSE) goes to slot `split` of the split-K workspace; the members' own keys are
-// handled by paged_decode_kernel (kv_start = shared length) in later slots, and
-// paged_decode_combine_kernel merges all slots.
+// The G <= 8 members of a group share the K/V pages of their common prompt.  Work items,
+// each owned by ONE warp from start to finish:
+//   shared item (split, kv head, group): keys [split*S, min(shared_len, (split+1)*S)) in the
+//     pages of the group's first member, read once for all 2*G query heads of the kv head:
+//     16 query rows (member r/2, head h0 + r%2) = one M=16 MMA tile; S = Q K^T, online
+//     softmax, O += P V;
+//   own item (split, kv head, sequence): keys [kv_start + split*S, ...) of the sequence's own
+//     page-table row, the 16 staged tokens in the M dimension (S^T = K Q^T, O^T += V^T P^T)
+//     so that the kv head's two query heads still fill one MMA.
+// Keys in [shared_len, kv_start) are never read.  An item writes one split-K partial (O / l and
+// its log2-domain LSE) per (sequence, head) it covers; the warp that writes the last partial of
+// a (sequence, kv head) merges all of its slots, found through a ticket counter that it resets
+// to zero.  Nothing waits on another warp or CTA.
+//
+// Each warp runs its own 3-deep ring of 16-token stages (K 4 KB, V 4 KB, and the item's query
+// rows with its first stage) through cp.async, its load cursor crossing item boundaries so the
+// next item's data is in flight while an item finishes.  Warp w of the grid takes items w,
+// w + total_warps, ... (shared items first).  There is no __syncthreads in the kernel.
 constexpr int GMAX = 8;
+constexpr int WD_TOK = 16;                              // tokens per stage (one MMA M tile)
+constexpr int WD_STAGES = 3;
+constexpr int WD_KV_BYTES = WD_TOK * ROWB;              // 4 KB of K (and of V) per stage
+constexpr int WD_STAGE_BYTES = 2 * WD_KV_BYTES + 16 * ROWB;  // K, V, up to 16 query rows
+constexpr int WD_WARP_BYTES = WD_STAGES * WD_STAGE_BYTES;
+constexpr int WD_WARPS = 6;                             // per CTA; one CTA per SM
+constexpr int WD_SMEM = WD_WARPS * WD_WARP_BYTES;       // 216 KB
 
-struct SharedParams {
-  DecodeParams d;             // q, caches, page tables, workspace (n_slots), scale, err
+struct CascadeParams {
+  DecodeParams d;             // slot_off = shared_splits; kv_start = first own key per sequence
   const int32_t* members;     // [n_groups, GMAX] sequence indices, -1 padded
   const int32_t* shared_len;  // [n_groups] keys shared by the group (pages of members[g][0])
+  int batch;
+  int shared_splits, own_splits;
+  int n_shared_items, n_items;
+  int* tickets;               // [batch * hkv], zero between calls
 };
 
-__global__ void __launch_bounds__(DEC_WARPS * 32)
-paged_decode_shared_kernel(SharedParams sp) {
+struct Item {
+  int shared;                        // 1: shared item, 0: own item
+  int kvh, idx;                      // kv head; group (shared) or sequence (own)
+  int slot;                          // split-K slot of its partials
+  int tok_begin, tok_end, n_stages;  // keys [tok_begin, tok_end) in 16-token stages
+  const int32_t* btrow;              // page-table row holding those keys
+};
+
+// Member i of group grp, -1 when absent; an index outside the batch raises SHAPE.
+QB_DEVICE int group_member(const CascadeParams& cp, int grp, int i) {
+  const int m = cp.members[grp * GMAX + i];
+  if (m >= cp.batch) {
+    qb_set_err(cp.d.err, QB_DEVERR_SHAPE);
+    return -1;
+  }
+  return m < 0 ? -1 : m;
+}
+
+QB_DEVICE Item decode_item(const CascadeParams& cp, int i) {
+  const DecodeParams& p = cp.d;
+  Item it;
+  if (i < cp.n_shared_items) {
+    const int split = i % cp.shared_splits;
+    i /= cp.shared_splits;
+    it.shared = 1;
+    it.kvh = i % p.hkv;
+    it.idx = i / p.hkv;
+    it.slot = split;
+    const int leader = group_member(cp, it.idx, 0);
+    it.tok_begin = split * p.split_tokens;
+    it.tok_end = leader < 0 ? 0 : min(cp.shared_len[it.idx], it.tok_begin + p.split_tokens);
+    it.btrow = p.bt + (int64_t)(leader < 0 ? 0 : leader) * p.bt_stride;
+  } else {
+    i -= cp.n_shared_items;
+    const int split = i % cp.own_splits;
+    i /= cp.own_splits;
+    it.shared = 0;
+    it.kvh = i % p.hkv;
+    it.idx = i / p.hkv;
+    it.slot = p.slot_off + split;
+    it.tok_begin = p.kv_start[it.idx] + split * p.split_tokens;
+    it.tok_end = min(p.seqlens[it.idx] + p.seqlen_add, it.tok_begin + p.split_tokens);
+    // stages must not straddle a page: the first key of an item is 64-aligned
+    if ((it.tok_begin & 63) != 0 || it.tok_begin < 0) {
+      qb_set_err(p.err, QB_DEVERR_SHAPE);
+      it.tok_begin = it.tok_end = 0;
+    }
+    it.btrow = p.bt + (int64_t)it.idx * p.bt_stride;
+  }
+  it.n_stages = it.tok_end > it.tok_begin ? (it.tok_end - it.tok_begin + WD_TOK - 1) / WD_TOK : 0;
+  return it;
+}
+
+QB_DEVICE uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Merges the n_slots partials of sequence b, heads h0 and h0+1 (one warp: lane -> head
+// h0 + lane/16, eight dims).  The partials come from other warps of this launch; __ldcg
+// reads them from L2.
+QB_DEVICE void merge_partials_warp(const DecodeParams& p, int b, int h0, int lane) {
+  const int h = h0 + (lane >> 4), d0 = (lane & 15) * 8;
+  const float* base = p.ws + ((int64_t)b * p.n_slots * p.hq + h) * WS_ROW;
+  const int64_t sstride = (int64_t)p.hq * WS_ROW;
+  float M = NEG_INF;
+  for (int s = 0; s < p.n_slots; ++s) M = fmaxf(M, __ldcg(base + s * sstride + D));
+  float W = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < p.n_slots; ++s) {
+    const float ls = __ldcg(base + s * sstride + D);
+    if (ls == NEG_INF) continue;  // empty partial: its outputs were never written
+    const float w = exp2f(ls - M);
+    W += w;
+    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(base + s * sstride + d0));
+    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(base + s * sstride + d0 + 4));
+    acc[0] += w * v0.x; acc[1] += w * v0.y; acc[2] += w * v0.z; acc[3] += w * v0.w;
+    acc[4] += w * v1.x; acc[5] += w * v1.y; acc[6] += w * v1.z; acc[7] += w * v1.w;
+  }
+  const float inv = (W > 0.f) ? 1.f / W : 0.f;
+  uint4 r;
+  r.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  r.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  r.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
+  r.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
+  *reinterpret_cast<uint4*>(p.out + ((int64_t)b * p.hq + h) * D + d0) = r;
+}
+
+// After the warp wrote its partials: lane i < 8 takes the ticket of sequence seq_i (-1 = none)
+// for this kv head; the holder of ticket n_slots - 1 saw every other slot published and
+// merges that sequence.
+QB_DEVICE void publish_and_merge_warp(const CascadeParams& cp, int kvh, int seq_i, int lane) {
+  const DecodeParams& p = cp.d;
+  __threadfence();
+  __syncwarp();
+  bool last = false;
+  if (lane < GMAX && seq_i >= 0) {
+    last = atomicAdd(cp.tickets + (int64_t)seq_i * p.hkv + kvh, 1) == p.n_slots - 1;
+    if (last) __threadfence();
+  }
+  unsigned todo = __ballot_sync(0xffffffffu, last);
+  while (todo) {
+    const int i = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const int b = __shfl_sync(0xffffffffu, seq_i, i);
+    merge_partials_warp(p, b, kvh * 2, lane);
+    if (lane == 0) cp.tickets[(int64_t)b * p.hkv + kvh] = 0;
+  }
+}
+
+__global__ void __launch_bounds__(WD_WARPS * 32, 1)
+paged_decode_cascade_kernel(CascadeParams cp) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const DecodeParams& p = sp.d;
-  const int split = blockIdx.x, kvh = blockIdx.y, grp = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const DecodeParams& p = cp.d;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  const int h0 = kvh * 2;
-  const int32_t* mem = sp.members + grp * GMAX;
-  const int len = sp.shared_len[grp];
-  const int tok_begin = split * p.split_tokens;
-  const int leader = mem[0];
-  if (tok_begin >= len || leader < 0) {
-    if (tid < 2 * GMAX) {
-      const int m = mem[tid >> 1];
-      if (m >= 0) write_empty_partial(p, m, split, h0 + (tid & 1));
-    }
-    return;
-  }
-  const int tok_end = min(len, tok_begin + p.split_tokens);
-  const int n_stages = (tok_end - tok_begin + DEC_TOK - 1) / DEC_TOK;
+  uint8_t* wsm = smem + warp * WD_WARP_BYTES;  // this warp's stage ring
+  const int total = gridDim.x * WD_WARPS;
+  const int first = blockIdx.x * WD_WARPS + warp;
+  if (first >= cp.n_items) return;
 
-  // Q as the A operand (row r = member r/2, head h0 + r%2): a0 rows g, a1 rows g+8.
-  uint32_t qa[8][4];
-  {
-    const int r0 = g, r1 = g + 8;
-    const int m0 = mem[r0 >> 1], m1 = mem[r1 >> 1];
-    const bf16* q0 = p.q + ((int64_t)(m0 < 0 ? 0 : m0) * p.hq + h0 + (r0 & 1)) * D;
-    const bf16* q1 = p.q + ((int64_t)(m1 < 0 ? 0 : m1) * p.hq + h0 + (r1 & 1)) * D;
+  // ---- load cursor: next stage to copy (item, stage within it, flat counter), current page
+  int l_item = first, l_stage = 0, l_flat = 0, l_page = -1, l_page_col = -1;
+  Item l_it = decode_item(cp, l_item);
+  auto issue = [&]() {
+    if (l_item < cp.n_items) {
+      uint8_t* buf = wsm + (l_flat % WD_STAGES) * WD_STAGE_BYTES;
+      const uint32_t kbase = smem_u32(buf), vbase = kbase + WD_KV_BYTES, qbase = vbase + WD_KV_BYTES;
+      if (l_stage < l_it.n_stages) {
+        const int tok0 = l_it.tok_begin + l_stage * WD_TOK;
+        const int col = tok0 / PAGE;
+        if (col != l_page_col) {  // one page-table read per page (16 stages)
+          l_page_col = col;
+          l_page = col < p.bt_stride ? l_it.btrow[col] : -1;
+          if (l_page < 0 || l_page >= p.num_blocks) {
+            qb_set_err(p.err, QB_DEVERR_PAGE);
+            l_page = -1;
+          }
+        }
+        const bool page_ok = l_page >= 0;
+        const int64_t row0 = ((int64_t)(page_ok ? l_page : 0) * PAGE + (tok0 % PAGE)) * p.hkv + l_it.kvh;
+        // 16 rows x 16 chunks of K and of V: 8 + 8 copies per lane
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int c = kk * 16 + 2 * t4;
-      qa[kk][0] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
-      qa[kk][1] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
-      qa[kk][2] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
-      qa[kk][3] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
-    }
-  }
-
-  const int32_t* btrow = p.bt + (int64_t)leader * p.bt_stride;
-  auto load_stage = [&](int s) {
-    const int buf = s % DEC_STAGES;
-    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
-    const uint32_t vbase = kbase + DEC_TOK * ROWB;
-    const int tok0 = tok_begin + s * DEC_TOK;
-    const bool col_ok = tok0 / PAGE < p.bt_stride;
-    int page = col_ok ? btrow[tok0 / PAGE] : -1;
-    bool page_ok = page >= 0 && page < p.num_blocks;
-    if (!page_ok) {
-      if (tid == 0) qb_set_err(p.err, QB_DEVERR_PAGE);
-      page = 0;
-    }
-    const int64_t row0 = ((int64_t)page * PAGE + (tok0 % PAGE)) * p.hkv + kvh;
+        for (int i = 0; i < (WD_TOK * 16) / 32; ++i) {
+          const int idx = lane + i * 32;
+          const int r = idx >> 4, c = idx & 15;
+          const bool ok = page_ok && (tok0 + r < l_it.tok_end);
+          const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
+          cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
+          cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
+        }
+      }
+      if (l_stage == 0) {  // the item's query rows
+        const int h0 = l_it.kvh * 2;
+        if (l_it.shared) {  // 16 rows: member r/2, head h0 + r%2 (absent members zero filled)
 #pragma unroll
-    for (int i = 0; i < (DEC_TOK * 16) / (DEC_WARPS * 32); ++i) {
-      const int idx = tid + i * DEC_WARPS * 32;
-      const int r = idx >> 4, c = idx & 15;
-      const bool ok = page_ok && (tok0 + r < tok_end);
-      const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
-      cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
-      cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
+          for (int i = 0; i < 8; ++i) {
+            const int idx = lane + i * 32;
+            const int r = idx >> 4, c = idx & 15;
+            const int m = group_member(cp, l_it.idx, r >> 1);
+            const bf16* src = p.q + ((int64_t)(m < 0 ? 0 : m) * p.hq + h0 + (r & 1)) * D + c * 8;
+            cp_async_16(qbase + swz128(r, c), src, m >= 0 ? 16 : 0);
+          }
+        } else {  // 2 rows: heads h0, h0 + 1 of the sequence
+          const int r = lane >> 4, c = lane & 15;
+          cp_async_16(qbase + swz128(r, c), p.q + ((int64_t)l_it.idx * p.hq + h0 + r) * D + c * 8, 16);
+        }
+      }
+      if (++l_stage >= max(1, l_it.n_stages)) {  // an empty item still takes one stage slot
+        l_stage = 0;
+        l_page_col = -1;
+        l_item += total;
+        if (l_item < cp.n_items) l_it = decode_item(cp, l_item);
+      }
     }
+    cp_async_commit();
+    ++l_flat;
   };
 #pragma unroll
-  for (int s = 0; s < DEC_STAGES - 1; ++s) {
-    if (s < n_stages) load_stage(s);
-    cp_async_commit();
-  }
+  for (int s = 0; s < WD_STAGES - 1; ++s) issue();
 
-  float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
-  float o[16][4];
+  int f = 0;  // flat index of the stage being consumed
+  for (int k = 0;; ++k) {
+    if (first + k * total >= cp.n_items) break;
+    const Item it = decode_item(cp, first + k * total);
+    const int ns = max(1, it.n_stages);
+    const int h0 = it.kvh * 2;
+    if (it.shared) {
+      float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
+      float o[16][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-  for (int s = 0; s < n_stages; ++s) {
-    if (s + DEC_STAGES - 1 < n_stages) load_stage(s + DEC_STAGES - 1);
-    cp_async_commit();
-    cp_async_wait<DEC_STAGES - 1>();
-    __syncthreads();
-    const int buf = s % DEC_STAGES;
-    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
-    const uint32_t vbase = kbase + DEC_TOK * ROWB;
-    const int wrow = warp * 16;
-    // S[16 q x 16 tok] = Q K^T over this warp's 16 tokens (two n-tiles of 8 tokens)
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      uint32_t qa[8][4];
+      for (int s = 0; s < ns; ++s, ++f) {
+        issue();
+        cp_async_wait<WD_STAGES - 1>();
+        __syncwarp();
+        const uint8_t* buf = wsm + (f % WD_STAGES) * WD_STAGE_BYTES;
+        const uint32_t kbase = smem_u32(buf), vbase = kbase + WD_KV_BYTES;
+        if (s == 0) {  // Q as the A operand: a0/a2 row g, a1/a3 row g + 8
+          const uint8_t* qs = buf + 2 * WD_KV_BYTES;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t r0, r1, r2, r3;
-      ldmatrix_x4(kbase + swz128(wrow + (lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2,
-                  r3);
-      mma_bf16_16816(sc[0], qa[kk], r0, r1);
-      mma_bf16_16816(sc[1], qa[kk], r2, r3);
+          for (int kk = 0; kk < 8; ++kk) {
+            qa[kk][0] = lds32(qs + swz128(g, kk * 2) + 4 * t4);
+            qa[kk][1] = lds32(qs + swz128(g + 8, kk * 2) + 4 * t4);
+            qa[kk][2] = lds32(qs + swz128(g, kk * 2 + 1) + 4 * t4);
+            qa[kk][3] = lds32(qs + swz128(g + 8, kk * 2 + 1) + 4 * t4);
+          }
+        }
+        if (s < it.n_stages) {
+          // S[16 q x 16 tok] = Q K^T (two n-tiles of 8 tokens)
+          float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            uint32_t r0, r1, r2, r3;
+            ldmatrix_x4(kbase + swz128((lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2, r3);
+            mma_bf16_16816(sc[0], qa[kk], r0, r1);
+            mma_bf16_16816(sc[1], qa[kk], r2, r3);
+          }
+          const int key0 = it.tok_begin + s * WD_TOK;
+          float mt[2] = {NEG_INF, NEG_INF};
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int kc = key0 + nt * 8 + 2 * t4;
+            sc[nt][0] = kc < it.tok_end ? sc[nt][0] * p.scale_log2 : NEG_INF;
+            sc[nt][1] = kc + 1 < it.tok_end ? sc[nt][1] * p.scale_log2 : NEG_INF;
+            sc[nt][2] = kc < it.tok_end ? sc[nt][2] * p.scale_log2 : NEG_INF;
+            sc[nt][3] = kc + 1 < it.tok_end ? sc[nt][3] * p.scale_log2 : NEG_INF;
+            mt[0] = fmaxf(mt[0], fmaxf(sc[nt][0], sc[nt][1]));
+            mt[1] = fmaxf(mt[1], fmaxf(sc[nt][2], sc[nt][3]));
+          }
+          float alpha[2], mnew[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 1));
+            mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 2));
+            mnew[r] = fmaxf(m_run[r], mt[r]);
+            alpha[r] = (mnew[r] == NEG_INF) ? 1.f : exp2f(m_run[r] - mnew[r]);
+            m_run[r] = mnew[r];
+          }
+          uint32_t pa[4];
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const float p0 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][0] - mnew[0]);
+            const float p1 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][1] - mnew[0]);
+            const float p2 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][2] - mnew[1]);
+            const float p3 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][3] - mnew[1]);
+            rs[0] += p0 + p1;
+            rs[1] += p2 + p3;
+            pa[2 * nt] = pack_bf16x2(p0, p1);
+            pa[2 * nt + 1] = pack_bf16x2(p2, p3);
+          }
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+            l_run[r] = l_run[r] * alpha[r] + rs[r];
+          }
+#pragma unroll
+          for (int dt = 0; dt < 16; ++dt) {
+            o[dt][0] *= alpha[0];
+            o[dt][1] *= alpha[0];
+            o[dt][2] *= alpha[1];
+            o[dt][3] *= alpha[1];
+          }
+          // O[16 x 128] += P[16 x 16 tok] V[16 tok x 128]
+#pragma unroll
+          for (int dp = 0; dp < 8; ++dp) {
+            uint32_t r0, r1, r2, r3;
+            ldmatrix_x4_trans(vbase + swz128((lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1, r2,
+                              r3);
+            mma_bf16_16816(o[2 * dp], pa, r0, r1);
+            mma_bf16_16816(o[2 * dp + 1], pa, r2, r3);
+          }
+        }
+        __syncwarp();  // every lane is done with this buffer before the next issue refills it
+      }
+      // partials of rows g (member g/2, head h0 + g%2) and g + 8 (member 4 + g/2)
+      const int mem_lane = lane < GMAX ? group_member(cp, it.idx, lane) : -1;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = g + 8 * r;
+        const int m = __shfl_sync(0xffffffffu, mem_lane, row >> 1);
+        if (m >= 0) {
+          const float inv = (l_run[r] > 0.f) ? 1.f / l_run[r] : 0.f;
+          float* wrow = p.ws + (((int64_t)m * p.n_slots + it.slot) * p.hq + h0 + (row & 1)) * WS_ROW;
+#pragma unroll
+          for (int dt = 0; dt < 16; ++dt)
+            *reinterpret_cast<float2*>(wrow + dt * 8 + 2 * t4) = make_float2(o[dt][2 * r] * inv, o[dt][2 * r + 1] * inv);
+          if (t4 == 0) wrow[D] = (l_run[r] > 0.f) ? m_run[r] + log2f(l_run[r]) : NEG_INF;
+        }
+      }
+      publish_and_merge_warp(cp, it.kvh, mem_lane, lane);
+    } else {
+      float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
+      float o[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      uint32_t qb[8][2];
+      for (int s = 0; s < ns; ++s, ++f) {
+        issue();
+        cp_async_wait<WD_STAGES - 1>();
+        __syncwarp();
+        const uint8_t* buf = wsm + (f % WD_STAGES) * WD_STAGE_BYTES;
+        const uint32_t kbase = smem_u32(buf), vbase = kbase + WD_KV_BYTES;
+        if (s == 0) {  // Q^T as the B operand: b0 = Q[h0+g][kk*16 + 2t4, +1], b1 = ... + 8
+          const uint8_t* qs = buf + 2 * WD_KV_BYTES;
+          const bool valid = g < 2;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            qb[kk][0] = valid ? lds32(qs + swz128(g, kk * 2) + 4 * t4) : 0u;
+            qb[kk][1] = valid ? lds32(qs + swz128(g, kk * 2 + 1) + 4 * t4) : 0u;
+          }
+        }
+        if (s < it.n_stages) {
+          // S^T[16 tok x 8] = K[16 x 128] * Q^T[128 x 8]
+          float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            uint32_t a[4];
+            ldmatrix_x4(kbase + swz128(lane & 15, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+            mma_bf16_16816(sc, a, qb[kk][0], qb[kk][1]);
+          }
+          const int tokA = it.tok_begin + s * WD_TOK + g;  // rows g and g+8
+          float x[4];
+          x[0] = (t4 == 0 && tokA < it.tok_end) ? sc[0] * p.scale_log2 : NEG_INF;
+          x[1] = (t4 == 0 && tokA < it.tok_end) ? sc[1] * p.scale_log2 : NEG_INF;
+          x[2] = (t4 == 0 && tokA + 8 < it.tok_end) ? sc[2] * p.scale_log2 : NEG_INF;
+          x[3] = (t4 == 0 && tokA + 8 < it.tok_end) ? sc[3] * p.scale_log2 : NEG_INF;
+          float mloc[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1)
+              mloc[h] = fmaxf(mloc[h], __shfl_xor_sync(0xffffffffu, mloc[h], off));
+            mloc[h] = __shfl_sync(0xffffffffu, mloc[h], 0);
+          }
+          float alpha[2], mnew[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            mnew[h] = fmaxf(m_run[h], mloc[h]);
+            alpha[h] = (mnew[h] == NEG_INF) ? 1.f : exp2f(m_run[h] - mnew[h]);
+          }
+          float pv[4];
+          pv[0] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[0] - mnew[0]);
+          pv[1] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[1] - mnew[1]);
+          pv[2] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[2] - mnew[0]);
+          pv[3] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[3] - mnew[1]);
+          float lsum[2] = {pv[0] + pv[2], pv[1] + pv[3]};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) lsum[h] += __shfl_xor_sync(0xffffffffu, lsum[h], off);
+            lsum[h] = __shfl_sync(0xffffffffu, lsum[h], 0);
+            l_run[h] = l_run[h] * alpha[h] + lsum[h];
+            m_run[h] = mnew[h];
+          }
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            o[mt][0] *= alpha[0];
+            o[mt][1] *= alpha[1];
+            o[mt][2] *= alpha[0];
+            o[mt][3] *= alpha[1];
+          }
+          // P^T as the B operand: lane (g, t4) needs P[tok 2t4, 2t4+1, 2t4+8, 2t4+9][head g].
+          const int srcA = 8 * t4, srcB = 8 * t4 + 4;
+          const float a0 = __shfl_sync(0xffffffffu, pv[0], srcA), a1 = __shfl_sync(0xffffffffu, pv[1], srcA);
+          const float a2 = __shfl_sync(0xffffffffu, pv[2], srcA), a3 = __shfl_sync(0xffffffffu, pv[3], srcA);
+          const float c0 = __shfl_sync(0xffffffffu, pv[0], srcB), c1 = __shfl_sync(0xffffffffu, pv[1], srcB);
+          const float c2 = __shfl_sync(0xffffffffu, pv[2], srcB), c3 = __shfl_sync(0xffffffffu, pv[3], srcB);
+          uint32_t pb0 = 0u, pb1 = 0u;
+          if (g == 0) {
+            pb0 = pack_bf16x2(a0, c0);
+            pb1 = pack_bf16x2(a2, c2);
+          } else if (g == 1) {
+            pb0 = pack_bf16x2(a1, c1);
+            pb1 = pack_bf16x2(a3, c3);
+          }
+          // O^T[128 x 8] += V^T[128 x 16 tok] * P^T[16 tok x 8]
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a[4];
+            ldmatrix_x4_trans(vbase + swz128((lane & 7) + ((lane >> 4) << 3), mt * 2 + ((lane >> 3) & 1)), a[0], a[1],
+                              a[2], a[3]);
+            mma_bf16_16816(o[mt], a, pb0, pb1);
+          }
+        }
+        __syncwarp();
+      }
+      // partial: lanes with t4 == 0 hold O^T rows (dims) mt*16 + g and + 8 for both heads
+      if (t4 == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float inv = (l_run[h] > 0.f) ? 1.f / l_run[h] : 0.f;
+          float* wrow = p.ws + (((int64_t)it.idx * p.n_slots + it.slot) * p.hq + h0 + h) * WS_ROW;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            wrow[mt * 16 + g] = o[mt][h] * inv;
+            wrow[mt * 16 + g + 8] = o[mt][2 + h] * inv;
+          }
+          if (g == 0) wrow[D] = (l_run[h] > 0.f) ? m_run[h] + log2f(l_run[h]) : NEG_INF;
+        }
+      }
+      publish_and_merge_warp(cp, it.kvh, lane == 0 ? it.idx : -1, lane);
     }
-    const int key0 = tok_begin + s * DEC_TOK + wrow;
-    float mt[2] = {NEG_INF, NEG_INF};
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int kc = key0 + nt * 8 + 2 * t4;
-      sc[nt][0] = kc < tok_end ? sc[nt][0] * p.scale_log2 : NEG_INF;
-      sc[nt][1] = kc + 1 < tok_end ? sc[nt][1] * p.scale_log2 : NEG_INF;
-      sc[nt][2] = kc < tok_end ? sc[nt][2] * p.scale_log2 : NEG_INF;
-      sc[nt][3] = kc + 1 < tok_end ? sc[nt][3] * p.scale_log2 : NEG_INF;
-      mt[0] = fmaxf(mt[0], fmaxf(sc[nt][0], sc[nt][1]));
-      mt[1] = fmaxf(mt[1], fmaxf(sc[nt][2], sc[nt][3]));
-    }
-    float alpha[2], mnew[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 1));
-      mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 2));
-      mnew[r] = fmaxf(m_run[r], mt[r]);
-      alpha[r] = (mnew[r] == NEG_INF) ? 1.f : exp2f(m_run[r] - mnew[r]);
-      m_run[r] = mnew[r];
-    }
-    uint32_t pa[4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const float p0 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][0] - mnew[0]);
-      const float p1 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][1] - mnew[0]);
-      const float p2 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][2] - mnew[1]);
-      const float p3 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][3] - mnew[1]);
-      rs[0] += p0 + p1;
-      rs[1] += p2 + p3;
-      pa[2 * nt] = pack_bf16x2(p0, p1);
-      pa[2 * nt + 1] = pack_bf16x2(p2, p3);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-      l_run[r] = l_run[r] * alpha[r] + rs[r];
-    }
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      o[dt][0] *= alpha[0];
-      o[dt][1] *= alpha[0];
-      o[dt][2] *= alpha[1];
-      o[dt][3] *= alpha[1];
-    }
-    // O[16 x 128] += P[16 x 16 tok] V[16 tok x 128]
-#pragma unroll
-    for (int dp = 0; dp < 8; ++dp) {
-      uint32_t r0, r1, r2, r3;
-      ldmatrix_x4_trans(vbase + swz128(wrow + (lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1,
-                        r2, r3);
-      mma_bf16_16816(o[2 * dp], pa, r0, r1);
-      mma_bf16_16816(o[2 * dp + 1], pa, r2, r3);
-    }
-    __syncthreads();
   }
   cp_async_wait<0>();
-
-  // Merge the four warps: smem [warp][16 rows][128] floats + m, l per (warp, row).
-  float* so = reinterpret_cast<float*>(smem);
-  float* sm = so + DEC_WARPS * 16 * D;
-  float* sl = sm + DEC_WARPS * 16;
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = g + 8 * r;
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      so[(warp * 16 + row) * D + dt * 8 + 2 * t4] = o[dt][2 * r];
-      so[(warp * 16 + row) * D + dt * 8 + 2 * t4 + 1] = o[dt][2 * r + 1];
-    }
-    if (t4 == 0) {
-      sm[warp * 16 + row] = m_run[r];
-      sl[warp * 16 + row] = l_run[r];
-    }
-  }
-  __syncthreads();
-  {
-    const int row = tid >> 3;          // 16 rows x 8 threads
-    const int d0 = (tid & 7) * 16;     // 16 dims per thread
-    const int member = mem[row >> 1];
-    float M = NEG_INF;
-#pragma unroll
-    for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, sm[w * 16 + row]);
-    float L = 0.f, f[DEC_WARPS];
-#pragma unroll
-    for (int w = 0; w < DEC_WARPS; ++w) {
-      const float mw = sm[w * 16 + row];
-      f[w] = (mw == NEG_INF) ? 0.f : exp2f(mw - M);
-      L += sl[w * 16 + row] * f[w];
-    }
-    if (member >= 0) {
-      const float inv = (L > 0.f) ? 1.f / L : 0.f;
-      float* wrow = p.ws + (((int64_t)member * p.n_slots + split) * p.hq + h0 + (row & 1)) * WS_ROW;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float acc = 0.f;
-#pragma unroll
-        for (int w = 0; w < DEC_WARPS; ++w) acc += so[(w * 16 + row) * D + d0 + i] * f[w];
-        wrow[d0 + i] = acc * inv;
-      }
-      if (d0 == 0) wrow[D] = (L > 0.f) ? M + log2f(L) : NEG_INF;
-    }
-  }
 }
 
 // ============================================================================
@@ -1025,6 +1262,20 @@ attn_bwd_dq_kernel(BwdParams p) {
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// SM count of the current device (cached per device).
+inline int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
 }  // namespace
 
 // ================================================================ C ABI
@@ -1066,7 +1317,8 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
 }
 
 extern "C" size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int Dh, int n_slots) {
-  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float);
+  // split-K partials, then one int32 ticket per (sequence, head)
+  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float) + (size_t)batch * hq * sizeof(int32_t);
 }
 
 extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
@@ -1083,34 +1335,26 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
   if (batch == 0) return QB_OK;
   QB_CHECK_ARG(q && k_cache && v_cache && block_tables && seqlens && out && workspace && group_members &&
                shared_len && kv_start && al16(q) && al16(k_cache) && al16(v_cache) && al16(workspace) &&
-               bt_stride > 0);
+               al16(out) && bt_stride > 0);
   const int n_slots = shared_splits + own_splits;
+  const int64_t n_shared = (int64_t)shared_splits * hkv * n_groups;
+  const int64_t n_items = n_shared + (int64_t)own_splits * hkv * batch;
+  QB_CHECK_ARG(n_items < (1ll << 30));
   DecodeParams d{(const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, num_blocks, block_tables, bt_stride,
                  seqlens, seqlen_add, hq, hkv, scale * LOG2E, split_tokens, n_slots, workspace, (bf16*)out, err,
-                 n_slots, 0, nullptr};
+                 n_slots, shared_splits, kv_start};
+  int* tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) +
+                                        (size_t)batch * n_slots * hq * WS_ROW * sizeof(float));
+  CascadeParams cp{d, group_members, shared_len, batch, shared_splits, own_splits, (int)n_shared, (int)n_items,
+                   tickets};
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(paged_decode_shared_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
-    cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(paged_decode_cascade_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WD_SMEM);
     attr_set = true;
   }
-  cudaStream_t st = (cudaStream_t)stream;
-  if (n_groups > 0) {
-    SharedParams sp{d, group_members, shared_len};
-    paged_decode_shared_kernel<<<dim3((unsigned)shared_splits, (unsigned)hkv, (unsigned)n_groups), DEC_WARPS * 32,
-                                 DEC_SMEM, st>>>(sp);
-    int s0 = qb_launch_status();
-    if (s0 != QB_OK) return s0;
-  }
-  DecodeParams own = d;
-  own.slot_off = shared_splits;
-  own.kv_start = kv_start;
-  paged_decode_kernel<<<dim3((unsigned)own_splits, (unsigned)hkv, (unsigned)batch), DEC_WARPS * 32, DEC_SMEM, st>>>(
-      own);
-  int s1 = qb_launch_status();
-  if (s1 != QB_OK) return s1;
-  const int wpb = 8;
-  paged_decode_combine_kernel<<<(unsigned)((batch * hq + wpb - 1) / wpb), wpb * 32, 0, st>>>(d, batch);
+  // persistent: one CTA of WD_WARPS independent warps per SM
+  const int64_t grid = std::min<int64_t>((n_items + WD_WARPS - 1) / WD_WARPS, (int64_t)device_sm_count());
+  paged_decode_cascade_kernel<<<(unsigned)grid, WD_WARPS * 32, WD_SMEM, (cudaStream_t)stream>>>(cp);
   return qb_launch_status();
 }
 

@@ -1,7 +1,7 @@
 // Library-wide entry points of the C ABI: version and status strings.
 #include "common.cuh"
 
-extern "C" int qb_abi_version(void) { return 1; }
+extern "C" int qb_abi_version(void) { return 2; }
 
 extern "C" const char* qb_status_string(int status) {
   if (status == QB_OK) return "ok";

@@ -459,22 +459,6 @@ __global__ void accumulate_bf16_kernel(const bf16* __restrict__ src, float* __re
     acc[i] += bf2f(src[i]);
 }
 
-// Copies the first `nbytes` of page `src` to each page of `dst` in every layer of the K and
-// V pools.  grid = (n_dst, layers, 2); pages are `page_bytes` apart, layers `layer_bytes`.
-__global__ void copy_page_prefix_kernel(uint8_t* __restrict__ k_pool, uint8_t* __restrict__ v_pool,
-                                        int64_t layer_bytes, int64_t page_bytes, int64_t num_pages, int src,
-                                        const int32_t* __restrict__ dst, int64_t nbytes, int* err) {
-  const int d = dst[blockIdx.x];
-  if (d < 0 || d >= num_pages || src < 0 || src >= num_pages) {
-    if (threadIdx.x == 0) qb_set_err(err, QB_DEVERR_PAGE);
-    return;
-  }
-  uint8_t* pool = blockIdx.z == 0 ? k_pool : v_pool;
-  const uint4* s = reinterpret_cast<const uint4*>(pool + blockIdx.y * layer_bytes + (int64_t)src * page_bytes);
-  uint4* t = reinterpret_cast<uint4*>(pool + blockIdx.y * layer_bytes + (int64_t)d * page_bytes);
-  for (int64_t i = threadIdx.x; i < nbytes / 16; i += blockDim.x) t[i] = s[i];
-}
-
 inline int grid_for(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   const int64_t cap = 148 * 16;
@@ -632,20 +616,6 @@ extern "C" int qb_add_bf16(const void* a, const void* b, void* out, int64_t n, q
   QB_CHECK_ARG(a && b && out && aligned16(a) && aligned16(b) && aligned16(out));
   add_bf16_kernel<<<grid_for(n / 8 + 1, 256), 256, 0, (cudaStream_t)stream>>>(
       (const bf16*)a, (const bf16*)b, (bf16*)out, n);
-  return qb_launch_status();
-}
-
-extern "C" int qb_copy_page_prefix(void* k_pool, void* v_pool, int64_t layers, int64_t layer_bytes,
-                                   int64_t page_bytes, int64_t num_pages, int src_page, const int32_t* dst_pages,
-                                   int n_dst, int64_t nbytes, int* err, qb_stream_t stream) {
-  QB_CHECK_ARG(layers >= 0 && n_dst >= 0 && nbytes >= 0 && nbytes <= page_bytes && nbytes % 16 == 0);
-  if (layers == 0 || n_dst == 0 || nbytes == 0) return QB_OK;
-  QB_CHECK_ARG(k_pool && v_pool && dst_pages && aligned16(k_pool) && aligned16(v_pool) && layer_bytes % 16 == 0 &&
-               page_bytes % 16 == 0 && layers <= 65535 && n_dst <= 65535);
-  dim3 grid((unsigned)n_dst, (unsigned)layers, 2);
-  copy_page_prefix_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((uint8_t*)k_pool, (uint8_t*)v_pool, layer_bytes,
-                                                                   page_bytes, num_pages, src_page, dst_pages, nbytes,
-                                                                   err);
   return qb_launch_status();
 }
 

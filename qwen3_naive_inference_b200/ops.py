@@ -278,15 +278,16 @@ def attention_packed(qkv_rot, cu_seqlens, tiles, hq, hkv, scale):
 
 
 def attention_paged_prefill(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, block_tables,
-                            scale, tiles=None, hkv=None):
+                            scale, tiles=None, hkv=None, out=None):
     """flash_attn_varlen_func(q, k_cache, v_cache, ..., causal=True, block_table=) equivalent.
 
-    q: [Tq, hq, 128]; caches [num_blocks, 256, hkv, 128]; returns [Tq, hq, 128].
+    q: [Tq, hq, 128]; caches [num_blocks, 256, hkv, 128]; returns [Tq, hq, 128] (``out`` if given).
     """
     _cuda(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, block_tables)
     Tq, hq, D = q.shape
     num_blocks, page, hkv_c, _ = k_cache.shape
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
     batch = cu_seqlens_q.numel() - 1
     tps = (int(max_seqlen_q) + 63) // 64
     n_tiles = 0 if tiles is None else tiles.numel() // 2
@@ -338,25 +339,33 @@ def grouped_decode_plan(batch, hkv, max_shared, max_own, sm_count=148):
     return split, max(1, math.ceil(max(1, max_shared) / split)), max(1, math.ceil(own_max / split))
 
 
+def grouped_workspace(batch, hq, D, plan, device):
+    """Workspace of :func:`paged_decode_attention_grouped`, zeroed (its merge tickets must be)."""
+    nbytes = lib().qb_paged_decode_grouped_workspace_bytes(batch, hq, D, plan[1] + plan[2])
+    return torch.zeros(nbytes // 4, dtype=torch.float32, device=device)
+
+
 def paged_decode_attention_grouped(q, k_cache, v_cache, block_tables, seqlens, scale, group_members, shared_len,
-                                   kv_start, plan, workspace=None, seqlen_add=1):
-    """Decode attention where groups of sequences share their first ``shared_len`` keys
-    (same pages); equals :func:`paged_decode_attention` with the shared keys read once per group.
-    group_members int32 [n_groups, 8] (-1 padded), shared_len int32 [n_groups], kv_start int32 [B]."""
+                                   kv_start, plan, workspace=None, seqlen_add=1, out=None):
+    """Decode attention where groups of sequences share their first ``shared_len`` keys (the
+    pages of the group's first member): sequence b attends to those and to its own keys
+    [kv_start[b], seqlens[b] + seqlen_add) of its page table; keys in between are skipped.
+    With kv_start == shared_len this equals :func:`paged_decode_attention`, the shared keys
+    read once per group.  group_members int32 [n_groups, 8] (-1 padded), shared_len int32
+    [n_groups], kv_start int32 [B] (multiples of 64)."""
     _cuda(q, k_cache, v_cache, block_tables, seqlens, group_members, shared_len, kv_start)
     B, hq, D = q.shape
     num_blocks, page, hkv, _ = k_cache.shape
     split_tokens, s_sh, s_own = plan
     if workspace is None:
-        nbytes = lib().qb_paged_decode_grouped_workspace_bytes(B, hq, D, s_sh + s_own)
-        workspace = torch.empty(nbytes // 4, dtype=torch.float32, device=q.device)
-    out = torch.empty_like(q)
+        workspace = grouped_workspace(B, hq, D, plan, q.device)
+    if out is None:
+        out = torch.empty_like(q)
     check(lib().qb_paged_decode_attn_grouped(_p(q), _p(k_cache), _p(v_cache), num_blocks, page, _p(block_tables),
                                              block_tables.stride(0), _p(seqlens), seqlen_add, B, hq, hkv, D, scale,
                                              _p(group_members), _p(shared_len), group_members.shape[0],
                                              _p(kv_start), split_tokens, s_sh, s_own, _p(workspace), _p(out),
-                                             _p(err_flag()), stream_ptr()), "qb_paged_decode_attn_grouped",
-          kernels=3)
+                                             _p(err_flag()), stream_ptr()), "qb_paged_decode_attn_grouped")
     return out
 
 

@@ -308,18 +308,48 @@ class Qwen3Attention(nn.Module):
         return self.forward_packed(x.reshape(B * S, H), positions, cu, tiles).view(B, S, H)
 
     def forward_prefill(self, x, positions, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
-                        block_mapping, block_tables=None, *, tiles=None):
+                        block_mapping, block_tables=None, *, tiles=None, decode_tail=None):
         """Paged prefill (qwen3_naive.py:597-640): K/V of the new tokens go to the cache rows
-        ``block_mapping``, then queries attend to the cache through ``block_tables``."""
+        ``block_mapping``, then queries attend to the cache through ``block_tables``.
+
+        ``decode_tail`` = (n_prefill_rows, context_lens, block_tables, decode_plan): the rows from
+        n_prefill_rows on are single decode tokens whose attention runs on the decode kernel of
+        ``decode_plan`` (cu_seqlens and ``block_tables`` then describe the prefill rows only)."""
         qkv = ops.linear(x, self.qkv_proj.weight)
         q = ops.qk_norm_rope_store(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
                                    self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads,
                                    self.k_cache, self.v_cache, block_mapping)
         if block_tables is None:
             raise ValueError("the paged prefill kernel reads K/V through block_tables")
-        o = ops.attention_paged_prefill(q, self.k_cache, self.v_cache, cu_seqlens_q, cu_seqlens_k,
-                                        max_seqlen_q, block_tables, self.scale, tiles=tiles)
+        if decode_tail is None:
+            o = ops.attention_paged_prefill(q, self.k_cache, self.v_cache, cu_seqlens_q, cu_seqlens_k,
+                                            max_seqlen_q, block_tables, self.scale, tiles=tiles)
+        else:
+            tp, context_lens, bt_d, plan = decode_tail
+            o = torch.empty_like(q)
+            if tp:
+                ops.attention_paged_prefill(q[:tp], self.k_cache, self.v_cache, cu_seqlens_q, cu_seqlens_k,
+                                            max_seqlen_q, block_tables, self.scale, tiles=tiles, out=o[:tp])
+            self._decode_attention(q[tp:], context_lens, bt_d, plan, out=o[tp:])
         return ops.linear(o.view(x.shape[0], -1), self.o_proj.weight)
+
+    def _decode_attention(self, q, context_lens, block_tables, decode_plan, out=None):
+        if decode_plan is None:
+            o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale)
+        elif decode_plan[0] == "grouped":
+            # prompt pages shared by G completions: read once per group (cascade attention)
+            _, plan, ws, members, shared_len, kv_start = decode_plan
+            return ops.paged_decode_attention_grouped(q, self.k_cache, self.v_cache, block_tables, context_lens,
+                                                      self.scale, members, shared_len, kv_start, plan, workspace=ws,
+                                                      out=out)
+        else:
+            _, split_tokens, max_splits, ws = decode_plan
+            o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale,
+                                           split_tokens=split_tokens, max_splits=max_splits, workspace=ws)
+        if out is not None:
+            out.copy_(o)
+            return out
+        return o
 
     def forward_decode(self, x, positions, context_lens, block_tables, slot_mapping=None, *, decode_plan=None):
         """One new token per sequence (qwen3_naive.py:642-683); attends to context_lens + 1 keys."""
@@ -327,17 +357,7 @@ class Qwen3Attention(nn.Module):
         q = ops.qk_norm_rope_store(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
                                    self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads,
                                    self.k_cache, self.v_cache, slot_mapping)
-        if decode_plan is None:
-            o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale)
-        elif decode_plan[0] == "grouped":
-            # prompt pages shared by G completions: read once per group (cascade attention)
-            _, plan, ws, members, shared_len, kv_start = decode_plan
-            o = ops.paged_decode_attention_grouped(q, self.k_cache, self.v_cache, block_tables, context_lens,
-                                                   self.scale, members, shared_len, kv_start, plan, workspace=ws)
-        else:
-            _, split_tokens, max_splits, ws = decode_plan
-            o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale,
-                                           split_tokens=split_tokens, max_splits=max_splits, workspace=ws)
+        o = self._decode_attention(q, context_lens, block_tables, decode_plan)
         return ops.linear(o.view(x.shape[0], -1), self.o_proj.weight)
 
 
@@ -377,14 +397,14 @@ class Qwen3DecoderLayer(nn.Module):
         return self.forward_packed(x.reshape(B * S, H), positions, cu, tiles).view(B, S, H)
 
     def forward_prefill(self, x, positions, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
-                        block_mapping, block_tables=None, residual=None, *, tiles=None):
+                        block_mapping, block_tables=None, residual=None, *, tiles=None, decode_tail=None):
         if residual is None:
             hidden_states, residual = self.input_layernorm(x), x
         else:
             hidden_states, residual = self.input_layernorm(x, residual)
         hidden_states = self.self_attn.forward_prefill(hidden_states, positions, cu_seqlens_q, cu_seqlens_k,
                                                        max_seqlen_q, max_seqlen_k, block_mapping, block_tables,
-                                                       tiles=tiles)
+                                                       tiles=tiles, decode_tail=decode_tail)
         hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
         return self.mlp(hidden_states), residual
 
@@ -452,12 +472,13 @@ class Qwen3Model(nn.Module):
         return self.forward_packed(x.reshape(-1), positions, cu, tiles).view(B, S, -1)
 
     def forward_prefill(self, x, positions, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
-                        block_mapping, block_tables=None, *, tiles=None):
+                        block_mapping, block_tables=None, *, tiles=None, decode_tail=None):
         h = ops.embedding(x, self.embed_tokens.weight)
         residual = None
         for layer in self.layers:
             h, residual = layer.forward_prefill(h, positions, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
-                                                max_seqlen_k, block_mapping, block_tables, residual, tiles=tiles)
+                                                max_seqlen_k, block_mapping, block_tables, residual, tiles=tiles,
+                                                decode_tail=decode_tail)
         h, _ = self.norm(h, residual)
         return h
 
@@ -703,8 +724,7 @@ class Qwen3ForCausalLM(nn.Module):
         if grouped:
             b = self._graph_bufs
             plan = ops.grouped_decode_plan(bs, a.num_kv_heads, self._graph_max_shared, self._graph_max_ctx)
-            nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(bs, a.num_heads, a.head_dim, plan[1] + plan[2])
-            ws = torch.empty(nb // 4, dtype=torch.float32, device=dev)
+            ws = ops.grouped_workspace(bs, a.num_heads, a.head_dim, plan, dev)
             return ("grouped", plan, ws, b["members"][:bs], b["shared_len"][:bs], b["kv_start"][:bs])
         split_tokens, max_splits = ops.decode_split_plan(bs, a.num_kv_heads, self._graph_max_ctx)
         ws = None
@@ -752,7 +772,7 @@ class Qwen3ForCausalLM(nn.Module):
     def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None):
         """Fill the static inputs with one H2D copy, replay, return (tokens, logp) device views.
 
-        ``groups`` (grouped graphs): list of (member row indices, shared key count)."""
+        ``groups`` (grouped graphs): list of (member row indices, shared key count, first own key)."""
         bs = len(seqs)
         gbs = _round_bs(bs, self._graph_bs)
         if gbs is None:
@@ -775,12 +795,7 @@ class Qwen3ForCausalLM(nn.Module):
             mem[:gbs] = -1
             sl[:gbs] = 0
             ks[:gbs] = 0
-            g_i = 0
-            for rows, shared in (groups or [([i], 0) for i in range(bs)]):
-                mem[g_i, :len(rows)] = rows
-                sl[g_i] = shared
-                ks[rows] = shared
-                g_i += 1
+            g_i = _fill_groups(groups or [([i], 0, 0) for i in range(bs)], mem, sl, ks)
             for r in range(bs, gbs):  # padding rows are singleton groups
                 mem[g_i, 0] = r
                 g_i += 1
@@ -836,47 +851,53 @@ class Qwen3ForCausalLM(nn.Module):
 
     def _grouped_launch(self, ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples):
         """Enqueues one grouped-rollout step: a cascade-attention decode graph when only decode
-        rows run, else a varlen paged prefill with the donors' chunks and the decode rows; the
-        partial last prompt page of each finished prefill is copied to the other members; then
-        lm_head + sampling (G draws from each finished prefill's last row) and the read-back."""
+        rows run, else one forward over the donors' prompt chunks (paged varlen attention) and
+        the decode rows (cascade attention); then lm_head + sampling (G draws from each finished
+        prefill's last row) and the read-back."""
         dev, temperature, top_k = ctx["dev"], ctx["temperature"], ctx["top_k"]
         r = None
+        a = self.model.layers[0].self_attn
+        nd = len(decode_rows)
         if not prefill:
             if self._has_cuda_graphs:
                 r = self._run_decode_graph(decode_rows, step, ctx["seed"], groups=groups_rows)
             if r is None:  # eager decode with the same cascade attention
-                bs = len(decode_rows)
                 ids, pos, cl, bt, slots = self._decode_arrays(decode_rows)
-                mem = np.full((len(groups_rows), 8), -1, dtype=np.int32)
-                sl = np.zeros(len(groups_rows), dtype=np.int32)
-                ks = np.zeros(bs, dtype=np.int32)
-                for gi, (rows_g, shared) in enumerate(groups_rows):
-                    mem[gi, :len(rows_g)] = rows_g
-                    sl[gi] = shared
-                    ks[rows_g] = shared
-                a = self.model.layers[0].self_attn
-                plan = ops.grouped_decode_plan(bs, a.num_kv_heads, int(sl.max(initial=0)), int(cl.max(initial=0)) + 1)
+                mem, sl, ks = _group_arrays(groups_rows, nd)
+                plan = ops.grouped_decode_plan(nd, a.num_kv_heads, int(sl.max(initial=0)),
+                                               int((cl + 1 - ks).max(initial=1)))
                 ids, pos, cl, bt, slots, mem_d, sl_d, ks_d = self._staging().put([ids, pos, cl, bt, slots, mem, sl, ks])
-                nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(bs, a.num_heads, a.head_dim, plan[1] + plan[2])
-                ws = torch.empty(nb // 4, dtype=torch.float32, device=dev)
+                ws = ops.grouped_workspace(nd, a.num_heads, a.head_dim, plan, dev)
                 h = self.model.forward_decode(ids, pos, cl, bt, slots,
                                               decode_plan=("grouped", plan, ws, mem_d, sl_d, ks_d))
                 logits = ops.linear(h, self.lm_head.weight)
                 ctx["rng"][0].fill_(step)
                 r = ops.sample(logits, temperature, top_k, 0, ctx["rng"])
         else:
-            seqs = [g.donor for g in prefill] + decode_rows
-            arrays, m_q, m_k = self._step_arrays(seqs)
-            ends = np.cumsum([s.num_scheduled_tokens for s in seqs]) - 1
+            # prefill rows (the donors' prompt chunks) on the paged varlen kernel; decode rows,
+            # whose keys skip the unused tail of the shared prompt page, on the cascade kernel
+            donors = [g.donor for g in prefill]
+            (ids, pos, cu_q, cu_k, blk_map, bt, tiles), m_q, m_k = self._step_arrays(donors)
+            tp = len(ids)
+            ends = np.cumsum([d.num_scheduled_tokens for d in donors]) - 1
             rows_np = np.asarray([ends[prefill.index(g)] for g in done for _ in range(G)]
-                                 + [ends[len(prefill) + j] for j in range(len(decode_rows))], dtype=np.int64)
-            ids, pos, cu_q, cu_k, blk_map, bt, tiles, rows = self._staging().put(arrays + [rows_np])
-            h = self.model.forward_prefill(ids, pos, cu_q, cu_k, m_q, m_k, blk_map, bt, tiles=tiles)
-            for g in done:  # each member gets its own copy of the partial last prompt page
-                if g.partial and G > 1:
-                    dst = torch.tensor([m.block_table[g.n_full] for m in g.members[1:]], dtype=torch.int32,
-                                       device=dev)
-                    _copy_page_prefix(self, g.members[0].block_table[g.n_full], dst, g.partial)
+                                 + [tp + j for j in range(nd)], dtype=np.int64)
+            if nd:
+                ids_d, pos_d, cl, bt_d, slots = self._decode_arrays(decode_rows)
+                mem, sl, ks = _group_arrays(groups_rows, nd)
+                plan = ops.grouped_decode_plan(nd, a.num_kv_heads, int(sl.max(initial=0)),
+                                               int((cl + 1 - ks).max(initial=1)))
+                (ids, pos, blk_map, cu_q, cu_k, bt, tiles, rows, cl_d, bt_d, mem_d, sl_d, ks_d) = self._staging().put(
+                    [np.concatenate([ids, ids_d]), np.concatenate([pos, pos_d]), np.concatenate([blk_map, slots]),
+                     cu_q, cu_k, bt, tiles, rows_np, cl, bt_d, mem, sl, ks])
+                ws = ops.grouped_workspace(nd, a.num_heads, a.head_dim, plan, dev)
+                tail = (tp, cl_d, bt_d, ("grouped", plan, ws, mem_d, sl_d, ks_d))
+            else:
+                ids, pos, cu_q, cu_k, blk_map, bt, tiles, rows = self._staging().put(
+                    [ids, pos, cu_q, cu_k, blk_map, bt, tiles, rows_np])
+                tail = None
+            h = self.model.forward_prefill(ids, pos, cu_q, cu_k, m_q, m_k, blk_map, bt, tiles=tiles,
+                                           decode_tail=tail)
             logits = ops.linear(h.index_select(0, rows), self.lm_head.weight)
             ctx["rng"][0].fill_(step)
             r = ops.sample(logits, temperature, top_k, 0, ctx["rng"])
@@ -1091,7 +1112,13 @@ class Qwen3ForCausalLM(nn.Module):
 
 
 class _Group:
-    """G completions of one prompt: one prefill (``donor``), shared full prompt pages."""
+    """G completions of one prompt: one prefill (``donor``) into pages that all members share.
+
+    Every prompt page, the partially filled last one included, is shared; a member's own
+    tokens start on a fresh page at key position ``own_start`` of its page table (positions
+    for RoPE stay the true token positions).  The unused tail of the last prompt page is
+    never read: decode attention takes keys [0, L) from the shared pages and
+    [own_start, kv_len] from the member's own."""
 
     def __init__(self, idx, prompt, G, sp):
         self.idx = idx
@@ -1116,30 +1143,50 @@ class _Group:
             m.num_scheduled_tokens = 0
 
     @property
-    def n_full(self):
-        return self.L // Sequence.BLOCK_SIZE
+    def n_shared(self):
+        return -(-self.L // Sequence.BLOCK_SIZE)
 
     @property
-    def partial(self):
-        return self.L % Sequence.BLOCK_SIZE
+    def own_start(self):
+        return self.n_shared * Sequence.BLOCK_SIZE
 
     def pages_needed(self):
-        return self.n_full + (self.G if self.partial else 0)
+        return self.n_shared
+
+
+def _group_arrays(groups_rows, n_rows):
+    """(members [n_groups, 8], shared_len [n_groups], kv_start [n_rows]) int32 for the cascade kernel."""
+    mem = np.full((len(groups_rows), 8), -1, dtype=np.int32)
+    sl = np.zeros(len(groups_rows), dtype=np.int32)
+    ks = np.zeros(n_rows, dtype=np.int32)
+    _fill_groups(groups_rows, mem, sl, ks)
+    return mem, sl, ks
+
+
+def _fill_groups(groups_rows, mem, sl, ks):
+    g_i = 0
+    for rows, shared, start in groups_rows:
+        mem[g_i, :len(rows)] = rows
+        sl[g_i] = shared
+        ks[rows] = start
+        g_i += 1
+    return g_i
 
 
 def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos_token_ids, record_logprobs=True):
     """Continuous-batching rollout of G completions per prompt with the prompt computed once.
 
     Scheduling follows the reference's loop (decode first, 2048-token budget, chunked prefill,
-    LIFO preemption) at the granularity of a group.  A group's full prompt pages are shared by
-    its members (reference-counted once per member); each member owns a copy of the partially
-    filled last prompt page and everything it generates.  The first token of every member is
+    LIFO preemption) at the granularity of a group.  A group's prompt pages are shared by its
+    members (reference-counted once per member); each member owns the pages of what it
+    generates, starting on a fresh page (see _Group).  The first token of every member is
     sampled from the single prefill's last row (G independent draws)."""
     BS = model.BLOCK_SIZE
     sp = {"temperature": temperature, "max_tokens": max_new_tokens}
     groups = [_Group(i, p, G, sp) for i, p in enumerate(prompts)]
-    max_ctx = model.max_model_len or (max((len(p) for p in prompts), default=1) + max_new_tokens)
-    max_shared = max((g.n_full * BS for g in groups), default=0)
+    # key positions run up to own_start + max_new_tokens (own tokens start page-aligned)
+    max_ctx = (model.max_model_len or (max((len(p) for p in prompts), default=1) + max_new_tokens)) + BS
+    max_shared = max((g.L for g in groups), default=0)
     model.rollout_stats = {"t_start": time.perf_counter()}
     ctx = model._grouped_setup(max_ctx, max_shared, temperature, top_k)
     model.rollout_stats["setup_s"] = time.perf_counter() - model.rollout_stats["t_start"]
@@ -1211,13 +1258,12 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
             if grp.state == "WAITING":
                 if bm.available < grp.pages_needed():
                     break
-                grp.shared = [bm._take_free() for _ in range(grp.n_full)]
+                grp.shared = [bm._take_free() for _ in range(grp.n_shared)]
                 for p in grp.shared:
                     bm.ref_count[p] = G  # one reference per member
-                own = [bm._take_free() for _ in range(G)] if grp.partial else []
-                for i, m in enumerate(grp.members):
-                    m.block_table = grp.shared + ([own[i]] if own else [])
-                grp.donor.block_table = grp.members[0].block_table
+                for m in grp.members:
+                    m.block_table = list(grp.shared)
+                grp.donor.block_table = grp.shared
                 grp.state = "PREFILL"
             waiting.popleft()
             running.append(grp)
@@ -1240,13 +1286,12 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
         step += 1
         done = [g for g in prefill if g.donor.kv_len + g.donor.num_scheduled_tokens >= g.L]
         n_samples = len(decode_rows) + G * len(done)
-        groups_rows = []
-        if not prefill:
-            pos_of = {id(m): i for i, m in enumerate(decode_rows)}
-            for grp in running:
-                rows = [pos_of[id(m)] for m in grp.members if id(m) in pos_of]
-                if rows:
-                    groups_rows.append((rows, grp.n_full * BS))
+        groups_rows = []  # (decode row indices, shared prompt keys, first own key) per group
+        pos_of = {id(m): i for i, m in enumerate(decode_rows)}
+        for grp in running:
+            rows = [pos_of[id(m)] for m in grp.members if id(m) in pos_of]
+            if rows:
+                groups_rows.append((rows, grp.L, grp.own_start))
         if not prefill:
             model.rollout_stats["decode_steps"] = model.rollout_stats.get("decode_steps", 0) + 1
         model._grouped_launch(ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples)
@@ -1274,7 +1319,7 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
         for g in done:
             g.state = "DECODE"
             for m in g.members:
-                m.kv_len = g.L
+                m.kv_len = g.own_start  # next key goes to a fresh page
                 m.status = "RUNNING"
                 take(m)
         for m in decode_rows:
@@ -1288,22 +1333,6 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
     st = model.rollout_stats
     st["total_s"] = time.perf_counter() - st.pop("t_start")
     return [m for g in groups for m in g.members]
-
-
-def _copy_page_prefix(model, src_page, dst_pages, n_tokens):
-    """Copy the first n_tokens rows of KV page src_page to dst_pages in every layer."""
-    a0 = model.model.layers[0].self_attn
-    k, v = a0.k_cache, a0.v_cache  # views of the [layers, blocks, 256, hkv, D] pools
-    layers = len(model.model.layers)
-    layer_bytes = k.numel() * k.element_size()
-    if layers > 1:
-        layer_bytes = (model.model.layers[1].self_attn.k_cache.data_ptr() - k.data_ptr())
-    page_bytes = k.stride(0) * k.element_size()
-    row_bytes = k.stride(1) * k.element_size()
-    ops.check(ops.lib().qb_copy_page_prefix(k.data_ptr(), v.data_ptr(), layers, layer_bytes, page_bytes, k.shape[0],
-                                            int(src_page), dst_pages.data_ptr(), dst_pages.numel(),
-                                            n_tokens * row_bytes, ops.err_flag().data_ptr(), ops.stream_ptr()),
-              "qb_copy_page_prefix")
 
 
 def use_reference_defaults():

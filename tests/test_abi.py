@@ -31,7 +31,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_version_and_status_strings():
     lib = _lib.load()
-    assert lib.qb_abi_version() == 1
+    assert lib.qb_abi_version() == 2
     assert lib.qb_status_string(0) == b"ok"
     assert b"invalid" in lib.qb_status_string(1)
     assert b"unsupported" in lib.qb_status_string(2)

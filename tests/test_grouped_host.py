@@ -37,18 +37,24 @@ class HostGrouped(Qwen3ForCausalLM):
             for i in range(G):
                 toks.append((nxt(g.prompt[-1], g.L - 1) + i) % V)
         for m in decode_rows:
-            toks.append(nxt(m.last_token, m.kv_len))
-        # structural checks on the page tables of everything that runs this step
+            toks.append(nxt(m.last_token, m.num_tokens - 1))
+        # structural checks on the page tables of everything that runs this step: the whole
+        # prompt is shared, own tokens start on a fresh page, own pages belong to one member
         own_seen = set()
-        for rows, shared in groups_rows:
+        seen_rows = set()
+        for rows, shared, start in groups_rows:
             members = [decode_rows[r] for r in rows]
-            n_full = shared // 256
-            first = members[0].block_table[:n_full]
+            n_sh = -(-shared // 256)
+            assert shared == members[0].num_prompt_tokens and start == n_sh * 256
+            first = members[0].block_table[:n_sh]
             for m in members:
-                assert m.block_table[:n_full] == first
-                for p in m.block_table[n_full:]:
-                    assert p not in own_seen
+                assert m.block_table[:n_sh] == first
+                assert start <= m.kv_len < len(m.block_table) * 256
+                for p in m.block_table[n_sh:]:
+                    assert p not in own_seen and p not in first
                     own_seen.add(p)
+            seen_rows.update(rows)
+        assert seen_rows == set(range(len(decode_rows)))  # every decode row is in one group
         self.checks += 1
         ctx["toks"] = toks
         assert len(toks) == n_samples

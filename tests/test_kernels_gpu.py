@@ -323,25 +323,40 @@ def test_grpo_advantage_and_loss(cuda):
 @pytest.mark.parametrize("split", [64, 256])
 def test_paged_decode_grouped_shared_prefix(cuda, split):
     """Groups sharing prompt pages: the cascade (shared keys once per group + own keys per
-    sequence + merge) equals plain paged decode attention on the same page tables."""
+    sequence, merged in the same launch) equals plain attention over the concatenation of the
+    shared keys [0, shared_len) and the own keys [kv_start, len).  Groups whose prompt ends
+    inside a page leave a hole [shared_len, kv_start) filled with large garbage that must never
+    be read; page-aligned groups use kv_start == shared_len.  Two calls check that the merge
+    tickets are left zero."""
     g = gen(77 + split)
     hq, hkv = 16, 8
-    groups = [(8, 512), (3, 256), (1, 0), (5, 768), (8, 0)]  # (members, shared keys)
-    n_pages = 200
+    # (members, shared keys, own keys start on a fresh page?)
+    groups = [(8, 512, False), (3, 256, False), (1, 0, False), (5, 768, False), (8, 0, False),
+              (8, 300, True), (2, 17, True), (4, 511, True), (1, 700, True)]
+    n_pages = 300
     kc = torch.randn(n_pages, 256, hkv, 128, generator=g).to(BF)
     vc = torch.randn(n_pages, 256, hkv, 128, generator=g).to(BF)
     perm = torch.randperm(n_pages, generator=g).tolist()
-    tables, lens, members, shared, kv_start = [], [], [], [], []
-    for G_, sl in groups:
-        shared_pages = [perm.pop() for _ in range(sl // 256)]
+    tables, lens, members, shared, kv_start, keys = [], [], [], [], [], []
+    for G_, sl, fresh in groups:
+        sh_pages = [perm.pop() for _ in range(-(-sl // 256))]
+        ks = len(sh_pages) * 256 if fresh else sl
+        for idx, p in enumerate(sh_pages):  # garbage in the hole after the shared keys (never read)
+            start = max(0, sl - idx * 256)
+            kc[p, start:] = 1e4
+            vc[p, start:] = 1e4
         row = []
         for _ in range(G_):
-            L = sl + int(torch.randint(1, 700, (1,), generator=g))
-            own = [perm.pop() for _ in range((L - sl + 255) // 256)]
+            n_own = int(torch.randint(1, 700, (1,), generator=g))
+            own = [perm.pop() for _ in range(-(-(ks % 256 + n_own) // 256))]
+            tab = sh_pages[:ks // 256] + own
             row.append(len(tables))
-            tables.append(shared_pages + own)
-            lens.append(L)
-            kv_start.append(sl)
+            tables.append(tab)
+            lens.append(ks + n_own)
+            kv_start.append(ks)
+            # the keys this sequence attends to, as (page, slot) pairs in order
+            keys.append([(sh_pages[t // 256], t % 256) for t in range(sl)]
+                        + [(tab[t // 256], t % 256) for t in range(ks, ks + n_own)])
         members.append(row + [-1] * (8 - len(row)))
         shared.append(sl)
     B = len(tables)
@@ -350,12 +365,31 @@ def test_paged_decode_grouped_shared_prefix(cuda, split):
     for i, t in enumerate(tables):
         bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
     q = torch.randn(B, hq, 128, generator=g).to(BF)
+    # oracle: gather each sequence's keys into a contiguous paged copy, plain decode attention
+    n_ref = sum(-(-len(k) // 256) for k in keys)
+    rk = torch.zeros(n_ref, 256, hkv, 128, dtype=BF)
+    rv = torch.zeros_like(rk)
+    rbt = torch.full((B, max(-(-len(k) // 256) for k in keys)), -1, dtype=torch.int32)
+    nxt_page = 0
+    for b, kl in enumerate(keys):
+        for t, (p, j) in enumerate(kl):
+            if t % 256 == 0:
+                rbt[b, t // 256] = nxt_page
+                nxt_page += 1
+            rk[rbt[b, t // 256], t % 256] = kc[p, j]
+            rv[rbt[b, t // 256], t % 256] = vc[p, j]
+    ref = R.paged_decode(q, rk, rv, rbt, torch.tensor([len(k) for k in keys]), 128 ** -0.5)
     ctx = torch.tensor(lens, dtype=torch.int32) - 1
-    ref = R.paged_decode(q, kc, vc, bt, ctx + 1, 128 ** -0.5)
-    plan = (split, -(-max(shared) // split) if max(shared) else 1, -(-max(L - s for L, s in zip(lens, kv_start)) // split))
-    out = ops.paged_decode_attention_grouped(q.to(cuda), kc.to(cuda), vc.to(cuda), bt.to(cuda), ctx.to(cuda),
-                                             128 ** -0.5, torch.tensor(members, dtype=torch.int32).to(cuda),
-                                             torch.tensor(shared, dtype=torch.int32).to(cuda),
-                                             torch.tensor(kv_start, dtype=torch.int32).to(cuda), plan)
-    close_bf16(out, ref, 2e-2)
+    plan = (split, -(-max(shared) // split) if max(shared) else 1,
+            -(-max(L - s for L, s in zip(lens, kv_start)) // split))
+    ws = ops.grouped_workspace(B, hq, 128, plan, cuda)
+    args = (q.to(cuda), kc.to(cuda), vc.to(cuda), bt.to(cuda), ctx.to(cuda), 128 ** -0.5,
+            torch.tensor(members, dtype=torch.int32).to(cuda), torch.tensor(shared, dtype=torch.int32).to(cuda),
+            torch.tensor(kv_start, dtype=torch.int32).to(cuda), plan)
+    for _ in range(2):
+        out = ops.paged_decode_attention_grouped(*args, workspace=ws)
+        close_bf16(out, ref, 2e-2)
+    nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(B, hq, 128, plan[1] + plan[2])
+    tickets = ws.view(torch.uint8)[nb - B * hq * 4:nb].view(torch.int32)
+    assert int(tickets.abs().sum()) == 0
     ops.check_device_errors()

@@ -285,6 +285,35 @@ def test_grouped_rollout_teacher_forced(setup, cuda):
     ops.check_device_errors()
 
 
+@pytest.mark.parametrize("graphs", [True, False])
+def test_grouped_rollout_mixed_steps(setup, cuda, graphs):
+    """Prompts longer in total than one step's 2048-token budget: the last prompt's prefill
+    runs in the same step as the other groups' first decode tokens (prefill rows on the paged
+    varlen kernel, decode rows on the cascade kernel, whose keys skip the unused tail of the
+    shared last prompt page).  Greedy tokens match the oracle teacher-forced; eager decode
+    (graphs=False) and graph replay produce the same tokens."""
+    cfg, params, model = setup
+    g = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, L), generator=g).to(cuda) for L in (30, 260, 520, 1400)]
+    model.use_cuda_graphs = graphs
+    try:
+        toks, gen, lps, plens = model.generate_grouped_with_logprobs(prompts, 4, max_new_tokens=10,
+                                                                     temperature=1.0, top_k=1)
+    finally:
+        model.use_cuda_graphs = True
+    assert model.rollout_stats["steps"] > model.rollout_stats.get("decode_steps", 0) + 1  # a mixed step ran
+    checked = 0
+    for t, pl in zip(toks, plens):
+        lg, _ = _oracle_lp(params, cfg, t)
+        for pos in range(pl, len(t)):
+            top2 = lg[pos - 1].topk(2).values
+            if (top2[0] - top2[1]).item() > 0.05:
+                assert t[pos] == lg[pos - 1].argmax().item(), (pl, pos, graphs)
+                checked += 1
+    assert checked > 60
+    ops.check_device_errors()
+
+
 def test_grouped_rollout_matches_plain_greedy(setup, cuda):
     cfg, params, model = setup
     g = torch.Generator().manual_seed(11)
