@@ -13,7 +13,7 @@
 // 256-byte row at ((page*256 + j)*hkv + h)*128.
 #include <algorithm>
 
-#include "common.cuh"
+#include "tma.cuh"
 
 namespace {
 
@@ -304,7 +304,7 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 }
 
 // ============================================================================
-// Shared-prefix decode attention (GRPO groups): warp-independent, persistent
+// Shared-prefix decode attention (GRPO groups): warp-independent, persistent, TMA
 // ============================================================================
 // The G <= 8 members of a group share the K/V pages of their common prompt.  Work items,
 // each owned by ONE warp from start to finish:
@@ -318,22 +318,29 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 // Keys in [shared_len, kv_start) are never read.  An item writes one split-K partial (O / l and
 // its log2-domain LSE) per (sequence, head) it covers; the warp that writes the last partial of
 // a (sequence, kv head) merges all of its slots, found through a ticket counter that it resets
-// to zero.  Nothing waits on another warp or CTA.
+// to zero.  No warp waits on another warp or CTA.
 //
-// Each warp runs its own 3-deep ring of 16-token stages (K 4 KB, V 4 KB, and the item's query
-// rows with its first stage) through cp.async, its load cursor crossing item boundaries so the
-// next item's data is in flight while an item finishes.  Warp w of the grid takes items w,
-// w + total_warps, ... (shared items first).  There is no __syncthreads in the kernel.
+// Each warp streams its items' keys in 16-token stages through its own 3-slot ring: lane 0
+// issues two TMA box loads for K and two for V (16 tokens x 64 dims each, 128-byte swizzle)
+// plus, with an own item's first stage, one for its two query rows, all completing on the
+// slot's mbarrier.  The ring runs across item boundaries, so the next item's keys are in flight
+// while an item finishes.  Warp w of the grid takes items w, w + total_warps, ... (shared items
+// first).  Every mbarrier wait is bounded (QB_DEVERR_TIMEOUT, then the warp drains its copies
+// with a bounded wait and leaves).
 constexpr int GMAX = 8;
-constexpr int WD_TOK = 16;                              // tokens per stage (one MMA M tile)
-constexpr int WD_STAGES = 3;
-constexpr int WD_KV_BYTES = WD_TOK * ROWB;              // 4 KB of K (and of V) per stage
-constexpr int WD_STAGE_BYTES = 2 * WD_KV_BYTES + 16 * ROWB;  // K, V, up to 16 query rows
-constexpr int WD_WARP_BYTES = WD_STAGES * WD_STAGE_BYTES;
-constexpr int WD_WARPS = 6;                             // per CTA; one CTA per SM
-constexpr int WD_SMEM = WD_WARPS * WD_WARP_BYTES;       // 216 KB
+constexpr int WD_TOK = 16;                   // tokens per stage (one MMA M tile)
+constexpr int WD_SLOTS = 3;
+constexpr int WD_KV_BYTES = WD_TOK * ROWB;   // 4 KB of K (and of V) per stage: two 2 KB halves
+constexpr int WD_Q_OFF = WD_SLOTS * 2 * WD_KV_BYTES;       // 24 KB: query rows of own items
+constexpr int WD_BAR_OFF = WD_Q_OFF + WD_SLOTS * 2 * ROWB;  // + 3 x 512 B
+constexpr int WD_WARP_BYTES = 26 * 1024;     // 1024-aligned per-warp region
+constexpr int WD_WARPS = 8;                  // per CTA; one CTA per SM
+constexpr int WD_SMEM = WD_WARPS * WD_WARP_BYTES + 1024;  // + alignment slack
+static_assert(WD_BAR_OFF + WD_SLOTS * 8 <= WD_WARP_BYTES, "per-warp region");
 
 struct CascadeParams {
+  CUtensorMap tk, tv;         // caches as {D, hkv, num_blocks*page}, box {64, 1, 16}, 128B swizzle
+  CUtensorMap tq;             // q as {D, batch*hq}, box {D, 2}, no swizzle
   DecodeParams d;             // slot_off = shared_splits; kv_start = first own key per sequence
   const int32_t* members;     // [n_groups, GMAX] sequence indices, -1 padded
   const int32_t* shared_len;  // [n_groups] keys shared by the group (pages of members[g][0])
@@ -398,6 +405,10 @@ QB_DEVICE Item decode_item(const CascadeParams& cp, int i) {
 
 QB_DEVICE uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
+// Byte offset of (token row r, 16-byte chunk c of the 256-byte row) in a K or V stage: two
+// 2 KB halves (dims 0-63, 64-127) of 16 rows x 128 B, each 128-byte swizzled by TMA.
+QB_DEVICE uint32_t tsw(int r, int c) { return (c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4); }
+
 // Merges the n_slots partials of sequence b, heads h0 and h0+1 (one warp: lane -> head
 // h0 + lane/16, eight dims).  The partials come from other warps of this launch; __ldcg
 // reads them from L2.
@@ -449,79 +460,84 @@ QB_DEVICE void publish_and_merge_warp(const CascadeParams& cp, int kvh, int seq_
   }
 }
 
+// Bounded wait on a ring slot; false (QB_DEVERR_TIMEOUT raised) if it did not complete.
+QB_DEVICE bool slot_wait(uint32_t bar, uint32_t parity, int* err) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 255 && clock64() - t0 > WAIT_CYCLES) break;
+  }
+  qb_set_err(err, QB_DEVERR_TIMEOUT);
+  return false;
+}
+
 __global__ void __launch_bounds__(WD_WARPS * 32, 1)
-paged_decode_cascade_kernel(CascadeParams cp) {
-  extern __shared__ __align__(128) uint8_t smem[];
+paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   const DecodeParams& p = cp.d;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  uint8_t* wsm = smem + warp * WD_WARP_BYTES;  // this warp's stage ring
   const int total = gridDim.x * WD_WARPS;
   const int first = blockIdx.x * WD_WARPS + warp;
   if (first >= cp.n_items) return;
+  // this warp's region: K/V slots, own-item query rows, ring mbarriers (1024-aligned base)
+  uint8_t* wsm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023) + warp * WD_WARP_BYTES;
+  const uint32_t wbase = smem_u32(wsm);
+  auto kv_addr = [&](int slot) { return wbase + slot * 2 * WD_KV_BYTES; };
+  auto q_addr = [&](int slot) { return wbase + WD_Q_OFF + slot * 2 * ROWB; };
+  auto bar_addr = [&](int slot) { return wbase + WD_BAR_OFF + slot * 8; };
+  if (lane == 0) {
+    for (int s = 0; s < WD_SLOTS; ++s) mbar_init(bar_addr(s), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
 
-  // ---- load cursor: next stage to copy (item, stage within it, flat counter), current page
+  // ---- load cursor (state kept by every lane; lane 0 issues the copies)
   int l_item = first, l_stage = 0, l_flat = 0, l_page = -1, l_page_col = -1;
   Item l_it = decode_item(cp, l_item);
   auto issue = [&]() {
     if (l_item < cp.n_items) {
-      uint8_t* buf = wsm + (l_flat % WD_STAGES) * WD_STAGE_BYTES;
-      const uint32_t kbase = smem_u32(buf), vbase = kbase + WD_KV_BYTES, qbase = vbase + WD_KV_BYTES;
-      if (l_stage < l_it.n_stages) {
-        const int tok0 = l_it.tok_begin + l_stage * WD_TOK;
-        const int col = tok0 / PAGE;
-        if (col != l_page_col) {  // one page-table read per page (16 stages)
-          l_page_col = col;
-          l_page = col < p.bt_stride ? l_it.btrow[col] : -1;
-          if (l_page < 0 || l_page >= p.num_blocks) {
-            qb_set_err(p.err, QB_DEVERR_PAGE);
-            l_page = -1;
+      const int slot = l_flat % WD_SLOTS;
+      const bool kv = l_stage < l_it.n_stages;
+      const bool q = l_stage == 0 && !l_it.shared;
+      if (lane == 0) {
+        const uint32_t bar = bar_addr(slot);
+        mbar_expect_tx(bar, (kv ? 2 * WD_KV_BYTES : 0) + (q ? 2 * ROWB : 0));
+        if (kv) {
+          const int tok0 = l_it.tok_begin + l_stage * WD_TOK;
+          const int col = tok0 / PAGE;
+          if (col != l_page_col) {  // one page-table read per page (16 stages)
+            l_page_col = col;
+            l_page = col < p.bt_stride ? l_it.btrow[col] : -1;
+            if (l_page < 0 || l_page >= p.num_blocks) {
+              qb_set_err(p.err, QB_DEVERR_PAGE);  // read page 0 instead; the result is flagged
+              l_page = 0;
+            }
           }
+          const int row = l_page * PAGE + tok0 % PAGE;
+          const uint32_t kb = kv_addr(slot), vb = kb + WD_KV_BYTES;
+          tma_load_3d(kb, &cp.tk, 0, l_it.kvh, row, bar);
+          tma_load_3d(kb + 2048, &cp.tk, 64, l_it.kvh, row, bar);
+          tma_load_3d(vb, &cp.tv, 0, l_it.kvh, row, bar);
+          tma_load_3d(vb + 2048, &cp.tv, 64, l_it.kvh, row, bar);
         }
-        const bool page_ok = l_page >= 0;
-        const int64_t row0 = ((int64_t)(page_ok ? l_page : 0) * PAGE + (tok0 % PAGE)) * p.hkv + l_it.kvh;
-        // 16 rows x 16 chunks of K and of V: 8 + 8 copies per lane
-#pragma unroll
-        for (int i = 0; i < (WD_TOK * 16) / 32; ++i) {
-          const int idx = lane + i * 32;
-          const int r = idx >> 4, c = idx & 15;
-          const bool ok = page_ok && (tok0 + r < l_it.tok_end);
-          const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
-          cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
-          cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
-        }
+        if (q) tma_load_2d(q_addr(slot), &cp.tq, 0, l_it.idx * p.hq + l_it.kvh * 2, bar);
       }
-      if (l_stage == 0) {  // the item's query rows
-        const int h0 = l_it.kvh * 2;
-        if (l_it.shared) {  // 16 rows: member r/2, head h0 + r%2 (absent members zero filled)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int idx = lane + i * 32;
-            const int r = idx >> 4, c = idx & 15;
-            const int m = group_member(cp, l_it.idx, r >> 1);
-            const bf16* src = p.q + ((int64_t)(m < 0 ? 0 : m) * p.hq + h0 + (r & 1)) * D + c * 8;
-            cp_async_16(qbase + swz128(r, c), src, m >= 0 ? 16 : 0);
-          }
-        } else {  // 2 rows: heads h0, h0 + 1 of the sequence
-          const int r = lane >> 4, c = lane & 15;
-          cp_async_16(qbase + swz128(r, c), p.q + ((int64_t)l_it.idx * p.hq + h0 + r) * D + c * 8, 16);
-        }
-      }
-      if (++l_stage >= max(1, l_it.n_stages)) {  // an empty item still takes one stage slot
+      if (++l_stage >= max(1, l_it.n_stages)) {  // an empty item still takes one slot
         l_stage = 0;
         l_page_col = -1;
         l_item += total;
         if (l_item < cp.n_items) l_it = decode_item(cp, l_item);
       }
+      ++l_flat;  // counts armed slots only
     }
-    cp_async_commit();
-    ++l_flat;
   };
 #pragma unroll
-  for (int s = 0; s < WD_STAGES - 1; ++s) issue();
+  for (int s = 0; s < WD_SLOTS - 1; ++s) issue();
 
   int f = 0;  // flat index of the stage being consumed
-  for (int k = 0;; ++k) {
+  bool ok = true;
+  for (int k = 0; ok; ++k) {
     if (first + k * total >= cp.n_items) break;
     const Item it = decode_item(cp, first + k * total);
     const int ns = max(1, it.n_stages);
@@ -531,34 +547,49 @@ paged_decode_cascade_kernel(CascadeParams cp) {
       float o[16][4];
 #pragma unroll
       for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      // Q as the A operand, straight from global: a0/a2 row g, a1/a3 row g + 8
       uint32_t qa[8][4];
+      {
+        const int m0 = group_member(cp, it.idx, g >> 1), m1 = group_member(cp, it.idx, 4 + (g >> 1));
+        const bf16* q0 = p.q + ((int64_t)(m0 < 0 ? 0 : m0) * p.hq + h0 + (g & 1)) * D;
+        const bf16* q1 = p.q + ((int64_t)(m1 < 0 ? 0 : m1) * p.hq + h0 + (g & 1)) * D;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int c = kk * 16 + 2 * t4;
+          qa[kk][0] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+          qa[kk][1] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+          qa[kk][2] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+          qa[kk][3] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+        }
+      }
       for (int s = 0; s < ns; ++s, ++f) {
         issue();
-        cp_async_wait<WD_STAGES - 1>();
-        __syncwarp();
-        const uint8_t* buf = wsm + (f % WD_STAGES) * WD_STAGE_BYTES;
-        const uint32_t kbase = smem_u32(buf), vbase = kbase + WD_KV_BYTES;
-        if (s == 0) {  // Q as the A operand: a0/a2 row g, a1/a3 row g + 8
-          const uint8_t* qs = buf + 2 * WD_KV_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            qa[kk][0] = lds32(qs + swz128(g, kk * 2) + 4 * t4);
-            qa[kk][1] = lds32(qs + swz128(g + 8, kk * 2) + 4 * t4);
-            qa[kk][2] = lds32(qs + swz128(g, kk * 2 + 1) + 4 * t4);
-            qa[kk][3] = lds32(qs + swz128(g + 8, kk * 2 + 1) + 4 * t4);
-          }
+        const int slot = f % WD_SLOTS;
+        if (!slot_wait(bar_addr(slot), (f / WD_SLOTS) & 1, p.err)) {
+          ok = false;
+          break;
         }
+        const uint32_t kbase = kv_addr(slot), vbase = kbase + WD_KV_BYTES;
         if (s < it.n_stages) {
+          const int key0 = it.tok_begin + s * WD_TOK;
+          const int valid = it.tok_end - key0;  // rows of this stage that are keys
+          if (valid < WD_TOK) {  // zero the V rows past the keys (they may hold any bits)
+            for (int i = lane; i < (WD_TOK - valid) * 16; i += 32) {
+              const int r = valid + (i >> 4), c = i & 15;
+              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vbase + tsw(r, c)), "r"(0u) : "memory");
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+          }
           // S[16 q x 16 tok] = Q K^T (two n-tiles of 8 tokens)
           float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             uint32_t r0, r1, r2, r3;
-            ldmatrix_x4(kbase + swz128((lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2, r3);
+            ldmatrix_x4(kbase + tsw((lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2, r3);
             mma_bf16_16816(sc[0], qa[kk], r0, r1);
             mma_bf16_16816(sc[1], qa[kk], r2, r3);
           }
-          const int key0 = it.tok_begin + s * WD_TOK;
           float mt[2] = {NEG_INF, NEG_INF};
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
@@ -608,14 +639,15 @@ paged_decode_cascade_kernel(CascadeParams cp) {
 #pragma unroll
           for (int dp = 0; dp < 8; ++dp) {
             uint32_t r0, r1, r2, r3;
-            ldmatrix_x4_trans(vbase + swz128((lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1, r2,
+            ldmatrix_x4_trans(vbase + tsw((lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1, r2,
                               r3);
             mma_bf16_16816(o[2 * dp], pa, r0, r1);
             mma_bf16_16816(o[2 * dp + 1], pa, r2, r3);
           }
         }
-        __syncwarp();  // every lane is done with this buffer before the next issue refills it
+        __syncwarp();  // every lane is done with this slot before the next issue refills it
       }
+      if (!ok) break;
       // partials of rows g (member g/2, head h0 + g%2) and g + 8 (member 4 + g/2)
       const int mem_lane = lane < GMAX ? group_member(cp, it.idx, lane) : -1;
 #pragma unroll
@@ -640,29 +672,45 @@ paged_decode_cascade_kernel(CascadeParams cp) {
       uint32_t qb[8][2];
       for (int s = 0; s < ns; ++s, ++f) {
         issue();
-        cp_async_wait<WD_STAGES - 1>();
-        __syncwarp();
-        const uint8_t* buf = wsm + (f % WD_STAGES) * WD_STAGE_BYTES;
-        const uint32_t kbase = smem_u32(buf), vbase = kbase + WD_KV_BYTES;
+        const int slot = f % WD_SLOTS;
+        if (!slot_wait(bar_addr(slot), (f / WD_SLOTS) & 1, p.err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t kbase = kv_addr(slot), vbase = kbase + WD_KV_BYTES;
         if (s == 0) {  // Q^T as the B operand: b0 = Q[h0+g][kk*16 + 2t4, +1], b1 = ... + 8
-          const uint8_t* qs = buf + 2 * WD_KV_BYTES;
+          const uint8_t* qs = wsm + WD_Q_OFF + slot * 2 * ROWB;
           const bool valid = g < 2;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            qb[kk][0] = valid ? lds32(qs + swz128(g, kk * 2) + 4 * t4) : 0u;
-            qb[kk][1] = valid ? lds32(qs + swz128(g, kk * 2 + 1) + 4 * t4) : 0u;
+            qb[kk][0] = valid ? lds32(qs + g * ROWB + kk * 32 + 4 * t4) : 0u;
+            qb[kk][1] = valid ? lds32(qs + g * ROWB + kk * 32 + 16 + 4 * t4) : 0u;
           }
         }
         if (s < it.n_stages) {
-          // S^T[16 tok x 8] = K[16 x 128] * Q^T[128 x 8]
-          float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            uint32_t a[4];
-            ldmatrix_x4(kbase + swz128(lane & 15, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
-            mma_bf16_16816(sc, a, qb[kk][0], qb[kk][1]);
+          const int key0 = it.tok_begin + s * WD_TOK;
+          const int valid = it.tok_end - key0;
+          if (valid < WD_TOK) {  // zero the V rows past the keys (they may hold any bits)
+            for (int i = lane; i < (WD_TOK - valid) * 16; i += 32) {
+              const int r = valid + (i >> 4), c = i & 15;
+              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vbase + tsw(r, c)), "r"(0u) : "memory");
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
           }
-          const int tokA = it.tok_begin + s * WD_TOK + g;  // rows g and g+8
+          // S^T[16 tok x 8] = K[16 x 128] * Q^T[128 x 8]; two accumulators halve the MMA chain
+          float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int kk = 0; kk < 8; kk += 2) {
+            uint32_t a[4], b[4];
+            ldmatrix_x4(kbase + tsw(lane & 15, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+            ldmatrix_x4(kbase + tsw(lane & 15, kk * 2 + 2 + (lane >> 4)), b[0], b[1], b[2], b[3]);
+            mma_bf16_16816(sc, a, qb[kk][0], qb[kk][1]);
+            mma_bf16_16816(sd, b, qb[kk + 1][0], qb[kk + 1][1]);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sc[i] += sd[i];
+          const int tokA = key0 + g;  // rows g and g+8
           float x[4];
           x[0] = (t4 == 0 && tokA < it.tok_end) ? sc[0] * p.scale_log2 : NEG_INF;
           x[1] = (t4 == 0 && tokA < it.tok_end) ? sc[1] * p.scale_log2 : NEG_INF;
@@ -721,13 +769,14 @@ paged_decode_cascade_kernel(CascadeParams cp) {
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt) {
             uint32_t a[4];
-            ldmatrix_x4_trans(vbase + swz128((lane & 7) + ((lane >> 4) << 3), mt * 2 + ((lane >> 3) & 1)), a[0], a[1],
+            ldmatrix_x4_trans(vbase + tsw((lane & 7) + ((lane >> 4) << 3), mt * 2 + ((lane >> 3) & 1)), a[0], a[1],
                               a[2], a[3]);
             mma_bf16_16816(o[mt], a, pb0, pb1);
           }
         }
         __syncwarp();
       }
+      if (!ok) break;
       // partial: lanes with t4 == 0 hold O^T rows (dims) mt*16 + g and + 8 for both heads
       if (t4 == 0) {
 #pragma unroll
@@ -745,7 +794,14 @@ paged_decode_cascade_kernel(CascadeParams cp) {
       publish_and_merge_warp(cp, it.kvh, lane == 0 ? it.idx : -1, lane);
     }
   }
-  cp_async_wait<0>();
+  // Drain: the copies of every slot issued but not consumed complete before the warp leaves
+  // (bounded waits; after a timeout they are the copies that did not arrive in time).
+  for (; f < l_flat; ++f) {
+    const uint32_t bar = bar_addr(f % WD_SLOTS), parity = (f / WD_SLOTS) & 1;
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity))
+      if (clock64() - t0 > WAIT_CYCLES) break;
+  }
 }
 
 // ============================================================================
@@ -1262,6 +1318,34 @@ attn_bwd_dq_kernel(BwdParams p) {
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// K or V cache of one layer, [num_blocks*256 tokens][hkv][128] bf16, as a 3-D TMA map
+// {128 dims, hkv, tokens}; box {64 dims, 1 head, 16 tokens}, 128-byte swizzle.
+bool cache_tmap(CUtensorMap* map, const void* base, int hkv, int64_t num_blocks) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)hkv, (cuuint64_t)num_blocks * PAGE};
+  cuuint64_t strides[2] = {(cuuint64_t)ROWB, (cuuint64_t)hkv * ROWB};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)WD_TOK};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Queries [rows = batch*hq][128] bf16 as a 2-D TMA map; box {128, 2} (one kv head's two query
+// heads), no swizzle.
+bool query_tmap(CUtensorMap* map, const void* base, int64_t rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ROWB};
+  cuuint32_t box[2] = {(cuuint32_t)D, 2};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // SM count of the current device (cached per device).
 inline int device_sm_count() {
   static int cache[64] = {0};
@@ -1345,8 +1429,19 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
                  n_slots, shared_splits, kv_start};
   int* tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) +
                                         (size_t)batch * n_slots * hq * WS_ROW * sizeof(float));
-  CascadeParams cp{d, group_members, shared_len, batch, shared_splits, own_splits, (int)n_shared, (int)n_items,
-                   tickets};
+  CascadeParams cp;
+  if (!cache_tmap(&cp.tk, k_cache, hkv, num_blocks) || !cache_tmap(&cp.tv, v_cache, hkv, num_blocks) ||
+      !query_tmap(&cp.tq, q, (int64_t)batch * hq))
+    return QB_ERR_UNSUPPORTED;
+  cp.d = d;
+  cp.members = group_members;
+  cp.shared_len = shared_len;
+  cp.batch = batch;
+  cp.shared_splits = shared_splits;
+  cp.own_splits = own_splits;
+  cp.n_shared_items = (int)n_shared;
+  cp.n_items = (int)n_items;
+  cp.tickets = tickets;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(paged_decode_cascade_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WD_SMEM);
