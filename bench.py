@@ -451,14 +451,24 @@ def run_rollout_attn():
     sl_d = torch.tensor(shared, dtype=torch.int32, device=dev)
     ks_d = torch.tensor(kv_start, dtype=torch.int32, device=dev)
     split, ms = ops.decode_split_plan(B, hkv, max(plain_lens) + gen)
-    plan = ops.grouped_decode_plan(B, hkv, max(shared), gen)
+    # the rollout's decode graphs plan with the captured context bound (prompt + 512 new + a page)
+    ctx_bound = 512 + 512 + 256
+    plan = ops.grouped_decode_plan(B, hkv, ctx_bound, ctx_bound)
     ws_p = torch.empty(max(1, ops.lib().qb_paged_decode_workspace_bytes(B, hq, D, ms) // 4), device=dev)
     ws_g = ops.grouped_workspace(B, hq, D, plan, dev)
+    # the cascade kernel on the plain layout (every sequence its own group, nothing shared)
+    mem_1 = torch.full((B, 8), -1, dtype=torch.int32, device=dev)
+    mem_1[:, 0] = torch.arange(B, dtype=torch.int32, device=dev)
+    zeros_b = torch.zeros(B, dtype=torch.int32, device=dev)
+    plan_1 = ops.grouped_decode_plan(B, hkv, 64, ctx_bound)
+    ws_1 = ops.grouped_workspace(B, hq, D, plan_1, dev)
     runs = {
         "plain": lambda: ops.paged_decode_attention(q, kc, vc, bt_plain, cl_plain, D ** -0.5, split_tokens=split,
                                                     max_splits=ms, workspace=ws_p),
         "grouped": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt, cl, D ** -0.5, mem_d, sl_d, ks_d, plan,
                                                               workspace=ws_g),
+        "cascade_unshared": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt_plain, cl_plain, D ** -0.5, mem_1,
+                                                                       zeros_b, zeros_b, plan_1, workspace=ws_1),
     }
     out = {}
     for name, fn in runs.items():
@@ -472,12 +482,14 @@ def run_rollout_attn():
         b.record()
         torch.cuda.synchronize()
         out[name] = a.elapsed_time(b) / 20
-    err = (runs["plain"]().float() - runs["grouped"]().float()).abs().max().item()
+    ref = runs["plain"]().float()
+    err = max((runs[k]().float() - ref).abs().max().item() for k in ("grouped", "cascade_unshared"))
     ops.check_device_errors()
     kv_plain = (sum(plain_lens) + B * gen) * hkv * D * 4
     kv_grouped = (sum(shared) + B * gen) * hkv * D * 4
     print(json.dumps({"rollout_attn": {"ms": out, "kv_bytes": {"plain": kv_plain, "grouped": kv_grouped},
                                        "gbs": {"plain": kv_plain / out["plain"] / 1e6,
+                                               "cascade_unshared": kv_plain / out["cascade_unshared"] / 1e6,
                                                "grouped_effective": kv_plain / out["grouped"] / 1e6,
                                                "grouped_actual": kv_grouped / out["grouped"] / 1e6},
                                        "plan": {"plain": [split, ms], "grouped": list(plan)},

@@ -320,7 +320,7 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 // a (sequence, kv head) merges all of its slots, found through a ticket counter that it resets
 // to zero.  No warp waits on another warp or CTA.
 //
-// Each warp streams its items' keys in 16-token stages through its own 3-slot ring: lane 0
+// Each warp streams its items' keys in 16-token stages through its own small ring: lane 0
 // issues two TMA box loads for K and two for V (16 tokens x 64 dims each, 128-byte swizzle)
 // plus, with an own item's first stage, one for its two query rows, all completing on the
 // slot's mbarrier.  The ring runs across item boundaries, so the next item's keys are in flight
@@ -331,9 +331,9 @@ constexpr int GMAX = 8;
 constexpr int WD_TOK = 16;                   // tokens per stage (one MMA M tile)
 constexpr int WD_SLOTS = 3;
 constexpr int WD_KV_BYTES = WD_TOK * ROWB;   // 4 KB of K (and of V) per stage: two 2 KB halves
-constexpr int WD_Q_OFF = WD_SLOTS * 2 * WD_KV_BYTES;       // 24 KB: query rows of own items
-constexpr int WD_BAR_OFF = WD_Q_OFF + WD_SLOTS * 2 * ROWB;  // + 3 x 512 B
-constexpr int WD_WARP_BYTES = 26 * 1024;     // 1024-aligned per-warp region
+constexpr int WD_Q_OFF = WD_SLOTS * 2 * WD_KV_BYTES;       // query rows of own items
+constexpr int WD_BAR_OFF = WD_Q_OFF + WD_SLOTS * 2 * ROWB;  // + 512 B per slot
+constexpr int WD_WARP_BYTES = (WD_BAR_OFF + WD_SLOTS * 8 + 1023) / 1024 * 1024;  // 1024-aligned
 constexpr int WD_WARPS = 8;                  // per CTA; one CTA per SM
 constexpr int WD_SMEM = WD_WARPS * WD_WARP_BYTES + 1024;  // + alignment slack
 static_assert(WD_BAR_OFF + WD_SLOTS * 8 <= WD_WARP_BYTES, "per-warp region");
@@ -493,28 +493,36 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
   __syncwarp();
 
   // ---- load cursor (state kept by every lane; lane 0 issues the copies)
-  int l_item = first, l_stage = 0, l_flat = 0, l_page = -1, l_page_col = -1;
+  // The next item's metadata and the next page id are read one step ahead so that their
+  // global-load latency never sits between two copies.
+  int l_item = first, l_stage = 0, l_flat = 0;
   Item l_it = decode_item(cp, l_item);
+  Item n_it = l_it;
+  if (l_item + total < cp.n_items) n_it = decode_item(cp, l_item + total);
+  auto page_at = [&](const Item& it, int col) { return col < p.bt_stride ? it.btrow[col] : -1; };
+  int l_col = l_it.tok_begin / PAGE;
+  int l_page = page_at(l_it, l_col), l_page_nx = page_at(l_it, l_col + 1);
   auto issue = [&]() {
     if (l_item < cp.n_items) {
       const int slot = l_flat % WD_SLOTS;
       const bool kv = l_stage < l_it.n_stages;
       const bool q = l_stage == 0 && !l_it.shared;
+      const int tok0 = l_it.tok_begin + l_stage * WD_TOK;
+      if (kv && tok0 / PAGE != l_col) {  // crossed into the next page: use the prefetched id
+        l_col = tok0 / PAGE;
+        l_page = l_page_nx;
+        l_page_nx = page_at(l_it, l_col + 1);
+      }
       if (lane == 0) {
         const uint32_t bar = bar_addr(slot);
         mbar_expect_tx(bar, (kv ? 2 * WD_KV_BYTES : 0) + (q ? 2 * ROWB : 0));
         if (kv) {
-          const int tok0 = l_it.tok_begin + l_stage * WD_TOK;
-          const int col = tok0 / PAGE;
-          if (col != l_page_col) {  // one page-table read per page (16 stages)
-            l_page_col = col;
-            l_page = col < p.bt_stride ? l_it.btrow[col] : -1;
-            if (l_page < 0 || l_page >= p.num_blocks) {
-              qb_set_err(p.err, QB_DEVERR_PAGE);  // read page 0 instead; the result is flagged
-              l_page = 0;
-            }
+          int page = l_page;
+          if (page < 0 || page >= p.num_blocks) {
+            qb_set_err(p.err, QB_DEVERR_PAGE);  // read page 0 instead; the result is flagged
+            page = 0;
           }
-          const int row = l_page * PAGE + tok0 % PAGE;
+          const int row = page * PAGE + tok0 % PAGE;
           const uint32_t kb = kv_addr(slot), vb = kb + WD_KV_BYTES;
           tma_load_3d(kb, &cp.tk, 0, l_it.kvh, row, bar);
           tma_load_3d(kb + 2048, &cp.tk, 64, l_it.kvh, row, bar);
@@ -525,9 +533,12 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
       }
       if (++l_stage >= max(1, l_it.n_stages)) {  // an empty item still takes one slot
         l_stage = 0;
-        l_page_col = -1;
         l_item += total;
-        if (l_item < cp.n_items) l_it = decode_item(cp, l_item);
+        l_it = n_it;
+        if (l_item + total < cp.n_items) n_it = decode_item(cp, l_item + total);
+        l_col = l_it.tok_begin / PAGE;
+        l_page = page_at(l_it, l_col);
+        l_page_nx = page_at(l_it, l_col + 1);
       }
       ++l_flat;  // counts armed slots only
     }
