@@ -58,6 +58,9 @@ def parse():
                     help="only plain vs grouped decode attention on a mid-rollout batch")
     ap.add_argument("--no-graphs", action="store_true",
                     help="eager decode launches (for launch-list profiling; ncu and graph replays do not mix)")
+    ap.add_argument("--kernel-profile", default=None, metavar="PATH",
+                    help="after the timed steps, run one more step under torch.profiler (CUPTI kernel records) and "
+                         "write per-kernel launches / device time / share to PATH")
     ap.add_argument("--no-share-prefix", action="store_true",
                     help="roll out with the reference's scheduler (every completion prefilled and stored)")
     return ap.parse_args()
@@ -333,6 +336,8 @@ def run_ours(args):
     sampler.start()
     ms, tokens, wall, launches, _, _, last = timed(args.steps, host_inputs=False)
     clocks = sampler.stop()
+    if args.kernel_profile and rank == 0:
+        kernel_profile(args, torch, lambda: step(0, make_prompts(args, rank, 200, dev)), args.kernel_profile)
     value = tokens / (ms / 1000.0)
     e2e = None
     if not args.no_e2e:
@@ -376,6 +381,38 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def kernel_profile(args, torch, run_step, path):
+    """One GRPO step under torch.profiler: every kernel's device time from CUPTI activity records
+    (graph replays included), summed per kernel name.  Not a timed number: it gives shares."""
+    from collections import Counter
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        out = run_step()
+        torch.cuda.synchronize()
+    tot, cnt = Counter(), Counter()
+    for e in prof.events():
+        if str(getattr(e, "device_type", "")).endswith("CUDA"):
+            name = e.name
+            for pre in ("void ", "(anonymous namespace)::", "<unnamed>::"):
+                name = name.replace(pre, "")
+            name = name.split("(")[0]
+            tot[name] += e.time_range.elapsed_us()
+            cnt[name] += 1
+    T = sum(tot.values()) or 1.0
+    lines = [f"# Kernel time of one GRPO step (CUPTI records via torch.profiler)", "",
+             f"Command: python bench.py --warmup {args.warmup} --steps {args.steps} --kernel-profile {path}"
+             + (" --no-graphs" if args.no_graphs else ""), "",
+             f"Workload: {WORKLOAD}.  Phases of this step (host wall clock): rollout {out['t_rollout']:.2f} s, "
+             f"ref log-probs {out['t_ref']:.2f} s, train {out['t_train']:.2f} s.", "",
+             f"Total kernel time {T / 1e3:.1f} ms over {sum(cnt.values())} kernel records.", "",
+             "| kernel | launches | total ms | share |", "|---|---|---|---|"]
+    for k, v in tot.most_common(40):
+        lines.append(f"| {k[:90]} | {cnt[k]} | {v / 1e3:.2f} | {100 * v / T:.1f}% |")
+    Path(path).parent.mkdir(parents=True, exist_ok=True)
+    Path(path).write_text("\n".join(lines) + "\n")
 
 
 def run_decode_only(batch):

@@ -205,9 +205,11 @@ int qb_logprob_bwd(void* logits, int64_t n, int64_t V, int64_t ld, const int64_t
  * softmax / multinomial / log_softmax.gather block of
  * generate_continuous_with_logprobs (qwen3_naive.py:1632-1650).
  *   x = float(logits)/temperature; top_k = 0 keeps all V entries, otherwise the k
- *   largest (ties broken toward the lower index); token ~ softmax(x over kept) by
- *   the Gumbel-max rule on a counter-based Philox4x32-10 stream keyed by
- *   (seed ^ rng_state[1], rng_state[0], row, column); logp = log_softmax(x over kept)[token].
+ *   largest (ties broken toward the lower index); token ~ softmax(x over kept) drawn from
+ *   a counter-based Philox4x32-10 stream keyed by (seed ^ rng_state[1], rng_state[0], row):
+ *   with every entry kept by inverse-CDF sampling on one 53-bit uniform per row, with top-k
+ *   by the Gumbel-max rule over the kept entries (noise per column);
+ *   logp = log_softmax(x over kept)[token].
  *   top_k = 1 is greedy argmax with logp = 0.  rng_state (nullable): device uint64[2]
  *   {counter, seed mix}, read at run time so a captured graph draws new noise per replay. */
 int qb_sample(const void* logits, int64_t n, int64_t V, int64_t ld, float temperature,

@@ -1,7 +1,8 @@
 // Sampling, token log-probabilities and the fused GRPO loss.
 //
-//   qb_sample        temperature / top-k / Gumbel-max sampling with the sampled
-//                    token's log-prob (qwen3_naive.py:1632-1650)
+//   qb_sample        temperature / top-k sampling (inverse CDF over the full row,
+//                    Gumbel-max over a top-k set) with the sampled token's log-prob
+//                    (qwen3_naive.py:1632-1650)
 //   qb_logprob_fwd   log_softmax + gather from bf16 logits (qwen3_grpo_train.py:48-52)
 //   qb_logprob_bwd   its gradient w.r.t. the logits, in place
 //   qb_grpo_*        advantages, clipped surrogate, k3 KL, masked token mean and
@@ -177,6 +178,58 @@ QB_DEVICE int block_excl_scan(int v, int* sh, int* total) {
   return before + x - v;
 }
 
+// Exclusive prefix sum over the block of a float; the block total goes to *total.
+template <int NT>
+QB_DEVICE float block_excl_scan_f(float v, float* sh, float* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) sh[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    float w = (lane < NT / 32) ? sh[lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < NT / 32) sh[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  const float before = (wid == 0) ? 0.f : sh[wid - 1];
+  *total = sh[NT / 32 - 1];
+  __syncthreads();
+  return before + x - v;
+}
+
+template <int NT>
+QB_DEVICE float block_max_f(float v, float* sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) sh[wid] = v;
+  __syncthreads();
+  float r = sh[0];
+#pragma unroll 1
+  for (int w = 1; w < NT / 32; ++w) r = fmaxf(r, sh[w]);
+  __syncthreads();
+  return r;
+}
+
+// Uniform in the open interval (0, 1) with 53 random bits, one per (row, stream position).
+QB_DEVICE double row_uniform(uint64_t seed, uint64_t offset, int64_t row) {
+  const U4 r = philox4x32_10(U4{0xFFFFFFFFu, (uint32_t)row, (uint32_t)offset, (uint32_t)(offset >> 32)},
+                             (uint32_t)seed, (uint32_t)(seed >> 32));
+  const uint64_t a = r.x >> 5, b = r.y >> 6;  // 27 + 26 bits
+  return ((double)(a * 67108864ull + b) + 0.5) * (1.0 / 9007199254740992.0);
+}
+
 // ---------------------------------------------------------------- sampling
 constexpr int SNT = 512;
 
@@ -192,7 +245,7 @@ struct SampleParams {
   int* err;
 };
 
-__global__ void __launch_bounds__(SNT) sample_kernel(SampleParams p) {
+__global__ void __launch_bounds__(SNT, 4) sample_kernel(SampleParams p) {
   __shared__ MS sh_ms[32];
   __shared__ AM sh_am[32];
   __shared__ int hist[256];
@@ -226,19 +279,93 @@ __global__ void __launch_bounds__(SNT) sample_kernel(SampleParams p) {
     return;
   }
 
+  const bool use_topk = k > 1 && k < p.V;
+  // --------------------------------------------------------- all V entries kept: inverse-CDF sampling
+  // The row is visited in a fixed order (thread t, then its vectors t, t + SNT, ... in turn, then
+  // the 8 entries of a vector).  One pass accumulates each thread's share of the softmax mass in
+  // the log2 domain (running max, one exp2 per entry); a block scan of the shares places the row's
+  // uniform draw u * S in one thread's range, and that thread walks its entries again to find the
+  // token whose cumulative mass first exceeds it.  One uniform per row; no per-entry noise.
+  if (!use_topk) {
+    __shared__ float sh_f[32];
+    __shared__ int sh_pick[2];
+    const float k2 = 1.4426950408889634f / p.temperature;  // x / T in log2 units = x * k2
+    float m = -INFINITY, sacc = 0.f;
+    for (int64_t v = threadIdx.x; v < nvec; v += SNT) {
+      const bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+      float x[8];
+      unpack8(r, x);
+      float mx = x[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) mx = fmaxf(mx, x[i]);
+      const float mn = fmaxf(m, mx * k2);
+      if (mn == -INFINITY) continue;
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc += exp2f(fmaf(x[i], k2, -mn));
+      sacc = sacc * exp2f(m - mn) + acc;
+      m = mn;
+    }
+    const float M = block_max_f<SNT>(m, sh_f);
+    const float w = (m == -INFINITY || M == -INFINITY) ? 0.f : sacc * exp2f(m - M);
+    float S = 0.f;
+    const float before = block_excl_scan_f<SNT>(w, sh_f, &S);
+    const float target = (float)(row_uniform(seed, off, row) * (double)S);
+    if (threadIdx.x == 0) {
+      sh_pick[0] = SNT;  // lowest thread whose range holds the target
+      sh_pick[1] = -1;   // highest thread with mass (rounding fallback)
+    }
+    __syncthreads();
+    if (w > 0.f) {
+      if (target >= before && target < before + w) atomicMin(&sh_pick[0], (int)threadIdx.x);
+      atomicMax(&sh_pick[1], (int)threadIdx.x);
+    }
+    __syncthreads();
+    const int t_pick = sh_pick[0] < SNT ? sh_pick[0] : sh_pick[1];
+    if ((int)threadIdx.x == t_pick) {
+      const float rem = target - before;
+      float acc = 0.f;
+      int64_t tok = -1, last = -1;
+      for (int64_t v = threadIdx.x; v < nvec && tok < 0; v += SNT) {
+        const bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+        float x[8];
+        unpack8(r, x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float e = exp2f(fmaf(x[i], k2, -M));
+          if (e > 0.f) last = v * 8 + i;
+          acc += e;
+          if (tok < 0 && e > 0.f && acc > rem) tok = v * 8 + i;
+        }
+      }
+      if (tok < 0) tok = last;  // the target fell past this thread's re-summed mass by rounding
+      p.tokens[row] = tok;
+      p.logp[row] = (fmaf(bf2f(lrow[tok]), k2, -M) - log2f(S)) * 0.6931471805599453f;
+    }
+    if (t_pick < 0 && threadIdx.x == 0) {  // no finite logit in the row
+      qb_set_err(p.err, QB_DEVERR_TOKEN);
+      p.tokens[row] = 0;
+      p.logp[row] = 0.f;
+    }
+    return;
+  }
+
   // --------------------------------------------------------- top-k threshold (radix select on bf16 keys)
   uint32_t thr_key = 0;  // keep keys > thr_key, plus the first need_eq keys == thr_key
   int need_eq = 0;
-  const bool use_topk = k > 1 && k < p.V;
-  if (use_topk) {
+  {
     for (int i = threadIdx.x; i < 256; i += SNT) hist[i] = 0;
     __syncthreads();
+    // logits of similar size share a high byte: lanes with equal bins add once (warp aggregated)
     for (int64_t v = threadIdx.x; v < nvec; v += SNT) {
       bf16x8 r = *reinterpret_cast<const bf16x8*>(lrow + v * 8);
+      const unsigned act = __activemask();
+      const int lane = threadIdx.x & 31;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        atomicAdd(&hist[bf16_key(r.u[i] & 0xFFFFu) >> 8], 1);
-        atomicAdd(&hist[bf16_key(r.u[i] >> 16) >> 8], 1);
+      for (int i = 0; i < 8; ++i) {
+        const int bin = (int)(bf16_key((i & 1) ? (r.u[i >> 1] >> 16) : (r.u[i >> 1] & 0xFFFFu)) >> 8);
+        const unsigned peers = __match_any_sync(act, bin);
+        if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
       }
     }
     __syncthreads();
@@ -304,6 +431,10 @@ __global__ void __launch_bounds__(SNT) sample_kernel(SampleParams p) {
       eq_carry += tot;
     }
     if (!live) continue;
+    bool any_kept = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) any_kept |= keys[i] >= thr_key;
+    if (!any_kept) continue;  // noise is drawn only where an entry survives the top-k filter
     float gn[8];
     gumbel8(seed, off, row, v * 8, gn);
 #pragma unroll
