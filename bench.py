@@ -536,7 +536,8 @@ def run_rollout_attn():
 GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
     "qkv_proj": (8192, 4096, 1024), "o_proj": (8192, 1024, 2048), "gate_up_proj": (8192, 6144, 1024),
     "down_proj": (8192, 1024, 3072), "lm_head": (4096, 151936, 1024), "qkv_decode512": (512, 4096, 1024),
-    "lm_head_decode512": (512, 151936, 1024),
+    "lm_head_decode512": (512, 151936, 1024), "o_decode512": (512, 1024, 2048), "down_decode512": (512, 1024, 3072),
+    "gate_up_decode512": (512, 6144, 1024),
 }
 
 

@@ -177,7 +177,8 @@ size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits)
  * partials (shared_splits + own_splits slots per sequence and head) are merged inside it.
  * workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D, shared_splits + own_splits)
  * bytes whose last batch*hq*4 bytes (merge tickets) are zero before the first call; every
- * call leaves them zero again. */
+ * call leaves them zero again.  The tickets' place depends on (batch, hq, slots): a workspace
+ * is reused only by calls of the same shape, and calls sharing one must not overlap. */
 int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
                                  int64_t num_blocks, int page_size, const int32_t* block_tables,
                                  int64_t bt_stride, const int32_t* seqlens, int seqlen_add,
