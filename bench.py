@@ -169,15 +169,16 @@ def decode_microbench(torch, ops, device, n_iter=20, batch=256):
     return ms, nbytes, int(ctx.sum())
 
 
-def profiled_traffic(n_ctx_tokens):
-    """DRAM bytes of one decode launch from the committed ncu summary (bytes per context token,
-    measured on a smaller case of the same kernel) scaled to ``n_ctx_tokens``; None if absent."""
+def profiled_traffic(profile, key, scale=1):
+    """DRAM bytes (read + write) of one launch from a committed ncu summary under profiles/: the
+    figure after ``key:`` times ``scale`` (per-token figures are scaled to the launch); None if
+    the summary is absent."""
     import re
-    f = ROOT / "profiles" / "paged_decode_kernel_config3.md"
+    f = ROOT / "profiles" / profile
     if not f.exists():
         return None
-    m = re.search(r"traffic_bytes_per_kv_token:\s*([0-9.]+)", f.read_text())
-    return float(m.group(1)) * n_ctx_tokens if m else None
+    m = re.search(key + r":\s*([0-9.]+)", f.read_text())
+    return float(m.group(1)) * scale if m else None
 
 
 def cpu_baseline_sample(steps=1, threads=None):
@@ -344,20 +345,36 @@ def run_ours(args):
         ems, etok, _, _, h2d, d2h, _ = timed(args.steps, host_inputs=True)
         e2e = {"value": etok / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.steps),
                "d2h_bytes_per_step": d2h // max(1, args.steps)}
-    # roofline of the dominant kernel (paged decode attention), config-3 shapes, timed alone
-    dec_ms, dec_bytes, dec_tokens = decode_microbench(torch, ops, dev)
+    # roofline of the dominant kernel: the cascade decode attention (30% of the step's kernel
+    # time), on the mid-rollout case, launches back to back between events on its stream
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
         peaks = json.loads(pk.read_text())
     hbm = peaks.get("hbm_gbs", 6650.0)
-    achieved = dec_bytes / (dec_ms / 1000.0) / 1e9
+    case = rollout_attn_case(torch, ops, dev)
+    cas_ms = time_launches(torch, case["runs"]["grouped"])
+    plain_ms = time_launches(torch, case["runs"]["plain"])
+    ops.check_device_errors()
+    achieved = case["alg_grouped"] / (cas_ms / 1000.0) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": profiled_traffic(dec_tokens), "kernel": "paged_decode_kernel",
-                "case": "config 3: batch 256, ctx U[1k,8k], 16q/8kv, d128; back-to-back launches, K/V >> L2",
-                "traffic_source": "profiles/paged_decode_kernel_config3.md (ncu, batch-64 case, scaled by tokens)",
-                "ms_per_launch": dec_ms, "algorithmic_bytes": dec_bytes,
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if pk.exists() else "fallback"}
+                "traffic": profiled_traffic("paged_decode_cascade_kernel_rollout.md", "traffic_bytes_per_launch"),
+                "kernel": "paged_decode_cascade_kernel",
+                "case": "mid-rollout: 64 groups x 8, prompt U[64,512] shared per group, 256 own tokens per "
+                        "completion, 16q/8kv, d128; back-to-back launches, K/V 4.7x L2",
+                "algorithmic_bytes": case["alg_grouped"], "ms_per_launch": cas_ms,
+                "traffic_source": "profiles/paged_decode_cascade_kernel_rollout.md (ncu, same case)",
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if pk.exists() else "fallback",
+                "vs_reference_layout": {"kernel": "paged_decode_kernel", "ms_per_launch": plain_ms,
+                                        "kv_bytes": case["kv_plain"],
+                                        "effective_gbs_of_cascade": case["kv_plain"] / (cas_ms / 1000.0) / 1e9}}
+    del case
+    # the plain paged decode kernel alone on config-3 shapes (long contexts)
+    dec_ms, dec_bytes, dec_tokens = decode_microbench(torch, ops, dev)
+    decode_plain = {"kernel": "paged_decode_kernel", "case": "config 3: batch 256, ctx U[1k,8k]",
+                    "ms_per_launch": dec_ms, "achieved_gbs": dec_bytes / (dec_ms / 1000.0) / 1e9,
+                    "traffic": profiled_traffic("paged_decode_kernel_config3.md", "traffic_bytes_per_kv_token",
+                                                dec_tokens)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sample, th = cpu_baseline_sample(1)
@@ -376,7 +393,7 @@ def run_ours(args):
                 "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"],
                              "rollout_detail": last.get("rollout_stats")},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
-                "cpu_baseline": cpu, "decode_attn_gbs": achieved}
+                "cpu_baseline": cpu, "decode_attn_plain": decode_plain}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -426,16 +443,12 @@ def run_decode_only(batch):
                       "achieved_gbs": nbytes / (ms / 1000) / 1e9}), flush=True)
 
 
-def run_rollout_attn():
+def rollout_attn_case(torch, ops, dev):
     """Decode attention mid-rollout (config 4 shapes): 64 groups x 8 completions, prompt U[64,512],
-    256 generated tokens each.  Plain paged decode (every completion reads its own copy of the
-    prompt K/V, the reference's layout) vs the grouped cascade (all prompt pages shared and read
-    once per group; generated tokens on the members' own pages).  Both read the same K/V values.
-    Prints ms and K/V bytes read."""
-    import torch
-
-    from qwen3_naive_inference_b200 import ops
-    dev = torch.device("cuda", 0)
+    256 generated tokens each.  Builds the K/V pool twice over the same values: the reference's
+    layout (every completion holds its own copy of the prompt K/V; plain paged decode) and the
+    grouped layout (prompt pages shared, own tokens on fresh pages; cascade kernel).  Returns the
+    launch closures and the K/V bytes each layout needs per launch."""
     g = torch.Generator().manual_seed(5)
     G, n_groups, gen, hq, hkv, D = 8, 64, 256, 16, 8, 128
     B = G * n_groups
@@ -507,31 +520,50 @@ def run_rollout_attn():
         "cascade_unshared": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt_plain, cl_plain, D ** -0.5, mem_1,
                                                                        zeros_b, zeros_b, plan_1, workspace=ws_1),
     }
-    out = {}
-    for name, fn in runs.items():
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(20):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        out[name] = a.elapsed_time(b) / 20
+    kv_plain = (sum(plain_lens) + B * gen) * hkv * D * 4
+    kv_grouped = (sum(shared) + B * gen) * hkv * D * 4
+    small = 2 * B * hq * D * 2 + bt.numel() * 4 + B * 4 * 2 + mem_d.numel() * 4  # q, out, tables
+    return {"runs": runs, "kv_plain": kv_plain, "kv_grouped": kv_grouped, "alg_grouped": kv_grouped + small,
+            "plan": {"plain": [split, ms], "grouped": list(plan)}, "own_tokens": B * gen,
+            "shared_tokens": sum(shared)}
+
+
+def time_launches(torch, fn, n=20):
+    """Mean ms of ``fn`` over n back-to-back launches between two events on the launching stream
+    (after 3 untimed ones).  The K/V read per launch is several times the 126 MB L2."""
+    for _ in range(3):
+        fn()
+    st = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(n):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
+def run_rollout_attn():
+    """Plain paged decode (reference layout) vs the cascade kernel (grouped layout) vs the cascade
+    kernel with nothing shared, on the mid-rollout case; prints ms and K/V bytes read."""
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    case = rollout_attn_case(torch, ops, dev)
+    runs = case["runs"]
+    out = {name: time_launches(torch, fn) for name, fn in runs.items()}
     ref = runs["plain"]().float()
     err = max((runs[k]().float() - ref).abs().max().item() for k in ("grouped", "cascade_unshared"))
     ops.check_device_errors()
-    kv_plain = (sum(plain_lens) + B * gen) * hkv * D * 4
-    kv_grouped = (sum(shared) + B * gen) * hkv * D * 4
+    kv_plain, kv_grouped = case["kv_plain"], case["kv_grouped"]
     print(json.dumps({"rollout_attn": {"ms": out, "kv_bytes": {"plain": kv_plain, "grouped": kv_grouped},
                                        "gbs": {"plain": kv_plain / out["plain"] / 1e6,
                                                "cascade_unshared": kv_plain / out["cascade_unshared"] / 1e6,
                                                "grouped_effective": kv_plain / out["grouped"] / 1e6,
                                                "grouped_actual": kv_grouped / out["grouped"] / 1e6},
-                                       "plan": {"plain": [split, ms], "grouped": list(plan)},
-                                       "max_abs_diff": err}}), flush=True)
-
+                                       "plan": case["plan"], "max_abs_diff": err}}), flush=True)
 
 GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
     "qkv_proj": (8192, 4096, 1024), "o_proj": (8192, 1024, 2048), "gate_up_proj": (8192, 6144, 1024),
