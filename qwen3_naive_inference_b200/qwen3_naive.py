@@ -567,6 +567,7 @@ class Qwen3ForCausalLM(nn.Module):
         self._graphs = {}
         self._has_cuda_graphs = False
         self.use_cuda_graphs = True  # decode steps replay captured graphs (False: eager launches)
+        self.pipeline_decode = True  # grouped rollout: submit decode step k+1 before step k's bookkeeping
         self.rollout_stats: dict = {}  # per generate call: steps, decode steps, host time waiting on the GPU
         self.max_model_len = None  # KV positions a sequence may reach; default = prompt + max_new_tokens
 
@@ -769,21 +770,26 @@ class Qwen3ForCausalLM(nn.Module):
         torch.cuda.synchronize()
         self._has_cuda_graphs = True
 
-    def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None):
+    def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None, arrays=None):
         """Fill the static inputs with one H2D copy, replay, return (tokens, logp) device views.
 
-        ``groups`` (grouped graphs): list of (member row indices, shared key count, first own key)."""
+        ``groups`` (grouped graphs): list of (member row indices, shared key count, first own key).
+        ``arrays``: (ids, positions, context_lens, block_tables, slots) already built for ``seqs``."""
         bs = len(seqs)
         gbs = _round_bs(bs, self._graph_bs)
-        if gbs is None:
+        if gbs is None or (arrays is not None and arrays[3].shape[1] > self._graph_max_blocks):
             return None
         hb = self._graph_host
-        ids, pos, ctx, bt, slots = self._decode_arrays(seqs, width=self._graph_max_blocks)
+        if arrays is None:
+            ids, pos, ctx, bt, slots = self._decode_arrays(seqs, width=self._graph_max_blocks)
+        else:
+            ids, pos, ctx, bt, slots = arrays
+            hb["block_tables"][:bs] = -1
         hb["input_ids"][:bs] = ids
         hb["positions"][:bs] = pos
         hb["context_lens"][:bs] = ctx
         hb["slot_mapping"][:bs] = slots
-        hb["block_tables"][:bs] = bt
+        hb["block_tables"][:bs, :bt.shape[1]] = bt
         if gbs > bs:  # padding rows: harmless length-1 attention on page 0, cache writes skipped
             hb["input_ids"][bs:gbs] = 0
             hb["positions"][bs:gbs] = 0
@@ -862,17 +868,7 @@ class Qwen3ForCausalLM(nn.Module):
             if self._has_cuda_graphs:
                 r = self._run_decode_graph(decode_rows, step, ctx["seed"], groups=groups_rows)
             if r is None:  # eager decode with the same cascade attention
-                ids, pos, cl, bt, slots = self._decode_arrays(decode_rows)
-                mem, sl, ks = _group_arrays(groups_rows, nd)
-                plan = ops.grouped_decode_plan(nd, a.num_kv_heads, int(sl.max(initial=0)),
-                                               int((cl + 1 - ks).max(initial=1)))
-                ids, pos, cl, bt, slots, mem_d, sl_d, ks_d = self._staging().put([ids, pos, cl, bt, slots, mem, sl, ks])
-                ws = ops.grouped_workspace(nd, a.num_heads, a.head_dim, plan, dev)
-                h = self.model.forward_decode(ids, pos, cl, bt, slots,
-                                              decode_plan=("grouped", plan, ws, mem_d, sl_d, ks_d))
-                logits = ops.linear(h, self.lm_head.weight)
-                ctx["rng"][0].fill_(step)
-                r = ops.sample(logits, temperature, top_k, 0, ctx["rng"])
+                r = self._grouped_decode_eager(ctx, self._decode_arrays(decode_rows), groups_rows, step)
         else:
             # prefill rows (the donors' prompt chunks) on the paged varlen kernel; decode rows,
             # whose keys skip the unused tail of the shared prompt page, on the cascade kernel
@@ -905,6 +901,65 @@ class Qwen3ForCausalLM(nn.Module):
         ctx["tok_host"][:n_samples].copy_(toks_dev, non_blocking=True)
         ctx["lp_host"][:n_samples].copy_(logp_dev, non_blocking=True)
         ctx["err_host"].copy_(ctx["err"], non_blocking=True)
+
+    def _grouped_decode_eager(self, ctx, arrays, groups_rows, step):
+        """One grouped decode step without graphs (cascade attention); returns (tokens, logp) on the device."""
+        dev = ctx["dev"]
+        a = self.model.layers[0].self_attn
+        ids, pos, cl, bt, slots = arrays
+        nd = len(ids)
+        mem, sl, ks = _group_arrays(groups_rows, nd)
+        plan = ops.grouped_decode_plan(nd, a.num_kv_heads, int(sl.max(initial=0)), int((cl + 1 - ks).max(initial=1)))
+        ids, pos, cl, bt, slots, mem_d, sl_d, ks_d = self._staging().put([ids, pos, cl, bt, slots, mem, sl, ks])
+        ws = ops.grouped_workspace(nd, a.num_heads, a.head_dim, plan, dev)
+        h = self.model.forward_decode(ids, pos, cl, bt, slots, decode_plan=("grouped", plan, ws, mem_d, sl_d, ks_d))
+        logits = ops.linear(h, self.lm_head.weight)
+        ctx["rng"][0].fill_(step)
+        return ops.sample(logits, ctx["temperature"], ctx["top_k"], 0, ctx["rng"])
+
+    # -- pipelined decode steps of the grouped rollout: the host submits step k+1 right after step k's
+    #    read-back and does step k's bookkeeping while step k+1 runs (_generate_grouped)
+    def _decode_step_arrays(self, rows):
+        """(positions, context_lens, block_tables, slots) of a decode step over ``rows``; a row's
+        position counts its tokens still in flight (``inflight`` submitted steps not yet read back)."""
+        BS = self.BLOCK_SIZE
+        n = len(rows)
+        pos = np.fromiter((len(s.token_ids) + s.inflight - 1 for s in rows), dtype=np.int64, count=n)
+        cl = np.fromiter((s.kv_len for s in rows), dtype=np.int32, count=n)
+        slots = np.fromiter((s.block_table[s.kv_len // BS] * BS + s.kv_len % BS for s in rows), dtype=np.int32,
+                            count=n)
+        return pos, cl, self._block_table_array(rows), slots
+
+    def _decode_submit(self, ctx, rows, groups_rows, step, ids, arrays):
+        """Enqueue one decode step over ``rows`` (input token ``ids``, metadata ``arrays`` from
+        _decode_step_arrays) and the read-back of its samples; returns a handle for _decode_collect."""
+        pos, cl, bt, slots = arrays
+        full = (ids, pos, cl, bt, slots)
+        r = None
+        if self._has_cuda_graphs:
+            r = self._run_decode_graph(rows, step, ctx["seed"], groups=groups_rows, arrays=full)
+        if r is None:
+            r = self._grouped_decode_eager(ctx, full, groups_rows, step)
+        n = len(rows)
+        toks_dev, logp_dev = r
+        ctx["tok_host"][:n].copy_(toks_dev, non_blocking=True)
+        ctx["lp_host"][:n].copy_(logp_dev, non_blocking=True)
+        ctx["err_host"].copy_(ctx["err"], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return {"n": n, "event": ev}
+
+    def _decode_collect(self, ctx, handle):
+        """Waits for a submitted step; returns its (tokens, log-probs) as numpy arrays."""
+        t0 = time.perf_counter()
+        handle["event"].synchronize()
+        st = self.rollout_stats
+        st["gpu_wait_s"] = st.get("gpu_wait_s", 0.0) + time.perf_counter() - t0
+        st["steps"] = st.get("steps", 0) + 1
+        if int(ctx["err_host"][0]):
+            ops.check_device_errors(ctx["dev"])
+        n = handle["n"]
+        return ctx["tok_host"][:n].numpy().copy(), ctx["lp_host"][:n].numpy().copy()
 
     @torch.no_grad()
     def generate_grouped_with_logprobs(self, prompt_ids_list, group_size, max_new_tokens=256, temperature=0.6,
@@ -1141,6 +1196,7 @@ class _Group:
             m.response_log_probs = []
             m.status = "WAITING"
             m.num_scheduled_tokens = 0
+            m.inflight = 0  # decode steps submitted for this member and not yet read back
 
     @property
     def n_shared(self):
@@ -1208,7 +1264,95 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
         running.remove(grp)
         waiting.appendleft(grp)
 
+    def accept(m, tok, lp):
+        m.append_token(tok)
+        if record_logprobs:
+            m.response_log_probs.append(lp)
+        if (eos is not None and tok in eos) or m.num_completion_tokens >= m.max_tokens:
+            m.status = "FINISHED"
+            bm.deallocate(m.block_table)
+            m.block_table = []
+
+    def groups_of(rows):
+        pos_of = {id(m): i for i, m in enumerate(rows)}
+        out = []  # (decode row indices, shared prompt keys, first own key) per group
+        for grp in running:
+            idx = [pos_of[id(m)] for m in grp.members if id(m) in pos_of]
+            if idx:
+                out.append((idx, grp.L, grp.own_start))
+        return out
+
+    # ---- pipelined decode: with no group waiting and every running group decoding, the rows of
+    # step k+1 are known before step k's tokens are (a member leaves only by EOS, found after
+    # the fact, or by its token budget, known ahead).  Step k+1 is planned while step k runs,
+    # submitted right after step k's read-back with step k's tokens as its inputs, and step k's
+    # bookkeeping runs while step k+1 is on the GPU.  A member that sampled EOS at step k has
+    # already been submitted for step k+1: that sample is discarded.  The rows' random draws
+    # are independent, so the others are unaffected; pages it still writes at step k+1 are
+    # freed on the host first but reused only by steps that run after it on the stream.
+    def plan_step(prev_rows=None):
+        """Rows, groups, metadata and, per row, its index in ``prev_rows`` (the step in flight,
+        whose samples are this step's inputs) of the next decode step; None when no row is left
+        or a page is missing (the synchronous loop then preempts)."""
+        rows = [m for g in running for m in g.members
+                if m.status == "RUNNING" and m.num_completion_tokens + m.inflight < m.max_tokens]
+        if not rows or len(rows) > model.MAX_TOKENS_PER_STEP:
+            return None
+        for m in rows:
+            if len(m.block_table) * BS <= m.kv_len:
+                if not bm.free:
+                    return None
+                m.block_table.append(bm._take_free())
+        src = None
+        if prev_rows is not None:
+            pos_of = {id(m): i for i, m in enumerate(prev_rows)}
+            src = np.fromiter((pos_of.get(id(m), -1) for m in rows), dtype=np.int64, count=len(rows))
+        return rows, groups_of(rows), model._decode_step_arrays(rows), src
+
+    def submit(plan, ids):
+        nonlocal step
+        rows, grows, arrays, _ = plan
+        step += 1
+        model.rollout_stats["decode_steps"] = model.rollout_stats.get("decode_steps", 0) + 1
+        h = model._decode_submit(ctx, rows, grows, step, ids, arrays)
+        for m in rows:
+            m.kv_len += 1
+            m.inflight += 1
+        return h
+
+    def run_pipelined():
+        plan = plan_step()
+        if plan is None:
+            return False
+        rows = plan[0]
+        h = submit(plan, np.fromiter((m.last_token for m in rows), dtype=np.int64, count=len(rows)))
+        while True:
+            nplan = plan_step(rows)  # overlaps the step in flight
+            toks, lps = model._decode_collect(ctx, h)
+            h_nxt = None
+            if nplan is not None:
+                src = nplan[3]
+                if (src >= 0).all():
+                    ids = toks[src]
+                else:
+                    ids = np.array([toks[j] if j >= 0 else m.last_token for j, m in zip(src, nplan[0])], dtype=np.int64)
+                h_nxt = submit(nplan, ids)
+            for j, m in enumerate(rows):  # overlaps the step just submitted
+                m.inflight -= 1
+                if m.status == "RUNNING":
+                    accept(m, int(toks[j]), float(lps[j]))
+            for g in list(running):
+                if all(m.status == "FINISHED" for m in g.members):
+                    g.state = "FINISHED"
+                    running.remove(g)
+            if h_nxt is None:
+                return True
+            rows, h = nplan[0], h_nxt
+
     while waiting or running:
+        if (getattr(model, "pipeline_decode", True) and not waiting and running
+                and all(g.state == "DECODE" for g in running) and run_pipelined()):
+            continue
         budget = model.MAX_TOKENS_PER_STEP
         decode_rows: list[Sequence] = []
         prefill: list[_Group] = []
@@ -1226,7 +1370,7 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
                         bm.deallocate(m.block_table)
                         m.block_table = []
                         continue
-                    if m.kv_len % BS == 0:
+                    if len(m.block_table) * BS <= m.kv_len:  # the next key needs a new page
                         while not bm.free:
                             victim = running[-1]
                             preempt(victim)
@@ -1286,12 +1430,7 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
         step += 1
         done = [g for g in prefill if g.donor.kv_len + g.donor.num_scheduled_tokens >= g.L]
         n_samples = len(decode_rows) + G * len(done)
-        groups_rows = []  # (decode row indices, shared prompt keys, first own key) per group
-        pos_of = {id(m): i for i, m in enumerate(decode_rows)}
-        for grp in running:
-            rows = [pos_of[id(m)] for m in grp.members if id(m) in pos_of]
-            if rows:
-                groups_rows.append((rows, grp.L, grp.own_start))
+        groups_rows = groups_of(decode_rows)
         if not prefill:
             model.rollout_stats["decode_steps"] = model.rollout_stats.get("decode_steps", 0) + 1
         model._grouped_launch(ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples)
@@ -1303,27 +1442,16 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
             m.num_scheduled_tokens = 0
         toks, lps = model._finish_step(ctx, None, n_samples, True)
         k = 0
-
-        def take(m):
-            nonlocal k
-            tok, lp = toks[k], lps[k]
-            k += 1
-            m.append_token(tok)
-            if record_logprobs:
-                m.response_log_probs.append(lp)
-            if (eos is not None and tok in eos) or m.num_completion_tokens >= m.max_tokens:
-                m.status = "FINISHED"
-                bm.deallocate(m.block_table)
-                m.block_table = []
-
         for g in done:
             g.state = "DECODE"
             for m in g.members:
                 m.kv_len = g.own_start  # next key goes to a fresh page
                 m.status = "RUNNING"
-                take(m)
+                accept(m, toks[k], lps[k])
+                k += 1
         for m in decode_rows:
-            take(m)
+            accept(m, toks[k], lps[k])
+            k += 1
         for g in list(running):
             if g.state == "DECODE" and all(m.status == "FINISHED" for m in g.members):
                 g.state = "FINISHED"
