@@ -58,6 +58,8 @@ def parse():
                     help="only plain vs grouped decode attention on a mid-rollout batch")
     ap.add_argument("--no-graphs", action="store_true",
                     help="eager decode launches (for launch-list profiling; ncu and graph replays do not mix)")
+    ap.add_argument("--attn-only", action="store_true",
+                    help="training attention forward + backward on one microbatch of the bench's sequences")
     ap.add_argument("--kernel-profile", default=None, metavar="PATH",
                     help="after the timed steps, run one more step under torch.profiler (CUPTI kernel records) and "
                          "write per-kernel launches / device time / share to PATH")
@@ -609,10 +611,47 @@ def run_gemm_only(shape=None):
     print(json.dumps({"gemm": out, "peak_tflops": peak}), flush=True)
 
 
+def run_attn_only():
+    """Packed causal attention of the training step (16 q / 8 kv heads, d128) on one 32k-token
+    microbatch of bench-shaped sequences (prompt U[64,512] + 512 completion tokens): forward and
+    backward timed with events, TFLOP/s from the causal FLOP count (fwd 4*H*D per (query, key)
+    pair, bwd 2.5x fwd)."""
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    from qwen3_naive_inference_b200.qwen3_naive import packed_meta
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(7)
+    lens = []
+    while sum(lens) < 32768 - 1024:
+        lens.append(int(torch.randint(64, 513, (1,), generator=g)) + 512)
+    hq, hkv, D = 16, 8, 128
+    T = sum(lens)
+    pos, cu, tiles = packed_meta(lens, dev)
+    qkv = (torch.randn(T, (hq + 2 * hkv) * D, device=dev) * 0.5).to(torch.bfloat16).requires_grad_(True)
+    pairs = sum(L * (L + 1) // 2 for L in lens)
+    fwd_flop = 4 * hq * D * pairs
+
+    def fwd():
+        return ops.attention_packed(qkv, cu, tiles, hq, hkv, D ** -0.5)
+
+    out = fwd()
+    dout = torch.randn_like(out)
+    ms_f = time_launches(torch, fwd, n=10)
+    o = fwd()
+    ms_fb = time_launches(torch, lambda: torch.autograd.grad(o, qkv, dout, retain_graph=True), n=10)
+    ops.check_device_errors()
+    print(json.dumps({"attn": {"tokens": T, "sequences": len(lens), "fwd_ms": ms_f, "bwd_ms": ms_fb,
+                               "fwd_tflops": fwd_flop / (ms_f / 1e3) / 1e12,
+                               "bwd_tflops": 2.5 * fwd_flop / (ms_fb / 1e3) / 1e12}}), flush=True)
+
+
 def main():
     args = parse()
     if args.rollout_attn:
         run_rollout_attn()
+    elif args.attn_only:
+        run_attn_only()
     elif args.gemm_only:
         run_gemm_only(args.gemm_shape)
     elif args.decode_only:
