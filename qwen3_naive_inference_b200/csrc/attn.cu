@@ -1085,9 +1085,13 @@ QB_DEVICE void load_tile64(uint32_t dst, const bf16* base, int64_t stride, int r
 }
 
 // CTA = (64-key tile, kv head), 4 warps x 16 keys.  Loops over the query tiles at
-// or after the key tile and over the hq/hkv query heads of the group.
-// Smem: K 16K, V 16K, Q 16K, dO 16K = 64 KB (single buffered).
-constexpr int BWD_SMEM = 4 * 64 * ROWB;
+// or after the key tile and over the hq/hkv query heads of the group, as one flat sequence
+// whose next (Q, dO, lse, delta) tile is copied in while the current one is used.
+// Smem: K 16K, V 16K, 2 x (Q 16K, dO 16K, lse 256 B, delta 256 B) = 97 KB.
+constexpr int DKDV_SMEM = 6 * 64 * ROWB + 2 * 2 * 64 * 4;
+// dQ: Q 16K, dO 16K, 2 x (K 16K, V 16K) = 96 KB; the next key tile is copied in while the
+// current one is used.
+constexpr int DQ_SMEM = 6 * 64 * ROWB;
 
 __global__ void __launch_bounds__(128)
 attn_bwd_dkdv_kernel(BwdParams p) {
@@ -1099,13 +1103,31 @@ attn_bwd_dkdv_kernel(BwdParams p) {
   const int base = p.cu[b], L = p.cu[b + 1] - base;
   if (k_start >= L) return;
   const int group = p.hq / p.hkv;
-  const uint32_t sK = smem_u32(smem), sV = sK + 64 * ROWB, sQ = sV + 64 * ROWB, sD = sQ + 64 * ROWB;
+  const uint32_t sK = smem_u32(smem), sV = sK + 64 * ROWB;
+  // buffer b: Q at sQb(b), dO 16 KB after it; lse and delta (64 fp32 each) at sLb(b)
+  auto sQb = [&](int buf) { return sV + 64 * ROWB + buf * 2 * 64 * ROWB; };
+  auto sLb = [&](int buf) { return sK + 6 * 64 * ROWB + buf * 2 * 64 * 4; };
+  const float* sLf = reinterpret_cast<const float*>(smem + 6 * 64 * ROWB);
   const int nk = min(64, L - k_start);
+  const int q0 = (k_start / 64) * 64;
+  const int nqt = (L - q0 + 63) / 64;  // query tiles per head
+  const int n_it = group * nqt;
+  auto load_it = [&](int it, int buf) {
+    const int h = kvh * group + it / nqt, q_start = q0 + (it % nqt) * 64;
+    const int nq = min(64, L - q_start);
+    load_tile64(sQb(buf), p.q, p.stride, base + q_start, nq, h * D, tid, 128);
+    load_tile64(sQb(buf) + 64 * ROWB, p.dout, p.o_stride, base + q_start, nq, h * D, tid, 128);
+    {  // lse (idx < 64) and delta (idx >= 64) of the tile's queries, zero past the sequence
+      const int which = tid >> 6, j = tid & 63;
+      const bool ok = j < nq;
+      const float* src = (which ? p.delta : p.lse) + (int64_t)h * p.total + base + q_start + (ok ? j : 0);
+      cp_async_4(sLb(buf) + which * 256 + j * 4, src, ok ? 4 : 0);
+    }
+  };
   load_tile64(sK, p.k, p.stride, base + k_start, nk, kvh * D, tid, 128);
   load_tile64(sV, p.v, p.stride, base + k_start, nk, kvh * D, tid, 128);
+  load_it(0, 0);
   cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
   float dk[16][4], dv[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -1113,16 +1135,16 @@ attn_bwd_dkdv_kernel(BwdParams p) {
     dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.f;
   }
   const int key_g = k_start + warp * 16 + g;  // key index of rows g / g+8 in this warp
-  for (int hh = 0; hh < group; ++hh) {
-    const int h = kvh * group + hh;
-    for (int q_start = (k_start / 64) * 64; q_start < L; q_start += 64) {
-      const int nq = min(64, L - q_start);
-      __syncthreads();
-      load_tile64(sQ, p.q, p.stride, base + q_start, nq, h * D, tid, 128);
-      load_tile64(sD, p.dout, p.o_stride, base + q_start, nq, h * D, tid, 128);
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
+  for (int it = 0; it < n_it; ++it) {
+    const int h = kvh * group + it / nqt, q_start = q0 + (it % nqt) * 64;
+    const int buf = it & 1;
+    if (it + 1 < n_it) load_it(it + 1, buf ^ 1);  // the buffer read in iteration it - 1
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t sQ = sQb(buf), sD = sQ + 64 * ROWB;
+    const float* sl = sLf + buf * 128;  // lse [0, 64), delta [64, 128)
+    {
       // S^T[16 keys x 64 q] = K Q^T ; dP^T = V dO^T
       float st[8][4], dpt[8][4];
 #pragma unroll
@@ -1160,9 +1182,8 @@ attn_bwd_dkdv_kernel(BwdParams p) {
           const int qi = qc + (e & 1);
           const int ki = key_g + ((e >> 1) << 3);
           const bool ok = qi < L && ki <= qi && ki < L;
-          const int64_t qrow = base + (qi < L ? qi : 0);
-          const float l = p.lse[(int64_t)h * p.total + qrow];
-          const float dl = p.delta[(int64_t)h * p.total + qrow];
+          const float l = sl[qi - q_start];
+          const float dl = sl[64 + qi - q_start];
           const float pe = ok ? exp2f(st[nt][e] * p.scale_log2 - l * LOG2E) : 0.f;
           pv[e] = pe;
           dsv[e] = pe * (dpt[nt][e] - dl);
@@ -1196,6 +1217,7 @@ attn_bwd_dkdv_kernel(BwdParams p) {
         }
       }
     }
+    __syncthreads();  // this buffer is refilled by the copy issued in iteration it + 1
   }
   // Store dK (times scale) and dV for rows < L.
 #pragma unroll
@@ -1224,21 +1246,22 @@ attn_bwd_dq_kernel(BwdParams p) {
   const int base = p.cu[b], L = p.cu[b + 1] - base;
   if (q_start >= L) return;
   const int kvh = h / (p.hq / p.hkv);
-  const uint32_t sQ = smem_u32(smem), sD = sQ + 64 * ROWB, sK = sD + 64 * ROWB, sV = sK + 64 * ROWB;
+  const uint32_t sQ = smem_u32(smem), sD = sQ + 64 * ROWB;
+  // key tile buffer b: K at sKb(b), V 16 KB after it
+  auto sKb = [&](int buf) { return sD + 64 * ROWB + buf * 2 * 64 * ROWB; };
   const int nq = min(64, L - q_start);
+  const int kend = min(L, q_start + 64);
+  const int n_kt = (kend + 63) / 64;
+  auto load_kv = [&](int kt, int buf) {
+    const int nk = min(64, L - kt * 64);
+    load_tile64(sKb(buf), p.k, p.stride, base + kt * 64, nk, kvh * D, tid, 128);
+    load_tile64(sKb(buf) + 64 * ROWB, p.v, p.stride, base + kt * 64, nk, kvh * D, tid, 128);
+  };
   load_tile64(sQ, p.q, p.stride, base + q_start, nq, h * D, tid, 128);
   load_tile64(sD, p.dout, p.o_stride, base + q_start, nq, h * D, tid, 128);
+  load_kv(0, 0);
   cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
   uint32_t qa[8][4], da[8][4];
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    ldmatrix_x4(sQ + swz128(warp * 16 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
-                qa[kk][3]);
-    ldmatrix_x4(sD + swz128(warp * 16 + (lane & 15), kk * 2 + (lane >> 4)), da[kk][0], da[kk][1], da[kk][2],
-                da[kk][3]);
-  }
   const int qg = q_start + warp * 16 + g;
   float lse_r[2], dl_r[2];
 #pragma unroll
@@ -1250,15 +1273,22 @@ attn_bwd_dq_kernel(BwdParams p) {
   float dq[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
-  const int kend = min(L, q_start + 64);
-  for (int k_start = 0; k_start < kend; k_start += 64) {
-    const int nk = min(64, L - k_start);
-    __syncthreads();
-    load_tile64(sK, p.k, p.stride, base + k_start, nk, kvh * D, tid, 128);
-    load_tile64(sV, p.v, p.stride, base + k_start, nk, kvh * D, tid, 128);
+  for (int kt = 0; kt < n_kt; ++kt) {
+    const int k_start = kt * 64;
+    if (kt + 1 < n_kt) load_kv(kt + 1, (kt + 1) & 1);  // the buffer read in iteration kt - 1
     cp_async_commit();
-    cp_async_wait<0>();
+    cp_async_wait<1>();
     __syncthreads();
+    if (kt == 0) {  // Q and dO fragments stay in registers for the whole key loop
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        ldmatrix_x4(sQ + swz128(warp * 16 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
+                    qa[kk][3]);
+        ldmatrix_x4(sD + swz128(warp * 16 + (lane & 15), kk * 2 + (lane >> 4)), da[kk][0], da[kk][1], da[kk][2],
+                    da[kk][3]);
+      }
+    }
+    const uint32_t sK = sKb(kt & 1), sV = sK + 64 * ROWB;
     float s[8][4], dp[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -1314,6 +1344,7 @@ attn_bwd_dq_kernel(BwdParams p) {
         mma_bf16_16816(dq[2 * dpi + 1], dsa[ks], r2, r3);
       }
     }
+    __syncthreads();  // this buffer is refilled by the copy issued in iteration kt + 1
   }
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -1527,13 +1558,13 @@ extern "C" int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, i
   if (st != QB_OK) return st;
   static bool set = false;
   if (!set) {
-    cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
+    cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DKDV_SMEM);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM);
     set = true;
   }
-  attn_bwd_dkdv_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), 128, BWD_SMEM, (cudaStream_t)stream>>>(p);
+  attn_bwd_dkdv_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), 128, DKDV_SMEM, (cudaStream_t)stream>>>(p);
   st = qb_launch_status();
   if (st != QB_OK) return st;
-  attn_bwd_dq_kernel<<<dim3((unsigned)n_tiles, (unsigned)hq), 128, BWD_SMEM, (cudaStream_t)stream>>>(p);
+  attn_bwd_dq_kernel<<<dim3((unsigned)n_tiles, (unsigned)hq), 128, DQ_SMEM, (cudaStream_t)stream>>>(p);
   return qb_launch_status();
 }

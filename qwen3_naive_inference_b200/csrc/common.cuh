@@ -90,6 +90,10 @@ QB_DEVICE uint32_t smem_u32(const void* p) {
 QB_DEVICE void cp_async_16(uint32_t dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
 }
+// 4-byte copy (zero-filled when src_bytes == 0); no 16-byte alignment needed.
+QB_DEVICE void cp_async_4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
 QB_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 QB_DEVICE void cp_async_wait() {
