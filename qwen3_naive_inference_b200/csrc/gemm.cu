@@ -11,6 +11,9 @@
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator (each warp owns 32 TMEM lanes =
 //              32 rows), conversion and global stores, then release of the buffer so
 //              the next tile's MMAs overlap this tile's stores.
+// Products whose 256x256 tiles fill every SM pair run on gemm_pair_kernel instead: a cluster
+// of two CTAs issues tcgen05.mma.cta_group::2 (M = 256, N = 256), each CTA loading half of the
+// operands (see its comment).
 // Every mbarrier wait is bounded: on timeout the kernel raises QB_DEVERR_TIMEOUT, all
 // roles leave their loops, the producer waits (bounded) for its own copies, TMEM is
 // freed and the kernel returns.  Each CTA issues its own TMA loads from this GPU's memory.
@@ -88,6 +91,49 @@ struct GemmParams {
   int vec_ok;  // every output row starts on a 16-byte boundary: 16-byte stores allowed
   int* err;
 };
+
+// One epilogue thread's 32 consecutive fp32 accumulator columns of output row `row`, starting
+// at column `col` (< N): bf16 store, fp32 store or fp32 accumulate by MODE.
+template <int MODE>
+QB_DEVICE void store_row32(const GemmParams& p, int row, int col, const uint32_t (&r)[32]) {
+    const bool full = col + 32 <= p.N && p.vec_ok;
+    if (MODE == 0) {
+      bf16* dst = reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col;
+      if (full) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+          v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+          v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+          v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+          reinterpret_cast<uint4*>(dst)[q] = v;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col + i < p.N) dst[i] = f2bf(__uint_as_float(r[i]));
+      }
+    } else {
+      float* dst = reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc + col;
+      if (full) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          if (MODE == 2) {
+            const float4 o = reinterpret_cast<const float4*>(dst)[q];
+            v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+          }
+          reinterpret_cast<float4*>(dst)[q] = v;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col + i < p.N) dst[i] = (MODE == 2 ? dst[i] : 0.f) + __uint_as_float(r[i]);
+      }
+    }
+}
 
 template <int BN, int STAGES, int MODE, bool A_MN, bool B_MN>
 struct GemmCfg {
@@ -231,43 +277,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN + c, r);
         const int col = n0 + c;
         if (!row_ok || col >= p.N) continue;
-        const bool full = col + 32 <= p.N && p.vec_ok;
-        if (MODE == 0) {
-          bf16* dst = reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col;
-          if (full) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-              v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-              v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-              v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-              reinterpret_cast<uint4*>(dst)[q] = v;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col + i < p.N) dst[i] = f2bf(__uint_as_float(r[i]));
-          }
-        } else {
-          float* dst = reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc + col;
-          if (full) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                     __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-              if (MODE == 2) {
-                const float4 o = reinterpret_cast<const float4*>(dst)[q];
-                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-              }
-              reinterpret_cast<float4*>(dst)[q] = v;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col + i < p.N) dst[i] = (MODE == 2 ? dst[i] : 0.f) + __uint_as_float(r[i]);
-          }
-        }
+        store_row32<MODE>(p, row, col, r);
       }
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));  // accumulator free for the tile after next
@@ -279,6 +289,235 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------- CTA-pair kernel (cta_group::2)
+// A cluster of two CTAs on two SMs computes a 256 x 256 tile.  Per 64-deep K block each CTA
+// loads its own 128 rows of A and its own 128-row half of B (N) -- 32 KB -- into its ring,
+// signalling the stage barrier of the even CTA (the leader), whose one thread issues
+// tcgen05.mma.cta_group::2 (M = 256, N = 256) reading both CTAs' stages; each CTA's TMEM receives
+// its 128 rows of the accumulator (double-buffered, 2 x 256 columns).  Each SM pulls 32 KB per
+// 0.5 us of MMA work instead of the 48 KB of a 128 x 256 tile, and 6 stages fit, so the ring
+// covers the operands' latency.  The leader's commits release both CTAs' stages and
+// accumulators (one commit per CTA's barrier); each CTA's epilogue drains its own TMEM rows and
+// tells the leader through a remote arrive.  Every wait is bounded; each CTA loads from this
+// GPU's memory only.
+constexpr int P_STAGES = 6;
+constexpr int P_HALF_BYTES = 128 * BK * 2;             // 16 KB: 128 rows x 64 K of A, or of B
+constexpr int P_STAGE_BYTES = 2 * P_HALF_BYTES;        // this CTA's A rows + B half
+constexpr int P_TMEM_COLS = 512;                       // 2 accumulators x 256 columns
+constexpr int P_SMEM = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+template <bool A_MN, bool B_MN>
+struct PairCfg {
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                                    ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(256 >> 3) << 17) |
+                                    ((uint32_t)(256 >> 4) << 24);
+};
+
+QB_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory byte in CTA `rank` of the cluster.
+QB_DEVICE uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+QB_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrivals on a barrier of either CTA of the pair, with the default (CTA-scope release)
+// semantics: the data they guard arrives by TMA transaction counts or is TMEM read back with
+// tcgen05.wait, so no cluster-wide fence is needed (one would stall the producer on its own
+// copies in flight).
+QB_DEVICE void mbar_expect_tx_remote(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+QB_DEVICE void mbar_arrive_remote(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Bounded wait on a barrier of this CTA that the other CTA of the pair may signal.
+QB_DEVICE bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 255) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > WAIT_CYCLES) break;
+    }
+  }
+  *abort_flag = 1;
+  qb_set_err(err, QB_DEVERR_TIMEOUT);
+  return false;
+}
+// TMA load into this CTA's shared memory whose completion is counted on a barrier of either CTA
+// of the pair; each CTA fetches only its own half of the operands.
+QB_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+template <bool MN_MAJOR>
+QB_DEVICE void load_half(uint32_t dst, const CUtensorMap* map, int k0, int mn0, uint32_t bar) {
+  if (MN_MAJOR) {
+    tma_load_2d_pair(dst, map, mn0, k0, bar);
+    tma_load_2d_pair(dst + 64 * 128, map, mn0 + 64, k0, bar);
+  } else {
+    tma_load_2d_pair(dst, map, k0, mn0, bar);
+  }
+}
+QB_DEVICE void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Arrive (once) on a barrier of either CTA when the pair's prior MMAs have completed.
+QB_DEVICE void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+template <int MODE, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;  // the same offset in both CTAs of the pair
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + P_STAGES * P_STAGE_BYTES;
+  // full[S] (leader: one expect_tx arrive per CTA), empty[S], tfull[2], tempty[2] (leader: 256
+  // epilogue threads of both CTAs), done, then tmem base and abort flag
+  auto full_bar = [&](int s) { return bar0 + 8 * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8 * (P_STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8 * (2 * P_STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8 * (2 * P_STAGES + 2 + a); };
+  const uint32_t done_bar = bar0 + 8 * (2 * P_STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + P_STAGES * P_STAGE_BYTES + 8 * (2 * P_STAGES + 5));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank(), peer = rank ^ 1;
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int tiles_m = (p.M + 255) / 256, tiles_n = (p.N + 255) / 256;
+  const int n_tiles = tiles_m * tiles_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(full_bar(s), 2);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 2 * 4 * 32);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+  }
+  if (warp == 1) {  // both CTAs of the pair allocate together
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(P_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers and TMEM of both CTAs exist before either uses the other's
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer (each CTA)
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * 256 + (int)rank * 128;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
+        const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
+        const uint32_t lf = cluster_addr(full_bar(stage), 0);
+        mbar_expect_tx_remote(lf, P_STAGE_BYTES);
+        load_half<A_MN>(sa, &tmap_a, kb * BK, m0, lf);
+        load_half<B_MN>(sb, &tmap_b, kb * BK, n0, lf);
+        if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+      if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1, abort_flag, p.err)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + acc * 256;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait_cluster(full_bar(stage), phase, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
+#pragma unroll
+        for (int j = 0; j < BK / 16; ++j)
+          umma_pair(d, operand_desc<A_MN>(sa, j), operand_desc<B_MN>(sb, j), PairCfg<A_MN, B_MN>::IDESC,
+                    (kb | j) != 0);
+        umma_commit_pair(empty_bar(stage));  // both CTAs' stage is free once these MMAs read it
+        umma_commit_pair(cluster_addr(empty_bar(stage), peer));
+        if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      umma_commit_pair(tfull_bar(acc));  // both CTAs' accumulator rows are complete
+      umma_commit_pair(cluster_addr(tfull_bar(acc), peer));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    umma_commit_pair(done_bar);
+    mbar_drain(done_bar, 0);
+    if (*abort_flag) {  // copies the producers may still have in flight land before the CTAs leave
+      for (int s = 0; s < P_STAGES; ++s) mbar_drain(full_bar(s), s < stage ? phase ^ 1 : phase);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue (each CTA, its 128 rows)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t leader_tempty0 = cluster_addr(tempty_bar(0), 0), leader_tempty1 = cluster_addr(tempty_bar(1), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * 256;
+      if (!mbar_wait_cluster(tfull_bar(acc), acc_phase, abort_flag, p.err)) break;
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < 256; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * 256 + c, r);
+        const int col = n0 + c;
+        if (!row_ok || col >= p.N) continue;
+        store_row32<MODE>(p, row, col, r);
+      }
+      tc_fence_before();
+      mbar_arrive_remote(acc == 0 ? leader_tempty0 : leader_tempty1);  // the leader may reuse it
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still signal its barriers or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P_TMEM_COLS));
   }
 }
 
@@ -332,6 +571,40 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStrea
   return qb_launch_status();
 }
 
+template <int MODE, bool A_MN, bool B_MN>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  auto kern = gemm_pair_kernel<MODE, A_MN, B_MN>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM) != cudaSuccess)
+      return qb_launch_status();
+    attr = true;
+  }
+  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = P_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return qb_launch_status();
+  return qb_launch_status();
+}
+
+template <bool A_MN, bool B_MN>
+int launch_pair_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  if (mode == 0) return launch_pair<0, A_MN, B_MN>(ta, tb, p, st);
+  if (mode == 1) return launch_pair<1, A_MN, B_MN>(ta, tb, p, st);
+  return launch_pair<2, A_MN, B_MN>(ta, tb, p, st);
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 int launch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
   if (mode == 0) return launch<BN, STAGES, 0, A_MN, B_MN>(ta, tb, p, st);
@@ -363,7 +636,18 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   // skinny decode-step products)
   const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
   const bool wide = N >= 256 && tiles256 >= sm_count();
+  // 256x256 tiles on CTA pairs when they fill every SM pair at least once
+  const bool pair = N >= 256 && M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sm_count() / 2;
   CUtensorMap ta, tb;
+  if (pair) {
+    if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
+    if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128)) return QB_ERR_INVALID;
+    GemmParams pp{C, ldc, (int)M, (int)N, (int)K, 0, 0, vec_ok, err};
+    if (!a_mn && !b_mn) return launch_pair_mode<false, false>(mode, ta, tb, pp, st);
+    if (!a_mn && b_mn) return launch_pair_mode<false, true>(mode, ta, tb, pp, st);
+    if (a_mn && !b_mn) return launch_pair_mode<true, false>(mode, ta, tb, pp, st);
+    return launch_pair_mode<true, true>(mode, ta, tb, pp, st);
+  }
   if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
   if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;
   GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), (int)((N + (wide ? 255 : 127)) / (wide ? 256 : 128)),

@@ -17,7 +17,9 @@ def ref(a, b):
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 128, 64), (7, 300, 128), (300, 1000, 1024),
                                    (512, 4096, 1024), (257, 6144, 1024), (513, 1024, 3072), (64, 151936, 1024),
-                                   (1000, 2048, 4096)])
+                                   (1000, 2048, 4096),
+                                   # 256x256 tiles on CTA pairs (>= one tile per SM pair), with M/N/K tails
+                                   (2048, 2560, 512), (2000, 2600, 648), (8192, 6144, 1024)])
 def test_gemm_bf16_out(cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M * 7 + N)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -30,8 +32,8 @@ def test_gemm_bf16_out(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("mode", [1, 2])
-def test_gemm_fp32_out_and_accumulate(cuda, mode):
-    M, N, K = 200, 384, 512
+@pytest.mark.parametrize("M,N,K", [(200, 384, 512), (2000, 2600, 648)])
+def test_gemm_fp32_out_and_accumulate(cuda, mode, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(mode)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
     b = torch.randn(N, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -64,7 +66,8 @@ def test_gemm_repeated_calls_stable(cuda):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 1024, 776), (1000, 384, 4096), (64, 151936, 200)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 1024, 776), (1000, 384, 4096), (64, 151936, 200),
+                                   (2048, 2560, 512), (2000, 2600, 648)])
 def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
     """Backward layouts: A stored [K, M] and/or B stored [K, N]; K need not be a multiple of 64
     (row pitches stay multiples of 8 elements, the TMA rule)."""
