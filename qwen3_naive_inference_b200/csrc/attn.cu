@@ -546,7 +546,16 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
 #pragma unroll
   for (int s = 0; s < WD_SLOTS - 1; ++s) issue();
 
-  int f = 0;  // flat index of the stage being consumed
+  int f = 0;                  // flat index of the stage being consumed
+  int f_slot = 0;             // its ring slot (f % WD_SLOTS)
+  uint32_t f_par = 0;         // its mbarrier phase parity ((f / WD_SLOTS) & 1)
+  auto next_stage = [&]() {
+    ++f;
+    if (++f_slot == WD_SLOTS) {
+      f_slot = 0;
+      f_par ^= 1;
+    }
+  };
   bool ok = true;
   for (int k = 0; ok; ++k) {
     if (first + k * total >= cp.n_items) break;
@@ -573,10 +582,10 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
           qa[kk][3] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
         }
       }
-      for (int s = 0; s < ns; ++s, ++f) {
+      for (int s = 0; s < ns; ++s, next_stage()) {
         issue();
-        const int slot = f % WD_SLOTS;
-        if (!slot_wait(bar_addr(slot), (f / WD_SLOTS) & 1, p.err)) {
+        const int slot = f_slot;
+        if (!slot_wait(bar_addr(slot), f_par, p.err)) {
           ok = false;
           break;
         }
@@ -639,12 +648,14 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
             rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
             l_run[r] = l_run[r] * alpha[r] + rs[r];
           }
+          if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {  // a row's max moved
 #pragma unroll
-          for (int dt = 0; dt < 16; ++dt) {
-            o[dt][0] *= alpha[0];
-            o[dt][1] *= alpha[0];
-            o[dt][2] *= alpha[1];
-            o[dt][3] *= alpha[1];
+            for (int dt = 0; dt < 16; ++dt) {
+              o[dt][0] *= alpha[0];
+              o[dt][1] *= alpha[0];
+              o[dt][2] *= alpha[1];
+              o[dt][3] *= alpha[1];
+            }
           }
           // O[16 x 128] += P[16 x 16 tok] V[16 tok x 128]
 #pragma unroll
@@ -681,10 +692,10 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
       uint32_t qb[8][2];
-      for (int s = 0; s < ns; ++s, ++f) {
+      for (int s = 0; s < ns; ++s, next_stage()) {
         issue();
-        const int slot = f % WD_SLOTS;
-        if (!slot_wait(bar_addr(slot), (f / WD_SLOTS) & 1, p.err)) {
+        const int slot = f_slot;
+        if (!slot_wait(bar_addr(slot), f_par, p.err)) {
           ok = false;
           break;
         }
@@ -755,12 +766,14 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
             l_run[h] = l_run[h] * alpha[h] + lsum[h];
             m_run[h] = mnew[h];
           }
+          if (alpha[0] != 1.f || alpha[1] != 1.f) {  // warp-uniform: the running max moved
 #pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            o[mt][0] *= alpha[0];
-            o[mt][1] *= alpha[1];
-            o[mt][2] *= alpha[0];
-            o[mt][3] *= alpha[1];
+            for (int mt = 0; mt < 8; ++mt) {
+              o[mt][0] *= alpha[0];
+              o[mt][1] *= alpha[1];
+              o[mt][2] *= alpha[0];
+              o[mt][3] *= alpha[1];
+            }
           }
           // P^T as the B operand: lane (g, t4) needs P[tok 2t4, 2t4+1, 2t4+8, 2t4+9][head g].
           const int srcA = 8 * t4, srcB = 8 * t4 + 4;
@@ -807,8 +820,8 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
   }
   // Drain: the copies of every slot issued but not consumed complete before the warp leaves
   // (bounded waits; after a timeout they are the copies that did not arrive in time).
-  for (; f < l_flat; ++f) {
-    const uint32_t bar = bar_addr(f % WD_SLOTS), parity = (f / WD_SLOTS) & 1;
+  for (; f < l_flat; next_stage()) {
+    const uint32_t bar = bar_addr(f_slot), parity = f_par;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity))
       if (clock64() - t0 > WAIT_CYCLES) break;
