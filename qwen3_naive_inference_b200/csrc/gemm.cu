@@ -140,7 +140,8 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator (power of two)
+  static constexpr int ACC_STRIDE = BN <= 128 ? BN : 256;  // TMEM columns between the two accumulators
+  static constexpr int TMEM_COLS = 2 * ACC_STRIDE;          // double-buffered (power of two)
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static constexpr uint32_t IDESC = (1u << 4)            // D fp32
                                     | (1u << 7)          // A bf16
@@ -239,7 +240,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
       if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1, abort_flag, p.err)) break;
       tc_fence_after();
-      const uint32_t d = tmem + acc * BN;
+      const uint32_t d = tmem + acc * Cfg::ACC_STRIDE;
       bool ok = true;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) { ok = false; break; }
@@ -274,7 +275,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * BN + c, r);
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE + c, r);
         const int col = n0 + c;
         if (!row_ok || col >= p.N) continue;
         store_row32<MODE>(p, row, col, r);
@@ -521,6 +522,208 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   }
 }
 
+// ---------------------------------------------------------------- split-K clusters
+// Skinny products with few output tiles and a long K (the decode step's o_proj and down_proj at
+// M = 512: 32 tiles of 128 x 128 over K = 2048 / 3072) leave most SMs idle, and each busy SM
+// pulls the whole K extent of its tile through its own port.  A cluster of S CTAs computes one
+// 128 x 128 tile instead, CTA r over K blocks [r*KB/S, (r+1)*KB/S), so S SMs share the tile's
+// loads.  The fp32 partials are summed in distributed shared memory: the tile's 128 rows are cut
+// into S slices, CTA j owns slice j, and every other CTA pushes its partial rows of slice j into
+// a receive buffer of CTA j with st.async, counted in bytes on CTA j's receive barrier; the
+// owner's epilogue warps add them to their own accumulator rows and store the result (any MODE).
+// One tile per cluster and one cluster per S SMs at most: the host launches this only when every
+// cluster is resident at once.  Every wait is bounded; each CTA loads from this GPU's memory.
+constexpr int S_STAGES = 4;
+constexpr int S_BN = 128;
+constexpr int S_STAGE_BYTES = (BM + S_BN) * BK * 2;  // 32 KB
+constexpr int S_ROW = S_BN + 4;  // receive-buffer row pitch in floats: 16-byte pad, conflict-free v4 reads
+
+template <int S>
+struct SplitCfg {
+  static constexpr int SLICE_ROWS = BM / S;                             // rows each CTA finishes
+  static constexpr int RECV_BYTES = (S - 1) * SLICE_ROWS * S_ROW * 4;   // one slot per other CTA
+  static constexpr uint32_t RECV_TX = (S - 1) * SLICE_ROWS * S_BN * 4;  // bytes pushed to each owner
+  static constexpr int SMEM = S_STAGES * S_STAGE_BYTES + RECV_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// Stores four fp32 words into another CTA's shared memory; the bytes count on that CTA's barrier.
+QB_DEVICE void st_async_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"(bar)
+               : "memory");
+}
+
+// Bounded wait for the partial rows the other CTAs pushed (cluster-scope acquire: the bytes were
+// written by other CTAs' st.async).
+QB_DEVICE bool recv_wait(uint32_t bar, volatile int* abort_flag, int* err) {
+  const long long t0 = clock64();
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255) == 255) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > WAIT_CYCLES) break;
+    }
+  }
+  *abort_flag = 1;
+  qb_set_err(err, QB_DEVERR_TIMEOUT);
+  return false;
+}
+
+template <int S, int MODE, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_split_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                  GemmParams p) {
+  using Cfg = GemmCfg<S_BN, S_STAGES, MODE, A_MN, B_MN>;
+  using Sc = SplitCfg<S>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;  // the same offset in every CTA of the cluster
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t recv = base + S_STAGES * S_STAGE_BYTES;
+  const uint32_t bar0 = recv + Sc::RECV_BYTES;
+  // barrier block: full[S_STAGES], empty[S_STAGES], tfull, recv, done, then tmem base and abort flag
+  auto full_bar = [&](int s) { return bar0 + 8 * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8 * (S_STAGES + s); };
+  const uint32_t tfull_bar = bar0 + 8 * (2 * S_STAGES);
+  const uint32_t recv_bar = tfull_bar + 8;
+  const uint32_t done_bar = recv_bar + 8;
+  const int bar_off = S_STAGES * S_STAGE_BYTES + Sc::RECV_BYTES + 8 * (2 * S_STAGES + 3);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + bar_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)cluster_rank();
+  const int tile = blockIdx.x / S;
+  const int m0 = (tile % p.tiles_m) * BM, n0 = (tile / p.tiles_m) * S_BN;
+  const int kblocks = (p.K + BK - 1) / BK;  // >= S (host check): every CTA gets a K block
+  const int kb0 = rank * kblocks / S, kb1 = (rank + 1) * kblocks / S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S_STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(recv_bar, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // the receive phase completes once the other CTAs' partial rows have all landed
+    mbar_expect_tx(recv_bar, Sc::RECV_TX);
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(S_BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();  // every CTA's receive barrier exists before any CTA pushes into it
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0, last_parity = 0;
+    for (int kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
+      if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
+      const uint32_t sa = base + stage * S_STAGE_BYTES, sb = sa + BM * BK * 2;
+      mbar_expect_tx(full_bar(stage), S_STAGE_BYTES);
+      load_operand<A_MN, BM>(sa, &tmap_a, kb * BK, m0, full_bar(stage));
+      load_operand<B_MN, S_BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
+      issued |= 1u << stage;
+      last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+      if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
+    }
+    for (int s = 0; s < S_STAGES; ++s)
+      if (issued & (1u << s)) mbar_drain(full_bar(s), (last_parity >> s) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int kb = kb0; kb < kb1; ++kb) {
+      if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sa = base + stage * S_STAGE_BYTES, sb = sa + BM * BK * 2;
+#pragma unroll
+      for (int j = 0; j < BK / 16; ++j)
+        umma_bf16(tmem, operand_desc<A_MN>(sa, j), operand_desc<B_MN>(sb, j), Cfg::IDESC, ((kb - kb0) | j) != 0);
+      umma_commit(empty_bar(stage));
+      if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
+    }
+    if (ok) umma_commit(tfull_bar);
+    umma_commit(done_bar);
+    mbar_drain(done_bar, 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue: push or reduce
+    const int quarter = warp & 3;                   // TMEM lanes [32*quarter, 32*quarter+32)
+    const int owner = quarter / (4 / S);            // CTA that finishes these 32 rows
+    const int slice_row = (quarter % (4 / S)) * 32 + lane;  // row within the owner's slice
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    if (mbar_wait(tfull_bar, 0, abort_flag, p.err)) {
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin
+      tc_fence_after();
+      if (owner != rank) {
+        const int slot = (rank - owner - 1 + S) % S;  // this CTA's slot in the owner's buffer
+        const uint32_t dst = cluster_addr(recv + (uint32_t)((slot * Sc::SLICE_ROWS + slice_row) * S_ROW * 4),
+                                          (uint32_t)owner);
+        const uint32_t rbar = cluster_addr(recv_bar, (uint32_t)owner);
+#pragma unroll 1
+        for (int c = 0; c < S_BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_lane + c, r);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            st_async_v4(dst + (uint32_t)(c + 4 * v) * 4, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3], rbar);
+        }
+      } else if (recv_wait(recv_bar, abort_flag, p.err)) {
+        __syncwarp();
+        const int row = m0 + quarter * 32 + lane;
+        const bool row_ok = row < p.M;
+        const float* slots = reinterpret_cast<const float*>(gbase + S_STAGES * S_STAGE_BYTES) + slice_row * S_ROW;
+#pragma unroll 1
+        for (int c = 0; c < S_BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_lane + c, r);
+#pragma unroll
+          for (int sl = 0; sl < S - 1; ++sl) {
+            const float4* src = reinterpret_cast<const float4*>(slots + sl * Sc::SLICE_ROWS * S_ROW + c);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const float4 x = src[v];
+              r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + x.x);
+              r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + x.y);
+              r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + x.z);
+              r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + x.w);
+            }
+          }
+          const int col = n0 + c;
+          if (row_ok && col < p.N) store_row32<MODE>(p, row, col, r);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while another may still push into its receive buffer
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S_BN));
+  }
+}
+
 // ---------------------------------------------------------------- host side
 // 2-D bf16 tensor map: inner dim `inner` (contiguous), outer dim `outer`, row pitch ld elements,
 // box {64, box_outer}, 128-byte swizzle, zero fill out of bounds.
@@ -598,6 +801,75 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cuda
   return qb_launch_status();
 }
 
+template <int S, int MODE, bool A_MN, bool B_MN>
+int launch_split(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  auto kern = gemm_split_kernel<S, MODE, A_MN, B_MN>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SplitCfg<S>::SMEM) != cudaSuccess)
+      return qb_launch_status();
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.tiles_m * p.tiles_n * S));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SplitCfg<S>::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = S;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return qb_launch_status();
+  return qb_launch_status();
+}
+
+template <int S, bool A_MN, bool B_MN>
+int launch_split_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  if (mode == 0) return launch_split<S, 0, A_MN, B_MN>(ta, tb, p, st);
+  if (mode == 1) return launch_split<S, 1, A_MN, B_MN>(ta, tb, p, st);
+  return launch_split<S, 2, A_MN, B_MN>(ta, tb, p, st);
+}
+
+template <bool A_MN, bool B_MN>
+int launch_split_s(int S, int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  return S == 2 ? launch_split_mode<2, A_MN, B_MN>(mode, ta, tb, p, st)
+                : launch_split_mode<4, A_MN, B_MN>(mode, ta, tb, p, st);
+}
+
+// How many S-CTA clusters of the split kernel are resident at once (0 if none fit): a split
+// launch with more tiles than this would run in waves, which the split layout is not meant for.
+int split_clusters(int S) {
+  static int cached[5] = {-1, -1, -1, -1, -1};
+  if (cached[S] >= 0) return cached[S];
+  auto kern = S == 2 ? gemm_split_kernel<2, 0, false, false> : gemm_split_kernel<4, 0, false, false>;
+  const int smem = S == 2 ? SplitCfg<2>::SMEM : SplitCfg<4>::SMEM;
+  int n = 0;
+  bool ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess;
+  if (ok) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(S * 64));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = S;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    ok = cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess;
+  }
+  if (!ok) {
+    n = 0;
+    (void)cudaGetLastError();  // the failed query's own error: the split layout is just not used
+  }
+  cached[S] = n;
+  return n;
+}
+
 template <bool A_MN, bool B_MN>
 int launch_pair_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
   if (mode == 0) return launch_pair<0, A_MN, B_MN>(ta, tb, p, st);
@@ -613,10 +885,10 @@ int launch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmPara
 }
 
 template <bool A_MN, bool B_MN>
-int launch_layout(bool wide, int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p,
-                  cudaStream_t st) {
-  return wide ? launch_mode<256, 4, A_MN, B_MN>(mode, ta, tb, p, st)
-              : launch_mode<128, 6, A_MN, B_MN>(mode, ta, tb, p, st);
+int launch_layout(int bn, int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
+  if (bn == 256) return launch_mode<256, 4, A_MN, B_MN>(mode, ta, tb, p, st);
+  if (bn == 192) return launch_mode<192, 5, A_MN, B_MN>(mode, ta, tb, p, st);
+  return launch_mode<128, 6, A_MN, B_MN>(mode, ta, tb, p, st);
 }
 
 inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
@@ -632,12 +904,10 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
   const int64_t elem = mode == 0 ? 2 : 4;
   const int vec_ok = al16(C) && (ldc * elem) % 16 == 0;
-  // 128x256 tiles when they cover every SM at least once, else 128x128 (twice the CTAs for the
-  // skinny decode-step products)
-  const int64_t tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
-  const bool wide = N >= 256 && tiles256 >= sm_count();
+  const int sms = sm_count();
+  const int64_t tm = (M + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
   // 256x256 tiles on CTA pairs when they fill every SM pair at least once
-  const bool pair = N >= 256 && M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sm_count() / 2;
+  const bool pair = N >= 256 && M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2;
   CUtensorMap ta, tb;
   if (pair) {
     if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
@@ -648,14 +918,38 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
     if (a_mn && !b_mn) return launch_pair_mode<true, false>(mode, ta, tb, pp, st);
     return launch_pair_mode<true, true>(mode, ta, tb, pp, st);
   }
+  // Single-CTA tiles.  128x256 when they cover every SM at least once; otherwise the layout whose
+  // busiest SM pulls the fewest operand bytes: 128x128 or 128x192 tiles (in waves over the SMs),
+  // or 128x128 tiles split along K over a cluster of 2 or 4 CTAs (one wave, plus the partials'
+  // exchange, costed as two K blocks).
+  const int64_t t128 = tm * ((N + 127) / 128), t192 = tm * ((N + 191) / 192);
+  int bn = 128, split = 1;
+  if (N >= 256 && tm * ((N + 255) / 256) >= sms) {
+    bn = 256;
+  } else {
+    const int64_t kb_bytes = (int64_t)(BM + 128) * BK * 2;
+    int64_t best = (t128 + sms - 1) / sms * kblocks * kb_bytes;
+    const int64_t c192 = (t192 + sms - 1) / sms * kblocks * (int64_t)(BM + 192) * BK * 2;
+    if (N > 128 && c192 < best) { best = c192; bn = 192; }
+    for (int S = 2; S <= 4; S *= 2) {
+      if (kblocks < 2 * S || t128 > split_clusters(S)) continue;
+      const int64_t c = (kblocks + S - 1) / S * kb_bytes + 2 * kb_bytes;
+      if (c < best) { best = c; bn = 128; split = S; }
+    }
+  }
   if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
-  if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, wide ? 256 : 128)) return QB_ERR_INVALID;
-  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)((M + BM - 1) / BM), (int)((N + (wide ? 255 : 127)) / (wide ? 256 : 128)),
-               vec_ok, err};
-  if (!a_mn && !b_mn) return launch_layout<false, false>(wide, mode, ta, tb, p, st);
-  if (!a_mn && b_mn) return launch_layout<false, true>(wide, mode, ta, tb, p, st);
-  if (a_mn && !b_mn) return launch_layout<true, false>(wide, mode, ta, tb, p, st);
-  return launch_layout<true, true>(wide, mode, ta, tb, p, st);
+  if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)bn)) return QB_ERR_INVALID;
+  GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)tm, (int)((N + bn - 1) / bn), vec_ok, err};
+  if (split > 1) {
+    if (!a_mn && !b_mn) return launch_split_s<false, false>(split, mode, ta, tb, p, st);
+    if (!a_mn && b_mn) return launch_split_s<false, true>(split, mode, ta, tb, p, st);
+    if (a_mn && !b_mn) return launch_split_s<true, false>(split, mode, ta, tb, p, st);
+    return launch_split_s<true, true>(split, mode, ta, tb, p, st);
+  }
+  if (!a_mn && !b_mn) return launch_layout<false, false>(bn, mode, ta, tb, p, st);
+  if (!a_mn && b_mn) return launch_layout<false, true>(bn, mode, ta, tb, p, st);
+  if (a_mn && !b_mn) return launch_layout<true, false>(bn, mode, ta, tb, p, st);
+  return launch_layout<true, true>(bn, mode, ta, tb, p, st);
 }
 
 }  // namespace

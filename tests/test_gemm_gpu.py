@@ -19,7 +19,11 @@ def ref(a, b):
                                    (512, 4096, 1024), (257, 6144, 1024), (513, 1024, 3072), (64, 151936, 1024),
                                    (1000, 2048, 4096),
                                    # 256x256 tiles on CTA pairs (>= one tile per SM pair), with M/N/K tails
-                                   (2048, 2560, 512), (2000, 2600, 648), (8192, 6144, 1024)])
+                                   (2048, 2560, 512), (2000, 2600, 648), (8192, 6144, 1024),
+                                   # split-K clusters of 4 (decode-step o_proj / down_proj) and of 2
+                                   (512, 1024, 2048), (512, 1024, 3072), (300, 1000, 1024),
+                                   # 128x192 tiles (one wave where 128x128 would need two), N and K tails
+                                   (512, 6144, 1024), (500, 5000, 1000)])
 def test_gemm_bf16_out(cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M * 7 + N)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -32,7 +36,7 @@ def test_gemm_bf16_out(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("mode", [1, 2])
-@pytest.mark.parametrize("M,N,K", [(200, 384, 512), (2000, 2600, 648)])
+@pytest.mark.parametrize("M,N,K", [(200, 384, 512), (2000, 2600, 648), (513, 1024, 3072), (500, 5000, 1000)])
 def test_gemm_fp32_out_and_accumulate(cuda, mode, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(mode)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -55,6 +59,17 @@ def test_gemm_strided_operands(cuda):
     assert (c.float() - r).abs().max().item() <= 1e-2 * r.abs().max().item()
 
 
+def test_gemm_split_k_deterministic(cuda):
+    """Split-K partials are summed in a fixed order: repeated launches give identical bits."""
+    g = torch.Generator(device=cuda).manual_seed(11)
+    a = torch.randn(512, 3072, device=cuda, generator=g).to(torch.bfloat16)
+    b = torch.randn(1024, 3072, device=cuda, generator=g).to(torch.bfloat16)
+    first = ops.gemm(a, b)
+    for _ in range(20):
+        assert torch.equal(ops.gemm(a, b), first)
+    ops.check_device_errors()
+
+
 def test_gemm_repeated_calls_stable(cuda):
     """Persistent kernel reuse: many launches, same answer every time."""
     g = torch.Generator(device=cuda).manual_seed(9)
@@ -67,7 +82,7 @@ def test_gemm_repeated_calls_stable(cuda):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 1024, 776), (1000, 384, 4096), (64, 151936, 200),
-                                   (2048, 2560, 512), (2000, 2600, 648)])
+                                   (2048, 2560, 512), (2000, 2600, 648), (400, 6000, 200)])
 def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
     """Backward layouts: A stored [K, M] and/or B stored [K, N]; K need not be a multiple of 64
     (row pitches stay multiples of 8 elements, the TMA rule)."""
