@@ -412,6 +412,7 @@ def kernel_profile(args, torch, run_step, path):
         out = run_step()
         torch.cuda.synchronize()
     tot, cnt = Counter(), Counter()
+    recs = []
     for e in prof.events():
         if str(getattr(e, "device_type", "")).endswith("CUDA"):
             name = e.name
@@ -420,9 +421,22 @@ def kernel_profile(args, torch, run_step, path):
             name = name.split("(")[0]
             tot[name] += e.time_range.elapsed_us()
             cnt[name] += 1
+            recs.append((e.time_range.start, name, e.time_range.elapsed_us()))
+    # The rollout ends with a device->host read of its tokens, so every rollout kernel runs before
+    # the first kernel of the log-prob/training phases; the rollout's last sampling launch marks it.
+    ends = [t for t, n, _ in recs if n == "sample_kernel"]
+    split = max(ends) if ends else float("inf")
+    phase_tot = {"rollout": Counter(), "ref log-probs + train": Counter()}
+    phase_cnt = {"rollout": Counter(), "ref log-probs + train": Counter()}
+    for t, n, d in recs:
+        ph = "rollout" if t <= split else "ref log-probs + train"
+        phase_tot[ph][n] += d
+        phase_cnt[ph][n] += 1
     T = sum(tot.values()) or 1.0
     lines = [f"# Kernel time of one GRPO step (CUPTI records via torch.profiler)", "",
-             f"Command: python bench.py --warmup {args.warmup} --steps {args.steps} --kernel-profile {path}"
+             f"Command: python bench.py --warmup {args.warmup} --steps {args.steps}"
+             + (" --no-e2e" if args.no_e2e else "") + (" --no-cpu-baseline" if args.no_cpu_baseline else "")
+             + f" --kernel-profile {path}"
              + (" --no-graphs" if args.no_graphs else ""), "",
              f"Workload: {WORKLOAD}.  Phases of this step (host wall clock): rollout {out['t_rollout']:.2f} s, "
              f"ref log-probs {out['t_ref']:.2f} s, train {out['t_train']:.2f} s.", "",
@@ -430,6 +444,22 @@ def kernel_profile(args, torch, run_step, path):
              "| kernel | launches | total ms | share |", "|---|---|---|---|"]
     for k, v in tot.most_common(40):
         lines.append(f"| {k[:90]} | {cnt[k]} | {v / 1e3:.2f} | {100 * v / T:.1f}% |")
+    recs.sort()
+    gaps = {"rollout": [0.0, 0], "ref log-probs + train": [0.0, 0]}
+    for (t0, n0, d0), (t1, _, _) in zip(recs, recs[1:]):
+        g = t1 - (t0 + d0)
+        ph = "rollout" if t1 <= split else "ref log-probs + train"
+        if 0 < g < 100:  # idle time between back-to-back launches (longer gaps are host waits)
+            gaps[ph][0] += g
+            gaps[ph][1] += 1
+    for ph in phase_tot:
+        PT = sum(phase_tot[ph].values()) or 1.0
+        lines += ["", f"## {ph}: {PT / 1e3:.1f} ms of kernel time; {gaps[ph][0] / 1e3:.1f} ms idle in "
+                  f"{gaps[ph][1]} gaps under 100 us between consecutive kernels", "",
+                  "| kernel | launches | total ms | us per launch | share of phase |", "|---|---|---|---|---|"]
+        for k, v in phase_tot[ph].most_common(20):
+            c = phase_cnt[ph][k]
+            lines.append(f"| {k[:90]} | {c} | {v / 1e3:.2f} | {v / c:.2f} | {100 * v / PT:.1f}% |")
     Path(path).parent.mkdir(parents=True, exist_ok=True)
     Path(path).write_text("\n".join(lines) + "\n")
 
@@ -615,7 +645,13 @@ def run_gemm_only(shape=None):
             e1.record(st)
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / (reps * len(bs))
-            res[impl] = {"ms": ms, "tflops": 2 * M * N * K / (ms / 1000) / 1e12}
+            from torch.profiler import ProfilerActivity, profile
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                fn(bs[0])
+                torch.cuda.synchronize()
+            names = sorted({e.name.split("(")[0][:120] for e in prof.events()
+                            if str(getattr(e, "device_type", "")).endswith("CUDA")})
+            res[impl] = {"ms": ms, "tflops": 2 * M * N * K / (ms / 1000) / 1e12, "kernels": names}
             del graph
         ref = (a.float() @ b.float().t())
         ops.gemm(a, b, out=c)

@@ -151,7 +151,8 @@ int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, int64_t stri
  * Qwen3Attention.forward_decode (qwen3_naive.py:672-680).
  *   q: [batch, hq, D] bf16; caches [num_blocks, page_size, hkv, D];
  *   kv length of sequence b = seqlens[b] + seqlen_add (the reference passes
- *   cache_seqlens = context_lens + 1, i.e. seqlen_add = 1 on context_lens);
+ *   cache_seqlens = context_lens + 1, i.e. seqlen_add = 1 on context_lens); a sequence
+ *   with length <= 0 reads no keys and gets zero output (batch padding rows);
  *   the key range is split into chunks of split_tokens (multiple of 64) processed by
  *   separate CTAs; with max_splits > 1 partial results go to `workspace`
  *   (qb_paged_decode_workspace_bytes) and a second kernel merges them.
@@ -176,8 +177,8 @@ size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits)
  * for all members' query heads and each member's own keys separately, in one launch; split-K
  * partials (shared_splits + own_splits slots per sequence and head) are merged inside it.
  * workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D, shared_splits + own_splits)
- * bytes whose last batch*hq*4 bytes (merge tickets) are zero before the first call; every
- * call leaves them zero again.  The tickets' place depends on (batch, hq, slots): a workspace
+ * bytes whose last batch*hq*4 + 16 bytes (merge tickets, then two work-claim counters) are
+ * zero before the first call; every call leaves them zero again.  The tickets' place depends on (batch, hq, slots): a workspace
  * is reused only by calls of the same shape, and calls sharing one must not overlap. */
 int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
                                  int64_t num_blocks, int page_size, const int32_t* block_tables,

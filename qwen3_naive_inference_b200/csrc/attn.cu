@@ -79,7 +79,12 @@ QB_DEVICE void decode_own_tile(const DecodeParams& p, uint8_t* smem, int split, 
   const bool misaligned = (tok_begin & (DEC_TOK - 1)) != 0 || tok_begin < 0;
   if (tok_begin >= len || misaligned) {
     if (misaligned && tid == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
-    if (p.max_splits > 1 && threadIdx.x < 2) write_empty_partial(p, b, p.slot_off + split, kvh * 2 + threadIdx.x);
+    if (p.max_splits > 1) {
+      if (threadIdx.x < 2) write_empty_partial(p, b, p.slot_off + split, kvh * 2 + threadIdx.x);
+    } else {  // no keys at all (len <= 0): the output rows of both heads are zero
+      for (int i = tid; i < D; i += blockDim.x)
+        reinterpret_cast<uint32_t*>(p.out + ((int64_t)b * p.hq + kvh * 2) * D)[i] = 0u;
+    }
     return;
   }
   const int tok_end = min(len, tok_begin + p.split_tokens);
@@ -324,19 +329,21 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 // issues two TMA box loads for K and two for V (16 tokens x 64 dims each, 128-byte swizzle)
 // plus, with an own item's first stage, one for its two query rows, all completing on the
 // slot's mbarrier.  The ring runs across item boundaries, so the next item's keys are in flight
-// while an item finishes.  Warp w of the grid takes items w, w + total_warps, ... (shared items
-// first).  Every mbarrier wait is bounded (QB_DEVERR_TIMEOUT, then the warp drains its copies
-// with a bounded wait and leaves).
+// while an item finishes.  Warp w of the grid starts on item w (shared items first) and then
+// claims items from a counter in the workspace, so warps that drew long items take fewer.
+// Every mbarrier wait is bounded (QB_DEVERR_TIMEOUT, then the warp drains its copies with a
+// bounded wait and leaves).
 constexpr int GMAX = 8;
 constexpr int WD_TOK = 16;                   // tokens per stage (one MMA M tile)
 constexpr int WD_SLOTS = 3;
 constexpr int WD_KV_BYTES = WD_TOK * ROWB;   // 4 KB of K (and of V) per stage: two 2 KB halves
 constexpr int WD_Q_OFF = WD_SLOTS * 2 * WD_KV_BYTES;       // query rows of own items
 constexpr int WD_BAR_OFF = WD_Q_OFF + WD_SLOTS * 2 * ROWB;  // + 512 B per slot
-constexpr int WD_WARP_BYTES = (WD_BAR_OFF + WD_SLOTS * 8 + 1023) / 1024 * 1024;  // 1024-aligned
+constexpr int WD_QUEUE_OFF = WD_BAR_OFF + WD_SLOTS * 8;     // 4 item ids: loader -> consumer
+constexpr int WD_WARP_BYTES = (WD_QUEUE_OFF + 16 + 1023) / 1024 * 1024;  // 1024-aligned
 constexpr int WD_WARPS = 8;                  // per CTA; one CTA per SM
 constexpr int WD_SMEM = WD_WARPS * WD_WARP_BYTES + 1024;  // + alignment slack
-static_assert(WD_BAR_OFF + WD_SLOTS * 8 <= WD_WARP_BYTES, "per-warp region");
+static_assert(WD_QUEUE_OFF + 16 <= WD_WARP_BYTES, "per-warp region");
 
 struct CascadeParams {
   CUtensorMap tk, tv;         // caches as {D, hkv, num_blocks*page}, box {64, 1, 16}, 128B swizzle
@@ -348,6 +355,7 @@ struct CascadeParams {
   int shared_splits, own_splits;
   int n_shared_items, n_items;
   int* tickets;               // [batch * hkv], zero between calls
+  int* work;                  // [2]: next dynamically claimed item, finished warps; zero between calls
 };
 
 struct Item {
@@ -493,12 +501,28 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
   __syncwarp();
 
   // ---- load cursor (state kept by every lane; lane 0 issues the copies)
-  // The next item's metadata and the next page id are read one step ahead so that their
-  // global-load latency never sits between two copies.
-  int l_item = first, l_stage = 0, l_flat = 0;
+  // Items are scheduled dynamically: each warp starts on item `first` (the shared items, the
+  // longest, come first) and then claims item total + atomicAdd(work[0], 1) whenever its loader
+  // moves on, so warps that drew long items take fewer.  The claim is issued one item ahead
+  // (its latency hides behind a whole item), and the next item's metadata and the next page id
+  // are read one step ahead so that their global-load latency never sits between two copies.
+  // The loader hands each item id to the consumer through a 4-entry queue in this warp's shared
+  // memory: it runs at most WD_SLOTS - 1 = 2 stages ahead and every item takes at least one
+  // stage, so at most 4 ids are live.  An id >= n_items ends the queue.
+  volatile int* queue = reinterpret_cast<volatile int*>(wsm + WD_QUEUE_OFF);
+  int l_item = first, l_stage = 0, l_flat = 0, l_k = 0;
   Item l_it = decode_item(cp, l_item);
+  int claim = 0;  // lane 0: the claim in flight for the item after n_item
+  if (lane == 0) {
+    queue[0] = first;
+    claim = atomicAdd(cp.work, 1);
+  }
+  int n_item = total + __shfl_sync(0xffffffffu, claim, 0);
   Item n_it = l_it;
-  if (l_item + total < cp.n_items) n_it = decode_item(cp, l_item + total);
+  if (n_item < cp.n_items) {
+    n_it = decode_item(cp, n_item);
+    if (lane == 0) claim = atomicAdd(cp.work, 1);
+  }
   auto page_at = [&](const Item& it, int col) { return col < p.bt_stride ? it.btrow[col] : -1; };
   int l_col = l_it.tok_begin / PAGE;
   int l_page = page_at(l_it, l_col), l_page_nx = page_at(l_it, l_col + 1);
@@ -533,9 +557,17 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
       }
       if (++l_stage >= max(1, l_it.n_stages)) {  // an empty item still takes one slot
         l_stage = 0;
-        l_item += total;
+        l_item = n_item;
         l_it = n_it;
-        if (l_item + total < cp.n_items) n_it = decode_item(cp, l_item + total);
+        ++l_k;
+        if (lane == 0) queue[l_k & 3] = l_item;
+        if (l_item < cp.n_items) {
+          n_item = total + __shfl_sync(0xffffffffu, claim, 0);
+          if (n_item < cp.n_items) {
+            n_it = decode_item(cp, n_item);
+            if (lane == 0) claim = atomicAdd(cp.work, 1);
+          }
+        }
         l_col = l_it.tok_begin / PAGE;
         l_page = page_at(l_it, l_col);
         l_page_nx = page_at(l_it, l_col + 1);
@@ -558,8 +590,10 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
   };
   bool ok = true;
   for (int k = 0; ok; ++k) {
-    if (first + k * total >= cp.n_items) break;
-    const Item it = decode_item(cp, first + k * total);
+    __syncwarp();  // the loader's queue write (lane 0) is visible to every lane
+    const int item = queue[k & 3];
+    if (item >= cp.n_items) break;
+    const Item it = decode_item(cp, item);
     const int ns = max(1, it.n_stages);
     const int h0 = it.kvh * 2;
     if (it.shared) {
@@ -825,6 +859,17 @@ paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
     const long long t0 = clock64();
     while (!mbar_try(bar, parity))
       if (clock64() - t0 > WAIT_CYCLES) break;
+  }
+  // The last warp to finish resets the claim counters for the next call: every other warp's
+  // claims precede its finishing increment (fenced), so no claim can follow the reset.
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    const int active = min(total, cp.n_items);
+    if (atomicAdd(cp.work + 1, 1) == active - 1) {
+      cp.work[0] = 0;
+      cp.work[1] = 0;
+    }
   }
 }
 
@@ -1456,8 +1501,9 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
 }
 
 extern "C" size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int Dh, int n_slots) {
-  // split-K partials, then one int32 ticket per (sequence, head)
-  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float) + (size_t)batch * hq * sizeof(int32_t);
+  // split-K partials, one int32 ticket per (sequence, head), then the two work-claim counters
+  // (padded to 16 bytes)
+  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float) + (size_t)batch * hq * sizeof(int32_t) + 16;
 }
 
 extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
@@ -1497,6 +1543,7 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
   cp.n_shared_items = (int)n_shared;
   cp.n_items = (int)n_items;
   cp.tickets = tickets;
+  cp.work = tickets + (size_t)batch * hq;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(paged_decode_cascade_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WD_SMEM);

@@ -749,7 +749,9 @@ class Qwen3ForCausalLM(nn.Module):
         self._gin_dev.zero_()
         b = self._graph_bufs
         mb = b["members"].shape[0]
-        # warm-up inputs: every row its own group, nothing shared, writes to slot 0 skipped
+        # warm-up inputs: every row its own group with no keys (its attention reads nothing: pages
+        # not yet written may hold any bits), nothing shared, cache writes skipped
+        b["context_lens"].fill_(-1)
         b["slot_mapping"].fill_(-1)
         b["members"].fill_(-1)
         b["members"][:, 0] = torch.arange(mb, dtype=torch.int32, device=b["members"].device)
@@ -790,10 +792,10 @@ class Qwen3ForCausalLM(nn.Module):
         hb["context_lens"][:bs] = ctx
         hb["slot_mapping"][:bs] = slots
         hb["block_tables"][:bs, :bt.shape[1]] = bt
-        if gbs > bs:  # padding rows: harmless length-1 attention on page 0, cache writes skipped
+        if gbs > bs:  # padding rows: no keys (zero attention output, nothing read), cache writes skipped
             hb["input_ids"][bs:gbs] = 0
             hb["positions"][bs:gbs] = 0
-            hb["context_lens"][bs:gbs] = 0
+            hb["context_lens"][bs:gbs] = -1
             hb["slot_mapping"][bs:gbs] = -1
             hb["block_tables"][bs:gbs] = 0
         if self._graph_key[2]:

@@ -21,7 +21,8 @@ def ref(a, b):
                                    # 256x256 tiles on CTA pairs (>= one tile per SM pair), with M/N/K tails
                                    (2048, 2560, 512), (2000, 2600, 648), (8192, 6144, 1024),
                                    # split-K clusters of 4 (decode-step o_proj / down_proj) and of 2
-                                   (512, 1024, 2048), (512, 1024, 3072), (300, 1000, 1024),
+                                   (512, 1024, 2048), (512, 1024, 3072), (300, 1000, 1024), (4, 256, 512),
+                                   (809, 256, 512),
                                    # 128x192 tiles (one wave where 128x128 would need two), N and K tails
                                    (512, 6144, 1024), (500, 5000, 1000)])
 def test_gemm_bf16_out(cuda, M, N, K):

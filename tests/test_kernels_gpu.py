@@ -320,6 +320,74 @@ def test_grpo_advantage_and_loss(cuda):
         assert torch.allclose(nd.grad.cpu(), grad_ref, rtol=1e-4, atol=1e-7)
 
 
+@pytest.mark.parametrize("split", [False, True])
+def test_paged_decode_keyless_rows(cuda, split):
+    """Rows of length <= 0 (decode-graph batch padding) read no keys and get zero output, with
+    and without split-K; page 0, which they point at, holds NaN and must not leak into them."""
+    g = gen(31)
+    hq, hkv = 16, 8
+    kc = torch.randn(6, 256, hkv, 128, generator=g).to(BF)
+    vc = torch.randn(6, 256, hkv, 128, generator=g).to(BF)
+    kc[0] = float("nan")
+    vc[0] = float("nan")
+    bt = torch.tensor([[1, 2], [0, 0], [3, 4], [0, 0]], dtype=torch.int32)
+    ctx = torch.tensor([300, -1, 40, -1], dtype=torch.int32)  # key counts ctx + 1: 301, 0, 41, 0
+    q = torch.randn(4, hq, 128, generator=g).to(BF)
+    kw = dict(split_tokens=64, max_splits=8) if split else dict(split_tokens=512, max_splits=1)
+    out = ops.paged_decode_attention(q.to(cuda), kc.to(cuda), vc.to(cuda), bt.to(cuda), ctx.to(cuda), 128 ** -0.5,
+                                     **kw).cpu()
+    ops.check_device_errors()
+    live = [0, 2]
+    ref = R.paged_decode(q[live], kc, vc, bt[live], ctx[live] + 1, 128 ** -0.5)
+    close_bf16(out[live], ref, 2e-2)
+    assert torch.equal(out[[1, 3]].float(), torch.zeros(2, hq, 128))
+
+
+def test_paged_decode_grouped_rollout_scale(cuda):
+    """Rollout-sized cascade launch (64 groups x 8 completions, page-aligned prompts shared per
+    group, 1-600 own keys each; ~4.6k work items for 1184 warps, so warps claim items
+    dynamically) equals the plain paged decode kernel over the same pages, on four back-to-back
+    launches (the claim counters and merge tickets reset in between)."""
+    g = torch.Generator(device=cuda).manual_seed(123)
+    gc = torch.Generator().manual_seed(123)
+    hq, hkv, G, n_groups = 16, 8, 8, 64
+    plen = [256 * int(x) for x in torch.randint(0, 3, (n_groups,), generator=gc)]
+    own = torch.randint(1, 601, (G * n_groups,), generator=gc).tolist()
+    n_pages = sum(p // 256 for p in plen) + sum(-(-o // 256) for o in own)
+    kc = torch.randn(n_pages, 256, hkv, 128, device=cuda, generator=g).to(BF)
+    vc = torch.randn(n_pages, 256, hkv, 128, device=cuda, generator=g).to(BF)
+    perm = torch.randperm(n_pages, generator=gc).tolist()
+    tables, lens, members = [], [], []
+    for gi in range(n_groups):
+        sh = [perm.pop() for _ in range(plen[gi] // 256)]
+        row = []
+        for m in range(G):
+            b = gi * G + m
+            row.append(b)
+            tables.append(sh + [perm.pop() for _ in range(-(-own[b] // 256))])
+            lens.append(plen[gi] + own[b])
+        members.append(row)
+    B = len(tables)
+    bt = torch.full((B, max(len(t) for t in tables)), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    q = torch.randn(B, hq, 128, device=cuda, generator=g).to(BF)
+    ctx = (torch.tensor(lens, dtype=torch.int32) - 1).to(cuda)
+    bt = bt.to(cuda)
+    ref = ops.paged_decode_attention(q, kc, vc, bt, ctx, 128 ** -0.5)
+    plan = ops.grouped_decode_plan(B, hkv, max(plen), max(own))
+    ws = ops.grouped_workspace(B, hq, 128, plan, cuda)
+    kv_start = torch.tensor([plen[b // G] for b in range(B)], dtype=torch.int32).to(cuda)
+    args = (q, kc, vc, bt, ctx, 128 ** -0.5, torch.tensor(members, dtype=torch.int32).to(cuda),
+            torch.tensor(plen, dtype=torch.int32).to(cuda), kv_start, plan)
+    for _ in range(4):
+        out = ops.paged_decode_attention_grouped(*args, workspace=ws)
+        close_bf16(out.cpu(), ref.cpu(), 2e-2)
+    nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(B, hq, 128, plan[1] + plan[2])
+    assert int(ws.view(torch.uint8)[nb - B * hq * 4 - 16:nb].view(torch.int32).abs().sum()) == 0
+    ops.check_device_errors()
+
+
 @pytest.mark.parametrize("split", [64, 256])
 def test_paged_decode_grouped_shared_prefix(cuda, split):
     """Groups sharing prompt pages: the cascade (shared keys once per group + own keys per
@@ -327,7 +395,7 @@ def test_paged_decode_grouped_shared_prefix(cuda, split):
     shared keys [0, shared_len) and the own keys [kv_start, len).  Groups whose prompt ends
     inside a page leave a hole [shared_len, kv_start) filled with large garbage that must never
     be read; page-aligned groups use kv_start == shared_len.  Two calls check that the merge
-    tickets are left zero."""
+    tickets and the work-claim counters are left zero."""
     g = gen(77 + split)
     hq, hkv = 16, 8
     # (members, shared keys, own keys start on a fresh page?)
@@ -390,6 +458,6 @@ def test_paged_decode_grouped_shared_prefix(cuda, split):
         out = ops.paged_decode_attention_grouped(*args, workspace=ws)
         close_bf16(out, ref, 2e-2)
     nb = ops.lib().qb_paged_decode_grouped_workspace_bytes(B, hq, 128, plan[1] + plan[2])
-    tickets = ws.view(torch.uint8)[nb - B * hq * 4:nb].view(torch.int32)
-    assert int(tickets.abs().sum()) == 0
+    tickets_and_counters = ws.view(torch.uint8)[nb - B * hq * 4 - 16:nb].view(torch.int32)
+    assert int(tickets_and_counters.abs().sum()) == 0
     ops.check_device_errors()

@@ -328,6 +328,32 @@ def test_grouped_rollout_matches_plain_greedy(setup, cuda):
     assert np.mean([x == y for x, y in zip(a, b)]) > 0.95
 
 
+def test_generation_reads_only_written_cache_slots(setup, cuda):
+    """Every K/V slot a step reads was written first: with the page pool filled with NaN
+    beforehand (memory left by earlier work can hold any bits), greedy generation -- the decode
+    graphs' capture warm-up and padded batch rows, which must read no keys, included -- and the
+    grouped rollout give the same tokens as on a zeroed pool, and no device error is raised."""
+    cfg, params, model = setup
+    g = torch.Generator().manual_seed(13)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, L), generator=g).to(cuda) for L in (3, 250, 256, 300, 17)]
+    model.allocate_global_kv_cache()
+
+    def run(fill):
+        for layer in model.model.layers:
+            layer.self_attn.k_cache.fill_(fill)
+            layer.self_attn.v_cache.fill_(fill)
+        model._has_cuda_graphs = False  # recapture: the capture warm-up runs on this pool too
+        torch.manual_seed(0)
+        plain = model.generate_continuous(prompts, max_new_tokens=20, top_k=1, temperature=1.0)[1]
+        torch.manual_seed(0)
+        grouped = model.generate_grouped_with_logprobs(prompts[:3], 3, max_new_tokens=20, top_k=1,
+                                                       temperature=1.0)[1]
+        ops.check_device_errors()
+        return plain, grouped
+
+    assert run(float("nan")) == run(0.0)
+
+
 def test_grpo_step_end_to_end(setup, cuda):
     cfg, params, model = setup
     ref = G.make_reference_copy(model)
