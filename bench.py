@@ -347,29 +347,31 @@ def run_ours(args):
         ems, etok, _, _, h2d, d2h, _ = timed(args.steps, host_inputs=True)
         e2e = {"value": etok / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.steps),
                "d2h_bytes_per_step": d2h // max(1, args.steps)}
-    # roofline of the dominant kernel: the cascade decode attention (30% of the step's kernel
-    # time), on the mid-rollout case, launches back to back between events on its stream
+    # roofline of the dominant kernel: the grouped (shared-prefix) decode attention, on the
+    # mid-rollout case, launches back to back between events on its stream; the timed call is the
+    # tile kernel plus its small split-K combine
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
         peaks = json.loads(pk.read_text())
     hbm = peaks.get("hbm_gbs", 6650.0)
     case = rollout_attn_case(torch, ops, dev)
-    cas_ms = time_launches(torch, case["runs"]["grouped"])
+    grp_ms = time_launches(torch, case["runs"]["grouped"])
     plain_ms = time_launches(torch, case["runs"]["plain"])
     ops.check_device_errors()
-    achieved = case["alg_grouped"] / (cas_ms / 1000.0) / 1e9
+    achieved = case["alg_grouped"] / (grp_ms / 1000.0) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                "traffic": profiled_traffic("paged_decode_cascade_kernel_rollout.md", "traffic_bytes_per_launch"),
-                "kernel": "paged_decode_cascade_kernel",
+                "traffic": profiled_traffic("paged_decode_grouped_kernel_rollout.md", "traffic_bytes_per_launch"),
+                "kernel": "paged_decode_grouped_kernel",
                 "case": "mid-rollout: 64 groups x 8, prompt U[64,512] shared per group, 256 own tokens per "
                         "completion, 16q/8kv, d128; back-to-back launches, K/V 4.7x L2",
-                "algorithmic_bytes": case["alg_grouped"], "ms_per_launch": cas_ms,
-                "traffic_source": "profiles/paged_decode_cascade_kernel_rollout.md (ncu, same case)",
+                "algorithmic_bytes": case["alg_grouped"], "ms_per_launch": grp_ms,
+                "traffic_source": "profiles/paged_decode_grouped_kernel_rollout.md (ncu, same case, "
+                                  "tile kernel + combine)",
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if pk.exists() else "fallback",
                 "vs_reference_layout": {"kernel": "paged_decode_kernel", "ms_per_launch": plain_ms,
                                         "kv_bytes": case["kv_plain"],
-                                        "effective_gbs_of_cascade": case["kv_plain"] / (cas_ms / 1000.0) / 1e9}}
+                                        "effective_gbs_of_grouped": case["kv_plain"] / (grp_ms / 1000.0) / 1e9}}
     del case
     # the plain paged decode kernel alone on config-3 shapes (long contexts)
     dec_ms, dec_bytes, dec_tokens = decode_microbench(torch, ops, dev)
@@ -389,7 +391,7 @@ def run_ours(args):
                            "new_tokens": args.new_tokens, "prompt_len": [args.prompt_min, args.prompt_max],
                            "layers": args.layers, "parallelism": f"dp{world}", "beta_kl": 0.04,
                            "rollout": "reference scheduler" if args.no_share_prefix else
-                           "grouped: prompt prefilled once per group, shared KV pages, cascade decode attention",
+                           "grouped: prompt prefilled once per group, shared KV pages, shared-prefix decode attention",
                            "l2": "inputs far larger than L2 (weights + 60+ GB KV cache per step)",
                            "tokens_per_step": tokens // max(1, args.steps)},
                 "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"],
@@ -479,7 +481,7 @@ def rollout_attn_case(torch, ops, dev):
     """Decode attention mid-rollout (config 4 shapes): 64 groups x 8 completions, prompt U[64,512],
     256 generated tokens each.  Builds the K/V pool twice over the same values: the reference's
     layout (every completion holds its own copy of the prompt K/V; plain paged decode) and the
-    grouped layout (prompt pages shared, own tokens on fresh pages; cascade kernel).  Returns the
+    grouped layout (prompt pages shared, own tokens on fresh pages; grouped decode).  Returns the
     launch closures and the K/V bytes each layout needs per launch."""
     g = torch.Generator().manual_seed(5)
     G, n_groups, gen, hq, hkv, D = 8, 64, 256, 16, 8, 128
@@ -538,7 +540,7 @@ def rollout_attn_case(torch, ops, dev):
     plan = ops.grouped_decode_plan(B, hkv, ctx_bound, ctx_bound)
     ws_p = torch.empty(max(1, ops.lib().qb_paged_decode_workspace_bytes(B, hq, D, ms) // 4), device=dev)
     ws_g = ops.grouped_workspace(B, hq, D, plan, dev)
-    # the cascade kernel on the plain layout (every sequence its own group, nothing shared)
+    # the grouped decode on the plain layout (every sequence its own group, nothing shared)
     mem_1 = torch.full((B, 8), -1, dtype=torch.int32, device=dev)
     mem_1[:, 0] = torch.arange(B, dtype=torch.int32, device=dev)
     zeros_b = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -549,7 +551,7 @@ def rollout_attn_case(torch, ops, dev):
                                                     max_splits=ms, workspace=ws_p),
         "grouped": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt, cl, D ** -0.5, mem_d, sl_d, ks_d, plan,
                                                               workspace=ws_g),
-        "cascade_unshared": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt_plain, cl_plain, D ** -0.5, mem_1,
+        "grouped_unshared": lambda: ops.paged_decode_attention_grouped(q, kc, vc, bt_plain, cl_plain, D ** -0.5, mem_1,
                                                                        zeros_b, zeros_b, plan_1, workspace=ws_1),
     }
     kv_plain = (sum(plain_lens) + B * gen) * hkv * D * 4
@@ -577,8 +579,8 @@ def time_launches(torch, fn, n=20):
 
 
 def run_rollout_attn():
-    """Plain paged decode (reference layout) vs the cascade kernel (grouped layout) vs the cascade
-    kernel with nothing shared, on the mid-rollout case; prints ms and K/V bytes read."""
+    """Plain paged decode (reference layout) vs the grouped decode (grouped layout) vs the grouped
+    decode with nothing shared, on the mid-rollout case; prints ms and K/V bytes read."""
     import torch
 
     from qwen3_naive_inference_b200 import ops
@@ -587,12 +589,12 @@ def run_rollout_attn():
     runs = case["runs"]
     out = {name: time_launches(torch, fn) for name, fn in runs.items()}
     ref = runs["plain"]().float()
-    err = max((runs[k]().float() - ref).abs().max().item() for k in ("grouped", "cascade_unshared"))
+    err = max((runs[k]().float() - ref).abs().max().item() for k in ("grouped", "grouped_unshared"))
     ops.check_device_errors()
     kv_plain, kv_grouped = case["kv_plain"], case["kv_grouped"]
     print(json.dumps({"rollout_attn": {"ms": out, "kv_bytes": {"plain": kv_plain, "grouped": kv_grouped},
                                        "gbs": {"plain": kv_plain / out["plain"] / 1e6,
-                                               "cascade_unshared": kv_plain / out["cascade_unshared"] / 1e6,
+                                               "grouped_unshared": kv_plain / out["grouped_unshared"] / 1e6,
                                                "grouped_effective": kv_plain / out["grouped"] / 1e6,
                                                "grouped_actual": kv_grouped / out["grouped"] / 1e6},
                                        "plan": case["plan"], "max_abs_diff": err}}), flush=True)

@@ -174,12 +174,11 @@ size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits)
  * multiple of 64.  Keys in [shared_len, kv_start) are never read, so a member's own tokens
  * may start on a fresh page after a partially filled shared prompt page; with kv_start ==
  * shared_len the result equals qb_paged_decode_attn.  The shared keys are read once per group
- * for all members' query heads and each member's own keys separately, in one launch; split-K
- * partials (shared_splits + own_splits slots per sequence and head) are merged inside it.
- * workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D, shared_splits + own_splits)
- * bytes whose last batch*hq*4 + 16 bytes (merge tickets, then two work-claim counters) are
- * zero before the first call; every call leaves them zero again.  The tickets' place depends on (batch, hq, slots): a workspace
- * is reused only by calls of the same shape, and calls sharing one must not overlap. */
+ * for all members' query heads and each member's own keys separately (one launch), then a
+ * second kernel merges the split-K partials (shared_splits + own_splits slots per sequence
+ * and head).  workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D,
+ * shared_splits + own_splits) bytes, any contents (every call rewrites the partials it reads);
+ * calls sharing one must not overlap. */
 int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
                                  int64_t num_blocks, int page_size, const int32_t* block_tables,
                                  int64_t bt_stride, const int32_t* seqlens, int seqlen_add,

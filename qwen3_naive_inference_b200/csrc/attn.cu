@@ -13,7 +13,7 @@
 // 256-byte row at ((page*256 + j)*hkv + h)*128.
 #include <algorithm>
 
-#include "tma.cuh"
+#include "common.cuh"
 
 namespace {
 
@@ -309,567 +309,247 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 }
 
 // ============================================================================
-// Shared-prefix decode attention (GRPO groups): warp-independent, persistent, TMA
+// Shared-prefix decode attention (GRPO groups)
 // ============================================================================
-// The G <= 8 members of a group share the K/V pages of their common prompt.  Work items,
-// each owned by ONE warp from start to finish:
-//   shared item (split, kv head, group): keys [split*S, min(shared_len, (split+1)*S)) in the
-//     pages of the group's first member, read once for all 2*G query heads of the kv head:
-//     16 query rows (member r/2, head h0 + r%2) = one M=16 MMA tile; S = Q K^T, online
-//     softmax, O += P V;
-//   own item (split, kv head, sequence): keys [kv_start + split*S, ...) of the sequence's own
-//     page-table row, the 16 staged tokens in the M dimension (S^T = K Q^T, O^T += V^T P^T)
-//     so that the kv head's two query heads still fill one MMA.
-// Keys in [shared_len, kv_start) are never read.  An item writes one split-K partial (O / l and
-// its log2-domain LSE) per (sequence, head) it covers; the warp that writes the last partial of
-// a (sequence, kv head) merges all of its slots, found through a ticket counter that it resets
-// to zero.  No warp waits on another warp or CTA.
-//
-// Each warp streams its items' keys in 16-token stages through its own small ring: lane 0
-// issues two TMA box loads for K and two for V (16 tokens x 64 dims each, 128-byte swizzle)
-// plus, with an own item's first stage, one for its two query rows, all completing on the
-// slot's mbarrier.  The ring runs across item boundaries, so the next item's keys are in flight
-// while an item finishes.  Warp w of the grid starts on item w (shared items first) and then
-// claims items from a counter in the workspace, so warps that drew long items take fewer.
-// Every mbarrier wait is bounded (QB_DEVERR_TIMEOUT, then the warp drains its copies with a
-// bounded wait and leaves).
-constexpr int GMAX = 8;
-constexpr int WD_TOK = 16;                   // tokens per stage (one MMA M tile)
-constexpr int WD_SLOTS = 3;
-constexpr int WD_KV_BYTES = WD_TOK * ROWB;   // 4 KB of K (and of V) per stage: two 2 KB halves
-constexpr int WD_Q_OFF = WD_SLOTS * 2 * WD_KV_BYTES;       // query rows of own items
-constexpr int WD_BAR_OFF = WD_Q_OFF + WD_SLOTS * 2 * ROWB;  // + 512 B per slot
-constexpr int WD_QUEUE_OFF = WD_BAR_OFF + WD_SLOTS * 8;     // 4 item ids: loader -> consumer
-constexpr int WD_WARP_BYTES = (WD_QUEUE_OFF + 16 + 1023) / 1024 * 1024;  // 1024-aligned
-constexpr int WD_WARPS = 8;                  // per CTA; one CTA per SM
-constexpr int WD_SMEM = WD_WARPS * WD_WARP_BYTES + 1024;  // + alignment slack
-static_assert(WD_QUEUE_OFF + 16 <= WD_WARP_BYTES, "per-warp region");
+// The G <= 8 completions of one prompt share the K/V pages of that prompt (the reference keeps
+// a copy per completion).  The grouped decode runs two kinds of CTA in one launch, then the
+// split-K combine:
+//   shared CTA (split, kv head, group): keys [split*S, min(shared_len, (split+1)*S)) in the
+//     pages of the group's first member, read once for the 2*G query heads of the kv head,
+//     which form the 16 rows of one M=16 MMA tile (row r: member r/2, head h0 + r%2);
+//   own CTA (split, kv head, sequence): decode_own_tile over keys [kv_start + split*S, ...).
+// Both stage 64 tokens of K and V per step with cp.async (three buffers), warp w on tokens
+// [16w, 16w+16), and write one split-K partial per (sequence, head): shared splits to slots
+// [0, shared_splits), own splits after them.  paged_decode_combine_kernel merges the slots.
+constexpr int GMAX = 8;  // members per group at most (2 * GMAX = 16 query rows, one MMA M tile)
 
-struct CascadeParams {
-  CUtensorMap tk, tv;         // caches as {D, hkv, num_blocks*page}, box {64, 1, 16}, 128B swizzle
-  CUtensorMap tq;             // q as {D, batch*hq}, box {D, 2}, no swizzle
-  DecodeParams d;             // slot_off = shared_splits; kv_start = first own key per sequence
+struct GroupParams {
   const int32_t* members;     // [n_groups, GMAX] sequence indices, -1 padded
-  const int32_t* shared_len;  // [n_groups] keys shared by the group (pages of members[g][0])
+  const int32_t* shared_len;  // [n_groups] keys shared by the group
   int batch;
   int shared_splits, own_splits;
-  int n_shared_items, n_items;
-  int* tickets;               // [batch * hkv], zero between calls
-  int* work;                  // [2]: next dynamically claimed item, finished warps; zero between calls
+  int n_shared_ctas;          // shared_splits * hkv * n_groups; the own CTAs follow
 };
 
-struct Item {
-  int shared;                        // 1: shared item, 0: own item
-  int kvh, idx;                      // kv head; group (shared) or sequence (own)
-  int slot;                          // split-K slot of its partials
-  int tok_begin, tok_end, n_stages;  // keys [tok_begin, tok_end) in 16-token stages
-  const int32_t* btrow;              // page-table row holding those keys
-};
-
-// Member i of group grp, -1 when absent; an index outside the batch raises SHAPE.
-QB_DEVICE int group_member(const CascadeParams& cp, int grp, int i) {
-  const int m = cp.members[grp * GMAX + i];
-  if (m >= cp.batch) {
-    qb_set_err(cp.d.err, QB_DEVERR_SHAPE);
-    return -1;
-  }
-  return m < 0 ? -1 : m;
-}
-
-QB_DEVICE Item decode_item(const CascadeParams& cp, int i) {
-  const DecodeParams& p = cp.d;
-  Item it;
-  if (i < cp.n_shared_items) {
-    const int split = i % cp.shared_splits;
-    i /= cp.shared_splits;
-    it.shared = 1;
-    it.kvh = i % p.hkv;
-    it.idx = i / p.hkv;
-    it.slot = split;
-    const int leader = group_member(cp, it.idx, 0);
-    it.tok_begin = split * p.split_tokens;
-    it.tok_end = leader < 0 ? 0 : min(cp.shared_len[it.idx], it.tok_begin + p.split_tokens);
-    it.btrow = p.bt + (int64_t)(leader < 0 ? 0 : leader) * p.bt_stride;
-  } else {
-    i -= cp.n_shared_items;
-    const int split = i % cp.own_splits;
-    i /= cp.own_splits;
-    it.shared = 0;
-    it.kvh = i % p.hkv;
-    it.idx = i / p.hkv;
-    it.slot = p.slot_off + split;
-    it.tok_begin = p.kv_start[it.idx] + split * p.split_tokens;
-    it.tok_end = min(p.seqlens[it.idx] + p.seqlen_add, it.tok_begin + p.split_tokens);
-    // stages must not straddle a page: the first key of an item is 64-aligned
-    if ((it.tok_begin & 63) != 0 || it.tok_begin < 0) {
-      qb_set_err(p.err, QB_DEVERR_SHAPE);
-      it.tok_begin = it.tok_end = 0;
-    }
-    it.btrow = p.bt + (int64_t)it.idx * p.bt_stride;
-  }
-  it.n_stages = it.tok_end > it.tok_begin ? (it.tok_end - it.tok_begin + WD_TOK - 1) / WD_TOK : 0;
-  return it;
-}
-
-QB_DEVICE uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-
-// Byte offset of (token row r, 16-byte chunk c of the 256-byte row) in a K or V stage: two
-// 2 KB halves (dims 0-63, 64-127) of 16 rows x 128 B, each 128-byte swizzled by TMA.
-QB_DEVICE uint32_t tsw(int r, int c) { return (c >> 3) * 2048 + r * 128 + (((c & 7) ^ (r & 7)) << 4); }
-
-// Merges the n_slots partials of sequence b, heads h0 and h0+1 (one warp: lane -> head
-// h0 + lane/16, eight dims).  The partials come from other warps of this launch; __ldcg
-// reads them from L2.
-QB_DEVICE void merge_partials_warp(const DecodeParams& p, int b, int h0, int lane) {
-  const int h = h0 + (lane >> 4), d0 = (lane & 15) * 8;
-  const float* base = p.ws + ((int64_t)b * p.n_slots * p.hq + h) * WS_ROW;
-  const int64_t sstride = (int64_t)p.hq * WS_ROW;
-  float M = NEG_INF;
-  for (int s = 0; s < p.n_slots; ++s) M = fmaxf(M, __ldcg(base + s * sstride + D));
-  float W = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < p.n_slots; ++s) {
-    const float ls = __ldcg(base + s * sstride + D);
-    if (ls == NEG_INF) continue;  // empty partial: its outputs were never written
-    const float w = exp2f(ls - M);
-    W += w;
-    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(base + s * sstride + d0));
-    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(base + s * sstride + d0 + 4));
-    acc[0] += w * v0.x; acc[1] += w * v0.y; acc[2] += w * v0.z; acc[3] += w * v0.w;
-    acc[4] += w * v1.x; acc[5] += w * v1.y; acc[6] += w * v1.z; acc[7] += w * v1.w;
-  }
-  const float inv = (W > 0.f) ? 1.f / W : 0.f;
-  uint4 r;
-  r.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-  r.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
-  r.z = pack_bf16x2(acc[4] * inv, acc[5] * inv);
-  r.w = pack_bf16x2(acc[6] * inv, acc[7] * inv);
-  *reinterpret_cast<uint4*>(p.out + ((int64_t)b * p.hq + h) * D + d0) = r;
-}
-
-// After the warp wrote its partials: lane i < 8 takes the ticket of sequence seq_i (-1 = none)
-// for this kv head; the holder of ticket n_slots - 1 saw every other slot published and
-// merges that sequence.
-QB_DEVICE void publish_and_merge_warp(const CascadeParams& cp, int kvh, int seq_i, int lane) {
-  const DecodeParams& p = cp.d;
-  __threadfence();
-  __syncwarp();
-  bool last = false;
-  if (lane < GMAX && seq_i >= 0) {
-    last = atomicAdd(cp.tickets + (int64_t)seq_i * p.hkv + kvh, 1) == p.n_slots - 1;
-    if (last) __threadfence();
-  }
-  unsigned todo = __ballot_sync(0xffffffffu, last);
-  while (todo) {
-    const int i = __ffs(todo) - 1;
-    todo &= todo - 1;
-    const int b = __shfl_sync(0xffffffffu, seq_i, i);
-    merge_partials_warp(p, b, kvh * 2, lane);
-    if (lane == 0) cp.tickets[(int64_t)b * p.hkv + kvh] = 0;
-  }
-}
-
-// Bounded wait on a ring slot; false (QB_DEVERR_TIMEOUT raised) if it did not complete.
-QB_DEVICE bool slot_wait(uint32_t bar, uint32_t parity, int* err) {
-  const long long t0 = clock64();
-  for (uint32_t i = 0;; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 255) == 255 && clock64() - t0 > WAIT_CYCLES) break;
-  }
-  qb_set_err(err, QB_DEVERR_TIMEOUT);
-  return false;
-}
-
-__global__ void __launch_bounds__(WD_WARPS * 32, 1)
-paged_decode_cascade_kernel(const __grid_constant__ CascadeParams cp) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const DecodeParams& p = cp.d;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, uint8_t* smem, int split, int kvh,
+                                  int grp) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  const int total = gridDim.x * WD_WARPS;
-  const int first = blockIdx.x * WD_WARPS + warp;
-  if (first >= cp.n_items) return;
-  // this warp's region: K/V slots, own-item query rows, ring mbarriers (1024-aligned base)
-  uint8_t* wsm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023) + warp * WD_WARP_BYTES;
-  const uint32_t wbase = smem_u32(wsm);
-  auto kv_addr = [&](int slot) { return wbase + slot * 2 * WD_KV_BYTES; };
-  auto q_addr = [&](int slot) { return wbase + WD_Q_OFF + slot * 2 * ROWB; };
-  auto bar_addr = [&](int slot) { return wbase + WD_BAR_OFF + slot * 8; };
-  if (lane == 0) {
-    for (int s = 0; s < WD_SLOTS; ++s) mbar_init(bar_addr(s), 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const int h0 = kvh * 2;
+  int mem = -1;  // lanes 0..GMAX-1: member `lane` of the group (-1 when absent)
+  if (lane < GMAX) {
+    mem = gp.members[grp * GMAX + lane];
+    if (mem >= gp.batch) {
+      qb_set_err(p.err, QB_DEVERR_SHAPE);
+      mem = -1;
+    }
+    if (mem < 0) mem = -1;
   }
-  __syncwarp();
+  const int leader = __shfl_sync(0xffffffffu, mem, 0);
+  const int tok_begin = split * p.split_tokens;
+  const int tok_end = leader < 0 ? 0 : min(gp.shared_len[grp], tok_begin + p.split_tokens);
+  if (tok_begin >= tok_end) {  // no shared keys in this split: empty partials
+    const int m = __shfl_sync(0xffffffffu, mem, (lane >> 1) & (GMAX - 1));
+    if (tid < 2 * GMAX && m >= 0) write_empty_partial(p, m, split, h0 + (tid & 1));
+    return;
+  }
+  const int n_stages = (tok_end - tok_begin + DEC_TOK - 1) / DEC_TOK;
 
-  // ---- load cursor (state kept by every lane; lane 0 issues the copies)
-  // Items are scheduled dynamically: each warp starts on item `first` (the shared items, the
-  // longest, come first) and then claims item total + atomicAdd(work[0], 1) whenever its loader
-  // moves on, so warps that drew long items take fewer.  The claim is issued one item ahead
-  // (its latency hides behind a whole item), and the next item's metadata and the next page id
-  // are read one step ahead so that their global-load latency never sits between two copies.
-  // The loader hands each item id to the consumer through a 4-entry queue in this warp's shared
-  // memory: it runs at most WD_SLOTS - 1 = 2 stages ahead and every item takes at least one
-  // stage, so at most 4 ids are live.  An id >= n_items ends the queue.
-  volatile int* queue = reinterpret_cast<volatile int*>(wsm + WD_QUEUE_OFF);
-  int l_item = first, l_stage = 0, l_flat = 0, l_k = 0;
-  Item l_it = decode_item(cp, l_item);
-  int claim = 0;  // lane 0: the claim in flight for the item after n_item
-  if (lane == 0) {
-    queue[0] = first;
-    claim = atomicAdd(cp.work, 1);
+  // Q as the A operand, rows g (member g/2) and g + 8 (member 4 + g/2), head h0 + g%2
+  uint32_t qa[8][4];
+  {
+    const int m0 = __shfl_sync(0xffffffffu, mem, g >> 1), m1 = __shfl_sync(0xffffffffu, mem, 4 + (g >> 1));
+    const bf16* q0 = p.q + ((int64_t)(m0 < 0 ? 0 : m0) * p.hq + h0 + (g & 1)) * D;
+    const bf16* q1 = p.q + ((int64_t)(m1 < 0 ? 0 : m1) * p.hq + h0 + (g & 1)) * D;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int c = kk * 16 + 2 * t4;
+      qa[kk][0] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+      qa[kk][1] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+      qa[kk][2] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+      qa[kk][3] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
   }
-  int n_item = total + __shfl_sync(0xffffffffu, claim, 0);
-  Item n_it = l_it;
-  if (n_item < cp.n_items) {
-    n_it = decode_item(cp, n_item);
-    if (lane == 0) claim = atomicAdd(cp.work, 1);
-  }
-  auto page_at = [&](const Item& it, int col) { return col < p.bt_stride ? it.btrow[col] : -1; };
-  int l_col = l_it.tok_begin / PAGE;
-  int l_page = page_at(l_it, l_col), l_page_nx = page_at(l_it, l_col + 1);
-  auto issue = [&]() {
-    if (l_item < cp.n_items) {
-      const int slot = l_flat % WD_SLOTS;
-      const bool kv = l_stage < l_it.n_stages;
-      const bool q = l_stage == 0 && !l_it.shared;
-      const int tok0 = l_it.tok_begin + l_stage * WD_TOK;
-      if (kv && tok0 / PAGE != l_col) {  // crossed into the next page: use the prefetched id
-        l_col = tok0 / PAGE;
-        l_page = l_page_nx;
-        l_page_nx = page_at(l_it, l_col + 1);
-      }
-      if (lane == 0) {
-        const uint32_t bar = bar_addr(slot);
-        mbar_expect_tx(bar, (kv ? 2 * WD_KV_BYTES : 0) + (q ? 2 * ROWB : 0));
-        if (kv) {
-          int page = l_page;
-          if (page < 0 || page >= p.num_blocks) {
-            qb_set_err(p.err, QB_DEVERR_PAGE);  // read page 0 instead; the result is flagged
-            page = 0;
-          }
-          const int row = page * PAGE + tok0 % PAGE;
-          const uint32_t kb = kv_addr(slot), vb = kb + WD_KV_BYTES;
-          tma_load_3d(kb, &cp.tk, 0, l_it.kvh, row, bar);
-          tma_load_3d(kb + 2048, &cp.tk, 64, l_it.kvh, row, bar);
-          tma_load_3d(vb, &cp.tv, 0, l_it.kvh, row, bar);
-          tma_load_3d(vb + 2048, &cp.tv, 64, l_it.kvh, row, bar);
-        }
-        if (q) tma_load_2d(q_addr(slot), &cp.tq, 0, l_it.idx * p.hq + l_it.kvh * 2, bar);
-      }
-      if (++l_stage >= max(1, l_it.n_stages)) {  // an empty item still takes one slot
-        l_stage = 0;
-        l_item = n_item;
-        l_it = n_it;
-        ++l_k;
-        if (lane == 0) queue[l_k & 3] = l_item;
-        if (l_item < cp.n_items) {
-          n_item = total + __shfl_sync(0xffffffffu, claim, 0);
-          if (n_item < cp.n_items) {
-            n_it = decode_item(cp, n_item);
-            if (lane == 0) claim = atomicAdd(cp.work, 1);
-          }
-        }
-        l_col = l_it.tok_begin / PAGE;
-        l_page = page_at(l_it, l_col);
-        l_page_nx = page_at(l_it, l_col + 1);
-      }
-      ++l_flat;  // counts armed slots only
+
+  const int32_t* btrow = p.bt + (int64_t)leader * p.bt_stride;
+  auto load_stage = [&](int s) {
+    const int buf = s % DEC_STAGES;
+    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
+    const uint32_t vbase = kbase + DEC_TOK * ROWB;
+    const int tok0 = tok_begin + s * DEC_TOK;
+    const bool col_ok = tok0 / PAGE < p.bt_stride;
+    int page = col_ok ? btrow[tok0 / PAGE] : -1;
+    const bool page_ok = page >= 0 && page < p.num_blocks;
+    if (!page_ok) {
+      if (tid == 0) qb_set_err(p.err, QB_DEVERR_PAGE);
+      page = 0;
+    }
+    const int64_t row0 = ((int64_t)page * PAGE + (tok0 % PAGE)) * p.hkv + kvh;
+#pragma unroll
+    for (int i = 0; i < (DEC_TOK * 16) / (DEC_WARPS * 32); ++i) {
+      const int idx = tid + i * DEC_WARPS * 32;
+      const int r = idx >> 4, c = idx & 15;
+      const bool ok = page_ok && (tok0 + r < tok_end);  // rows past the keys are zero-filled
+      const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
+      cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
+      cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
     }
   };
 #pragma unroll
-  for (int s = 0; s < WD_SLOTS - 1; ++s) issue();
+  for (int s = 0; s < DEC_STAGES - 1; ++s) {
+    if (s < n_stages) load_stage(s);
+    cp_async_commit();
+  }
 
-  int f = 0;                  // flat index of the stage being consumed
-  int f_slot = 0;             // its ring slot (f % WD_SLOTS)
-  uint32_t f_par = 0;         // its mbarrier phase parity ((f / WD_SLOTS) & 1)
-  auto next_stage = [&]() {
-    ++f;
-    if (++f_slot == WD_SLOTS) {
-      f_slot = 0;
-      f_par ^= 1;
-    }
-  };
-  bool ok = true;
-  for (int k = 0; ok; ++k) {
-    __syncwarp();  // the loader's queue write (lane 0) is visible to every lane
-    const int item = queue[k & 3];
-    if (item >= cp.n_items) break;
-    const Item it = decode_item(cp, item);
-    const int ns = max(1, it.n_stages);
-    const int h0 = it.kvh * 2;
-    if (it.shared) {
-      float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
-      float o[16][4];
+  float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
+  float o[16][4];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      // Q as the A operand, straight from global: a0/a2 row g, a1/a3 row g + 8
-      uint32_t qa[8][4];
-      {
-        const int m0 = group_member(cp, it.idx, g >> 1), m1 = group_member(cp, it.idx, 4 + (g >> 1));
-        const bf16* q0 = p.q + ((int64_t)(m0 < 0 ? 0 : m0) * p.hq + h0 + (g & 1)) * D;
-        const bf16* q1 = p.q + ((int64_t)(m1 < 0 ? 0 : m1) * p.hq + h0 + (g & 1)) * D;
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  const int wrow = warp * 16;
+  for (int s = 0; s < n_stages; ++s) {
+    if (s + DEC_STAGES - 1 < n_stages) load_stage(s + DEC_STAGES - 1);
+    cp_async_commit();
+    cp_async_wait<DEC_STAGES - 1>();
+    __syncthreads();
+    const int buf = s % DEC_STAGES;
+    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
+    const uint32_t vbase = kbase + DEC_TOK * ROWB;
+    const int key0 = tok_begin + s * DEC_TOK + wrow;
+    if (key0 < tok_end) {  // this warp's 16 tokens hold at least one key
+      // S[16 q x 16 tok] = Q K^T (two n-tiles of 8 tokens)
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const int c = kk * 16 + 2 * t4;
-          qa[kk][0] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
-          qa[kk][1] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
-          qa[kk][2] = m0 >= 0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
-          qa[kk][3] = m1 >= 0 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
-        }
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t r0, r1, r2, r3;
+        ldmatrix_x4(kbase + swz128(wrow + (lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2,
+                    r3);
+        mma_bf16_16816(sc[0], qa[kk], r0, r1);
+        mma_bf16_16816(sc[1], qa[kk], r2, r3);
       }
-      for (int s = 0; s < ns; ++s, next_stage()) {
-        issue();
-        const int slot = f_slot;
-        if (!slot_wait(bar_addr(slot), f_par, p.err)) {
-          ok = false;
-          break;
-        }
-        const uint32_t kbase = kv_addr(slot), vbase = kbase + WD_KV_BYTES;
-        if (s < it.n_stages) {
-          const int key0 = it.tok_begin + s * WD_TOK;
-          const int valid = it.tok_end - key0;  // rows of this stage that are keys
-          if (valid < WD_TOK) {  // zero the V rows past the keys (they may hold any bits)
-            for (int i = lane; i < (WD_TOK - valid) * 16; i += 32) {
-              const int r = valid + (i >> 4), c = i & 15;
-              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vbase + tsw(r, c)), "r"(0u) : "memory");
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-          }
-          // S[16 q x 16 tok] = Q K^T (two n-tiles of 8 tokens)
-          float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float mt[2] = {NEG_INF, NEG_INF};
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            uint32_t r0, r1, r2, r3;
-            ldmatrix_x4(kbase + tsw((lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)), r0, r1, r2, r3);
-            mma_bf16_16816(sc[0], qa[kk], r0, r1);
-            mma_bf16_16816(sc[1], qa[kk], r2, r3);
-          }
-          float mt[2] = {NEG_INF, NEG_INF};
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const int kc = key0 + nt * 8 + 2 * t4;
-            sc[nt][0] = kc < it.tok_end ? sc[nt][0] * p.scale_log2 : NEG_INF;
-            sc[nt][1] = kc + 1 < it.tok_end ? sc[nt][1] * p.scale_log2 : NEG_INF;
-            sc[nt][2] = kc < it.tok_end ? sc[nt][2] * p.scale_log2 : NEG_INF;
-            sc[nt][3] = kc + 1 < it.tok_end ? sc[nt][3] * p.scale_log2 : NEG_INF;
-            mt[0] = fmaxf(mt[0], fmaxf(sc[nt][0], sc[nt][1]));
-            mt[1] = fmaxf(mt[1], fmaxf(sc[nt][2], sc[nt][3]));
-          }
-          float alpha[2], mnew[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 1));
-            mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 2));
-            mnew[r] = fmaxf(m_run[r], mt[r]);
-            alpha[r] = (mnew[r] == NEG_INF) ? 1.f : exp2f(m_run[r] - mnew[r]);
-            m_run[r] = mnew[r];
-          }
-          uint32_t pa[4];
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const float p0 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][0] - mnew[0]);
-            const float p1 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][1] - mnew[0]);
-            const float p2 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][2] - mnew[1]);
-            const float p3 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][3] - mnew[1]);
-            rs[0] += p0 + p1;
-            rs[1] += p2 + p3;
-            pa[2 * nt] = pack_bf16x2(p0, p1);
-            pa[2 * nt + 1] = pack_bf16x2(p2, p3);
-          }
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-            l_run[r] = l_run[r] * alpha[r] + rs[r];
-          }
-          if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {  // a row's max moved
-#pragma unroll
-            for (int dt = 0; dt < 16; ++dt) {
-              o[dt][0] *= alpha[0];
-              o[dt][1] *= alpha[0];
-              o[dt][2] *= alpha[1];
-              o[dt][3] *= alpha[1];
-            }
-          }
-          // O[16 x 128] += P[16 x 16 tok] V[16 tok x 128]
-#pragma unroll
-          for (int dp = 0; dp < 8; ++dp) {
-            uint32_t r0, r1, r2, r3;
-            ldmatrix_x4_trans(vbase + tsw((lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1, r2,
-                              r3);
-            mma_bf16_16816(o[2 * dp], pa, r0, r1);
-            mma_bf16_16816(o[2 * dp + 1], pa, r2, r3);
-          }
-        }
-        __syncwarp();  // every lane is done with this slot before the next issue refills it
+      for (int nt = 0; nt < 2; ++nt) {
+        const int kc = key0 + nt * 8 + 2 * t4;
+        sc[nt][0] = kc < tok_end ? sc[nt][0] * p.scale_log2 : NEG_INF;
+        sc[nt][1] = kc + 1 < tok_end ? sc[nt][1] * p.scale_log2 : NEG_INF;
+        sc[nt][2] = kc < tok_end ? sc[nt][2] * p.scale_log2 : NEG_INF;
+        sc[nt][3] = kc + 1 < tok_end ? sc[nt][3] * p.scale_log2 : NEG_INF;
+        mt[0] = fmaxf(mt[0], fmaxf(sc[nt][0], sc[nt][1]));
+        mt[1] = fmaxf(mt[1], fmaxf(sc[nt][2], sc[nt][3]));
       }
-      if (!ok) break;
-      // partials of rows g (member g/2, head h0 + g%2) and g + 8 (member 4 + g/2)
-      const int mem_lane = lane < GMAX ? group_member(cp, it.idx, lane) : -1;
+      float alpha[2], mnew[2], rs[2] = {0.f, 0.f};
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const int row = g + 8 * r;
-        const int m = __shfl_sync(0xffffffffu, mem_lane, row >> 1);
-        if (m >= 0) {
-          const float inv = (l_run[r] > 0.f) ? 1.f / l_run[r] : 0.f;
-          float* wrow = p.ws + (((int64_t)m * p.n_slots + it.slot) * p.hq + h0 + (row & 1)) * WS_ROW;
-#pragma unroll
-          for (int dt = 0; dt < 16; ++dt)
-            *reinterpret_cast<float2*>(wrow + dt * 8 + 2 * t4) = make_float2(o[dt][2 * r] * inv, o[dt][2 * r + 1] * inv);
-          if (t4 == 0) wrow[D] = (l_run[r] > 0.f) ? m_run[r] + log2f(l_run[r]) : NEG_INF;
-        }
+        mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 1));
+        mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 2));
+        mnew[r] = fmaxf(m_run[r], mt[r]);
+        alpha[r] = (mnew[r] == NEG_INF) ? 1.f : exp2f(m_run[r] - mnew[r]);
+        m_run[r] = mnew[r];
       }
-      publish_and_merge_warp(cp, it.kvh, mem_lane, lane);
-    } else {
-      float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
-      float o[8][4];
+      uint32_t pa[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-      uint32_t qb[8][2];
-      for (int s = 0; s < ns; ++s, next_stage()) {
-        issue();
-        const int slot = f_slot;
-        if (!slot_wait(bar_addr(slot), f_par, p.err)) {
-          ok = false;
-          break;
-        }
-        const uint32_t kbase = kv_addr(slot), vbase = kbase + WD_KV_BYTES;
-        if (s == 0) {  // Q^T as the B operand: b0 = Q[h0+g][kk*16 + 2t4, +1], b1 = ... + 8
-          const uint8_t* qs = wsm + WD_Q_OFF + slot * 2 * ROWB;
-          const bool valid = g < 2;
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            qb[kk][0] = valid ? lds32(qs + g * ROWB + kk * 32 + 4 * t4) : 0u;
-            qb[kk][1] = valid ? lds32(qs + g * ROWB + kk * 32 + 16 + 4 * t4) : 0u;
-          }
-        }
-        if (s < it.n_stages) {
-          const int key0 = it.tok_begin + s * WD_TOK;
-          const int valid = it.tok_end - key0;
-          if (valid < WD_TOK) {  // zero the V rows past the keys (they may hold any bits)
-            for (int i = lane; i < (WD_TOK - valid) * 16; i += 32) {
-              const int r = valid + (i >> 4), c = i & 15;
-              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vbase + tsw(r, c)), "r"(0u) : "memory");
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-          }
-          // S^T[16 tok x 8] = K[16 x 128] * Q^T[128 x 8]; two accumulators halve the MMA chain
-          float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int kk = 0; kk < 8; kk += 2) {
-            uint32_t a[4], b[4];
-            ldmatrix_x4(kbase + tsw(lane & 15, kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
-            ldmatrix_x4(kbase + tsw(lane & 15, kk * 2 + 2 + (lane >> 4)), b[0], b[1], b[2], b[3]);
-            mma_bf16_16816(sc, a, qb[kk][0], qb[kk][1]);
-            mma_bf16_16816(sd, b, qb[kk + 1][0], qb[kk + 1][1]);
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) sc[i] += sd[i];
-          const int tokA = key0 + g;  // rows g and g+8
-          float x[4];
-          x[0] = (t4 == 0 && tokA < it.tok_end) ? sc[0] * p.scale_log2 : NEG_INF;
-          x[1] = (t4 == 0 && tokA < it.tok_end) ? sc[1] * p.scale_log2 : NEG_INF;
-          x[2] = (t4 == 0 && tokA + 8 < it.tok_end) ? sc[2] * p.scale_log2 : NEG_INF;
-          x[3] = (t4 == 0 && tokA + 8 < it.tok_end) ? sc[3] * p.scale_log2 : NEG_INF;
-          float mloc[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1)
-              mloc[h] = fmaxf(mloc[h], __shfl_xor_sync(0xffffffffu, mloc[h], off));
-            mloc[h] = __shfl_sync(0xffffffffu, mloc[h], 0);
-          }
-          float alpha[2], mnew[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            mnew[h] = fmaxf(m_run[h], mloc[h]);
-            alpha[h] = (mnew[h] == NEG_INF) ? 1.f : exp2f(m_run[h] - mnew[h]);
-          }
-          float pv[4];
-          pv[0] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[0] - mnew[0]);
-          pv[1] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[1] - mnew[1]);
-          pv[2] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[2] - mnew[0]);
-          pv[3] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[3] - mnew[1]);
-          float lsum[2] = {pv[0] + pv[2], pv[1] + pv[3]};
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1) lsum[h] += __shfl_xor_sync(0xffffffffu, lsum[h], off);
-            lsum[h] = __shfl_sync(0xffffffffu, lsum[h], 0);
-            l_run[h] = l_run[h] * alpha[h] + lsum[h];
-            m_run[h] = mnew[h];
-          }
-          if (alpha[0] != 1.f || alpha[1] != 1.f) {  // warp-uniform: the running max moved
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-              o[mt][0] *= alpha[0];
-              o[mt][1] *= alpha[1];
-              o[mt][2] *= alpha[0];
-              o[mt][3] *= alpha[1];
-            }
-          }
-          // P^T as the B operand: lane (g, t4) needs P[tok 2t4, 2t4+1, 2t4+8, 2t4+9][head g].
-          const int srcA = 8 * t4, srcB = 8 * t4 + 4;
-          const float a0 = __shfl_sync(0xffffffffu, pv[0], srcA), a1 = __shfl_sync(0xffffffffu, pv[1], srcA);
-          const float a2 = __shfl_sync(0xffffffffu, pv[2], srcA), a3 = __shfl_sync(0xffffffffu, pv[3], srcA);
-          const float c0 = __shfl_sync(0xffffffffu, pv[0], srcB), c1 = __shfl_sync(0xffffffffu, pv[1], srcB);
-          const float c2 = __shfl_sync(0xffffffffu, pv[2], srcB), c3 = __shfl_sync(0xffffffffu, pv[3], srcB);
-          uint32_t pb0 = 0u, pb1 = 0u;
-          if (g == 0) {
-            pb0 = pack_bf16x2(a0, c0);
-            pb1 = pack_bf16x2(a2, c2);
-          } else if (g == 1) {
-            pb0 = pack_bf16x2(a1, c1);
-            pb1 = pack_bf16x2(a3, c3);
-          }
-          // O^T[128 x 8] += V^T[128 x 16 tok] * P^T[16 tok x 8]
-#pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            uint32_t a[4];
-            ldmatrix_x4_trans(vbase + tsw((lane & 7) + ((lane >> 4) << 3), mt * 2 + ((lane >> 3) & 1)), a[0], a[1],
-                              a[2], a[3]);
-            mma_bf16_16816(o[mt], a, pb0, pb1);
-          }
-        }
-        __syncwarp();
+      for (int nt = 0; nt < 2; ++nt) {
+        const float p0 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][0] - mnew[0]);
+        const float p1 = (mnew[0] == NEG_INF) ? 0.f : exp2f(sc[nt][1] - mnew[0]);
+        const float p2 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][2] - mnew[1]);
+        const float p3 = (mnew[1] == NEG_INF) ? 0.f : exp2f(sc[nt][3] - mnew[1]);
+        rs[0] += p0 + p1;
+        rs[1] += p2 + p3;
+        pa[2 * nt] = pack_bf16x2(p0, p1);
+        pa[2 * nt + 1] = pack_bf16x2(p2, p3);
       }
-      if (!ok) break;
-      // partial: lanes with t4 == 0 hold O^T rows (dims) mt*16 + g and + 8 for both heads
-      if (t4 == 0) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float inv = (l_run[h] > 0.f) ? 1.f / l_run[h] : 0.f;
-          float* wrow = p.ws + (((int64_t)it.idx * p.n_slots + it.slot) * p.hq + h0 + h) * WS_ROW;
-#pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            wrow[mt * 16 + g] = o[mt][h] * inv;
-            wrow[mt * 16 + g + 8] = o[mt][2 + h] * inv;
-          }
-          if (g == 0) wrow[D] = (l_run[h] > 0.f) ? m_run[h] + log2f(l_run[h]) : NEG_INF;
-        }
+      for (int r = 0; r < 2; ++r) {
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+        rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+        l_run[r] = l_run[r] * alpha[r] + rs[r];
       }
-      publish_and_merge_warp(cp, it.kvh, lane == 0 ? it.idx : -1, lane);
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt) {
+        o[dt][0] *= alpha[0];
+        o[dt][1] *= alpha[0];
+        o[dt][2] *= alpha[1];
+        o[dt][3] *= alpha[1];
+      }
+      // O[16 x 128] += P[16 x 16 tok] V[16 tok x 128]
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t r0, r1, r2, r3;
+        ldmatrix_x4_trans(vbase + swz128(wrow + (lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)), r0, r1,
+                          r2, r3);
+        mma_bf16_16816(o[2 * dp], pa, r0, r1);
+        mma_bf16_16816(o[2 * dp + 1], pa, r2, r3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // Merge the four warps: smem [warp][16 rows][128] floats + m, l per (warp, row).
+  float* so = reinterpret_cast<float*>(smem);
+  float* sm = so + DEC_WARPS * 16 * D;
+  float* sl = sm + DEC_WARPS * 16;
+  __syncthreads();
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt) {
+    *reinterpret_cast<float2*>(so + (wrow + g) * D + dt * 8 + 2 * t4) = make_float2(o[dt][0], o[dt][1]);
+    *reinterpret_cast<float2*>(so + (wrow + g + 8) * D + dt * 8 + 2 * t4) = make_float2(o[dt][2], o[dt][3]);
+  }
+  if (t4 == 0) {
+    sm[wrow + g] = m_run[0];
+    sm[wrow + g + 8] = m_run[1];
+    sl[wrow + g] = l_run[0];
+    sl[wrow + g + 8] = l_run[1];
+  }
+  __syncthreads();
+  {
+    const int r = tid >> 3, d0 = (tid & 7) * 16;  // row r: member r/2, head h0 + r%2
+    const int b = __shfl_sync(0xffffffffu, mem, r >> 1);
+    float M = NEG_INF;
+#pragma unroll
+    for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    float L = 0.f, acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int w = 0; w < DEC_WARPS; ++w) {
+      const float mw = sm[w * 16 + r];
+      const float f = (mw == NEG_INF) ? 0.f : exp2f(mw - M);
+      L += sl[w * 16 + r] * f;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(so + (w * 16 + r) * D + d0 + i);
+        acc[i] += v.x * f;
+        acc[i + 1] += v.y * f;
+        acc[i + 2] += v.z * f;
+        acc[i + 3] += v.w * f;
+      }
+    }
+    if (b >= 0) {
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      float* wr = p.ws + (((int64_t)b * p.n_slots + split) * p.hq + h0 + (r & 1)) * WS_ROW;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<float4*>(wr + d0 + i) = make_float4(acc[i] * inv, acc[i + 1] * inv, acc[i + 2] * inv,
+                                                              acc[i + 3] * inv);
+      if ((tid & 7) == 0) wr[D] = (L > 0.f) ? M + log2f(L) : NEG_INF;
     }
   }
-  // Drain: the copies of every slot issued but not consumed complete before the warp leaves
-  // (bounded waits; after a timeout they are the copies that did not arrive in time).
-  for (; f < l_flat; next_stage()) {
-    const uint32_t bar = bar_addr(f_slot), parity = f_par;
-    const long long t0 = clock64();
-    while (!mbar_try(bar, parity))
-      if (clock64() - t0 > WAIT_CYCLES) break;
-  }
-  // The last warp to finish resets the claim counters for the next call: every other warp's
-  // claims precede its finishing increment (fenced), so no claim can follow the reset.
-  __syncwarp();
-  if (lane == 0) {
-    __threadfence();
-    const int active = min(total, cp.n_items);
-    if (atomicAdd(cp.work + 1, 1) == active - 1) {
-      cp.work[0] = 0;
-      cp.work[1] = 0;
-    }
+}
+
+__global__ void __launch_bounds__(DEC_WARPS * 32)
+paged_decode_grouped_kernel(DecodeParams p, GroupParams gp) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  int i = blockIdx.x;
+  if (i < gp.n_shared_ctas) {
+    const int split = i % gp.shared_splits;
+    i /= gp.shared_splits;
+    decode_shared_tile(p, gp, smem, split, i % p.hkv, i / p.hkv);
+  } else {
+    i -= gp.n_shared_ctas;
+    const int split = i % gp.own_splits;
+    i /= gp.own_splits;
+    decode_own_tile(p, smem, split, i % p.hkv, i / p.hkv);
   }
 }
 
@@ -1194,7 +874,7 @@ attn_bwd_dkdv_kernel(BwdParams p) {
   }
   const int key_g = k_start + warp * 16 + g;  // key index of rows g / g+8 in this warp
   for (int it = 0; it < n_it; ++it) {
-    const int h = kvh * group + it / nqt, q_start = q0 + (it % nqt) * 64;
+    const int q_start = q0 + (it % nqt) * 64;
     const int buf = it & 1;
     if (it + 1 < n_it) load_it(it + 1, buf ^ 1);  // the buffer read in iteration it - 1
     cp_async_commit();
@@ -1418,48 +1098,6 @@ attn_bwd_dq_kernel(BwdParams p) {
 
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// K or V cache of one layer, [num_blocks*256 tokens][hkv][128] bf16, as a 3-D TMA map
-// {128 dims, hkv, tokens}; box {64 dims, 1 head, 16 tokens}, 128-byte swizzle.
-bool cache_tmap(CUtensorMap* map, const void* base, int hkv, int64_t num_blocks) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)hkv, (cuuint64_t)num_blocks * PAGE};
-  cuuint64_t strides[2] = {(cuuint64_t)ROWB, (cuuint64_t)hkv * ROWB};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)WD_TOK};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// Queries [rows = batch*hq][128] bf16 as a 2-D TMA map; box {128, 2} (one kv head's two query
-// heads), no swizzle.
-bool query_tmap(CUtensorMap* map, const void* base, int64_t rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ROWB};
-  cuuint32_t box[2] = {(cuuint32_t)D, 2};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// SM count of the current device (cached per device).
-inline int device_sm_count() {
-  static int cache[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
-  if (cache[dev] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev] = n > 0 ? n : 148;
-  }
-  return cache[dev];
-}
-
 }  // namespace
 
 // ================================================================ C ABI
@@ -1501,9 +1139,8 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
 }
 
 extern "C" size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int Dh, int n_slots) {
-  // split-K partials, one int32 ticket per (sequence, head), then the two work-claim counters
-  // (padded to 16 bytes)
-  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float) + (size_t)batch * hq * sizeof(int32_t) + 16;
+  // split-K partials: n_slots per (sequence, head)
+  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float);
 }
 
 extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
@@ -1523,35 +1160,25 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
                al16(out) && bt_stride > 0);
   const int n_slots = shared_splits + own_splits;
   const int64_t n_shared = (int64_t)shared_splits * hkv * n_groups;
-  const int64_t n_items = n_shared + (int64_t)own_splits * hkv * batch;
-  QB_CHECK_ARG(n_items < (1ll << 30));
+  const int64_t n_ctas = n_shared + (int64_t)own_splits * hkv * batch;
+  QB_CHECK_ARG(n_ctas < (1ll << 31));
+  // shared splits fill slots [0, shared_splits), own splits the rest; n_slots >= 2, so every CTA
+  // writes a partial and the combine kernel produces the output
   DecodeParams d{(const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, num_blocks, block_tables, bt_stride,
                  seqlens, seqlen_add, hq, hkv, scale * LOG2E, split_tokens, n_slots, workspace, (bf16*)out, err,
                  n_slots, shared_splits, kv_start};
-  int* tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) +
-                                        (size_t)batch * n_slots * hq * WS_ROW * sizeof(float));
-  CascadeParams cp;
-  if (!cache_tmap(&cp.tk, k_cache, hkv, num_blocks) || !cache_tmap(&cp.tv, v_cache, hkv, num_blocks) ||
-      !query_tmap(&cp.tq, q, (int64_t)batch * hq))
-    return QB_ERR_UNSUPPORTED;
-  cp.d = d;
-  cp.members = group_members;
-  cp.shared_len = shared_len;
-  cp.batch = batch;
-  cp.shared_splits = shared_splits;
-  cp.own_splits = own_splits;
-  cp.n_shared_items = (int)n_shared;
-  cp.n_items = (int)n_items;
-  cp.tickets = tickets;
-  cp.work = tickets + (size_t)batch * hq;
+  GroupParams gp{group_members, shared_len, batch, shared_splits, own_splits, (int)n_shared};
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(paged_decode_cascade_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, WD_SMEM);
+    cudaFuncSetAttribute(paged_decode_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
     attr_set = true;
   }
-  // persistent: one CTA of WD_WARPS independent warps per SM
-  const int64_t grid = std::min<int64_t>((n_items + WD_WARPS - 1) / WD_WARPS, (int64_t)device_sm_count());
-  paged_decode_cascade_kernel<<<(unsigned)grid, WD_WARPS * 32, WD_SMEM, (cudaStream_t)stream>>>(cp);
+  paged_decode_grouped_kernel<<<(unsigned)n_ctas, DEC_WARPS * 32, DEC_SMEM, (cudaStream_t)stream>>>(d, gp);
+  int st = qb_launch_status();
+  if (st != QB_OK) return st;
+  const int wpb = 8;
+  paged_decode_combine_kernel<<<(unsigned)((batch * hq + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
+      d, batch);
   return qb_launch_status();
 }
 

@@ -337,7 +337,7 @@ class Qwen3Attention(nn.Module):
         if decode_plan is None:
             o = ops.paged_decode_attention(q, self.k_cache, self.v_cache, block_tables, context_lens, self.scale)
         elif decode_plan[0] == "grouped":
-            # prompt pages shared by G completions: read once per group (cascade attention)
+            # prompt pages shared by G completions: read once per group (shared-prefix decode)
             _, plan, ws, members, shared_len, kv_start = decode_plan
             return ops.paged_decode_attention_grouped(q, self.k_cache, self.v_cache, block_tables, context_lens,
                                                       self.scale, members, shared_len, kv_start, plan, workspace=ws,
@@ -858,9 +858,9 @@ class Qwen3ForCausalLM(nn.Module):
                 "err_host": torch.zeros(1, dtype=torch.int32, pin_memory=True), "err": ops.err_flag(dev)}
 
     def _grouped_launch(self, ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples):
-        """Enqueues one grouped-rollout step: a cascade-attention decode graph when only decode
+        """Enqueues one grouped-rollout step: a grouped-decode graph when only decode
         rows run, else one forward over the donors' prompt chunks (paged varlen attention) and
-        the decode rows (cascade attention); then lm_head + sampling (G draws from each finished
+        the decode rows (shared-prefix decode attention); then lm_head + sampling (G draws from each finished
         prefill's last row) and the read-back."""
         dev, temperature, top_k = ctx["dev"], ctx["temperature"], ctx["top_k"]
         r = None
@@ -869,11 +869,11 @@ class Qwen3ForCausalLM(nn.Module):
         if not prefill:
             if self._has_cuda_graphs:
                 r = self._run_decode_graph(decode_rows, step, ctx["seed"], groups=groups_rows)
-            if r is None:  # eager decode with the same cascade attention
+            if r is None:  # eager decode with the same shared-prefix attention
                 r = self._grouped_decode_eager(ctx, self._decode_arrays(decode_rows), groups_rows, step)
         else:
             # prefill rows (the donors' prompt chunks) on the paged varlen kernel; decode rows,
-            # whose keys skip the unused tail of the shared prompt page, on the cascade kernel
+            # whose keys skip the unused tail of the shared prompt page, on the grouped decode
             donors = [g.donor for g in prefill]
             (ids, pos, cu_q, cu_k, blk_map, bt, tiles), m_q, m_k = self._step_arrays(donors)
             tp = len(ids)
@@ -905,7 +905,7 @@ class Qwen3ForCausalLM(nn.Module):
         ctx["err_host"].copy_(ctx["err"], non_blocking=True)
 
     def _grouped_decode_eager(self, ctx, arrays, groups_rows, step):
-        """One grouped decode step without graphs (cascade attention); returns (tokens, logp) on the device."""
+        """One grouped decode step without graphs (shared-prefix attention); returns (tokens, logp) on the device."""
         dev = ctx["dev"]
         a = self.model.layers[0].self_attn
         ids, pos, cl, bt, slots = arrays
@@ -967,7 +967,7 @@ class Qwen3ForCausalLM(nn.Module):
     def generate_grouped_with_logprobs(self, prompt_ids_list, group_size, max_new_tokens=256, temperature=0.6,
                                        top_k=20, eos_token_ids=None):
         """GRPO rollout: ``group_size`` (<= 8) completions of every prompt, the prompt prefilled once
-        per group and its K/V pages shared (cascade decode attention reads them once per step).
+        per group and its K/V pages shared (the grouped decode attention reads them once per step).
 
         Returns the 4-tuple of :meth:`generate_continuous_with_logprobs` for the list in which each
         prompt is repeated ``group_size`` times consecutively.  Sampling and log-probs follow the same
@@ -1213,7 +1213,7 @@ class _Group:
 
 
 def _group_arrays(groups_rows, n_rows):
-    """(members [n_groups, 8], shared_len [n_groups], kv_start [n_rows]) int32 for the cascade kernel."""
+    """(members [n_groups, 8], shared_len [n_groups], kv_start [n_rows]) int32 for the grouped decode attention."""
     mem = np.full((len(groups_rows), 8), -1, dtype=np.int32)
     sl = np.zeros(len(groups_rows), dtype=np.int32)
     ks = np.zeros(n_rows, dtype=np.int32)

@@ -253,7 +253,7 @@ def test_fused_grpo_step_matches_autograd_path(setup, cuda):
 
 
 def test_grouped_rollout_teacher_forced(setup, cuda):
-    """Shared-prompt rollout (one prefill per group, cascade decode attention): greedy tokens and
+    """Shared-prompt rollout (one prefill per group, shared-prefix decode attention): greedy tokens and
     full-vocabulary log-probs match the oracle teacher-forced on the produced sequences."""
     cfg, params, model = setup
     g = torch.Generator().manual_seed(10)
@@ -289,7 +289,7 @@ def test_grouped_rollout_teacher_forced(setup, cuda):
 def test_grouped_rollout_mixed_steps(setup, cuda, graphs):
     """Prompts longer in total than one step's 2048-token budget: the last prompt's prefill
     runs in the same step as the other groups' first decode tokens (prefill rows on the paged
-    varlen kernel, decode rows on the cascade kernel, whose keys skip the unused tail of the
+    varlen kernel, decode rows on the grouped decode, whose keys skip the unused tail of the
     shared last prompt page).  Greedy tokens match the oracle teacher-forced; eager decode
     (graphs=False) and graph replay produce the same tokens."""
     cfg, params, model = setup
