@@ -68,167 +68,122 @@ QB_DEVICE void write_empty_partial(const DecodeParams& p, int b, int slot, int h
   p.ws[(((int64_t)b * p.n_slots + slot) * p.hq + h) * WS_ROW + D] = NEG_INF;
 }
 
-// One (split, kv head, sequence) work item of the per-sequence decode: keys
-// [kv_start[b] + split*split_tokens, +split_tokens) of sequence b.
-QB_DEVICE void decode_own_tile(const DecodeParams& p, uint8_t* smem, int split, int kvh, int b) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t4 = lane & 3;
-  const int len = p.seqlens[b] + p.seqlen_add;
-  const int tok_begin = (p.kv_start ? p.kv_start[b] : 0) + split * p.split_tokens;
-  // a 64-token stage must not straddle a page: the first key of a split is 64-aligned
-  const bool misaligned = (tok_begin & (DEC_TOK - 1)) != 0 || tok_begin < 0;
-  if (tok_begin >= len || misaligned) {
-    if (misaligned && tid == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
-    if (p.max_splits > 1) {
-      if (threadIdx.x < 2) write_empty_partial(p, b, p.slot_off + split, kvh * 2 + threadIdx.x);
-    } else {  // no keys at all (len <= 0): the output rows of both heads are zero
-      for (int i = tid; i < D; i += blockDim.x)
-        reinterpret_cast<uint32_t*>(p.out + ((int64_t)b * p.hq + kvh * 2) * D)[i] = 0u;
-    }
-    return;
-  }
-  const int tok_end = min(len, tok_begin + p.split_tokens);
-  const int n_stages = (tok_end - tok_begin + DEC_TOK - 1) / DEC_TOK;
-  const int h0 = kvh * 2;
-
-  // Q^T fragments: b0 = Q[h0+g][kk*16 + 2t4, +1], b1 = Q[h0+g][kk*16 + 2t4 + 8, +9].
-  uint32_t qb[8][2];
-  {
-    const bool valid = g < 2;
-    const bf16* qrow = p.q + ((int64_t)b * p.hq + h0 + (valid ? g : 0)) * D;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      qb[kk][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4) : 0u;
-      qb[kk][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4 + 8) : 0u;
-    }
-  }
-
+// Loads one 64-token stage of K and V for kv head kvh of sequence b (keys [tok0, tok0 + 64), rows
+// at or past tok_end zero-filled) into a stage buffer with 16-byte cp.async; a bad page id reads
+// nothing and raises QB_DEVERR_PAGE.
+QB_DEVICE void own_load_stage(const DecodeParams& p, uint32_t kbase, int b, int kvh, int tok0, int tok_end, int tid) {
+  const uint32_t vbase = kbase + DEC_TOK * ROWB;
   const int32_t* btrow = p.bt + (int64_t)b * p.bt_stride;
-  auto load_stage = [&](int s) {
-    const int buf = s % DEC_STAGES;
-    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
-    const uint32_t vbase = kbase + DEC_TOK * ROWB;
-    const int tok0 = tok_begin + s * DEC_TOK;
-    const bool col_ok = tok0 / PAGE < p.bt_stride;  // page-table row is bt_stride entries wide
-    int page = col_ok ? btrow[tok0 / PAGE] : -1;
-    bool page_ok = page >= 0 && page < p.num_blocks;
-    if (!page_ok) {
-      if (tid == 0) qb_set_err(p.err, QB_DEVERR_PAGE);
-      page = 0;
-    }
-    const int64_t row0 = ((int64_t)page * PAGE + (tok0 % PAGE)) * p.hkv + kvh;
-    // 64 rows x 16 chunks for K and for V: 2048 copies / 128 threads = 16 each.
-#pragma unroll
-    for (int i = 0; i < (DEC_TOK * 16) / (DEC_WARPS * 32); ++i) {
-      const int idx = tid + i * DEC_WARPS * 32;
-      const int r = idx >> 4, c = idx & 15;
-      const bool ok = page_ok && (tok0 + r < tok_end);
-      const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
-      cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
-      cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
-    }
-  };
-
-#pragma unroll
-  for (int s = 0; s < DEC_STAGES - 1; ++s) {
-    if (s < n_stages) load_stage(s);
-    cp_async_commit();
+  const bool col_ok = tok0 / PAGE < p.bt_stride;  // page-table row is bt_stride entries wide
+  int page = col_ok ? btrow[tok0 / PAGE] : -1;
+  const bool page_ok = page >= 0 && page < p.num_blocks;
+  if (!page_ok) {
+    if (tid == 0) qb_set_err(p.err, QB_DEVERR_PAGE);
+    page = 0;
   }
-
-  float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
-  float o[8][4];
+  const int64_t row0 = ((int64_t)page * PAGE + (tok0 % PAGE)) * p.hkv + kvh;
+  // 64 rows x 16 chunks for K and for V: 2048 copies / 128 threads = 16 each.
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-  for (int s = 0; s < n_stages; ++s) {
-    if (s + DEC_STAGES - 1 < n_stages) load_stage(s + DEC_STAGES - 1);
-    cp_async_commit();
-    cp_async_wait<DEC_STAGES - 1>();
-    __syncthreads();
-    const int buf = s % DEC_STAGES;
-    const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
-    const uint32_t vbase = kbase + DEC_TOK * ROWB;
-    const int wrow = warp * 16;
-
-    // S^T[16 tok x 8] = K[16 x 128] * Q^T[128 x 8]
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      uint32_t a[4];
-      ldmatrix_x4(kbase + swz128(wrow + (lane & 15), kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
-      mma_bf16_16816(sc, a, qb[kk][0], qb[kk][1]);
-    }
-    const int tokA = tok_begin + s * DEC_TOK + wrow + g;  // rows g and g+8
-    float x[4];
-    x[0] = (t4 == 0 && tokA < tok_end) ? sc[0] * p.scale_log2 : NEG_INF;
-    x[1] = (t4 == 0 && tokA < tok_end) ? sc[1] * p.scale_log2 : NEG_INF;
-    x[2] = (t4 == 0 && tokA + 8 < tok_end) ? sc[2] * p.scale_log2 : NEG_INF;
-    x[3] = (t4 == 0 && tokA + 8 < tok_end) ? sc[3] * p.scale_log2 : NEG_INF;
-    float mloc[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) mloc[h] = fmaxf(mloc[h], __shfl_xor_sync(0xffffffffu, mloc[h], off));
-      mloc[h] = __shfl_sync(0xffffffffu, mloc[h], 0);
-    }
-    float alpha[2], mnew[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mnew[h] = fmaxf(m_run[h], mloc[h]);
-      alpha[h] = (mnew[h] == NEG_INF) ? 1.f : exp2f(m_run[h] - mnew[h]);
-    }
-    float pv[4];
-    pv[0] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[0] - mnew[0]);
-    pv[1] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[1] - mnew[1]);
-    pv[2] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[2] - mnew[0]);
-    pv[3] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[3] - mnew[1]);
-    float lsum[2] = {pv[0] + pv[2], pv[1] + pv[3]};
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) lsum[h] += __shfl_xor_sync(0xffffffffu, lsum[h], off);
-      lsum[h] = __shfl_sync(0xffffffffu, lsum[h], 0);
-      l_run[h] = l_run[h] * alpha[h] + lsum[h];
-      m_run[h] = mnew[h];
-    }
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      o[mt][0] *= alpha[0];
-      o[mt][1] *= alpha[1];
-      o[mt][2] *= alpha[0];
-      o[mt][3] *= alpha[1];
-    }
-    // P^T as the B operand: lane (g, t4) needs P[tok 2t4, 2t4+1, 2t4+8, 2t4+9][head g].
-    const int srcA = 8 * t4, srcB = 8 * t4 + 4;
-    float a0 = __shfl_sync(0xffffffffu, pv[0], srcA), a1 = __shfl_sync(0xffffffffu, pv[1], srcA);
-    float a2 = __shfl_sync(0xffffffffu, pv[2], srcA), a3 = __shfl_sync(0xffffffffu, pv[3], srcA);
-    float c0 = __shfl_sync(0xffffffffu, pv[0], srcB), c1 = __shfl_sync(0xffffffffu, pv[1], srcB);
-    float c2 = __shfl_sync(0xffffffffu, pv[2], srcB), c3 = __shfl_sync(0xffffffffu, pv[3], srcB);
-    uint32_t pb0 = 0u, pb1 = 0u;
-    if (g == 0) {
-      pb0 = pack_bf16x2(a0, c0);
-      pb1 = pack_bf16x2(a2, c2);
-    } else if (g == 1) {
-      pb0 = pack_bf16x2(a1, c1);
-      pb1 = pack_bf16x2(a3, c3);
-    }
-    // O^T[128 x 8] += V^T[128 x 16 tok] * P^T[16 tok x 8]
-#pragma unroll
-    for (int mt = 0; mt < 8; ++mt) {
-      uint32_t a[4];
-      ldmatrix_x4_trans(vbase + swz128(wrow + (lane & 7) + ((lane >> 4) << 3), mt * 2 + ((lane >> 3) & 1)),
-                        a[0], a[1], a[2], a[3]);
-      mma_bf16_16816(o[mt], a, pb0, pb1);
-    }
-    __syncthreads();
+  for (int i = 0; i < (DEC_TOK * 16) / (DEC_WARPS * 32); ++i) {
+    const int idx = tid + i * DEC_WARPS * 32;
+    const int r = idx >> 4, c = idx & 15;
+    const bool ok = page_ok && (tok0 + r < tok_end);
+    const int64_t goff = (row0 + (int64_t)r * p.hkv) * D + c * 8;
+    cp_async_16(kbase + swz128(r, c), ok ? (const void*)(p.kc + goff) : (const void*)p.kc, ok ? 16 : 0);
+    cp_async_16(vbase + swz128(r, c), ok ? (const void*)(p.vc + goff) : (const void*)p.vc, ok ? 16 : 0);
   }
-  cp_async_wait<0>();
+}
 
-  // Merge the four warps: smem [warp][head][128] floats + m, l.
-  float* so = reinterpret_cast<float*>(smem);
+// One warp's share of a 64-token stage of an own-key tile: its 16 tokens (rows wrow.. of the
+// stage, keys tok_base + wrow + ...) against the kv head's two query heads.  S^T = K Q^T with the
+// tokens in the M dimension (the two heads fill 2 of the 8 N columns), online softmax, then
+// O^T += V^T P^T.
+QB_DEVICE void own_stage(const DecodeParams& p, uint32_t kbase, int wrow, int tok_base, int tok_end,
+                         const uint32_t (&qb)[8][2], float (&m_run)[2], float (&l_run)[2], float (&o)[8][4],
+                         int lane) {
+  const int g = lane >> 2, t4 = lane & 3;
+  const uint32_t vbase = kbase + DEC_TOK * ROWB;
+  // S^T[16 tok x 8] = K[16 x 128] * Q^T[128 x 8]
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    uint32_t a[4];
+    ldmatrix_x4(kbase + swz128(wrow + (lane & 15), kk * 2 + (lane >> 4)), a[0], a[1], a[2], a[3]);
+    mma_bf16_16816(sc, a, qb[kk][0], qb[kk][1]);
+  }
+  const int tokA = tok_base + wrow + g;  // rows g and g+8
+  float x[4];
+  x[0] = (t4 == 0 && tokA < tok_end) ? sc[0] * p.scale_log2 : NEG_INF;
+  x[1] = (t4 == 0 && tokA < tok_end) ? sc[1] * p.scale_log2 : NEG_INF;
+  x[2] = (t4 == 0 && tokA + 8 < tok_end) ? sc[2] * p.scale_log2 : NEG_INF;
+  x[3] = (t4 == 0 && tokA + 8 < tok_end) ? sc[3] * p.scale_log2 : NEG_INF;
+  float mloc[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) mloc[h] = fmaxf(mloc[h], __shfl_xor_sync(0xffffffffu, mloc[h], off));
+    mloc[h] = __shfl_sync(0xffffffffu, mloc[h], 0);
+  }
+  float alpha[2], mnew[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mnew[h] = fmaxf(m_run[h], mloc[h]);
+    alpha[h] = (mnew[h] == NEG_INF) ? 1.f : exp2f(m_run[h] - mnew[h]);
+  }
+  float pv[4];
+  pv[0] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[0] - mnew[0]);
+  pv[1] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[1] - mnew[1]);
+  pv[2] = (mnew[0] == NEG_INF) ? 0.f : exp2f(x[2] - mnew[0]);
+  pv[3] = (mnew[1] == NEG_INF) ? 0.f : exp2f(x[3] - mnew[1]);
+  float lsum[2] = {pv[0] + pv[2], pv[1] + pv[3]};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) lsum[h] += __shfl_xor_sync(0xffffffffu, lsum[h], off);
+    lsum[h] = __shfl_sync(0xffffffffu, lsum[h], 0);
+    l_run[h] = l_run[h] * alpha[h] + lsum[h];
+    m_run[h] = mnew[h];
+  }
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    o[mt][0] *= alpha[0];
+    o[mt][1] *= alpha[1];
+    o[mt][2] *= alpha[0];
+    o[mt][3] *= alpha[1];
+  }
+  // P^T as the B operand: lane (g, t4) needs P[tok 2t4, 2t4+1, 2t4+8, 2t4+9][head g].
+  const int srcA = 8 * t4, srcB = 8 * t4 + 4;
+  float a0 = __shfl_sync(0xffffffffu, pv[0], srcA), a1 = __shfl_sync(0xffffffffu, pv[1], srcA);
+  float a2 = __shfl_sync(0xffffffffu, pv[2], srcA), a3 = __shfl_sync(0xffffffffu, pv[3], srcA);
+  float c0 = __shfl_sync(0xffffffffu, pv[0], srcB), c1 = __shfl_sync(0xffffffffu, pv[1], srcB);
+  float c2 = __shfl_sync(0xffffffffu, pv[2], srcB), c3 = __shfl_sync(0xffffffffu, pv[3], srcB);
+  uint32_t pb0 = 0u, pb1 = 0u;
+  if (g == 0) {
+    pb0 = pack_bf16x2(a0, c0);
+    pb1 = pack_bf16x2(a2, c2);
+  } else if (g == 1) {
+    pb0 = pack_bf16x2(a1, c1);
+    pb1 = pack_bf16x2(a3, c3);
+  }
+  // O^T[128 x 8] += V^T[128 x 16 tok] * P^T[16 tok x 8]
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    uint32_t a[4];
+    ldmatrix_x4_trans(vbase + swz128(wrow + (lane & 7) + ((lane >> 4) << 3), mt * 2 + ((lane >> 3) & 1)), a[0],
+                      a[1], a[2], a[3]);
+    mma_bf16_16816(o[mt], a, pb0, pb1);
+  }
+}
+
+// Merges the four warps' (m, l, O) of an own-key tile through `scratch` (DEC_WARPS * 2 * (D + 2)
+// floats) and writes the result of sequence b, heads 2*kvh and 2*kvh + 1: the output itself when
+// max_splits == 1, else the split-K partial of slot slot_off + split.  Contains __syncthreads.
+QB_DEVICE void own_merge(const DecodeParams& p, float* scratch, int b, int kvh, int split, const float (&m_run)[2],
+                         const float (&l_run)[2], const float (&o)[8][4], int tid) {
+  const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+  float* so = scratch;
   float* sm = so + DEC_WARPS * 2 * D;
   float* sl = sm + DEC_WARPS * 2;
-  __syncthreads();
   if (t4 == 0) {
 #pragma unroll
     for (int mt = 0; mt < 8; ++mt) {
@@ -245,59 +200,138 @@ QB_DEVICE void decode_own_tile(const DecodeParams& p, uint8_t* smem, int split, 
     sl[warp * 2 + 1] = l_run[1];
   }
   __syncthreads();
+  const int h = tid >> 6;         // 0..1
+  const int d0 = (tid & 63) * 2;  // 2 dims per thread
+  float M = NEG_INF;
+#pragma unroll
+  for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, sm[w * 2 + h]);
+  float L = 0.f, acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+  for (int w = 0; w < DEC_WARPS; ++w) {
+    const float mw = sm[w * 2 + h];
+    const float f = (mw == NEG_INF) ? 0.f : exp2f(mw - M);
+    L += sl[w * 2 + h] * f;
+    acc0 += so[(w * 2 + h) * D + d0] * f;
+    acc1 += so[(w * 2 + h) * D + d0 + 1] * f;
+  }
+  const float inv = (L > 0.f) ? 1.f / L : 0.f;
+  if (p.max_splits == 1) {
+    bf16* orow = p.out + ((int64_t)b * p.hq + kvh * 2 + h) * D + d0;
+    *reinterpret_cast<uint32_t*>(orow) = pack_bf16x2(acc0 * inv, acc1 * inv);
+  } else {
+    float* wrow = p.ws + (((int64_t)b * p.n_slots + p.slot_off + split) * p.hq + kvh * 2 + h) * WS_ROW;
+    wrow[d0] = acc0 * inv;
+    wrow[d0 + 1] = acc1 * inv;
+    if (d0 == 0) wrow[D] = (L > 0.f) ? M + log2f(L) : NEG_INF;  // log2-domain LSE
+  }
+}
+
+// Key range of own-key item (split, sequence b): [kv_start[b] + split*split_tokens, +split_tokens)
+// clipped to the sequence length; false (and nothing to read) when it is empty or misaligned (a
+// 64-token stage must not straddle a page: the first key of a split is 64-aligned; SHAPE raised).
+QB_DEVICE bool own_range(const DecodeParams& p, int split, int b, int& tok_begin, int& tok_end, int tid) {
+  const int len = p.seqlens[b] + p.seqlen_add;
+  tok_begin = (p.kv_start ? p.kv_start[b] : 0) + split * p.split_tokens;
+  const bool misaligned = (tok_begin & (DEC_TOK - 1)) != 0 || tok_begin < 0;
+  if (misaligned && tid == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
+  tok_end = min(len, tok_begin + p.split_tokens);
+  return !misaligned && tok_begin < len;
+}
+
+// Result of an item with no keys: the empty partial (log2-domain LSE = -inf) of both heads, or
+// zero output rows when there are no split-K slots.
+QB_DEVICE void own_empty(const DecodeParams& p, int b, int kvh, int split, int tid) {
+  if (p.max_splits > 1) {
+    if (tid < 2) write_empty_partial(p, b, p.slot_off + split, kvh * 2 + tid);
+  } else {
+    for (int i = tid; i < D; i += DEC_WARPS * 32)
+      reinterpret_cast<uint32_t*>(p.out + ((int64_t)b * p.hq + kvh * 2) * D)[i] = 0u;
+  }
+}
+
+// One (split, kv head, sequence) work item of the per-sequence decode: keys
+// [kv_start[b] + split*split_tokens, +split_tokens) of sequence b, through STAGES stage buffers.
+template <int STAGES>
+QB_DEVICE void decode_own_tile(const DecodeParams& p, uint8_t* smem, int split, int kvh, int b) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  int tok_begin, tok_end;
+  if (!own_range(p, split, b, tok_begin, tok_end, tid)) {
+    own_empty(p, b, kvh, split, tid);
+    return;
+  }
+  const int n_stages = (tok_end - tok_begin + DEC_TOK - 1) / DEC_TOK;
+  const int h0 = kvh * 2;
+
+  // Q^T fragments: b0 = Q[h0+g][kk*16 + 2t4, +1], b1 = Q[h0+g][kk*16 + 2t4 + 8, +9].
+  uint32_t qb[8][2];
   {
-    const int h = tid >> 6;            // 0..1
-    const int d0 = (tid & 63) * 2;     // 2 dims per thread
-    float M = NEG_INF;
+    const bool valid = g < 2;
+    const bf16* qrow = p.q + ((int64_t)b * p.hq + h0 + (valid ? g : 0)) * D;
 #pragma unroll
-    for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, sm[w * 2 + h]);
-    float L = 0.f, acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-    for (int w = 0; w < DEC_WARPS; ++w) {
-      const float mw = sm[w * 2 + h];
-      const float f = (mw == NEG_INF) ? 0.f : exp2f(mw - M);
-      L += sl[w * 2 + h] * f;
-      acc0 += so[(w * 2 + h) * D + d0] * f;
-      acc1 += so[(w * 2 + h) * D + d0 + 1] * f;
-    }
-    const float inv = (L > 0.f) ? 1.f / L : 0.f;
-    if (p.max_splits == 1) {
-      bf16* orow = p.out + ((int64_t)b * p.hq + h0 + h) * D + d0;
-      *reinterpret_cast<uint32_t*>(orow) = pack_bf16x2(acc0 * inv, acc1 * inv);
-    } else {
-      float* wrow = p.ws + (((int64_t)b * p.n_slots + p.slot_off + split) * p.hq + h0 + h) * WS_ROW;
-      wrow[d0] = acc0 * inv;
-      wrow[d0 + 1] = acc1 * inv;
-      if (d0 == 0) wrow[D] = (L > 0.f) ? M + log2f(L) : NEG_INF;  // log2-domain LSE
+    for (int kk = 0; kk < 8; ++kk) {
+      qb[kk][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4) : 0u;
+      qb[kk][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + kk * 16 + 2 * t4 + 8) : 0u;
     }
   }
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < n_stages)
+      own_load_stage(p, smem_u32(smem + s * DEC_STAGE_BYTES), b, kvh, tok_begin + s * DEC_TOK, tok_end, tid);
+    cp_async_commit();
+  }
+  float m_run[2] = {NEG_INF, NEG_INF}, l_run[2] = {0.f, 0.f};
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int s = 0; s < n_stages; ++s) {
+    const int sn = s + STAGES - 1;
+    if (sn < n_stages)
+      own_load_stage(p, smem_u32(smem + (sn % STAGES) * DEC_STAGE_BYTES), b, kvh, tok_begin + sn * DEC_TOK,
+                     tok_end, tid);
+    cp_async_commit();
+    cp_async_wait<STAGES - 1>();
+    __syncthreads();
+    own_stage(p, smem_u32(smem + (s % STAGES) * DEC_STAGE_BYTES), warp * 16, tok_begin + s * DEC_TOK, tok_end,
+              qb, m_run, l_run, o, lane);
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  own_merge(p, reinterpret_cast<float*>(smem), b, kvh, split, m_run, l_run, o, tid);
 }
 
 __global__ void __launch_bounds__(DEC_WARPS * 32)
 paged_decode_kernel(DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  decode_own_tile(p, smem, blockIdx.x, blockIdx.y, blockIdx.z);
+  decode_own_tile<DEC_STAGES>(p, smem, blockIdx.x, blockIdx.y, blockIdx.z);
 }
 
-// One warp per (sequence, q head): weights w_s = 2^(lse_s - max lse).
+// One warp per (sequence, q head): weights w_s = 2^(lse_s - max lse).  Every lane reads the LSE of
+// slots lane, lane + 32, ... at once (one round trip instead of one per slot), then the slots'
+// outputs are accumulated four slots per step so their loads overlap.  Empty slots (LSE = -inf)
+// were never written: their outputs are not read.
 __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
   const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (item >= batch * p.hq) return;
   const int lane = threadIdx.x & 31;
   const int b = item / p.hq, h = item % p.hq;
-  // every slot of (b, h) was written by some CTA, empty ones with LSE = -inf
   const int ns = p.n_slots;
   const float* base = p.ws + ((int64_t)b * p.n_slots * p.hq + h) * WS_ROW;
   const int64_t sstride = (int64_t)p.hq * WS_ROW;
   float M = NEG_INF;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, base[s * sstride + D]);
+  for (int s = lane; s < ns; s += 32) M = fmaxf(M, base[s * sstride + D]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, W = 0.f;
+#pragma unroll 4
   for (int s = 0; s < ns; ++s) {
     const float ls = base[s * sstride + D];
-    if (ls == NEG_INF) continue;  // empty partial: its outputs were never written
-    const float w = exp2f(ls - M);
+    const bool live = ls != NEG_INF;
+    const float w = live ? exp2f(ls - M) : 0.f;
+    const float4 v = live ? *reinterpret_cast<const float4*>(base + s * sstride + lane * 4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
     W += w;
-    const float4 v = *reinterpret_cast<const float4*>(base + s * sstride + lane * 4);
     acc[0] += w * v.x; acc[1] += w * v.y; acc[2] += w * v.z; acc[3] += w * v.w;
   }
   const float inv = (W > 0.f) ? 1.f / W : 0.f;
@@ -318,7 +352,7 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
 //     pages of the group's first member, read once for the 2*G query heads of the kv head,
 //     which form the 16 rows of one M=16 MMA tile (row r: member r/2, head h0 + r%2);
 //   own CTA (split, kv head, sequence): decode_own_tile over keys [kv_start + split*S, ...).
-// Both stage 64 tokens of K and V per step with cp.async (three buffers), warp w on tokens
+// Both stage 64 tokens of K and V per step with cp.async (two buffers), warp w on tokens
 // [16w, 16w+16), and write one split-K partial per (sequence, head): shared splits to slots
 // [0, shared_splits), own splits after them.  paged_decode_combine_kernel merges the slots.
 constexpr int GMAX = 8;  // members per group at most (2 * GMAX = 16 query rows, one MMA M tile)
@@ -331,6 +365,7 @@ struct GroupParams {
   int n_shared_ctas;          // shared_splits * hkv * n_groups; the own CTAs follow
 };
 
+template <int STAGES>
 QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, uint8_t* smem, int split, int kvh,
                                   int grp) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -373,7 +408,7 @@ QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, 
 
   const int32_t* btrow = p.bt + (int64_t)leader * p.bt_stride;
   auto load_stage = [&](int s) {
-    const int buf = s % DEC_STAGES;
+    const int buf = s % STAGES;
     const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
     const uint32_t vbase = kbase + DEC_TOK * ROWB;
     const int tok0 = tok_begin + s * DEC_TOK;
@@ -396,7 +431,7 @@ QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, 
     }
   };
 #pragma unroll
-  for (int s = 0; s < DEC_STAGES - 1; ++s) {
+  for (int s = 0; s < STAGES - 1; ++s) {
     if (s < n_stages) load_stage(s);
     cp_async_commit();
   }
@@ -407,11 +442,11 @@ QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, 
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   const int wrow = warp * 16;
   for (int s = 0; s < n_stages; ++s) {
-    if (s + DEC_STAGES - 1 < n_stages) load_stage(s + DEC_STAGES - 1);
+    if (s + STAGES - 1 < n_stages) load_stage(s + STAGES - 1);
     cp_async_commit();
-    cp_async_wait<DEC_STAGES - 1>();
+    cp_async_wait<STAGES - 1>();
     __syncthreads();
-    const int buf = s % DEC_STAGES;
+    const int buf = s % STAGES;
     const uint32_t kbase = smem_u32(smem + buf * DEC_STAGE_BYTES);
     const uint32_t vbase = kbase + DEC_TOK * ROWB;
     const int key0 = tok_begin + s * DEC_TOK + wrow;
@@ -537,6 +572,11 @@ QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, 
   }
 }
 
+// Two stage buffers (64 KB): three CTAs per SM overlap one another's start-up latency, which
+// dominates the short own-key items of a decode step.
+constexpr int GRP_STAGES = 2;
+constexpr int GRP_SMEM = GRP_STAGES * DEC_STAGE_BYTES;
+
 __global__ void __launch_bounds__(DEC_WARPS * 32)
 paged_decode_grouped_kernel(DecodeParams p, GroupParams gp) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -544,12 +584,12 @@ paged_decode_grouped_kernel(DecodeParams p, GroupParams gp) {
   if (i < gp.n_shared_ctas) {
     const int split = i % gp.shared_splits;
     i /= gp.shared_splits;
-    decode_shared_tile(p, gp, smem, split, i % p.hkv, i / p.hkv);
+    decode_shared_tile<GRP_STAGES>(p, gp, smem, split, i % p.hkv, i / p.hkv);
   } else {
     i -= gp.n_shared_ctas;
     const int split = i % gp.own_splits;
     i /= gp.own_splits;
-    decode_own_tile(p, smem, split, i % p.hkv, i / p.hkv);
+    decode_own_tile<GRP_STAGES>(p, smem, split, i % p.hkv, i / p.hkv);
   }
 }
 
@@ -1170,10 +1210,10 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
   GroupParams gp{group_members, shared_len, batch, shared_splits, own_splits, (int)n_shared};
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(paged_decode_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM);
+    cudaFuncSetAttribute(paged_decode_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GRP_SMEM);
     attr_set = true;
   }
-  paged_decode_grouped_kernel<<<(unsigned)n_ctas, DEC_WARPS * 32, DEC_SMEM, (cudaStream_t)stream>>>(d, gp);
+  paged_decode_grouped_kernel<<<(unsigned)n_ctas, DEC_WARPS * 32, GRP_SMEM, (cudaStream_t)stream>>>(d, gp);
   int st = qb_launch_status();
   if (st != QB_OK) return st;
   const int wpb = 8;
