@@ -815,6 +815,117 @@ class Qwen3ForCausalLM(nn.Module):
         _lib.LAUNCHES[0] += n_kernels
         return self._graph_bufs["tokens"][:bs], self._graph_bufs["logp"][:bs]
 
+    # ---------------------------------------------------------------- non-paged generation modes
+    def _sample_rows(self, h, temperature, top_k, rng, step):
+        """One token per row of hidden states h: lm_head, then the sampler kernel (the reference's
+        logits / T -> top-k -> softmax -> multinomial as one pass); host ints."""
+        logits = ops.linear(h, self.lm_head.weight)
+        rng[0].fill_(step)
+        toks, _ = ops.sample(logits, temperature, top_k, 0, rng)
+        return toks.tolist()
+
+    def _new_rng(self):
+        seed = int(torch.randint(0, 2**62, (1,)).item())
+        return torch.tensor([0, seed], dtype=torch.int64, device=self.lm_head.weight.device)
+
+    def _recompute_step(self, seqs, temperature, top_k, rng, step):
+        """Packed forward over the full token lists ``seqs`` (dense varlen causal attention, no KV
+        cache) and one sampled token per sequence from its last position."""
+        dev = self.lm_head.weight.device
+        lens = [len(t) for t in seqs]
+        flat = np.fromiter((t for seq in seqs for t in seq), dtype=np.int64, count=sum(lens))
+        positions, cu, tiles = packed_meta(lens, dev)
+        h = self.model.forward_packed(torch.from_numpy(flat).to(dev), positions, cu, tiles)
+        return self._sample_rows(h.index_select(0, (cu[1:] - 1).long()), temperature, top_k, rng, step)
+
+    @torch.no_grad()
+    def generate_varlen(self, prompt_ids_list, max_new_tokens=256, temperature=0.6, top_k=20, eos_token_ids=None):
+        """Varlen batch generation without a KV cache (qwen3_naive.py:915-990): every step re-runs
+        the packed forward over each unfinished sequence's whole token list and samples one token
+        from its last position.  A sequence that samples an EOS keeps it and finishes.  Finished
+        sequences leave the batch (the reference recomputes them and drops the draws, which changes
+        no other sequence's result).  Returns (seq_tokens, generated) as lists of token-id lists."""
+        seq_tokens = [p[0].tolist() if isinstance(p, torch.Tensor) else list(p[0]) for p in prompt_ids_list]
+        generated = [[] for _ in seq_tokens]
+        eos = set(eos_token_ids) if eos_token_ids is not None else None
+        active = list(range(len(seq_tokens)))
+        rng = self._new_rng()
+        for step in range(max_new_tokens):
+            if not active:
+                break
+            toks = self._recompute_step([seq_tokens[i] for i in active], temperature, top_k, rng, step)
+            still = []
+            for i, t in zip(active, toks):
+                seq_tokens[i].append(t)
+                generated[i].append(t)
+                if eos is None or t not in eos:
+                    still.append(i)
+            active = still
+        ops.check_device_errors()
+        return seq_tokens, generated
+
+    @staticmethod
+    def _eos_hit(toks, eos_token_ids):
+        """The reference tests ``next_token.item() in eos_token_ids``: one row only."""
+        if eos_token_ids is None:
+            return False
+        if len(toks) != 1:
+            raise RuntimeError("EOS check reads a single sampled token (next_token.item()): batch size 1 only")
+        return toks[0] in eos_token_ids
+
+    @torch.no_grad()
+    def generate_naive(self, prompt, max_new_tokens=256, temperature=0.6, top_k=20, eos_token_ids=None):
+        """Autoregressive generation by full recomputation (qwen3_naive.py:892-913): prompt [B, L]
+        -> [B, L + n]; every step runs the whole sequences; an EOS stops generation before it is
+        appended."""
+        rows = prompt.tolist()
+        rng = self._new_rng()
+        for step in range(max_new_tokens):
+            toks = self._recompute_step(rows, temperature, top_k, rng, step)
+            if self._eos_hit(toks, eos_token_ids):
+                break
+            for r, t in zip(rows, toks):
+                r.append(t)
+        ops.check_device_errors()
+        return torch.tensor(rows, dtype=torch.long, device=prompt.device)
+
+    @torch.no_grad()
+    def generate_kvcache(self, prompt, max_new_tokens=256, temperature=0.6, top_k=20, eos_token_ids=None):
+        """Prefill once, then one decode step per token (qwen3_naive.py:842-889): prompt [B, L] ->
+        [B, L + n].  The reference's per-layer contiguous cache becomes a run of pages of the paged
+        pool for each row (prefill and decode on the paged kernels).  As in the reference, the first
+        sampled token is always appended and a later EOS stops generation before it is appended."""
+        dev = self.lm_head.weight.device
+        B, L = prompt.shape
+        pages = -(-(L + max_new_tokens) // self.BLOCK_SIZE)
+        self.allocate_global_kv_cache()
+        if self._num_blocks < B * pages:
+            raise ValueError(f"KV pool holds {self._num_blocks} pages; generate_kvcache needs {B * pages}")
+        bt = torch.arange(B * pages, dtype=torch.int32, device=dev).view(B, pages)
+        pos = torch.arange(L, dtype=torch.int64, device=dev)
+        slots = (bt[:, pos // self.BLOCK_SIZE].long() * self.BLOCK_SIZE + pos % self.BLOCK_SIZE).reshape(-1).int()
+        cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device=dev)
+        h = self.model.forward_prefill(prompt.to(dev).reshape(-1), pos.repeat(B), cu, cu, L, L, slots, bt)
+        rng = self._new_rng()
+        toks = self._sample_rows(h.index_select(0, (cu[1:] - 1).long()), temperature, top_k, rng, 0)
+        rows = prompt.tolist()
+        for r, t in zip(rows, toks):
+            r.append(t)
+        for step in range(max_new_tokens - 1):
+            p = L + step
+            ids = torch.tensor(toks, dtype=torch.long, device=dev)
+            positions = torch.full((B,), p, dtype=torch.int64, device=dev)
+            ctx = torch.full((B,), p, dtype=torch.int32, device=dev)  # keys already cached
+            slot = (bt[:, p // self.BLOCK_SIZE] * self.BLOCK_SIZE + p % self.BLOCK_SIZE).int()
+            h = self.model.forward_decode(ids, positions, ctx, bt, slot)
+            toks = self._sample_rows(h, temperature, top_k, rng, step + 1)
+            if self._eos_hit(toks, eos_token_ids):
+                break
+            for r, t in zip(rows, toks):
+                r.append(t)
+        ops.check_device_errors()
+        return torch.tensor(rows, dtype=torch.long, device=prompt.device)
+
     # ---------------------------------------------------------------- generation
     @torch.no_grad()
     def generate_continuous(self, prompt_ids_list, max_new_tokens=256, temperature=0.6, top_k=20,

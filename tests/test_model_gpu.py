@@ -354,6 +354,56 @@ def test_generation_reads_only_written_cache_slots(setup, cuda):
     assert run(float("nan")) == run(0.0)
 
 
+def _greedy_checked(params, cfg, toks, L):
+    """Positions of toks[L:] whose greedy choice the oracle confirms (top-2 logits more than bf16
+    noise apart); asserts every confirmed position matches.  Returns how many were confirmed."""
+    lg, _ = _oracle_lp(params, cfg, toks)
+    checked = 0
+    for t in range(L, len(toks)):
+        top2 = lg[t - 1].topk(2).values
+        if (top2[0] - top2[1]).item() > 0.05:
+            assert toks[t] == lg[t - 1].argmax().item(), (L, t)
+            checked += 1
+    return checked
+
+
+def test_non_paged_generation_modes(setup, cuda):
+    """generate_varlen (packed recompute), generate_naive (recompute) and generate_kvcache (prefill
+    + paged decode), qwen3_naive.py:842-990: greedy tokens match the oracle teacher-forced, and each
+    mode treats EOS as the reference does (naive: stop before appending; kvcache: the first token is
+    always appended, a later EOS stops before it; varlen: append, then the sequence finishes)."""
+    cfg, params, model = setup
+    g = torch.Generator().manual_seed(21)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, L), generator=g).to(cuda) for L in (5, 70, 260)]
+    seqs, gen = model.generate_varlen(prompts, max_new_tokens=12, top_k=1, temperature=1.0)
+    assert [len(x) for x in gen] == [12, 12, 12]
+    assert sum(_greedy_checked(params, cfg, t, p.shape[1]) for t, p in zip(seqs, prompts)) > 15
+    checked, naive = 0, []
+    for p in prompts:
+        out = model.generate_naive(p, max_new_tokens=12, top_k=1, temperature=1.0)
+        assert out.shape == (1, p.shape[1] + 12)
+        checked += _greedy_checked(params, cfg, out[0].tolist(), p.shape[1])
+        naive.append(out)
+    assert checked > 15
+    two = torch.cat([prompts[1], torch.randint(0, cfg.vocab_size, (1, 70), generator=g).to(cuda)])
+    out = model.generate_kvcache(two, max_new_tokens=12, top_k=1, temperature=1.0)
+    assert out.shape == (2, 82)
+    assert sum(_greedy_checked(params, cfg, row, 70) for row in out.tolist()) > 10
+    # EOS rules, each mode with its own first greedy token of prompts[0] as the EOS id
+    eos_n = naive[0][0, 5].item()
+    assert model.generate_naive(prompts[0], max_new_tokens=12, top_k=1, temperature=1.0,
+                                eos_token_ids=[eos_n]).shape == (1, 5)
+    eos_k = model.generate_kvcache(prompts[0], max_new_tokens=12, top_k=1, temperature=1.0)[0, 5].item()
+    kv = model.generate_kvcache(prompts[0], max_new_tokens=12, top_k=1, temperature=1.0, eos_token_ids=[eos_k])
+    assert kv[0, 5].item() == eos_k and eos_k not in kv[0, 6:].tolist()
+    eos_v = seqs[0][5]
+    _, g2 = model.generate_varlen(prompts, max_new_tokens=12, top_k=1, temperature=1.0, eos_token_ids=[eos_v])
+    assert g2[0] == [eos_v] and all(eos_v not in x[:-1] for x in g2[1:])
+    with pytest.raises(RuntimeError):
+        model.generate_naive(two, max_new_tokens=2, top_k=1, temperature=1.0, eos_token_ids=[eos_n])
+    ops.check_device_errors()
+
+
 def test_grpo_step_end_to_end(setup, cuda):
     cfg, params, model = setup
     ref = G.make_reference_copy(model)
