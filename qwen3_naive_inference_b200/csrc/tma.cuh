@@ -1,4 +1,4 @@
-// mbarrier and TMA helpers shared by the tcgen05 GEMM and the paged decode attention.
+// mbarrier and TMA helpers of the tcgen05 GEMM kernels.
 #pragma once
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -59,14 +59,6 @@ QB_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
-
-QB_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
 
