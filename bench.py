@@ -60,6 +60,8 @@ def parse():
                     help="eager decode launches (for launch-list profiling; ncu and graph replays do not mix)")
     ap.add_argument("--attn-only", action="store_true",
                     help="training attention forward + backward on one microbatch of the bench's sequences")
+    ap.add_argument("--loss-only", action="store_true",
+                    help="config 1: fused log-prob -> GRPO loss -> logit gradient over 1024 rows of logits")
     ap.add_argument("--kernel-profile", default=None, metavar="PATH",
                     help="after the timed steps, run one more step under torch.profiler (CUPTI kernel records) and "
                          "write per-kernel launches / device time / share to PATH")
@@ -599,6 +601,80 @@ def run_rollout_attn():
                                                "grouped_actual": kv_grouped / out["grouped"] / 1e6},
                                        "plan": case["plan"], "max_abs_diff": err}}), flush=True)
 
+def run_loss_only():
+    """Config 1 on one GPU: the fused log-prob -> GRPO loss -> logit-gradient pass over 1024 rows of
+    bf16 logits ~N(0,1) (2 prompts x G=4 x 128 tokens, vocab 151936; targets U[0,151643), rewards
+    Bernoulli(0.5), old/ref log-probs = current + N(0, 0.05), beta 0.04, clip 0.2, random tail
+    masks).  A timed pass is qb_logprob_fwd (fp32 log-sum-exp + gather), qb_grpo_loss (loss and
+    d loss / d logp) and qb_logprob_bwd (d logits in place), as in the training step's lm_head
+    chunks.  The backward overwrites the logits, so each pass starts from a fresh copy, followed by
+    an L2 flush, both outside the timed events.  Algorithmic minimum: read the logits once and
+    write their bf16 gradient once; this build reads them twice (forward, then backward)."""
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    N, S, V = 8, 128, 151936
+    g = torch.Generator(device=dev).manual_seed(1)
+    logits0 = torch.randn(N * S, V, device=dev, generator=g).to(torch.bfloat16)
+    work = torch.empty_like(logits0)
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    tgt = torch.randint(0, 151643, (N * S,), device=dev, generator=g)
+    dest = torch.arange(N * S, dtype=torch.int64, device=dev)
+    lens = torch.randint(1, S + 1, (N,), device=dev, generator=g)
+    mask = (torch.arange(S, device=dev)[None, :] < lens[:, None]).float()
+    rewards = torch.bernoulli(torch.full((N,), 0.5, device=dev), generator=g)
+    gids = torch.arange(N, device=dev) // 4
+    new_lp = torch.zeros(N, S, device=dev)
+    lse = torch.empty(N * S, device=dev)
+    grad = torch.zeros(N, S, device=dev)
+    loss = torch.zeros(3, device=dev)
+    L, err = ops.lib(), ops.err_flag(dev)
+    mask_total = ops.mask_sum(mask)
+
+    def fwd(x):
+        ops.check(L.qb_logprob_fwd(x.data_ptr(), N * S, V, x.stride(0), tgt.data_ptr(), dest.data_ptr(),
+                                   new_lp.data_ptr(), lse.data_ptr(), err.data_ptr(), ops.stream_ptr()),
+                  "qb_logprob_fwd")
+
+    work.copy_(logits0)
+    fwd(work)
+    old = new_lp + 0.05 * torch.randn(N, S, device=dev, generator=g)
+    ref = new_lp + 0.05 * torch.randn(N, S, device=dev, generator=g)
+
+    def step():
+        fwd(work)
+        ops.grpo_loss_raw(rewards, gids, new_lp, old, mask, ref_lp=ref, mask_total=mask_total, clip_eps=0.2,
+                          beta=0.04, row_begin=0, row_end=N, grad_new=grad, loss_out=loss)
+        ops.check(L.qb_logprob_bwd(work.data_ptr(), N * S, V, work.stride(0), tgt.data_ptr(), dest.data_ptr(),
+                                   lse.data_ptr(), grad.data_ptr(), err.data_ptr(), ops.stream_ptr()),
+                  "qb_logprob_bwd")
+
+    st = torch.cuda.current_stream()
+    total, n, warm = 0.0, 10, 3
+    for i in range(warm + n):
+        work.copy_(logits0)
+        loss.zero_()
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        step()
+        e1.record(st)
+        torch.cuda.synchronize()
+        if i >= warm:
+            total += e0.elapsed_time(e1)
+    ops.check_device_errors()
+    ms = total / n
+    alg = 2 * N * S * V * 2     # read the logits + write their gradient, once each
+    moved = 3 * N * S * V * 2   # this build: forward read, backward read + write
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    print(json.dumps({"loss_only": {"rows": N * S, "vocab": V, "ms": ms, "algorithmic_bytes": alg,
+                                    "achieved_gbs": alg / (ms / 1000) / 1e9, "frac_of_hbm": alg / (ms / 1000) / 1e9 / hbm,
+                                    "bytes_moved": moved, "moved_gbs": moved / (ms / 1000) / 1e9,
+                                    "loss": loss.tolist()}}), flush=True)
+
+
 GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
     "qkv_proj": (8192, 4096, 1024), "o_proj": (8192, 1024, 2048), "gate_up_proj": (8192, 6144, 1024),
     "down_proj": (8192, 1024, 3072), "lm_head": (4096, 151936, 1024), "qkv_decode512": (512, 4096, 1024),
@@ -708,6 +784,8 @@ def main():
         run_attn_only()
     elif args.gemm_only:
         run_gemm_only(args.gemm_shape)
+    elif args.loss_only:
+        run_loss_only()
     elif args.decode_only:
         run_decode_only(args.decode_batch)
     elif args.impl == "reference":
