@@ -13,6 +13,12 @@ Rewards are Bernoulli(0.5).  Under torchrun each rank runs its own 64 prompt gro
 steps AdamW on the global loss.  Inputs are synthetic (no dataset exists for this path).
 
 metric: GRPO step tokens/s = (prompt + completion tokens of all ranks) / step time.
+
+Kernel microbenchmarks (one GPU, each prints its own JSON line): --rollout-attn (decode attention
+mid-rollout, plain vs grouped layout), --decode-only (plain paged decode, config 3), --gemm-only
+(projection shapes, tcgen05 vs cuBLAS, graph-timed), --attn-only (training attention fwd/bwd),
+--loss-only (config 1: log-prob, GRPO loss and logit gradient); --kernel-profile PATH writes the
+per-kernel time of one step, split by phase.
 """
 from __future__ import annotations
 
