@@ -87,12 +87,14 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_gpu{index}.csv"
+        self.path = None
 
     def start(self):
+        import tempfile
         try:
-            self.path.parent.mkdir(exist_ok=True)
-            self.f = open(self.path, "w")
+            fd, name = tempfile.mkstemp(prefix=f"clocks_gpu{self.index}_", suffix=".csv")
+            self.path = Path(name)
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
@@ -109,7 +111,9 @@ class ClockSampler:
             self.proc.kill()
         self.f.close()
         rows = []
-        for line in self.path.read_text().splitlines():
+        text = self.path.read_text()
+        self.path.unlink()
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
                 rows.append(parts)

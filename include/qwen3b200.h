@@ -258,8 +258,11 @@ int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, const float* t
  *   - Scratch lives in a fixed device array inside this library (about 128 KiB, held by
  *     every GPU that loads the library until the process exits); n_rows above 16384 is
  *     rejected with QB_ERR_INVALID before anything runs.  Nothing is allocated.
- *   - The first call on a device looks up that array's device address (once per device,
- *     with the device current); make that first call before any stream capture.
+ *   - The first call on a device looks up that array's device address with the device
+ *     current, and again after the device's CUDA context changes (cudaDeviceReset);
+ *     make that first call before any stream capture.
+ *   - Arguments are checked as in qb_grpo_loss before the scratch or the stream is touched;
+ *     an empty row range returns QB_OK at once.
  *   - Every call reuses the same array and clears its 16-byte counter header on `stream`
  *     first; calls that overlap on the GPU (different streams, or another thread) race
  *     on it and must be serialised by the caller. */

@@ -12,6 +12,10 @@
 // write per-CTA partials to a caller workspace; the last CTA to finish (ticket
 // counter, no spinning) folds them in a fixed order, so results are
 // deterministic run to run.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -809,29 +813,56 @@ constexpr int64_t NOALLOC_MAX_ROWS = 16384;  // largest n_rows this variant acce
 constexpr size_t NOALLOC_SCRATCH_BYTES = ((16 + 2 * NOALLOC_MAX_ROWS * 4) + 255) / 256 * 256;
 static __device__ __align__(256) unsigned char g_grpo_scratch[NOALLOC_SCRATCH_BYTES];
 
-// The symbol's device address, looked up once per device (host code cannot use the
-// array's name as a device pointer).
+// The symbol's device address.  Host code cannot use the array's name as a device pointer, so
+// the address is looked up with cudaGetSymbolAddress, with the device current, the first time a
+// device calls in, and cached per device together with the CUDA context it belongs to: a call
+// under another context (after cudaDeviceReset, or on a context the caller made current) looks
+// the address up again instead of writing through a stale one.  A mutex orders the cache for
+// callers on several host threads.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  return fn;
+}
+
 void* noalloc_scratch_ptr(int* status) {
-  static void* ptrs[64] = {};
-  static bool ready[64] = {};
+  constexpr int MAX_DEVICES = 64;
+  static std::mutex mu;
+  static CUcontext ctxs[MAX_DEVICES] = {};
+  static void* ptrs[MAX_DEVICES] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+  if (e != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
     *status = e != cudaSuccess ? QB_ERR_CUDA_BASE + (int)e : QB_ERR_UNSUPPORTED;
     return nullptr;
   }
-  if (!ready[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_grpo_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      *status = QB_ERR_CUDA_BASE + (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-      return nullptr;
-    }
-    ptrs[dev] = p;
-    ready[dev] = true;
+  CtxGetCurrentFn get_ctx = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get_ctx && get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ctx != nullptr && ctxs[dev] == ctx && ptrs[dev] != nullptr) {
+    *status = QB_OK;
+    return ptrs[dev];
   }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_grpo_scratch);  // initialises the device's context if needed
+  if (e != cudaSuccess || p == nullptr) {
+    *status = QB_ERR_CUDA_BASE + (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+    return nullptr;
+  }
+  if (get_ctx && get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  ctxs[dev] = ctx;  // a null context is never matched above: the address is then looked up per call
+  ptrs[dev] = p;
   *status = QB_OK;
-  return ptrs[dev];
+  return p;
 }
 }  // namespace
 
@@ -840,7 +871,11 @@ extern "C" int qb_grpo_loss_noalloc(const float* rewards, const int64_t* group_i
                                     const float* ref_lp, const float* mask, const float* mask_total,
                                     float clip_eps, float beta, const float* grad_scale, float* grad_new,
                                     float* loss_out, float* adv_out, qb_stream_t stream) {
+  // The same argument checks as qb_grpo_loss, before the shared scratch or the stream is touched.
+  QB_CHECK_ARG(n_rows >= 0 && S >= 0 && row_begin >= 0 && row_end <= n_rows && row_begin <= row_end);
   if (n_rows > NOALLOC_MAX_ROWS) return QB_ERR_INVALID;  // the fixed scratch holds at most this many rows
+  if (row_end == row_begin) return QB_OK;
+  QB_CHECK_ARG(rewards && group_ids && new_lp && old_lp && mask);
   int st = QB_OK;
   void* ws = noalloc_scratch_ptr(&st);
   if (!ws) return st;

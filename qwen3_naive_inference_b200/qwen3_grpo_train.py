@@ -5,7 +5,7 @@ Reference functions kept with their signatures and semantics:
   compute_grpo_advantage                           (:162-173)
   ppo_clipped_loss                                 (:184-199)
   grpo_train_step                                  (:261-286)
-  rollout_batch                                    (:212-258, on the paged generator)
+  rollout_single, rollout_batch, compute_reward    (:69-151, :212-258, on the paged generator)
 
 Extensions (off by default, so defaults equal the reference):
   * ``ref_log_probs`` / ``beta``: k3 KL to a frozen reference policy;
@@ -284,15 +284,53 @@ def grpo_train_step(model, optimizer, input_ids, old_log_probs, response_mask, r
 
 
 # ---------------------------------------------------------------- rollout
+def compute_reward(response_text: str) -> float:
+    """The reference's placeholder reward (qwen3_grpo_train.py:141-151): 1.0 when the decoded
+    response has more than 5 non-blank characters, else 0.0."""
+    return 1.0 if len(response_text.strip()) > 5 else 0.0
+
+
+def _reward(tokenizer, completion, reward_fn):
+    if reward_fn is not None:
+        return float(reward_fn(completion))
+    if tokenizer is None:  # no tokenizer: the same rule on the completion's token count
+        return 1.0 if len(completion) > 5 else 0.0
+    return compute_reward(tokenizer.decode(completion, skip_special_tokens=True))
+
+
 @torch.no_grad()
-def rollout_batch(model, prompts, *, n_rollout=N_ROLLOUT, max_new_tokens=MAX_RESPONSE_LEN,
+def rollout_single(model, prompt_ids, tokenizer=None, *, max_new_tokens=MAX_RESPONSE_LEN,
+                   temperature=TEMPERATURE, top_k=TOP_K, eos_token_ids=(EOS_TOKEN_ID, BOS_TOKEN_ID)):
+    """One completion of ``prompt_ids`` [1, L] with each sampled token's log-prob
+    (qwen3_grpo_train.py:69-120): returns input_ids [1, T] (prompt + response, the stop token
+    included), old_log_probs [T] (0 on the prompt, the token's sampling log-prob at its own
+    position) and response_mask [T].  Runs on the paged generator; ``tokenizer`` is accepted
+    for signature compatibility (the reference does not use it here either)."""
+    dev = model.lm_head.weight.device
+    seq_tokens, _gen, lps, plens = model.generate_continuous_with_logprobs(
+        [prompt_ids], max_new_tokens=max_new_tokens, temperature=temperature, top_k=top_k,
+        eos_token_ids=list(eos_token_ids) if eos_token_ids else None)
+    toks, lp, pl = seq_tokens[0], lps[0], plens[0]
+    T = len(toks)
+    old = torch.zeros(T)
+    mask = torch.zeros(T)
+    old[pl:pl + len(lp)] = torch.tensor(lp)
+    mask[pl:pl + len(lp)] = 1.0
+    return torch.tensor([toks], dtype=torch.long).to(dev), old.to(dev), mask.to(dev)
+
+
+@torch.no_grad()
+def rollout_batch(model, tokenizer, prompts, *, n_rollout=N_ROLLOUT, max_new_tokens=MAX_RESPONSE_LEN,
                   temperature=TEMPERATURE, top_k=TOP_K, eos_token_ids=(EOS_TOKEN_ID, BOS_TOKEN_ID),
                   reward_fn=None):
-    """n_rollout completions per prompt on the paged generator, padded like the reference's
-    rollout_batch (qwen3_grpo_train.py:212-258): input_ids [B, L] (0-padded), old_log_probs and
+    """``n_rollout`` completions per prompt, padded like the reference's rollout_batch
+    (qwen3_grpo_train.py:212-258): input_ids [B, L] (0-padded), old_log_probs and
     response_mask [B, L] with each response token's sampling log-prob at its own position,
-    rewards [B] and prompt_ids [B].  ``reward_fn(prompt_tokens, completion_tokens) -> float``
-    replaces the tokenizer-based reward (default: 1.0 when the completion has > 5 tokens)."""
+    rewards [B] and prompt_ids [B].  All completions run in one batch on the paged generator
+    instead of one reference rollout_single call each.  Rewards: ``compute_reward`` of the
+    completion decoded by ``tokenizer`` (special tokens skipped), as the reference; with
+    ``tokenizer=None`` the same rule on the completion's token count; ``reward_fn(completion
+    token ids) -> float`` overrides both."""
     expanded, pid = [], []
     for i, p in enumerate(prompts):
         for _ in range(n_rollout):
@@ -301,7 +339,6 @@ def rollout_batch(model, prompts, *, n_rollout=N_ROLLOUT, max_new_tokens=MAX_RES
     seq_tokens, gen, lps, plens = model.generate_continuous_with_logprobs(
         expanded, max_new_tokens=max_new_tokens, temperature=temperature, top_k=top_k,
         eos_token_ids=list(eos_token_ids) if eos_token_ids else None)
-    reward_fn = reward_fn or (lambda p, c: 1.0 if len(c) > 5 else 0.0)
     dev = model.lm_head.weight.device
     B, Lmax = len(seq_tokens), max(len(t) for t in seq_tokens)
     ids = torch.zeros(B, Lmax, dtype=torch.long)
@@ -311,7 +348,7 @@ def rollout_batch(model, prompts, *, n_rollout=N_ROLLOUT, max_new_tokens=MAX_RES
         ids[i, :len(t)] = torch.tensor(t)
         old[i, pl:pl + len(lp)] = torch.tensor(lp)
         mask[i, pl:pl + len(lp)] = 1.0
-    rewards = torch.tensor([reward_fn(t[:pl], g) for t, g, pl in zip(seq_tokens, gen, plens)])
+    rewards = torch.tensor([_reward(tokenizer, g, reward_fn) for g in gen])
     return ids.to(dev), old.to(dev), mask.to(dev), rewards.to(dev), torch.tensor(pid, device=dev)
 
 

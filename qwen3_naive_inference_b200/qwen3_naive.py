@@ -1639,3 +1639,27 @@ def load_weights(model, checkpoint_path):
                     break
             else:
                 model.get_parameter(name).data.copy_(t)
+
+
+def tokenize(text, tokenizer, device=None):
+    """One user turn in the tokenizer's chat template, generation prompt appended, encoded to a
+    [1, L] int64 tensor (test_prefix_cache.py:37-43, test_chunked_prefill.py:38-44,
+    qwen3_grpo_train.py:317-324)."""
+    messages = [{"role": "user", "content": text}]
+    formatted = tokenizer.apply_chat_template(messages, tokenize=False, add_generation_prompt=True)
+    ids = tokenizer.encode(formatted, return_tensors="pt")
+    return ids.to(device) if device is not None else ids
+
+
+def load_model_and_tokenizer(model_path, device="cuda"):
+    """Tokenizer, config and weights of a Qwen3 checkpoint directory (config.json,
+    model.safetensors and the tokenizer files), as test_prefix_cache.py:22-35 loads them.
+    Returns (model, tokenizer, config)."""
+    from pathlib import Path
+
+    from transformers import AutoTokenizer
+    tokenizer = AutoTokenizer.from_pretrained(model_path)
+    config = Qwen3Config.from_json(str(Path(model_path) / "config.json"))
+    model = build_model(config, device=device, seed=None)
+    load_weights(model, str(Path(model_path) / "model.safetensors"))
+    return model, tokenizer, config

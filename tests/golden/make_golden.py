@@ -34,7 +34,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QWEN3_REFERENCE", "/root/reference"))
+if len(sys.argv) != 2 or not (Path(sys.argv[1]) / "qwen3_naive.py").is_file():
+    sys.exit("usage: python tests/golden/make_golden.py <reference checkout holding qwen3_naive.py>")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(HERE.parents[1]))
 
