@@ -17,8 +17,11 @@ metric: GRPO step tokens/s = (prompt + completion tokens of all ranks) / step ti
 Kernel microbenchmarks (one GPU, each prints its own JSON line): --rollout-attn (decode attention
 mid-rollout, plain vs grouped layout), --decode-only (plain paged decode, config 3), --gemm-only
 (projection shapes, tcgen05 vs cuBLAS, graph-timed), --attn-only (training attention fwd/bwd),
---loss-only (config 1: log-prob, GRPO loss and logit gradient); --kernel-profile PATH writes the
-per-kernel time of one step, split by phase.
+--loss-only (config 1: log-prob, GRPO loss and logit gradient, with the config-1 CPU baseline),
+--rollout-only (config 2: the grouped rollout alone, with its roofline and a CPU baseline);
+--kernel-profile PATH writes the per-kernel time of one step, split by phase.  The main line also
+carries the whole-step roofline fraction and the dominant kernel's in-step bandwidth, measured on
+one extra untimed step under CUPTI (--no-inner-profile skips it).
 """
 from __future__ import annotations
 
@@ -71,6 +74,10 @@ def parse():
     ap.add_argument("--kernel-profile", default=None, metavar="PATH",
                     help="after the timed steps, run one more step under torch.profiler (CUPTI kernel records) and "
                          "write per-kernel launches / device time / share to PATH")
+    ap.add_argument("--rollout-only", action="store_true",
+                    help="config 2: the grouped rollout alone (generated tokens/s, rollout roofline, CPU baseline)")
+    ap.add_argument("--no-inner-profile", action="store_true",
+                    help="skip the extra untimed step under CUPTI that measures the dominant kernel inside the step")
     ap.add_argument("--no-share-prefix", action="store_true",
                     help="roll out with the reference's scheduler (every completion prefilled and stored)")
     return ap.parse_args()
@@ -242,6 +249,84 @@ def cpu_baseline_sample(steps=1, threads=None):
     return tok_total / t_total, sample, torch.get_num_threads()
 
 
+# ------------------------------------------------------------------------------ whole-step roofline
+H, I, HQ, HKV, D, VOCAB = 1024, 3072, 16, 8, 128, 151936
+LAYER_PARAMS = (HQ + 2 * HKV) * D * H + H * HQ * D + 2 * I * H + H * I  # qkv, o, gate_up, down
+LM_HEAD_PARAMS = VOCAB * H
+KV_BYTES_PER_KEY_LAYER = 2 * HKV * D * 2                               # K and V, bf16
+
+
+def step_roofline(prompt_lens, group, new, layers, step_s, peaks):
+    """Roofline time of one GRPO step of this rank's workload, phase by phase: each phase costs
+    max(FLOP / tensor peak, bytes / HBM peak) at the sustained measured peaks, summed; the
+    fraction is that sum over the measured step time.  FLOPs are 2 per weight per token for
+    every projection (lm_head only where a token is scored or sampled) plus the causal attention
+    products; rollout bytes are the weights and the K/V each decode step must read (each group's
+    prompt once, every completion's own tokens)."""
+    tf = peaks.get("bf16_tflops_sustained", 1404.4) * 1e12
+    bw = peaks.get("hbm_gbs", 6539.5) * 1e9
+    lin = 2 * LAYER_PARAMS * layers
+    attn = lambda q_pairs: 4 * HQ * D * layers * q_pairs  # QK^T and PV over (query, key) pairs
+    # rollout: prefill of each prompt once (grouped), then `new` decode steps of every completion
+    pre_flop = sum(lin * L + attn(L * (L + 1) / 2) + 2 * LM_HEAD_PARAMS for L in prompt_lens)
+    t_roll = pre_flop / tf
+    weights = 2 * (LAYER_PARAMS * layers + LM_HEAD_PARAMS)
+    B = len(prompt_lens) * group
+    for s in range(new - 1):
+        keys_read = sum(prompt_lens) + B * (s + 1)  # shared prompts once + each completion's own keys
+        ctx_total = sum(L + s + 1 for L in prompt_lens) * group
+        flop = B * (lin + 2 * LM_HEAD_PARAMS) + attn(ctx_total)
+        byts = weights + keys_read * KV_BYTES_PER_KEY_LAYER * layers
+        t_roll += max(flop / tf, byts / bw)
+    # log-prob recompute (frozen reference) and the policy's forward + backward, packed sequences
+    seqs = [L + new for L in prompt_lens for _ in range(group)]
+    tokens = sum(seqs)
+    scored = B * new
+    fwd = lin * tokens + 2 * LM_HEAD_PARAMS * scored + attn(sum(L * (L + 1) / 2 for L in seqs))
+    attn_fwd = attn(sum(L * (L + 1) / 2 for L in seqs))
+    t_ref = fwd / tf
+    t_train = (3 * (fwd - attn_fwd) + 3.5 * attn_fwd) / tf  # backward: 2x the projections, 2.5x attention
+    total = t_roll + t_ref + t_train
+    return {"rollout_s": t_roll, "ref_logprob_s": t_ref, "train_s": t_train, "total_s": total,
+            "measured_s": step_s, "frac": total / step_s,
+            "peaks": {"bf16_tflops_sustained": tf / 1e12, "hbm_gbs": bw / 1e9},
+            "basis": "sum over phases of max(FLOP/peak, bytes/peak); decode steps HBM-bound, the rest tensor-bound"}
+
+
+def in_step_kernel_profile(torch, run_step):
+    """Device time per kernel name over one GRPO step (CUPTI records via torch.profiler, graph
+    replays included).  Returns ({name: (launches, total_us)}, step outputs)."""
+    from collections import defaultdict
+
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        out = run_step()
+        torch.cuda.synchronize()
+    agg = defaultdict(lambda: [0, 0.0])
+    for e in prof.events():
+        if str(getattr(e, "device_type", "")).endswith("CUDA"):
+            name = e.name
+            for pre in ("void ", "(anonymous namespace)::", "<unnamed>::"):
+                name = name.replace(pre, "")
+            name = name.split("(")[0].split("<")[0]
+            agg[name][0] += 1
+            agg[name][1] += e.time_range.elapsed_us()
+    return dict(agg), out
+
+
+def grouped_decode_alg_bytes(prompt_lens, group, new, layers):
+    """Algorithmic bytes of every grouped decode attention call of one rollout: per layer and
+    decode step, each group's prompt K/V once and each completion's own keys, plus q, out and
+    the page tables (as in rollout_attn_case)."""
+    B = len(prompt_lens) * group
+    total = 0
+    for s in range(new - 1):
+        keys = sum(prompt_lens) + B * (s + 1)
+        total += keys * KV_BYTES_PER_KEY_LAYER + 2 * B * HQ * D * 2 + B * 4 * (4 + 2)
+    return total * layers
+
+
 # ------------------------------------------------------------------------------ arms
 def run_reference(args):
     """CPU baseline arm: the oracle port of the reference's GRPO step on the host cores."""
@@ -351,6 +436,36 @@ def run_ours(args):
     sampler.start()
     ms, tokens, wall, launches, _, _, last = timed(args.steps, host_inputs=False)
     clocks = sampler.stop()
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    # whole-step roofline of the timed steps (this rank's workload; the time is the max over ranks)
+    roof_s = 0.0
+    for j in range(args.steps):
+        lens = [p.shape[1] for p in make_prompts(args, rank, 100 + j)]
+        roof_s += step_roofline(lens, args.group, args.new_tokens, args.layers, 1.0, peaks)["total_s"]
+    whole_step = step_roofline([p.shape[1] for p in make_prompts(args, rank, 100)], args.group, args.new_tokens,
+                               args.layers, ms / 1000.0 / args.steps, peaks)
+    whole_step["frac"] = roof_s / (ms / 1000.0)
+    whole_step["total_s_all_timed_steps"] = roof_s
+    # the dominant kernel inside the step: one more (untimed) step under CUPTI; every rank runs it
+    in_step = None
+    if not args.no_inner_profile:
+        prof_prompts = make_prompts(args, rank, 300, dev)
+        agg, _ = in_step_kernel_profile(torch, lambda: step(0, prof_prompts))
+        if rank == 0 and "paged_decode_grouped_kernel" in agg:
+            n_g, us_g = agg["paged_decode_grouped_kernel"]
+            n_c, us_c = agg.get("paged_decode_combine_kernel", (0, 0.0))
+            alg = grouped_decode_alg_bytes([p.shape[1] for p in prof_prompts], args.group, args.new_tokens,
+                                           args.layers)
+            tot_us = sum(v[1] for v in agg.values())
+            in_step = {"calls": n_g, "tile_kernel_us": us_g, "combine_us": us_c,
+                       "us_per_call": (us_g + us_c) / max(1, n_g), "algorithmic_bytes": alg,
+                       "achieved_gbs": alg / ((us_g + us_c) * 1e-6) / 1e9,
+                       "frac": alg / ((us_g + us_c) * 1e-6) / 1e9 / peaks.get("hbm_gbs", 6650.0),
+                       "share_of_step_kernel_time": (us_g + us_c) / max(tot_us, 1.0),
+                       "source": "CUPTI kernel records of one untimed bench step (all decode steps, all layers)"}
     if args.kernel_profile and rank == 0:
         kernel_profile(args, torch, lambda: step(0, make_prompts(args, rank, 200, dev)), args.kernel_profile)
     value = tokens / (ms / 1000.0)
@@ -362,10 +477,6 @@ def run_ours(args):
     # roofline of the dominant kernel: the grouped (shared-prefix) decode attention, on the
     # mid-rollout case, launches back to back between events on its stream; the timed call is the
     # tile kernel plus its small split-K combine
-    peaks = {}
-    pk = ROOT / "MEASURED_PEAKS.json"
-    if pk.exists():
-        peaks = json.loads(pk.read_text())
     hbm = peaks.get("hbm_gbs", 6650.0)
     case = rollout_attn_case(torch, ops, dev)
     grp_ms = time_launches(torch, case["runs"]["grouped"])
@@ -383,7 +494,8 @@ def run_ours(args):
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if pk.exists() else "fallback",
                 "vs_reference_layout": {"kernel": "paged_decode_kernel", "ms_per_launch": plain_ms,
                                         "kv_bytes": case["kv_plain"],
-                                        "effective_gbs_of_grouped": case["kv_plain"] / (grp_ms / 1000.0) / 1e9}}
+                                        "effective_gbs_of_grouped": case["kv_plain"] / (grp_ms / 1000.0) / 1e9},
+                "in_step": in_step}
     del case
     # the plain paged decode kernel alone on config-3 shapes (long contexts)
     dec_ms, dec_bytes, dec_tokens = decode_microbench(torch, ops, dev)
@@ -409,11 +521,103 @@ def run_ours(args):
                 "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"],
                              "rollout_detail": last.get("rollout_stats")},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "roofline": roofline,
+                "whole_step_roofline": whole_step,
                 "cpu_baseline": cpu, "decode_attn_plain": decode_plain}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_rollout_only(args):
+    """Config 2 on one GPU: the grouped rollout alone (64 prompts x G=8, prompt U[64,512], 512 new
+    tokens, temperature 1, no top-k, 256-token pages) on the bench's model.  value = generated
+    tokens/s; the roofline is the rollout phase's (prefill tensor-bound, decode steps HBM-bound:
+    weights + the K/V each step must read) over the measured rollout time; the CPU baseline is the
+    oracle's rollout by full recompute (the reference's rollout_single scheme) on a bounded sample."""
+    import torch
+
+    from qwen3_naive_inference_b200 import ops
+    from qwen3_naive_inference_b200.qwen3_naive import Qwen3Config, build_model
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = Qwen3Config(num_hidden_layers=args.layers)
+    model = build_model(cfg, device=dev, seed=0)
+    max_ctx = args.prompt_max + args.new_tokens
+    model._num_blocks = args.prompts * args.group * math.ceil(max_ctx / 256) + 64
+    model.max_model_len = max_ctx
+    model.use_cuda_graphs = not args.no_graphs
+    torch.manual_seed(1234)
+
+    def roll(prompts):
+        return model.generate_grouped_with_logprobs(prompts, args.group, max_new_tokens=args.new_tokens,
+                                                    temperature=1.0, top_k=None, eos_token_ids=None)
+
+    for i in range(args.warmup):
+        roll(make_prompts(args, 0, i, dev))
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    host = [make_prompts(args, 0, 100 + j) for j in range(args.steps)]
+    dev_prompts = [[p.to(dev) for p in ps] for ps in host]
+    sampler = ClockSampler(0)
+    sampler.start()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    gen_tokens = all_tokens = 0
+    for ps in dev_prompts:
+        seq_tokens, gen, _, _ = roll(ps)
+        gen_tokens += sum(len(x) for x in gen)
+        all_tokens += sum(len(x) for x in seq_tokens)
+    b.record(st)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(b)
+    ops.check_device_errors()
+    roof = sum(step_roofline([p.shape[1] for p in ps], args.group, args.new_tokens, args.layers, 1.0,
+                             peaks)["rollout_s"] for ps in host)
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, sample, th = cpu_rollout_sample()
+        cpu = {"value": v, "unit": "generated tokens/s", "cores": th, "kind": "port", "sample": sample}
+    print(json.dumps({"metric": "rollout generated tokens/s", "value": gen_tokens / (ms / 1000),
+                      "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": ms / args.steps, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": "config 2: grouped rollout, 64 prompts x G=8, prompt U[64,512], "
+                                             "512 new tokens, temperature 1, paged KV 256",
+                                 "prompts": args.prompts, "group": args.group, "new_tokens": args.new_tokens,
+                                 "layers": args.layers},
+                      "all_tokens_per_s": all_tokens / (ms / 1000),
+                      "roofline": {"bound": "hbm (decode) + tensor (prefill)", "roofline_s": roof,
+                                   "measured_s": ms / 1000, "frac": roof / (ms / 1000),
+                                   "basis": "sum over prefill and decode steps of max(FLOP/peak, bytes/peak)"},
+                      "clocks": clocks, "cpu_baseline": cpu}), flush=True)
+
+
+def cpu_rollout_sample(new=4, G=2, P=48):
+    """The oracle's rollout by full recompute (one forward of the whole sequence per new token, as
+    the reference's rollout_single, qwen3_grpo_train.py:69-120) at the Qwen3-0.6B shape on the host
+    cores: 1 prompt x G completions.  Returns (generated tokens/s, sample text, threads)."""
+    import torch
+
+    from oracle import ref_model
+    from oracle import ref_ops as R
+    from qwen3_naive_inference_b200.qwen3_naive import Qwen3Config
+    torch.set_num_threads(os.cpu_count())
+    cfg = Qwen3Config()
+    params = ref_model.init_params(cfg, seed=0)
+    g = torch.Generator().manual_seed(11)
+    cs = R.rope_cache(cfg.head_dim, P + new + 1, cfg.rope_theta)
+    ids = torch.randint(0, 151643, (1, P), generator=g).repeat(G, 1)
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for _ in range(new):
+            lg = ref_model.logits(params, cfg, ids, cos_sin=cs)[:, -1].float()
+            probs, _ = R.sample_distribution(lg, 1.0, None)
+            ids = torch.cat([ids, torch.multinomial(probs, 1, generator=g)], 1)
+    sec = time.perf_counter() - t0
+    return (G * new / sec, f"oracle rollout by full recompute, 1 prompt x G={G}, prompt {P}, {new} new tokens, "
+            "Qwen3-0.6B shape", torch.get_num_threads())
 
 
 def kernel_profile(args, torch, run_step, path):
@@ -486,7 +690,40 @@ def run_decode_only(batch):
     ms, nbytes, _ = decode_microbench(torch, ops, dev, n_iter=3, batch=batch)
     print(json.dumps({"kernel": "paged_decode_kernel", "case": f"config 3 shapes, batch {batch}",
                       "ms_per_launch": ms, "algorithmic_bytes": nbytes,
-                      "achieved_gbs": nbytes / (ms / 1000) / 1e9}), flush=True)
+                      "achieved_gbs": nbytes / (ms / 1000) / 1e9, "cpu_baseline": config3_cpu_baseline()}),
+          flush=True)
+
+
+def config3_cpu_baseline(n_seqs=8):
+    """The oracle's paged decode attention (gather K/V through the page table, GQA, fp32 softmax;
+    flash_attn_with_kvcache semantics, qwen3_naive.py:672-680) on the host cores, on a bounded
+    sample of config 3: n_seqs sequences with context U[1k, 8k] in randomly permuted 256-token
+    pages.  Returns GB/s of algorithmic bytes (K/V of every context token, q and out)."""
+    import torch
+
+    from oracle import ref_ops as R
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(3)
+    hq, hkv, Dh = 16, 8, 128
+    ctx = torch.randint(1024, 8193, (n_seqs,), generator=g)
+    pages = [(int(c) + 255) // 256 for c in ctx]
+    pool = sum(pages)
+    perm = torch.randperm(pool, generator=g)
+    bt = torch.full((n_seqs, max(pages)), -1, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(pages):
+        bt[i, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    kc = torch.randn(pool, 256, hkv, Dh, generator=g).to(torch.bfloat16)
+    vc = torch.randn(pool, 256, hkv, Dh, generator=g).to(torch.bfloat16)
+    q = torch.randn(n_seqs, hq, Dh, generator=g).to(torch.bfloat16)
+    R.paged_decode(q[:1], kc, vc, bt[:1], ctx[:1], Dh ** -0.5)
+    t0 = time.perf_counter()
+    R.paged_decode(q, kc, vc, bt, ctx, Dh ** -0.5)
+    sec = time.perf_counter() - t0
+    nbytes = int(ctx.sum()) * hkv * Dh * 2 * 2 + n_seqs * hq * Dh * 2 * 2
+    return {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n_seqs} sequences of config 3 (ctx U[1k,8k], 16q/8kv, d128), oracle paged decode"}
 
 
 def rollout_attn_case(torch, ops, dev):
@@ -679,10 +916,49 @@ def run_loss_only():
     moved = 3 * N * S * V * 2   # this build: forward read, backward read + write
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     hbm = peaks.get("hbm_gbs", 6650.0)
+    cpu = config1_cpu_baseline()
     print(json.dumps({"loss_only": {"rows": N * S, "vocab": V, "ms": ms, "algorithmic_bytes": alg,
                                     "achieved_gbs": alg / (ms / 1000) / 1e9, "frac_of_hbm": alg / (ms / 1000) / 1e9 / hbm,
                                     "bytes_moved": moved, "moved_gbs": moved / (ms / 1000) / 1e9,
-                                    "loss": loss.tolist()}}), flush=True)
+                                    "tokens_per_s": N * S / (ms / 1000), "loss": loss.tolist(),
+                                    "cpu_baseline": cpu}}), flush=True)
+
+
+def config1_cpu_baseline(reps=3):
+    """Config 1 exactly on the host cores with the oracle (the reference's pure-PyTorch path:
+    fp32 log_softmax + gather of [1024, 151936] bf16 logits, compute_grpo_advantage, the clipped
+    surrogate + 0.04 k3 KL masked token mean, backward to the logits;
+    qwen3_grpo_train.py:46-53, :162-199).  Returns tokens (rows) per second and ms per pass."""
+    import torch
+
+    from oracle import ref_ops as R
+    torch.set_num_threads(os.cpu_count())
+    N, S, V = 8, 128, 151936
+    g = torch.Generator().manual_seed(1)
+    logits = torch.randn(N * S, V, generator=g).to(torch.bfloat16)
+    tgt = torch.randint(0, 151643, (N * S,), generator=g)
+    lens = torch.randint(1, S + 1, (N,), generator=g)
+    mask = (torch.arange(S)[None, :] < lens[:, None]).float()
+    rewards = torch.bernoulli(torch.full((N,), 0.5), generator=g)
+    gids = torch.arange(N) // 4
+    with torch.no_grad():
+        base = R.log_probs(logits, tgt).view(N, S)
+    old = base + 0.05 * torch.randn(N, S, generator=g)
+    ref = base + 0.05 * torch.randn(N, S, generator=g)
+    times = []
+    for i in range(reps + 1):
+        t0 = time.perf_counter()
+        x = logits.float().requires_grad_(True)
+        lp = torch.log_softmax(x, dim=-1).gather(-1, tgt[:, None]).squeeze(-1).view(N, S)
+        adv = R.grpo_advantage(rewards, gids)
+        loss = R.ppo_loss(old, lp, adv[:, None] * mask, mask, 0.2, ref, 0.04)
+        loss.backward()
+        if i:
+            times.append(time.perf_counter() - t0)
+    ms = 1000 * sum(times) / len(times)
+    return {"value": N * S / (ms / 1000), "unit": "tokens/s", "ms_per_pass": ms, "cores": torch.get_num_threads(),
+            "kind": "port", "sample": "config 1 exactly: 1024 rows x 151936 bf16 logits, fp32 log-softmax + gather, "
+                                      "advantages, clipped + KL loss, backward to the logits (oracle, all host threads)"}
 
 
 GEMM_SHAPES = {  # (M, N, K): tokens x out x in of the model's projections
@@ -798,6 +1074,8 @@ def main():
         run_loss_only()
     elif args.decode_only:
         run_decode_only(args.decode_batch)
+    elif args.rollout_only:
+        run_rollout_only(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -197,6 +197,23 @@ size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int D, int n_s
  *   dest nullable (identity); dest[i] < 0 skips row i. */
 int qb_logprob_fwd(const void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
                    const int64_t* dest, float* logp, float* lse, int* err, qb_stream_t stream);
+/* lm_head -> log-softmax -> gather in one pass over the tensor cores, without storing logits;
+ * replaces `log_softmax(model(ids).float()).gather(ids)` of forward_logprob
+ * (qwen3_grpo_train.py:46-53) together with the tied lm_head GEMM (qwen3_naive.py:826).
+ *   h [n, K] bf16 (row pitch ldh), W [V, K] bf16 (the lm_head / embedding weight, pitch ldw).
+ *   The tcgen05 GEMM's epilogue folds each fp32 logit tile into per-row (max, sum of exp)
+ *   partials in `workspace` and keeps the target column's logit; a second kernel merges the
+ *   partials:  lse[i] = logsumexp_v(h_i . W_v),  logp[dest[i]] = h_i . W_{t_i} - lse[i].
+ *   The logits stay in fp32 (the reference rounds them to bf16 first; this is the more exact
+ *   value of the same quantity).  dest nullable (identity), dest[i] < 0 skips row i; lse
+ *   nullable; a target outside [0, V) sets QB_DEVERR_TOKEN and gives logp 0.
+ *   logits (nullable): when given, the bf16 logits [n, V] (pitch ld_logits) are stored as well,
+ *   for a backward pass that needs them.
+ *   workspace: qb_lm_head_logprob_workspace_bytes(n, V) bytes, 16-byte aligned, any contents. */
+int qb_lm_head_logprob(const void* h, int64_t ldh, const void* W, int64_t ldw, int64_t n, int64_t V,
+                       int64_t K, const int64_t* targets, const int64_t* dest, float* logp, float* lse,
+                       void* logits, int64_t ld_logits, void* workspace, int* err, qb_stream_t stream);
+size_t qb_lm_head_logprob_workspace_bytes(int64_t n, int64_t V);
 /* Backward: logits[i, v] <- bf16( g_i * (1[v == t_i] - exp(logits[i,v] - lse_i)) ), in place,
  * with g_i = grad_logp[dest[i]] (0 for skipped rows). */
 int qb_logprob_bwd(void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,

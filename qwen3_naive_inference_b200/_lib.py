@@ -45,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
     "qb_paged_decode_grouped_workspace_bytes": (c_size_t, [I, I, I, I]),
     "qb_logprob_fwd": (I, [P, L, L, L, P, P, P, P, P, P]),
     "qb_logprob_bwd": (I, [P, L, L, L, P, P, P, P, P, P]),
+    "qb_lm_head_logprob": (I, [P, L, P, L, L, L, L, P, P, P, P, P, L, P, P, P]),
+    "qb_lm_head_logprob_workspace_bytes": (c_size_t, [L, L]),
     "qb_sample": (I, [P, L, L, L, F, I, c_uint64, P, P, P, P, P]),
     "qb_grpo_advantage": (I, [P, P, L, P, P]),
     "qb_grpo_loss": (I, [P, P, L, L, L, L, P, P, P, P, P, F, F, P, P, P, P, P, P]),

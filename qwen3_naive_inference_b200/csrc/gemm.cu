@@ -90,6 +90,11 @@ struct GemmParams {
   int tiles_m, tiles_n;
   int vec_ok;  // every output row starts on a 16-byte boundary: 16-byte stores allowed
   int* err;
+  // MODE 3 (lm_head log-prob) only:
+  const int64_t* targets;  // [M] target column of each row
+  float2* lse_part;        // [M, n_part]: per N tile, (max, sum of exp) of the row in the log2 domain
+  float* tgt_logit;        // [M] fp32 logit at the target column
+  int n_part;              // row pitch of lse_part (= number of N tiles of the launch)
 };
 
 // One epilogue thread's 32 consecutive fp32 accumulator columns of output row `row`, starting
@@ -133,6 +138,60 @@ QB_DEVICE void store_row32(const GemmParams& p, int row, int col, const uint32_t
           if (col + i < p.N) dst[i] = (MODE == 2 ? dst[i] : 0.f) + __uint_as_float(r[i]);
       }
     }
+}
+
+// MODE 3 (lm_head -> log-softmax -> gather): the epilogue thread that holds row `row` of a tile
+// folds each 32-column chunk of fp32 logits into a running (max, sum of exp) pair in the log2
+// domain, keeps the target column's logit when the chunk holds it, and stores the bf16 logits
+// only when the caller asked for them (p.C != nullptr).  Logits never leave the SM otherwise.
+struct LseAcc {
+  float m2, s, tv;
+  bool has_t;
+};
+
+QB_DEVICE void lse_fold32(const GemmParams& p, int row, int col, int64_t tgt, const uint32_t (&r)[32], LseAcc& a) {
+  constexpr float L2E = 1.4426950408889634f;  // log2(e)
+  if (p.C) store_row32<0>(p, row, col, r);
+  const int nvalid = p.N - col < 32 ? p.N - col : 32;
+  float cm = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i < nvalid) cm = fmaxf(cm, __uint_as_float(r[i]));
+  if ((uint64_t)(tgt - col) < 32u) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col + i == tgt) a.tv = __uint_as_float(r[i]);
+    a.has_t = true;
+  }
+  const float cm2 = cm * L2E;
+  if (cm2 > a.m2) {
+    a.s *= exp2f(a.m2 - cm2);
+    a.m2 = cm2;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i < nvalid) s += exp2f(fmaf(__uint_as_float(r[i]), L2E, -a.m2));
+  a.s += s;
+}
+
+// Folds the accumulator rows of one tile (this thread's row, BN columns from TMEM column `tcol`).
+template <int BN>
+QB_DEVICE void lse_tile(const GemmParams& p, uint32_t taddr, int row, bool row_ok, int n0, int n_tile) {
+  LseAcc a{-INFINITY, 0.f, 0.f, false};
+  const int64_t tgt = (row_ok && p.targets) ? p.targets[row] : -1;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(taddr + c, r);  // warp-collective: every lane loads before any lane skips
+    const int col = n0 + c;
+    if (!row_ok || col >= p.N) continue;
+    lse_fold32(p, row, col, tgt, r, a);
+  }
+  if (row_ok) {
+    p.lse_part[(int64_t)row * p.n_part + n_tile] = make_float2(a.m2, a.s);
+    if (a.has_t) p.tgt_logit[row] = a.tv;
+  }
 }
 
 template <int BN, int STAGES, int MODE, bool A_MN, bool B_MN>
@@ -272,13 +331,18 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
+      if constexpr (MODE == 3) {
+        lse_tile<BN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE, row, row_ok, n0,
+                     t / p.tiles_m);
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE + c, r);
-        const int col = n0 + c;
-        if (!row_ok || col >= p.N) continue;
-        store_row32<MODE>(p, row, col, r);
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE + c, r);
+          const int col = n0 + c;
+          if (!row_ok || col >= p.N) continue;
+          store_row32<MODE>(p, row, col, r);
+        }
       }
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));  // accumulator free for the tile after next
@@ -500,13 +564,17 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
+      if constexpr (MODE == 3) {
+        lse_tile<256>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * 256, row, row_ok, n0, t / tiles_m);
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < 256; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * 256 + c, r);
-        const int col = n0 + c;
-        if (!row_ok || col >= p.N) continue;
-        store_row32<MODE>(p, row, col, r);
+        for (int c = 0; c < 256; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * 256 + c, r);
+          const int col = n0 + c;
+          if (!row_ok || col >= p.N) continue;
+          store_row32<MODE>(p, row, col, r);
+        }
       }
       tc_fence_before();
       mbar_arrive_remote(acc == 0 ? leader_tempty0 : leader_tempty1);  // the leader may reuse it
@@ -952,6 +1020,76 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   return launch_layout<true, true>(bn, mode, ta, tb, p, st);
 }
 
+// ---------------------------------------------------------------- lm_head -> log-softmax -> gather
+// The per-tile (max, sum of exp) pairs of a row are merged into the row's log-sum-exp, and the
+// target's log-prob is its fp32 logit minus that.  One warp per row.
+__global__ void __launch_bounds__(128)
+lse_combine_kernel(const float2* __restrict__ part, int n_part, const float* __restrict__ tgt_logit,
+                   const int64_t* __restrict__ targets, const int64_t* __restrict__ dest, int64_t n, int64_t V,
+                   float* __restrict__ logp, float* __restrict__ lse, int* err) {
+  constexpr float LN2 = 0.6931471805599453f;
+  const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const float2* pr = part + row * n_part;
+  float m = -INFINITY;
+  for (int i = lane; i < n_part; i += 32) m = fmaxf(m, pr[i].x);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int i = lane; i < n_part; i += 32) {
+    const float2 v = pr[i];
+    s += v.y * exp2f(v.x - m);
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    const float l = (m + log2f(s)) * LN2;
+    if (lse) lse[row] = l;
+    const int64_t d = dest ? dest[row] : row;
+    if (d >= 0) {
+      const int64_t t = targets[row];
+      if (t < 0 || t >= V) {
+        qb_set_err(err, QB_DEVERR_TOKEN);
+        logp[d] = 0.f;
+      } else {
+        logp[d] = tgt_logit[row] - l;
+      }
+    }
+  }
+}
+
+inline int64_t lse_parts_bound(int64_t V) { return (V + 127) / 128; }
+
+int lm_head_logprob(const void* h, int64_t ldh, const void* W, int64_t ldw, int64_t n, int64_t V, int64_t K,
+                    const int64_t* targets, const int64_t* dest, float* logp, float* lse, void* logits,
+                    int64_t ld_logits, void* workspace, int* err, cudaStream_t st) {
+  QB_CHECK_ARG(n >= 0 && V > 0 && K > 0);
+  if (n == 0) return QB_OK;
+  QB_CHECK_ARG(h && W && targets && logp && workspace && al16(h) && al16(W) && ldh % 8 == 0 && ldw % 8 == 0);
+  QB_CHECK_ARG(ldh >= K && ldw >= K && (!logits || ld_logits >= V));
+  QB_CHECK_ARG(n < (1ll << 31) && V < (1ll << 31) && K < (1ll << 31));
+  QB_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 15) == 0);
+  const int sms = sm_count();
+  const int64_t tm = (n + BM - 1) / BM;
+  const bool pair = V >= 256 && n >= 256 && ((n + 255) / 256) * ((V + 255) / 256) >= sms / 2;
+  const int bn = pair || V >= 256 ? 256 : 128;
+  const int n_part = (int)((V + bn - 1) / bn);
+  float2* part = reinterpret_cast<float2*>(workspace);
+  float* tgt = reinterpret_cast<float*>(part + n * lse_parts_bound(V));
+  const int vec_ok = logits && al16(logits) && (ld_logits * 2) % 16 == 0;
+  GemmParams p{logits, ld_logits, (int)n, (int)V, (int)K, (int)tm, n_part, vec_ok, err, targets, part, tgt, n_part};
+  CUtensorMap ta, tb;
+  if (!operand_tmap(&ta, h, false, (uint64_t)n, (uint64_t)K, (uint64_t)ldh, BM)) return QB_ERR_INVALID;
+  if (!operand_tmap(&tb, W, false, (uint64_t)V, (uint64_t)K, (uint64_t)ldw, pair ? 128 : (uint32_t)bn))
+    return QB_ERR_INVALID;
+  int status = pair ? launch_pair<3, false, false>(ta, tb, p, st)
+                    : (bn == 256 ? launch<256, 4, 3, false, false>(ta, tb, p, st)
+                                 : launch<128, 6, 3, false, false>(ta, tb, p, st));
+  if (status != QB_OK) return status;
+  lse_combine_kernel<<<(unsigned)((n + 3) / 4), 128, 0, st>>>(part, n_part, tgt, targets, dest, n, V, logp, lse,
+                                                              err);
+  return qb_launch_status();
+}
+
 }  // namespace
 
 extern "C" int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
@@ -964,4 +1102,17 @@ extern "C" int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const
                                int* err, qb_stream_t stream) {
   return gemm_dispatch(A, lda, a_mn_major != 0, B, ldb, b_mn_major != 0, C, ldc, M, N, K, mode, err,
                        (cudaStream_t)stream);
+}
+
+extern "C" int qb_lm_head_logprob(const void* h, int64_t ldh, const void* W, int64_t ldw, int64_t n, int64_t V,
+                                  int64_t K, const int64_t* targets, const int64_t* dest, float* logp, float* lse,
+                                  void* logits, int64_t ld_logits, void* workspace, int* err, qb_stream_t stream) {
+  return lm_head_logprob(h, ldh, W, ldw, n, V, K, targets, dest, logp, lse, logits, ld_logits, workspace, err,
+                         (cudaStream_t)stream);
+}
+
+extern "C" size_t qb_lm_head_logprob_workspace_bytes(int64_t n, int64_t V) {
+  if (n <= 0 || V <= 0) return 16;
+  const size_t bytes = (size_t)n * (size_t)lse_parts_bound(V) * sizeof(float2) + (size_t)n * sizeof(float);
+  return (bytes + 255) / 256 * 256;
 }

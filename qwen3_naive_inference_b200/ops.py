@@ -24,7 +24,7 @@ __all__ = [
     "NativeError", "lib", "stream_ptr", "err_flag", "check_device_errors", "embedding", "rmsnorm",
     "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "attention_packed", "attention_paged_prefill",
     "paged_decode_attention", "silu_mul", "add", "linear", "logprob", "sample", "grpo_advantage",
-    "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan",
+    "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan", "lm_head_logprob",
 ]
 
 BF16 = torch.bfloat16
@@ -502,29 +502,51 @@ def _logits_chunk(h, w):
     return gemm(_gemm_operand(h), _gemm_operand(w))
 
 
-def logprob_forward(h, weight, targets, dest=None, out=None, out_size=None, chunk_rows=4096, save_lse=True):
-    """Token log-probs of ``targets`` under ``lm_head(h)`` without materialising all logits.
+_LSE_WS: dict[tuple, torch.Tensor] = {}
 
-    Rows are processed ``chunk_rows`` at a time: a bf16 logits chunk is produced and
-    reduced by ``qb_logprob_fwd`` (fp32 log-sum-exp + gather).  ``dest`` (int64) scatters
-    row i to ``out[dest[i]]``; without it ``out`` is [n].  Returns (out, lse[n]).
+
+def lm_head_logprob(h, weight, targets, *, dest=None, out=None, lse=None, logits=None):
+    """One pass of ``qb_lm_head_logprob``: log-probs of ``targets`` under ``h @ weight.T`` with the
+    log-softmax folded into the tcgen05 GEMM's epilogue (fp32 logits, never stored unless
+    ``logits`` [n, V] bf16 is given).  ``out`` receives row i at ``out[dest[i]]`` (or ``out[i]``),
+    ``lse`` [n] the rows' log-sum-exp.  Returns (out, lse)."""
+    _cuda(h, weight, targets)
+    h, w = _gemm_operand(h), _gemm_operand(weight)
+    n, K = h.shape
+    V = w.shape[0]
+    if out is None:
+        out = torch.empty(n, dtype=torch.float32, device=h.device)
+    if lse is None:
+        lse = torch.empty(n, dtype=torch.float32, device=h.device)
+    nbytes = lib().qb_lm_head_logprob_workspace_bytes(n, V)
+    key = (h.device.index, torch.cuda.current_stream(h.device).cuda_stream)
+    ws = _LSE_WS.get(key)
+    if ws is None or ws.numel() * 4 < nbytes:
+        ws = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=h.device)
+        _LSE_WS[key] = ws
+    check(lib().qb_lm_head_logprob(_p(h), h.stride(0), _p(w), w.stride(0), n, V, K, _p(targets), _p(dest),
+                                   _p(out), _p(lse), _p(logits), 0 if logits is None else logits.stride(0), _p(ws),
+                                   _p(err_flag()), stream_ptr()), "qb_lm_head_logprob")
+    return out, lse
+
+
+def logprob_forward(h, weight, targets, dest=None, out=None, out_size=None, chunk_rows=4096, save_lse=True):
+    """Token log-probs of ``targets`` under ``lm_head(h)``; no logits are stored.
+
+    Rows are processed ``chunk_rows`` at a time by :func:`lm_head_logprob` (GEMM with the
+    log-sum-exp and the gather in its epilogue).  ``dest`` (int64) scatters row i to
+    ``out[dest[i]]``; without it ``out`` is [n].  Returns (out, lse[n]).
     """
     _cuda(h, weight, targets)
     n = h.shape[0]
-    V = weight.shape[0]
     if out is None:
         size = n if out_size is None else out_size
         out = (torch.zeros if dest is not None else torch.empty)(size, dtype=torch.float32, device=h.device)
     lse = torch.empty(n, dtype=torch.float32, device=h.device)
-    L = lib()
     for r0 in range(0, n, chunk_rows):
         r1 = min(n, r0 + chunk_rows)
-        logits = _logits_chunk(h[r0:r1], weight)
-        # without dest, row i of the chunk lands at out[r0 + i]
-        out_ptr = _p(out) if dest is not None else _p(out) + 4 * r0
-        check(L.qb_logprob_fwd(_p(logits), r1 - r0, V, logits.stride(0), _p(targets) + 8 * r0,
-                               0 if dest is None else _p(dest) + 8 * r0, out_ptr, _p(lse) + 4 * r0,
-                               _p(err_flag()), stream_ptr()), "qb_logprob_fwd")
+        lm_head_logprob(h[r0:r1], weight, targets[r0:r1], dest=None if dest is None else dest[r0:r1],
+                        out=out if dest is not None else out[r0:r1], lse=lse[r0:r1])
     return out, lse
 
 

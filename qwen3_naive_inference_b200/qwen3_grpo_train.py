@@ -236,17 +236,19 @@ def policy_loss_backward(model: Qwen3ForCausalLM, batch: PackedBatch, *, ref_lp=
 
 def _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, loss, dW, batch, ref_lp, beta,
                     clip_epsilon, mask_total, r0, row_tok, tok_off, chunk_rows):
-    """Per row chunk: logits once -> log-prob -> fused loss/grad -> d logits in place -> dh, dW.
+    """Per row chunk: logits once (GEMM with the log-softmax + gather in its epilogue) -> fused
+    loss/grad -> d logits in place -> dh, dW.
     Returns the updated fp32 dW accumulator."""
     for a, b in _row_chunks(row_tok, chunk_rows):
         t0, t1 = int(tok_off[a]), int(tok_off[b])
         if t1 == t0:
             continue
         hc = hs[t0:t1]
-        logits = ops.linear(hc, W)
-        ops.check(L.qb_logprob_fwd(logits.data_ptr(), t1 - t0, V, logits.stride(0), tgt.data_ptr() + 8 * t0,
-                                   dest.data_ptr() + 8 * t0, new_lp.data_ptr(), lse.data_ptr() + 4 * t0,
-                                   err.data_ptr(), ops.stream_ptr()), "qb_logprob_fwd")
+        # one GEMM: bf16 logits for the backward, and the log-softmax + gather from the fp32
+        # accumulators in its epilogue
+        logits = torch.empty(t1 - t0, V, dtype=torch.bfloat16, device=hs.device)
+        ops.lm_head_logprob(hc, W, tgt[t0:t1], dest=dest[t0:t1], out=new_lp.view(-1), lse=lse[t0:t1],
+                            logits=logits)
         ops.grpo_loss_raw(batch.rewards, batch.group_ids, new_lp, batch.old_lp, batch.mask, ref_lp=ref_lp,
                           mask_total=mask_total, clip_eps=clip_epsilon, beta=beta, row_begin=r0 + a,
                           row_end=r0 + b, grad_new=grad_new, loss_out=loss)

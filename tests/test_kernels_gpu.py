@@ -457,3 +457,47 @@ def test_paged_decode_grouped_shared_prefix(cuda, split):
     close_bf16(out, ref, 2e-2)
     assert torch.equal(ops.paged_decode_attention_grouped(*args, workspace=ws), out)
     ops.check_device_errors()
+
+
+@pytest.mark.parametrize("n,V", [(300, 151936), (100, 151936), (77, 1000), (40, 200)])
+def test_lm_head_logprob_fused(cuda, n, V):
+    """qb_lm_head_logprob (tcgen05 GEMM with the log-softmax and the gather in its epilogue) on the
+    CTA-pair, 128x256 and 128x128 tile paths, V with and without a partial last tile: log-probs
+    and log-sum-exp per element against the fp32 log_softmax of the same bf16 operands; the
+    optional bf16 logits within one bf16 ulp; dest scatter with a skipped row; a target outside
+    the vocabulary sets the token error bit and gives 0."""
+    g = gen(61 + n)
+    K = 1024
+    h = torch.randn(n, K, generator=g).to(BF)
+    W = (torch.randn(V, K, generator=g) * 0.05).to(BF)
+    t = torch.randint(0, V, (n,), generator=g)
+    ref_logits = h.float() @ W.float().t()
+    ref_lse = torch.logsumexp(ref_logits, -1)
+    ref = ref_logits.gather(-1, t[:, None]).squeeze(-1) - ref_lse
+    dest = torch.arange(n, dtype=torch.int64) * 2
+    dest[3] = -1
+    out = torch.full((2 * n,), 7.0, device=cuda)
+    lse = torch.empty(n, device=cuda)
+    logits = torch.empty(n, V, dtype=BF, device=cuda)
+    ops.lm_head_logprob(h.to(cuda), W.to(cuda), t.to(cuda), dest=dest.to(cuda), out=out, lse=lse, logits=logits)
+    ops.check_device_errors()
+    out = out.cpu()
+    keep = torch.ones(n, dtype=torch.bool)
+    keep[3] = False
+    assert out[7].item() == 7.0 and out[6].item() == 7.0  # row 3 skipped (dest -1), odd slots untouched
+    got = out[dest[keep]]
+    assert ((got - ref[keep]).abs() <= 1e-4 * ref[keep].abs() + 1e-5).all(), (got - ref[keep]).abs().max()
+    assert ((lse.cpu() - ref_lse).abs() <= 1e-5 * ref_lse.abs() + 1e-5).all()
+    rl = ref_logits.to(BF).float()
+    ulp = torch.exp2(torch.floor(torch.log2(rl.abs().clamp_min(2.0 ** -126))) - 7)
+    # fp32 accumulation order differs from the CPU GEMM: near-zero logits move by ~1e-6 absolute
+    assert ((logits.float().cpu() - rl).abs() <= ulp + 2e-5).all()
+    # without the logits output, and with a bad target
+    t2 = t.clone()
+    t2[1] = V + 5
+    out2, _ = ops.lm_head_logprob(h.to(cuda), W.to(cuda), t2.to(cuda))
+    with pytest.raises(ops.NativeError):
+        ops.check_device_errors()
+    out2 = out2.cpu()
+    assert out2[1].item() == 0.0
+    assert torch.equal(out2[keep & (torch.arange(n) != 1)], out[dest[keep & (torch.arange(n) != 1)]])

@@ -418,3 +418,28 @@ def test_grpo_step_end_to_end(setup, cuda):
     assert out["completion_tokens"] == 8 * 24
     assert not torch.equal(before, model.model.layers[0].mlp.down_proj.weight)
     ops.check_device_errors()
+
+
+def test_rollout_single_and_batch_reference_signatures(setup, cuda):
+    """rollout_single(model, prompt_ids, tokenizer) and rollout_batch(model, tokenizer, prompts)
+    with the reference's signatures (qwen3_grpo_train.py:69-120, :212-258): prompt + response ids,
+    each response token's log-prob at its own position, the response mask, per-completion rewards
+    and prompt ids; greedy completions equal generate_continuous's."""
+    cfg, params, model = setup
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, L), generator=g).to(cuda) for L in (20, 33)]
+    ids, old, mask = G.rollout_single(model, prompts[0], None, max_new_tokens=6, top_k=1, temperature=1.0,
+                                      eos_token_ids=None)
+    assert ids.shape == (1, 26) and old.shape == (26,) and mask.shape == (26,)
+    assert torch.equal(ids[0, :20], prompts[0][0])
+    assert mask[:20].sum().item() == 0 and mask[20:].sum().item() == 6
+    assert torch.all(old[:20] == 0) and torch.all(old[20:] == 0)  # greedy: log-prob 0
+    toks, _ = model.generate_continuous([prompts[0]], max_new_tokens=6, top_k=1, temperature=1.0)
+    assert ids[0].tolist() == toks[0]
+    ids, old, mask, rewards, pid = G.rollout_batch(model, None, prompts, n_rollout=2, max_new_tokens=7,
+                                                   temperature=1.0, top_k=20, eos_token_ids=None)
+    assert ids.shape == (4, 40) and old.shape == (4, 40) and mask.shape == (4, 40)
+    assert pid.tolist() == [0, 0, 1, 1]
+    assert mask.sum(1).tolist() == [7.0, 7.0, 7.0, 7.0]
+    assert torch.all(old[mask.bool()] <= 0) and torch.all(old[~mask.bool()] == 0)
+    assert rewards.tolist() == [1.0] * 4  # 7 completion tokens > 5 (no tokenizer: the token-count rule)
