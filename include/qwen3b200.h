@@ -289,6 +289,26 @@ int qb_grpo_loss_noalloc(const float* rewards, const int64_t* group_ids, int64_t
                          const float* mask_total, float clip_eps, float beta,
                          const float* grad_scale, float* grad_new, float* loss_out,
                          float* adv_out, qb_stream_t stream);
+/* Config 1's whole pass in one read and one write of the logits: log-prob of each token from its
+ * row of bf16 logits, group advantages, the clipped surrogate + beta * k3 KL loss and its
+ * gradient, written back over the logits as d loss / d logits; replaces forward_logprob's
+ * log_softmax + gather (qwen3_grpo_train.py:49-52), compute_grpo_advantage (:162-173),
+ * ppo_clipped_loss (:184-199) and the autograd backward to the logits.
+ *   logits [n_seqs * S, ld] bf16 (row = seq * S + position), overwritten with the gradient;
+ *   targets [n_seqs * S]; rewards / group_ids [n_seqs]; old_lp, ref_lp (nullable), mask
+ *   [n_seqs, S] fp32; mask_total as in qb_grpo_loss.  Outputs: new_lp [n_seqs, S] (0 and
+ *   QB_DEVERR_TOKEN for a target outside [0, V)), grad_new (nullable) d loss / d new_lp,
+ *   loss_out[3] += (loss, surrogate, kl), adv_out (nullable) [n_seqs].
+ *   A row's slices are shared by a cluster of 4 CTAs through distributed shared memory.
+ *   V % 8 == 0, V <= 409600; workspace: qb_grpo_logit_loss_workspace_bytes, 16-byte aligned,
+ *   any contents. */
+int qb_grpo_logit_loss(void* logits, int64_t ld, int64_t V, const int64_t* targets,
+                       const float* rewards, const int64_t* group_ids, int64_t n_seqs, int64_t S,
+                       const float* old_lp, const float* ref_lp, const float* mask,
+                       const float* mask_total, float clip_eps, float beta, float* new_lp,
+                       float* grad_new, float* loss_out, float* adv_out, void* workspace, int* err,
+                       qb_stream_t stream);
+size_t qb_grpo_logit_loss_workspace_bytes(int64_t n_seqs, int64_t S);
 /* mask_total[0] = sum of the [n] fp32 mask (the reference's response_mask.sum(),
  * qwen3_grpo_train.py:198); workspace as above. */
 int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace,

@@ -51,6 +51,8 @@ SIGNATURES: dict[str, tuple] = {
     "qb_grpo_advantage": (I, [P, P, L, P, P]),
     "qb_grpo_loss": (I, [P, P, L, L, L, L, P, P, P, P, P, F, F, P, P, P, P, P, P]),
     "qb_grpo_workspace_bytes": (c_size_t, [L]),
+    "qb_grpo_logit_loss": (I, [P, L, L, P, P, P, L, L, P, P, P, P, F, F, P, P, P, P, P, P, P]),
+    "qb_grpo_logit_loss_workspace_bytes": (c_size_t, [L, L]),
     "qb_ppo_clipped_loss": (I, [P, P, P, P, P, L, L, P, F, F, P, P, P, P, P]),
     "qb_grpo_loss_noalloc": (I, [P, P, L, L, L, L, P, P, P, P, P, F, F, P, P, P, P, P]),
     "qb_mask_sum": (I, [P, L, P, P, P]),

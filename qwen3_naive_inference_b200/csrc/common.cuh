@@ -126,3 +126,19 @@ QB_DEVICE void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0
 QB_DEVICE uint32_t swz128(int row, int chunk) {
   return (uint32_t)(row * 256 + ((chunk ^ (row & 7)) << 4));
 }
+
+// ---------------------------------------------------------------- thread-block clusters
+QB_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory byte in CTA `rank` of the cluster.
+QB_DEVICE uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+QB_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}

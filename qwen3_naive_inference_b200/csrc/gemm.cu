@@ -381,20 +381,6 @@ struct PairCfg {
                                     ((uint32_t)(256 >> 4) << 24);
 };
 
-QB_DEVICE uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Address of the same shared-memory byte in CTA `rank` of the cluster.
-QB_DEVICE uint32_t cluster_addr(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
-}
-QB_DEVICE void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
 // Arrivals on a barrier of either CTA of the pair, with the default (CTA-scope release)
 // semantics: the data they guard arrives by TMA transaction counts or is TMEM read back with
 // tcgen05.wait, so no cluster-wide fence is needed (one would stall the producer on its own

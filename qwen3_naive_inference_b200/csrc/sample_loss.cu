@@ -594,6 +594,39 @@ __global__ void advantage_kernel(const float* __restrict__ rewards, const int64_
   if (threadIdx.x == 0) adv[r] = a;
 }
 
+// One token of the clipped surrogate + beta * k3 KL (ppo_clipped_loss, qwen3_grpo_train.py:193-199,
+// and the GRPO paper's k3 estimator): its masked loss terms and d loss / d new_lp, where
+// u = d loss / d sum(loss_token * mask) (1 / denominator, times the caller's grad scale).
+struct TokenLoss {
+  float surr_m, kl_m, gnew;
+};
+
+QB_DEVICE TokenLoss token_loss(float nw, float old, float ref, bool has_ref, float A, float m, float lo, float hi,
+                               float beta, float u) {
+  const float ratio = expf(nw - old);
+  const float cr = fminf(fmaxf(ratio, lo), hi);
+  const float s1 = ratio * A, s2 = cr * A;
+  const float lt = -fminf(s1, s2);
+  TokenLoss t{lt * m, 0.f, 0.f};
+  float dkl = 0.f;
+  if (has_ref) {
+    const float d = ref - nw;
+    const float e = expf(d);
+    t.kl_m = (e - d - 1.f) * m;
+    dkl = 1.f - e;
+  }
+  const float gl = u * m;     // grad of loss_token * mask w.r.t. loss_token
+  const float gmin = -gl;     // loss_token = -min(s1, s2)
+  const bool eq = s1 == s2;
+  const float g1 = eq ? gmin * 0.5f : (s1 < s2 ? gmin : 0.f);
+  const float g2 = eq ? gmin * 0.5f : (s2 < s1 ? gmin : 0.f);
+  const float inr = (ratio >= lo && ratio <= hi) ? 1.f : 0.f;
+  const float gratio = g1 * A + (g2 * A) * inr;
+  t.gnew = gratio * ratio;
+  if (has_ref) t.gnew += beta * gl * dkl;
+  return t;
+}
+
 struct LossParams {
   const float* rewards;
   const int64_t* gids;
@@ -633,32 +666,11 @@ __global__ void grpo_loss_kernel(LossParams p) {
     const int64_t i = r * p.S + s;
     const float m = p.mask[i];
     const float A = FROM_REWARDS ? adv * m : p.token_adv[i];
-    const float nw = p.new_lp[i];
-    const float ratio = expf(nw - p.old_lp[i]);
-    const float cr = fminf(fmaxf(ratio, p.lo), p.hi);
-    const float s1 = ratio * A, s2 = cr * A;
-    const float lt = -fminf(s1, s2);
-    surr += lt * m;
-    float kl = 0.f, dkl = 0.f;
-    if (p.ref_lp) {
-      const float d = p.ref_lp[i] - nw;
-      const float e = expf(d);
-      kl = e - d - 1.f;
-      dkl = 1.f - e;
-      klsum += kl * m;
-    }
-    if (p.grad_new) {
-      const float gl = u * m;     // grad of loss_token * mask w.r.t. loss_token
-      const float gmin = -gl;     // loss_token = -min(s1, s2)
-      const bool eq = s1 == s2;
-      const float g1 = eq ? gmin * 0.5f : (s1 < s2 ? gmin : 0.f);
-      const float g2 = eq ? gmin * 0.5f : (s2 < s1 ? gmin : 0.f);
-      const float inr = (ratio >= p.lo && ratio <= p.hi) ? 1.f : 0.f;
-      const float gratio = g1 * A + (g2 * A) * inr;
-      float gnew = gratio * ratio;
-      if (p.ref_lp) gnew += p.beta * gl * dkl;
-      p.grad_new[i] = gnew;
-    }
+    const TokenLoss t = token_loss(p.new_lp[i], p.old_lp[i], p.ref_lp ? p.ref_lp[i] : 0.f, p.ref_lp != nullptr, A, m,
+                                   p.lo, p.hi, p.beta, u);
+    surr += t.surr_m;
+    klsum += t.kl_m;
+    if (p.grad_new) p.grad_new[i] = t.gnew;
   }
   surr = block_sum(surr, red);
   klsum = block_sum(klsum, red);
@@ -685,6 +697,203 @@ __global__ void grpo_loss_kernel(LossParams p) {
       p.loss_out[2] += lk;
     }
     p.ws[1] = 0u;
+  }
+}
+
+// ---------------------------------------------------------------- single-pass log-prob + loss + logit gradient
+// One row of bf16 logits (151,936 entries = 297 KB) is split over a cluster of LL_CTAS CTAs; each
+// CTA brings its slice into shared memory with bulk copies (one read from HBM), folds it into a
+// (max, sum of exp) pair, the cluster exchanges the pairs and the target's logit through
+// distributed shared memory, every CTA forms the row's log-sum-exp, the token's log-prob, its
+// GRPO loss terms and d loss / d logp identically, and writes d loss / d logits of its slice
+// back over the logits from shared memory (one write).  The logits cross HBM once each way.
+constexpr int LL_CTAS = 4;
+constexpr int LL_THREADS = 256;
+constexpr int LL_COPY = 32768;  // bytes per bulk copy
+
+struct LogitLossParams {
+  bf16* logits;
+  int64_t ld, V, n_rows, S;
+  const int64_t* targets;
+  const float* adv;  // [n_rows / S] advantages of the sequences
+  const float* old_lp;
+  const float* ref_lp;
+  const float* mask;
+  const float* mask_total;
+  float lo, hi, beta;
+  float* new_lp;
+  float* grad_new;
+  float* row_part;  // [2 * n_rows]: masked surrogate and KL terms of each token
+  int chunk;        // logits per CTA (multiple of 8)
+  int* err;
+};
+
+QB_DEVICE void ll_merge(float& m2, float& s, float om2, float os) {
+  const float nm = fmaxf(m2, om2);
+  if (nm == -INFINITY) return;
+  s = s * exp2f(m2 - nm) + os * exp2f(om2 - nm);
+  m2 = nm;
+}
+
+__global__ void __launch_bounds__(LL_THREADS)
+logit_loss_kernel(LogitLossParams p) {
+  constexpr float L2E = 1.4426950408889634f, LN2 = 0.6931471805599453f;
+  extern __shared__ __align__(128) uint8_t ll_smem[];
+  __shared__ float red[2][LL_THREADS / 32];
+  __shared__ __align__(16) float4 slot;  // (max2, sum, target logit, 1 if this slice holds the target)
+  __shared__ float bc[2];                // g, lse2
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t rank = cluster_rank();
+  const int64_t row = blockIdx.x / LL_CTAS;
+  const int64_t c0 = (int64_t)rank * p.chunk;
+  const int64_t c1 = c0 + p.chunk < p.V ? c0 + p.chunk : p.V;
+  const int nel = c1 > c0 ? (int)(c1 - c0) : 0;
+  bf16* grow = p.logits + row * p.ld;
+  const bf16* sx = reinterpret_cast<const bf16*>(ll_smem);
+  const uint32_t mb = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mb));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const uint32_t bytes = (uint32_t)nel * 2;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mb), "r"(bytes) : "memory");
+    for (uint32_t o = 0; o < bytes; o += LL_COPY) {
+      const uint32_t n = bytes - o < (uint32_t)LL_COPY ? bytes - o : (uint32_t)LL_COPY;
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(ll_smem) + o),
+          "l"(reinterpret_cast<const uint8_t*>(grow + c0) + o), "r"(n), "r"(mb)
+          : "memory");
+    }
+  }
+  __syncthreads();
+  // bounded wait for this CTA's slice (~2 s of SM clock)
+  bool ready = false;
+  const long long t0 = clock64();
+  while (!ready) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tmbarrier.try_wait.parity.shared::cta.b64 q, [%1], 0;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(ok)
+        : "r"(mb)
+        : "memory");
+    ready = ok != 0;
+    if (!ready && clock64() - t0 > 4000000000ll) break;
+  }
+  if (!ready && threadIdx.x == 0) qb_set_err(p.err, QB_DEVERR_TIMEOUT);
+  const int64_t tgt = p.targets[row];
+  // this CTA's (max, sum of exp) in the log2 domain
+  float m2 = -INFINITY, sm = 0.f;
+  if (ready) {
+    for (int v = threadIdx.x; v < nel / 8; v += LL_THREADS) {
+      const uint4 u = reinterpret_cast<const uint4*>(sx)[v];
+      float x[8];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(w[j]);
+        x[2 * j] = f.x;
+        x[2 * j + 1] = f.y;
+      }
+      float mx = x[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) mx = fmaxf(mx, x[j]);
+      const float nm2 = fmaxf(m2, mx * L2E);
+      float acc = sm * exp2f(m2 - nm2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc += exp2f(fmaf(x[j], L2E, -nm2));
+      sm = acc;
+      m2 = nm2;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m2, o), os = __shfl_xor_sync(0xffffffffu, sm, o);
+    ll_merge(m2, sm, om, os);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = m2;
+    red[1][threadIdx.x >> 5] = sm;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = red[0][0], Sx = red[1][0];
+    for (int w = 1; w < LL_THREADS / 32; ++w) ll_merge(M, Sx, red[0][w], red[1][w]);
+    const bool has_t = ready && tgt >= c0 && tgt < c1;
+    slot = make_float4(M, Sx, has_t ? bf2f(sx[tgt - c0]) : 0.f, has_t ? 1.f : 0.f);
+  }
+  cluster_sync();  // every CTA's slot is published
+  if (threadIdx.x == 0) {
+    float M = -INFINITY, Sx = 0.f, xt = 0.f;
+    bool found = false;
+    for (uint32_t r = 0; r < LL_CTAS; ++r) {
+      float4 o;
+      asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
+                   : "r"(cluster_addr(smem_u32(&slot), r)));
+      ll_merge(M, Sx, o.x, o.y);
+      if (o.w != 0.f) {
+        xt = o.z;
+        found = true;
+      }
+    }
+    const float lse2 = M + log2f(Sx);
+    const int64_t seq = row / p.S;
+    const float m = p.mask[row];
+    const bool valid = found && tgt >= 0 && tgt < p.V;
+    const float logp = valid ? xt - lse2 * LN2 : 0.f;
+    const float u = 1.f / (*p.mask_total + 1e-8f);
+    const TokenLoss t = token_loss(logp, p.old_lp[row], p.ref_lp ? p.ref_lp[row] : 0.f, p.ref_lp != nullptr,
+                                   p.adv[seq] * m, m, p.lo, p.hi, p.beta, u);
+    const float g = valid ? t.gnew : 0.f;
+    bc[0] = g;
+    bc[1] = lse2;
+    if (rank == 0) {
+      if (!valid) qb_set_err(p.err, QB_DEVERR_TOKEN);
+      p.new_lp[row] = logp;
+      if (p.grad_new) p.grad_new[row] = g;
+      p.row_part[2 * row] = t.surr_m;
+      p.row_part[2 * row + 1] = t.kl_m;
+    }
+  }
+  // done with the other CTAs' slots; they may leave once everyone has read
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  __syncthreads();
+  const float g = bc[0], lse2 = bc[1];
+  if (ready) {
+    for (int v = threadIdx.x; v < nel / 8; v += LL_THREADS) {
+      const uint4 u = reinterpret_cast<const uint4*>(sx)[v];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      uint32_t o[4];
+      const int64_t c = c0 + 8 * (int64_t)v;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(w[j]);
+        const float a = ((c + 2 * j == tgt) ? g : 0.f) - g * exp2f(fmaf(f.x, L2E, -lse2));
+        const float b = ((c + 2 * j + 1 == tgt) ? g : 0.f) - g * exp2f(fmaf(f.y, L2E, -lse2));
+        o[j] = pack_bf16x2(a, b);
+      }
+      reinterpret_cast<uint4*>(grow + c)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// loss_out (+=) from the per-token terms, summed in a fixed order.
+__global__ void logit_loss_reduce_kernel(const float* __restrict__ row_part, int64_t n_rows,
+                                         const float* __restrict__ mask_total, float beta, float* loss_out) {
+  __shared__ float red[32];
+  float su = 0.f, kl = 0.f;
+  for (int64_t i = threadIdx.x; i < n_rows; i += blockDim.x) {
+    su += row_part[2 * i];
+    kl += row_part[2 * i + 1];
+  }
+  su = block_sum(su, red);
+  kl = block_sum(kl, red);
+  if (threadIdx.x == 0 && loss_out) {
+    const float d = *mask_total + 1e-8f;
+    loss_out[0] += su / d + beta * (kl / d);
+    loss_out[1] += su / d;
+    loss_out[2] += kl / d;
   }
 }
 
@@ -885,4 +1094,72 @@ extern "C" int qb_grpo_loss_noalloc(const float* rewards, const int64_t* group_i
   if (e != cudaSuccess) return QB_ERR_CUDA_BASE + (int)e;
   return qb_grpo_loss(rewards, group_ids, n_rows, S, row_begin, row_end, new_lp, old_lp, ref_lp, mask, mask_total,
                       clip_eps, beta, grad_scale, grad_new, loss_out, adv_out, ws, stream);
+}
+
+// ================================================================ single-pass config-1 path
+namespace {
+size_t ll_align(size_t x) { return (x + 255) / 256 * 256; }
+}  // namespace
+
+extern "C" size_t qb_grpo_logit_loss_workspace_bytes(int64_t n_seqs, int64_t S) {
+  if (n_seqs <= 0 || S <= 0) return 256;
+  // advantages [n_seqs] | per-token terms [2 n S] | mask-sum scratch (qb_grpo_workspace_bytes)
+  return ll_align((size_t)n_seqs * 4) + ll_align((size_t)n_seqs * S * 8) + ll_align(qb_grpo_workspace_bytes(n_seqs * S));
+}
+
+extern "C" int qb_grpo_logit_loss(void* logits, int64_t ld, int64_t V, const int64_t* targets, const float* rewards,
+                                  const int64_t* group_ids, int64_t n_seqs, int64_t S, const float* old_lp,
+                                  const float* ref_lp, const float* mask, const float* mask_total, float clip_eps,
+                                  float beta, float* new_lp, float* grad_new, float* loss_out, float* adv_out,
+                                  void* workspace, int* err, qb_stream_t stream) {
+  QB_CHECK_ARG(n_seqs >= 0 && n_seqs <= 65536 && S >= 0 && V > 0 && ld >= V);
+  if (n_seqs == 0 || S == 0) return QB_OK;
+  QB_CHECK_ARG(logits && targets && rewards && group_ids && old_lp && mask && new_lp && workspace);
+  QB_CHECK_ARG(al16(logits) && ld % 8 == 0 && V % 8 == 0 && al16(workspace));
+  const int64_t n_rows = n_seqs * S;
+  QB_CHECK_ARG(n_rows <= (1ll << 29));  // grid = n_rows * LL_CTAS CTAs
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  float* adv = reinterpret_cast<float*>(ws);
+  float* part = reinterpret_cast<float*>(ws + ll_align((size_t)n_seqs * 4));
+  void* ms_ws = ws + ll_align((size_t)n_seqs * 4) + ll_align((size_t)n_rows * 8);
+  const float* denom = mask_total;
+  if (!denom) {
+    // the mask-sum scratch keeps its ticket at zero between calls; clear it once here
+    if (cudaMemsetAsync(ms_ws, 0, 16, st) != cudaSuccess) return qb_launch_status();
+    float* slot = reinterpret_cast<float*>(reinterpret_cast<uint32_t*>(ms_ws) + 2);
+    int e = qb_mask_sum(mask, n_rows, slot, ms_ws, stream);
+    if (e != QB_OK) return e;
+    denom = slot;
+  }
+  advantage_kernel<<<(unsigned)n_seqs, 256, 0, st>>>(rewards, group_ids, n_seqs, adv);
+  if (adv_out && cudaMemcpyAsync(adv_out, adv, n_seqs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return qb_launch_status();
+  const int chunk = (int)(((V + LL_CTAS - 1) / LL_CTAS + 7) / 8 * 8);
+  const int smem = chunk * 2;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(logit_loss_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+      return qb_launch_status();
+    attr = true;
+  }
+  if (smem > 200 * 1024) return QB_ERR_UNSUPPORTED;
+  LogitLossParams p{(bf16*)logits, ld, V, n_rows, S, targets, adv, old_lp, ref_lp, mask, denom,
+                    (float)(1.0 - (double)clip_eps), (float)(1.0 + (double)clip_eps), beta, new_lp, grad_new, part,
+                    chunk, err};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_rows * LL_CTAS));
+  cfg.blockDim = dim3(LL_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = LL_CTAS;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, logit_loss_kernel, p) != cudaSuccess) return qb_launch_status();
+  logit_loss_reduce_kernel<<<1, 1024, 0, st>>>(part, n_rows, denom, beta, loss_out);
+  return qb_launch_status();
 }

@@ -25,6 +25,7 @@ __all__ = [
     "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "attention_packed", "attention_paged_prefill",
     "paged_decode_attention", "silu_mul", "add", "linear", "logprob", "sample", "grpo_advantage",
     "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan", "lm_head_logprob",
+    "grpo_logit_loss",
 ]
 
 BF16 = torch.bfloat16
@@ -643,6 +644,32 @@ def grpo_workspace(n_rows: int, device) -> torch.Tensor:
         ws = torch.zeros((nbytes + 3) // 4, dtype=torch.float32, device=device)
         _WS[key] = ws
     return ws
+
+
+def grpo_logit_loss(logits, targets, rewards, group_ids, old_lp, mask, *, ref_lp=None, mask_total=None,
+                    clip_eps=0.2, beta=0.0, grad_new=None, loss_out=None):
+    """``qb_grpo_logit_loss``: log-probs, advantages, clipped + KL loss and d loss / d logits in one
+    read and one write of the bf16 ``logits`` [N*S, V] (overwritten with the gradient).
+    old_lp / mask / ref_lp are [N, S] fp32.  Returns (new_lp [N, S], loss[3], adv [N])."""
+    _cuda(logits, targets, rewards, group_ids, old_lp, mask, ref_lp, mask_total)
+    N, S = mask.shape
+    V = logits.shape[1]
+    if logits.dtype != BF16 or logits.stride(1) != 1 or logits.shape[0] != N * S:
+        raise NativeError("grpo_logit_loss needs bf16 logits [N*S, V] with unit column stride")
+    new_lp = torch.empty(N, S, dtype=torch.float32, device=logits.device)
+    if loss_out is None:
+        loss_out = torch.zeros(3, dtype=torch.float32, device=logits.device)
+    adv = torch.empty(N, dtype=torch.float32, device=logits.device)
+    ws = torch.empty((lib().qb_grpo_logit_loss_workspace_bytes(N, S) + 3) // 4, dtype=torch.float32,
+                     device=logits.device)
+    f = lambda t: None if t is None else t.float().contiguous()
+    old_lp, mask, ref_lp = f(old_lp), f(mask), f(ref_lp)
+    check(lib().qb_grpo_logit_loss(_p(logits), logits.stride(0), V, _p(targets.long().contiguous()),
+                                   _p(rewards.float().contiguous()), _p(group_ids.long().contiguous()), N, S,
+                                   _p(old_lp), _p(ref_lp), _p(mask), _p(mask_total), float(clip_eps), float(beta),
+                                   _p(new_lp), _p(grad_new), _p(loss_out), _p(adv), _p(ws), _p(err_flag()),
+                                   stream_ptr()), "qb_grpo_logit_loss")
+    return new_lp, loss_out, adv
 
 
 def mask_sum(mask: torch.Tensor, out=None) -> torch.Tensor:

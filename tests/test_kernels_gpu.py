@@ -501,3 +501,47 @@ def test_lm_head_logprob_fused(cuda, n, V):
     out2 = out2.cpu()
     assert out2[1].item() == 0.0
     assert torch.equal(out2[keep & (torch.arange(n) != 1)], out[dest[keep & (torch.arange(n) != 1)]])
+
+
+@pytest.mark.parametrize("V,with_ref,given_total", [(1000, True, False), (151936, True, True), (151936, False, False)])
+def test_grpo_logit_loss_single_pass(cuda, V, with_ref, given_total):
+    """qb_grpo_logit_loss (config 1's pass in one read and one write of the logits, rows split over
+    4-CTA clusters) against the oracle's fp32 autograd of log_softmax + gather -> advantages ->
+    clipped surrogate (+ 0.04 k3 KL): log-probs per element, advantages, loss, and d loss / d
+    logits per element within one bf16 ulp."""
+    g = gen(71 + V)
+    N, S = 8, 24
+    logits = (torch.randn(N * S, V, generator=g) * 1.5).to(BF)
+    tgt = torch.randint(0, V, (N * S,), generator=g)
+    rewards = torch.bernoulli(torch.full((N,), 0.5), generator=g)
+    gids = torch.arange(N) // 4
+    lens = torch.randint(1, S + 1, (N,), generator=g)
+    mask = (torch.arange(S)[None, :] < lens[:, None]).float()
+    x = logits.float().requires_grad_(True)
+    lp = torch.log_softmax(x, -1).gather(-1, tgt[:, None]).squeeze(-1).view(N, S)
+    old = lp.detach() + 0.05 * torch.randn(N, S, generator=g)
+    ref = lp.detach() + 0.05 * torch.randn(N, S, generator=g) if with_ref else None
+    adv = R.grpo_advantage(rewards, gids)
+    loss = R.ppo_loss(old, lp, adv[:, None] * mask, mask, 0.2, ref, 0.04 if with_ref else 0.0)
+    loss.backward()
+    work = logits.to(cuda)
+    new_lp, loss3, adv_d = ops.grpo_logit_loss(
+        work, tgt.to(cuda), rewards.to(cuda), gids.to(cuda), old.to(cuda), mask.to(cuda),
+        ref_lp=None if ref is None else ref.to(cuda), mask_total=mask.sum().reshape(1).to(cuda) if given_total else None,
+        beta=0.04 if with_ref else 0.0)
+    ops.check_device_errors()
+    assert ((new_lp.cpu() - lp.detach()).abs() <= 2e-5 * lp.detach().abs() + 1e-6).all()
+    assert torch.allclose(adv_d.cpu(), adv, rtol=1e-6, atol=1e-6)
+    assert abs(loss3[0].item() - loss.item()) <= 1e-5 * (abs(loss.item()) + 1e-3)
+    gr = x.grad
+    ulp = torch.exp2(torch.floor(torch.log2(gr.abs().clamp_min(2.0 ** -126))) - 7)
+    d = (work.float().cpu() - gr).abs()
+    assert (d <= ulp + 1e-10).all(), d.max().item()
+    # a target outside the vocabulary: error bit, log-prob 0, zero gradient row
+    tgt[5] = V + 3
+    work = logits.to(cuda)
+    new_lp, _, _ = ops.grpo_logit_loss(work, tgt.to(cuda), rewards.to(cuda), gids.to(cuda), old.to(cuda),
+                                       mask.to(cuda))
+    with pytest.raises(ops.NativeError):
+        ops.check_device_errors()
+    assert new_lp.view(-1)[5].item() == 0.0 and work[5].float().abs().max().item() == 0.0
