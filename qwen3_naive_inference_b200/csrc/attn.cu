@@ -1141,6 +1141,12 @@ inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) =
 }  // namespace
 
 // ================================================================ C ABI
+// tcgen05 forward for packed sequences (attn_tc.cu)
+int attn_fwd_tc_launch(const void* q, int64_t q_stride, const void* k, const void* v, int64_t kv_stride,
+                       const int32_t* cu_seqlens, int batch, const int32_t* tile_info, int n_tiles, int tiles_per_seq,
+                       int hq, int hkv, float scale, void* out, int64_t o_stride, float* lse, int64_t total_q, int* err,
+                       cudaStream_t st);
+
 extern "C" size_t qb_paged_decode_workspace_bytes(int batch, int hq, int Dh, int max_splits) {
   if (max_splits <= 1) return 0;
   return (size_t)batch * max_splits * hq * (Dh + 4) * sizeof(float);
@@ -1242,6 +1248,10 @@ extern "C" int qb_attn_varlen_fwd(const void* q, int64_t q_stride, const void* k
   QB_CHECK_ARG(al16(q) && al16(k) && al16(v) && al16(out) && q_stride % 8 == 0 && o_stride % 8 == 0);
   QB_CHECK_ARG(paged ? (num_blocks > 0 && bt_stride > 0) : (kv_stride % 8 == 0));
   QB_CHECK_ARG(lse == nullptr || total_q > 0);
+  if (!paged && hq == 2 * hkv && cu_seqlens_q == cu_seqlens_k)  // training / recompute: tcgen05 kernel
+    return attn_fwd_tc_launch(q, q_stride, k, v, kv_stride, cu_seqlens_q, batch, tile_info, n_tiles,
+                              tile_info ? 0 : tiles_per_seq, hq, hkv, scale, out, o_stride, lse, total_q, err,
+                              (cudaStream_t)stream);
   FwdParams p{(const bf16*)q, q_stride, (const bf16*)k, (const bf16*)v, kv_stride, block_tables, bt_stride,
               num_blocks, cu_seqlens_q, cu_seqlens_k, tile_info, tiles_per_seq, hq, hkv, scale * LOG2E,
               (bf16*)out, o_stride, lse, total_q, err};

@@ -1,0 +1,327 @@
+// Causal GQA attention forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Replaces the dense varlen branch of flash_attn_varlen_func used by the training / recompute
+// forward (qwen3_naive.py:540-548 and the manual attention of Qwen3Attention.forward,
+// :553-593) for packed sequences, Lq == Lk.
+//
+// One CTA owns 64 query positions of one sequence and one kv head.  Both query heads of the kv
+// group are stacked into the 128 rows of one MMA tile (rows 0-63: head 2*kvh, rows 64-127: head
+// 2*kvh+1), so each K/V tile is read from memory once for both heads.  Keys come in tiles of 64;
+// two CTAs share an SM (96 KB of shared memory and 256 TMEM columns each), so one CTA's start-up
+// and epilogue overlap the other's main loop.
+//   warp 0     TMA producer: Q once (4 boxes), then K (K-major) and V (MN-major, two 64-wide d
+//              atoms) of each key tile into a two-stage ring (32 KB per stage);
+//   warp 1     allocates 256 TMEM columns; one thread issues tcgen05.mma:
+//                S_b = Q K_j^T       (A, B from shared memory; fp32 S in TMEM columns [64 b, +64))
+//                O  += P_{j-1} V_{j-1} (A = P from TMEM, aliasing S_{b'}; B = V, MN-major)
+//              software-pipelined so that S_j is computed while the softmax works on S_{j-1};
+//   warps 2-5  softmax, one thread per row (TMEM lane): causal mask, running max in the log2
+//              domain, P = exp2(S - max) written back into TMEM as bf16 pairs, running row sum;
+//              the O accumulator (TMEM columns [128, 256)) is rescaled in place only when a row's
+//              max grows by more than 2^8 (otherwise the stale max keeps every P below 256); at
+//              the end O / l is stored as bf16 and the log-sum-exp for the backward.
+// Every mbarrier wait is bounded (~2 s): on timeout the kernel raises QB_DEVERR_TIMEOUT, all roles
+// leave their loops, the producer drains its copies, the MMA issuer waits for its MMAs, TMEM is
+// freed.  Every TMA load reads this GPU's memory; no cluster multicast.
+#include "tcgen05.cuh"
+
+namespace {
+
+constexpr int AT_THREADS = 192;                      // producer warp, MMA warp, softmax warpgroup
+constexpr int AT_QPOS = 64;                           // query positions per CTA (x 2 heads = 128 rows)
+constexpr int AT_KEYS = 64;                           // keys per tile
+constexpr int AT_Q_HALF = 128 * 64 * 2;               // Q sub-tile [128 rows x 64 d]: 16 KB
+constexpr int AT_Q_BYTES = 2 * AT_Q_HALF;             // Q: d halves 0-63, 64-127
+constexpr int AT_K_HALF = AT_KEYS * 64 * 2;           // K sub-tile [64 keys x 64 d]: 8 KB
+constexpr int AT_KV_BYTES = 2 * AT_K_HALF;            // K or V tile: 16 KB
+constexpr int AT_STAGE_BYTES = 2 * AT_KV_BYTES;       // K then V
+constexpr int AT_STAGES = 2;
+constexpr int AT_SMEM = AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES + 1024 /*align*/ + 128 /*barriers*/;
+constexpr int AT_TMEM_COLS = 256;                     // S buffers [0,64), [64,128); O [128,256)
+constexpr uint32_t AT_O_COL = 128;
+constexpr float AT_RESCALE = 8.f;                     // rescale O only when a max grows by > 2^8
+
+// kind::f16, D fp32, A/B bf16, M = 128; S: N = 64, both K-major; PV: N = 128, B (V) MN-major.
+constexpr uint32_t IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t IDESC_PV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((128u >> 3) << 17) |
+                              ((128u >> 4) << 24);
+
+struct AttnTcParams {
+  const int32_t* cu;     // [batch + 1] packed sequence starts (queries and keys alike)
+  const int32_t* tiles;  // [n_tiles, 2]: (sequence, first query position of a 64-position tile)
+  int tiles_per_seq;
+  int hq, hkv;
+  float scale_log2;      // softmax scale * log2(e)
+  bf16* out;
+  int64_t o_stride;
+  float* lse;            // nullable [hq, total_q], natural log
+  int64_t total_q;
+  int* err;
+};
+
+__global__ void __launch_bounds__(AT_THREADS, 2)
+attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                   const __grid_constant__ CUtensorMap tv, AttnTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const int tile = blockIdx.x, kvh = blockIdx.y;
+  const int b = p.tiles ? p.tiles[2 * tile] : tile / p.tiles_per_seq;
+  const int q_start = p.tiles ? p.tiles[2 * tile + 1] : (tile % p.tiles_per_seq) * AT_QPOS;
+  const int s0 = p.cu[b], L = p.cu[b + 1] - s0;
+  if (q_start >= L) return;  // uniform across the CTA, before any barrier or TMEM exists
+  const int n_kv = min(L, q_start + AT_QPOS);
+  const int n_tiles = (n_kv + AT_KEYS - 1) / AT_KEYS;
+  const int h0 = 2 * kvh;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023) & ~1023u;  // SW128 atoms need 1024-byte alignment
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sQ = base;
+  auto sK = [&](int s) { return base + AT_Q_BYTES + s * AT_STAGE_BYTES; };
+  auto sV = [&](int s) { return base + AT_Q_BYTES + s * AT_STAGE_BYTES + AT_KV_BYTES; };
+  const uint32_t bar0 = base + AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES;
+  // q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_ready[2], o_done, o_last, done
+  const uint32_t q_full = bar0;
+  auto kv_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto kv_empty = [&](int s) { return bar0 + 8 * (3 + s); };
+  auto s_full = [&](int x) { return bar0 + 8 * (5 + x); };
+  auto s_free = [&](int x) { return bar0 + 8 * (7 + x); };
+  auto p_ready = [&](int x) { return bar0 + 8 * (9 + x); };
+  const uint32_t o_done = bar0 + 8 * 11, o_last = bar0 + 8 * 12, done_bar = bar0 + 8 * 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES + 8 * 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(kv_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+      mbar_init(s_full(s), 1);
+      mbar_init(s_free(s), 1);
+      mbar_init(p_ready(s), 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_last, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tv)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(AT_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    mbar_expect_tx(q_full, AT_Q_BYTES);
+    for (int d = 0; d < 2; ++d)
+      for (int hh = 0; hh < 2; ++hh)
+        tma_load_2d(sQ + d * AT_Q_HALF + hh * (AT_Q_HALF / 2), &tq, (h0 + hh) * 128 + d * 64, s0 + q_start,
+                    q_full);
+    uint32_t issued = 0, last_parity = 0;  // per stage: a load is in flight; its phase parity
+    for (int j = 0; j < n_tiles && !*abort_flag; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+      if (!mbar_wait(kv_empty(st), ph ^ 1, abort_flag, p.err)) break;
+      mbar_expect_tx(kv_full(st), AT_STAGE_BYTES);
+      const int key0 = s0 + j * AT_KEYS;
+      for (int d = 0; d < 2; ++d) {
+        tma_load_2d(sK(st) + d * AT_K_HALF, &tk, kvh * 128 + d * 64, key0, kv_full(st));    // K-major
+        tma_load_2d(sV(st) + d * AT_K_HALF, &tv, kvh * 128 + d * 64, key0, kv_full(st));    // MN atom d
+      }
+      issued |= 1u << st;
+      last_parity = (last_parity & ~(1u << st)) | (ph << st);
+    }
+    // never leave with a copy in flight into this CTA's shared memory
+    mbar_drain(q_full, 0);
+    for (int st = 0; st < 2; ++st)
+      if (issued & (1u << st)) mbar_drain(kv_full(st), (last_parity >> st) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    bool ok = mbar_wait(q_full, 0, abort_flag, p.err);
+    for (int j = 0; ok && j <= n_tiles; ++j) {
+      if (j < n_tiles) {
+        const int st = j & 1, x = j & 1;
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (!mbar_wait(kv_full(st), ph, abort_flag, p.err) || !mbar_wait(s_free(x), ph ^ 1, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)  // d = 128 in K-steps of 16: sub-tile k/4, 32 B each inside it
+          umma_bf16(tmem + x * AT_KEYS, sw128_kmajor_desc(sQ + (k >> 2) * AT_Q_HALF + (k & 3) * 32),
+                    sw128_kmajor_desc(sK(st) + (k >> 2) * AT_K_HALF + (k & 3) * 32), IDESC_S, k > 0);
+        umma_commit(s_full(x));
+      }
+      if (j > 0) {
+        const int i = j - 1, st = i & 1, x = i & 1;
+        if (!mbar_wait(p_ready(x), (uint32_t)(i >> 1) & 1u, abort_flag, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // 64 keys in K-steps of 16: P columns x*64 + 8k; V rows 16k
+          umma_bf16_ts(tmem + AT_O_COL, tmem + x * AT_KEYS + 8 * k, sw128_mnmajor_desc(sV(st) + k * 16 * 128),
+                       IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(i + 1 == n_tiles ? o_last : o_done);
+        umma_commit(kv_empty(st));
+        umma_commit(s_free(x));
+      }
+    }
+    // no MMA may still be reading shared memory or writing TMEM when the CTA leaves
+    umma_commit(done_bar);
+    mbar_drain(done_bar, 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;       // TMEM lane = tile row
+    const int hh = r >> 6, pos = q_start + (r & 63);
+    const bool live = pos < L;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int lim = live ? pos : -1;  // inclusive causal limit (dense: query i sees keys <= i)
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int x = j & 1;
+      if (!mbar_wait(s_full(x), (uint32_t)(j >> 1) & 1u, abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      uint32_t v[64];
+      tmem_ld32(t_lane + x * AT_KEYS, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld32(t_lane + x * AT_KEYS + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      const int k0 = j * AT_KEYS;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i)
+        if (k0 + i <= lim) mt = fmaxf(mt, __uint_as_float(v[i]));
+      mt *= p.scale_log2;
+      if (mt > m_ref + AT_RESCALE || (m_ref == -INFINITY && mt > -INFINITY)) {
+        const float alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
+        m_ref = mt;
+        l *= alpha;
+        if (j > 0) {  // O holds P_0..P_{j-1} V: wait for the last of them, then rescale this row
+          if (!mbar_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          __syncwarp();
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 128; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + AT_O_COL + c, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_lane + AT_O_COL + c, o);
+          }
+        }
+      }
+      // P = exp2(S - max) as bf16 pairs over the first 32 columns of this S buffer
+      const float mref = m_ref == -INFINITY ? 0.f : m_ref;
+      float rs = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int k = k0 + 2 * i;
+        const float a = k <= lim ? exp2f(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, -mref)) : 0.f;
+        const float bb = k + 1 <= lim ? exp2f(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, -mref)) : 0.f;
+        rs += a + bb;
+        pk[i] = pack_bf16x2(a, bb);
+      }
+      tmem_st32(t_lane + x * AT_KEYS, pk);
+      l += rs;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_ready(x));
+    }
+    // epilogue: O / l -> bf16, and the row's log-sum-exp
+    if (ok && mbar_wait(o_last, 0, abort_flag, p.err)) {
+      __syncwarp();
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = p.out + (int64_t)(s0 + pos) * p.o_stride + (h0 + hh) * 128;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + AT_O_COL + c, o);
+        if (live) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+            reinterpret_cast<uint4*>(orow + c)[q] = w;
+          }
+        }
+      }
+      if (live && p.lse)
+        p.lse[(int64_t)(h0 + hh) * p.total_q + s0 + pos] = l > 0.f ? (m_ref + log2f(l)) * 0.6931471805599453f
+                                                                   : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AT_TMEM_COLS));
+  }
+}
+
+// 2-D bf16 tensor map over rows of `ld` elements: inner extent `inner`, box {64, box_rows}, 128-byte
+// swizzle, zero fill out of bounds.
+bool at_tmap(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+// Dense causal attention forward on tcgen05 for packed sequences (Lq == Lk); called by
+// qb_attn_varlen_fwd when block_tables is NULL, D == 128 and hq == 2 * hkv.
+int attn_fwd_tc_launch(const void* q, int64_t q_stride, const void* k, const void* v, int64_t kv_stride,
+                   const int32_t* cu_seqlens, int batch, const int32_t* tile_info, int n_tiles, int tiles_per_seq,
+                   int hq, int hkv, float scale, void* out, int64_t o_stride, float* lse, int64_t total_q, int* err,
+                   cudaStream_t st) {
+  const auto al16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
+  if (!al16(q) || !al16(k) || !al16(v) || q_stride % 8 || kv_stride % 8 || o_stride % 8 || !al16(out))
+    return QB_ERR_INVALID;
+  if (total_q <= 0 || n_tiles <= 0) return QB_OK;
+  CUtensorMap tq, tk, tv;
+  if (!at_tmap(&tq, q, (uint64_t)hq * 128, (uint64_t)total_q, (uint64_t)q_stride, 64) ||
+      !at_tmap(&tk, k, (uint64_t)hkv * 128, (uint64_t)total_q, (uint64_t)kv_stride, AT_KEYS) ||
+      !at_tmap(&tv, v, (uint64_t)hkv * 128, (uint64_t)total_q, (uint64_t)kv_stride, AT_KEYS))
+    return QB_ERR_INVALID;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM) != cudaSuccess)
+      return qb_launch_status();
+    attr = true;
+  }
+  AttnTcParams p{cu_seqlens, tile_info, tiles_per_seq, hq, hkv, scale * 1.4426950408889634f,
+                 (bf16*)out, o_stride, lse, total_q, err};
+  (void)batch;
+  attn_fwd_tc_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, p);
+  return qb_launch_status();
+}

@@ -17,71 +17,12 @@
 // Every mbarrier wait is bounded: on timeout the kernel raises QB_DEVERR_TIMEOUT, all
 // roles leave their loops, the producer waits (bounded) for its own copies, TMEM is
 // freed and the kernel returns.  Each CTA issues its own TMA loads from this GPU's memory.
-#include "tma.cuh"
+#include "tcgen05.cuh"
 
 namespace {
 
 constexpr int BM = 128, BK = 64;
 constexpr int THREADS = 192;
-QB_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-QB_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 bytes in
-// 8-row (1024-byte) groups: start>>4 | LBO 16 B | SBO 1024 B | version 1 | layout SW128.
-QB_DEVICE uint64_t sw128_kmajor_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)1 << 16;            // leading byte offset (16 B, unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset between 8-row groups
-  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
-  return d;
-}
-
-// MN-major operand (the matrix is stored [K rows][MN contiguous]): 64-element MN atoms of
-// 64 K-rows x 128 B (8 KB) side by side, each row 128-byte swizzled.  LBO = distance between
-// MN atoms (8 KB), SBO = distance between 8-row K groups (1024 B).
-QB_DEVICE uint64_t sw128_mnmajor_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-  d |= (uint64_t)(8192 >> 4) << 16;  // leading byte offset: next 64-wide MN atom
-  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8 K-rows
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Descriptor of K-step j (16 elements) inside a 64-deep K block.
-template <bool MN_MAJOR>
-QB_DEVICE uint64_t operand_desc(uint32_t stage_addr, int j) {
-  if (MN_MAJOR) return sw128_mnmajor_desc(stage_addr + j * 16 * 128);  // 16 K-rows of 128 B
-  return sw128_kmajor_desc(stage_addr + j * 32);                       // 16 elements = 32 B along the row
-}
-
-QB_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-QB_DEVICE void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// 32 lanes x 32 consecutive fp32 columns: lane i receives row (lane base + i), columns [col, col+32).
-QB_DEVICE void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // ---------------------------------------------------------------- kernel
 struct GemmParams {
   void* C;

@@ -208,8 +208,11 @@ def test_paged_prefill(cuda, qk):
         close_bf16(out, ref, 2e-2)
 
 
-@pytest.mark.parametrize("lens", [[1, 63, 64, 65, 200], [513]])
+@pytest.mark.parametrize("lens", [[1, 63, 64, 65, 200], [513], [1100, 40, 129]])
 def test_attention_packed_fwd_bwd(cuda, lens):
+    """Packed causal attention (the training path: tcgen05 forward, 64 query positions x 2 heads
+    per tile, 128-key tiles) against fp32 autograd; the forward per element within 2^-7 of
+    sum_j p_j |v_j| plus one bf16 ulp (P and the output are rounded to bf16)."""
     hq, hkv = 16, 8
     T = sum(lens)
     g = gen(T)
@@ -231,9 +234,24 @@ def test_attention_packed_fwd_bwd(cuda, lens):
         outs.append(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(L, -1))
     y = torch.cat(outs)
     y.backward(dout.float())
+    with torch.no_grad():
+        scale = []
+        for b in range(len(lens)):
+            s0, s1 = int(cu[b]), int(cu[b + 1])
+            L = s1 - s0
+            q = x[s0:s1, :hq * 128].reshape(L, hq, 128)
+            k = x[s0:s1, hq * 128:(hq + hkv) * 128].reshape(L, hkv, 128).repeat_interleave(2, 1)
+            v = x[s0:s1, (hq + hkv) * 128:].reshape(L, hkv, 128).repeat_interleave(2, 1)
+            s = torch.einsum("qhd,khd->hqk", q, k) * 128 ** -0.5
+            s = s.masked_fill(torch.triu(torch.ones(L, L), 1).bool()[None], float("-inf"))
+            scale.append(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v.abs()).reshape(L, -1))
+        scale = torch.cat(scale)
     xd = qkv.to(cuda).requires_grad_(True)
     yd = ops.attention_packed(xd, cu.to(cuda), tiles.to(cuda), hq, hkv, 128 ** -0.5)
     close_bf16(yd, y.detach(), 2e-2)
+    ym, yr = yd.detach().float().cpu(), y.detach()
+    ulp = torch.exp2(torch.floor(torch.log2(torch.maximum(ym.abs(), yr.abs()).clamp_min(2.0 ** -126))) - 7)
+    assert ((ym - yr).abs() <= 2 ** -7 * scale + ulp).all(), (ym - yr).abs().max().item()
     yd.backward(dout.to(cuda))
     close_bf16(xd.grad, x.grad, 3e-2)
 
