@@ -9,8 +9,9 @@
 // 2*kvh+1), so each K/V tile is read from memory once for both heads.  Keys come in tiles of 64;
 // two CTAs share an SM (96 KB of shared memory and 256 TMEM columns each), so one CTA's start-up
 // and epilogue overlap the other's main loop.
-//   warp 0     TMA producer: Q once (4 boxes), then K (K-major) and V (MN-major, two 64-wide d
-//              atoms) of each key tile into a two-stage ring (32 KB per stage);
+//   warp 0     TMA producers: lane 0 loads Q once (4 boxes) and runs the K ring (K-major, released
+//              as soon as S_j has read it), lane 1 the V ring (MN-major, two 64-wide d atoms,
+//              released after P_j V_j); two stages each;
 //   warp 1     allocates 256 TMEM columns; one thread issues tcgen05.mma:
 //                S_b = Q K_j^T       (A, B from shared memory; fp32 S in TMEM columns [64 b, +64))
 //                O  += P_{j-1} V_{j-1} (A = P from TMEM, aliasing S_{b'}; B = V, MN-major)
@@ -36,7 +37,7 @@ constexpr int AT_K_HALF = AT_KEYS * 64 * 2;           // K sub-tile [64 keys x 6
 constexpr int AT_KV_BYTES = 2 * AT_K_HALF;            // K or V tile: 16 KB
 constexpr int AT_STAGE_BYTES = 2 * AT_KV_BYTES;       // K then V
 constexpr int AT_STAGES = 2;
-constexpr int AT_SMEM = AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES + 1024 /*align*/ + 128 /*barriers*/;
+constexpr int AT_SMEM = AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES + 1024 /*align*/ + 160 /*barriers*/;
 constexpr int AT_TMEM_COLS = 256;                     // S buffers [0,64), [64,128); O [128,256)
 constexpr uint32_t AT_O_COL = 128;
 constexpr float AT_RESCALE = 8.f;                     // rescale O only when a max grows by > 2^8
@@ -79,23 +80,27 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
   auto sK = [&](int s) { return base + AT_Q_BYTES + s * AT_STAGE_BYTES; };
   auto sV = [&](int s) { return base + AT_Q_BYTES + s * AT_STAGE_BYTES + AT_KV_BYTES; };
   const uint32_t bar0 = base + AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES;
-  // q_full, kv_full[2], kv_empty[2], s_full[2], s_free[2], p_ready[2], o_done, o_last, done
+  // q_full, k_full[2], k_empty[2], s_full[2], s_free[2], p_ready[2], o_done, o_last, done, v_full[2], v_empty[2]
   const uint32_t q_full = bar0;
-  auto kv_full = [&](int s) { return bar0 + 8 * (1 + s); };
-  auto kv_empty = [&](int s) { return bar0 + 8 * (3 + s); };
+  auto k_full = [&](int s) { return bar0 + 8 * (1 + s); };
+  auto k_empty = [&](int s) { return bar0 + 8 * (3 + s); };
   auto s_full = [&](int x) { return bar0 + 8 * (5 + x); };
   auto s_free = [&](int x) { return bar0 + 8 * (7 + x); };
   auto p_ready = [&](int x) { return bar0 + 8 * (9 + x); };
+  auto v_full = [&](int s) { return bar0 + 8 * (14 + s); };
+  auto v_empty = [&](int s) { return bar0 + 8 * (16 + s); };
   const uint32_t o_done = bar0 + 8 * 11, o_last = bar0 + 8 * 12, done_bar = bar0 + 8 * 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES + 8 * 14);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + AT_Q_BYTES + AT_STAGES * AT_STAGE_BYTES + 8 * 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(kv_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
       mbar_init(s_full(s), 1);
       mbar_init(s_free(s), 1);
       mbar_init(p_ready(s), 128);
@@ -119,31 +124,38 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ TMA producer
-    mbar_expect_tx(q_full, AT_Q_BYTES);
-    for (int d = 0; d < 2; ++d)
-      for (int hh = 0; hh < 2; ++hh)
-        tma_load_2d(sQ + d * AT_Q_HALF + hh * (AT_Q_HALF / 2), &tq, (h0 + hh) * 128 + d * 64, s0 + q_start,
-                    q_full);
+  if (warp == 0 && lane < 2) {
+    // ------------------------------------------------------------ TMA producers
+    // lane 0: Q, then the K ring (a K tile is released as soon as S_j has read it);
+    // lane 1: the V ring (released after P_j V_j)
+    if (lane == 0) {
+      mbar_expect_tx(q_full, AT_Q_BYTES);
+      for (int d = 0; d < 2; ++d)
+        for (int hh = 0; hh < 2; ++hh)
+          tma_load_2d(sQ + d * AT_Q_HALF + hh * (AT_Q_HALF / 2), &tq, (h0 + hh) * 128 + d * 64, s0 + q_start,
+                      q_full);
+    }
     uint32_t issued = 0, last_parity = 0;  // per stage: a load is in flight; its phase parity
     for (int j = 0; j < n_tiles && !*abort_flag; ++j) {
       const int st = j & 1;
       const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-      if (!mbar_wait(kv_empty(st), ph ^ 1, abort_flag, p.err)) break;
-      mbar_expect_tx(kv_full(st), AT_STAGE_BYTES);
+      const uint32_t empty = lane == 0 ? k_empty(st) : v_empty(st), full = lane == 0 ? k_full(st) : v_full(st);
+      if (!mbar_wait(empty, ph ^ 1, abort_flag, p.err)) break;
+      mbar_expect_tx(full, AT_KV_BYTES);
       const int key0 = s0 + j * AT_KEYS;
       for (int d = 0; d < 2; ++d) {
-        tma_load_2d(sK(st) + d * AT_K_HALF, &tk, kvh * 128 + d * 64, key0, kv_full(st));    // K-major
-        tma_load_2d(sV(st) + d * AT_K_HALF, &tv, kvh * 128 + d * 64, key0, kv_full(st));    // MN atom d
+        if (lane == 0)
+          tma_load_2d(sK(st) + d * AT_K_HALF, &tk, kvh * 128 + d * 64, key0, full);  // K-major halves
+        else
+          tma_load_2d(sV(st) + d * AT_K_HALF, &tv, kvh * 128 + d * 64, key0, full);  // MN atom d
       }
       issued |= 1u << st;
       last_parity = (last_parity & ~(1u << st)) | (ph << st);
     }
     // never leave with a copy in flight into this CTA's shared memory
-    mbar_drain(q_full, 0);
+    if (lane == 0) mbar_drain(q_full, 0);
     for (int st = 0; st < 2; ++st)
-      if (issued & (1u << st)) mbar_drain(kv_full(st), (last_parity >> st) & 1);
+      if (issued & (1u << st)) mbar_drain(lane == 0 ? k_full(st) : v_full(st), (last_parity >> st) & 1);
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     bool ok = mbar_wait(q_full, 0, abort_flag, p.err);
@@ -151,7 +163,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       if (j < n_tiles) {
         const int st = j & 1, x = j & 1;
         const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(kv_full(st), ph, abort_flag, p.err) || !mbar_wait(s_free(x), ph ^ 1, abort_flag, p.err)) {
+        if (!mbar_wait(k_full(st), ph, abort_flag, p.err) || !mbar_wait(s_free(x), ph ^ 1, abort_flag, p.err)) {
           ok = false;
           break;
         }
@@ -161,10 +173,12 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
           umma_bf16(tmem + x * AT_KEYS, sw128_kmajor_desc(sQ + (k >> 2) * AT_Q_HALF + (k & 3) * 32),
                     sw128_kmajor_desc(sK(st) + (k >> 2) * AT_K_HALF + (k & 3) * 32), IDESC_S, k > 0);
         umma_commit(s_full(x));
+        umma_commit(k_empty(st));  // the K tile is free once S_j has read it
       }
       if (j > 0) {
         const int i = j - 1, st = i & 1, x = i & 1;
-        if (!mbar_wait(p_ready(x), (uint32_t)(i >> 1) & 1u, abort_flag, p.err)) {
+        if (!mbar_wait(p_ready(x), (uint32_t)(i >> 1) & 1u, abort_flag, p.err) ||
+            !mbar_wait(v_full(st), (uint32_t)(i >> 1) & 1u, abort_flag, p.err)) {
           ok = false;
           break;
         }
@@ -174,7 +188,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
           umma_bf16_ts(tmem + AT_O_COL, tmem + x * AT_KEYS + 8 * k, sw128_mnmajor_desc(sV(st) + k * 16 * 128),
                        IDESC_PV, (i > 0 || k > 0) ? 1u : 0u);
         umma_commit(i + 1 == n_tiles ? o_last : o_done);
-        umma_commit(kv_empty(st));
+        umma_commit(v_empty(st));
         umma_commit(s_free(x));
       }
     }
@@ -200,13 +214,23 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       __syncwarp();
       tc_fence_after();
       uint32_t v[64];
-      tmem_ld32(t_lane + x * AT_KEYS, *reinterpret_cast<uint32_t(*)[32]>(v));
-      tmem_ld32(t_lane + x * AT_KEYS + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld32_nowait(t_lane + x * AT_KEYS, v);
+      tmem_ld32_nowait(t_lane + x * AT_KEYS + 32, v + 32);
+      tmem_ld_wait();
       const int k0 = j * AT_KEYS;
-      float mt = -INFINITY;
+      const bool full = k0 + AT_KEYS - 1 <= lim;  // every key of the tile visible: no per-key mask
+      if (!full) {  // the diagonal tile: keys past the row's limit drop out of the max and the sum
 #pragma unroll
-      for (int i = 0; i < 64; ++i)
-        if (k0 + i <= lim) mt = fmaxf(mt, __uint_as_float(v[i]));
+        for (int i = 0; i < 64; ++i)
+          if (k0 + i > lim) v[i] = __float_as_uint(-INFINITY);
+      }
+      // row max over eight independent chains (a single chain would serialise 64 dependent maxes)
+      float mx[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx[c] = __uint_as_float(v[c]);
+#pragma unroll
+      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(v[i]));
+      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       mt *= p.scale_log2;
       if (mt > m_ref + AT_RESCALE || (m_ref == -INFINITY && mt > -INFINITY)) {
         const float alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
@@ -231,16 +255,17 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       }
       // P = exp2(S - max) as bf16 pairs over the first 32 columns of this S buffer
       const float mref = m_ref == -INFINITY ? 0.f : m_ref;
-      float rs = 0.f;
+      // masked keys hold -inf: exp2 gives 0 (a fully masked row has mref 0 and stays at 0)
+      float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const int k = k0 + 2 * i;
-        const float a = k <= lim ? exp2f(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, -mref)) : 0.f;
-        const float bb = k + 1 <= lim ? exp2f(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, -mref)) : 0.f;
-        rs += a + bb;
+        const float a = fast_exp2(fmaf(__uint_as_float(v[2 * i]), p.scale_log2, -mref));
+        const float bb = fast_exp2(fmaf(__uint_as_float(v[2 * i + 1]), p.scale_log2, -mref));
+        rsum[i & 7] += a + bb;
         pk[i] = pack_bf16x2(a, bb);
       }
+      const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
       tmem_st32(t_lane + x * AT_KEYS, pk);
       l += rs;
       tmem_st_wait();
