@@ -9,7 +9,7 @@ U[64, 512], ids U[0, 151643); 512 new tokens (no EOS), temperature 1.0, no top-k
 paged KV pages of 256; then log-prob recompute of the policy and a frozen reference
 copy, group advantages, clipped surrogate + 0.04 * k3 KL, backward, AdamW lr 1e-6.
 Rewards are Bernoulli(0.5).  Under torchrun each rank runs its own 64 prompt groups
-(weak scaling), sums the response-token count and the bf16 gradients with NCCL, and
+(weak scaling), sums the response-token count and the fp32 gradients with NCCL, and
 steps AdamW on the global loss.  Inputs are synthetic (no dataset exists for this path).
 
 metric: GRPO step tokens/s = (prompt + completion tokens of all ranks) / step time.
@@ -40,6 +40,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "GRPO step tokens/s"
 UNIT = "tokens/s"
 WORKLOAD = "grpo_step_cfg4: 64 prompts x G=8 per GPU, prompt U[64,512], 512 new tokens, Qwen3-0.6B shape"
+WORKLOAD5 = ("grpo_step_cfg5: 512 prompts x G=8 in total, groups sharded round-robin over the ranks, prompt "
+             "U[64,1024], 512 new tokens, Qwen3-0.6B shape")
 
 
 def parse():
@@ -49,6 +51,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompts", type=int, default=64, help="prompt groups per GPU")
+    ap.add_argument("--workload", default="cfg4", choices=["cfg4", "cfg5"],
+                    help="cfg4: 64 groups per GPU, prompt U[64,512] (weak scaling, the default); cfg5: 512 groups "
+                         "in total sharded over the ranks, prompt U[64,1024] (strong scaling)")
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--new-tokens", type=int, default=512)
     ap.add_argument("--prompt-min", type=int, default=64)
@@ -136,10 +141,18 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------------ workload
 def make_prompts(args, rank, step, device=None):
+    """This rank's prompt groups of one step.  cfg4: args.prompts groups per rank drawn per rank;
+    cfg5: one global list of args.total_prompts groups per step, rank r taking groups r, r+N, ..."""
     import torch
-    g = torch.Generator().manual_seed(1 + 1000 * rank + step)
-    lens = torch.randint(args.prompt_min, args.prompt_max + 1, (args.prompts,), generator=g)
-    prompts = [torch.randint(0, 151643, (1, int(L)), generator=g) for L in lens]
+    if args.workload == "cfg5":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        g = torch.Generator().manual_seed(1 + step)
+        lens = torch.randint(args.prompt_min, args.prompt_max + 1, (args.total_prompts,), generator=g)
+        prompts = [torch.randint(0, 151643, (1, int(L)), generator=g) for L in lens][rank::world]
+    else:
+        g = torch.Generator().manual_seed(1 + 1000 * rank + step)
+        lens = torch.randint(args.prompt_min, args.prompt_max + 1, (args.prompts,), generator=g)
+        prompts = [torch.randint(0, 151643, (1, int(L)), generator=g) for L in lens]
     if device is not None:
         prompts = [p.to(device) for p in prompts]
     return prompts
@@ -375,8 +388,12 @@ def run_ours(args):
     policy = build_model(cfg, device=dev, seed=0)
     ref = G.make_reference_copy(policy)
     max_ctx = args.prompt_max + args.new_tokens
-    # pages for every sequence of the step at once (64*8 seqs x 4 pages) plus slack
-    policy._num_blocks = args.prompts * args.group * math.ceil(max_ctx / 256) + 64
+    # pages for every sequence of the step at once (64*8 seqs x 4 pages) plus slack; a larger
+    # share (cfg5 on few GPUs) gets what fits in memory and the scheduler admits groups in waves
+    need = len(make_prompts(args, rank, 0)) * args.group * math.ceil(max_ctx / 256) + 64
+    free, _ = torch.cuda.mem_get_info(dev)
+    fit = int((free - (24 << 30)) // policy._block_bytes())  # keep 24 GB for activations and the step
+    policy._num_blocks = max(64, min(need, fit))
     policy.max_model_len = max_ctx
     policy.use_cuda_graphs = not args.no_graphs
     opt = torch.optim.AdamW(policy.parameters(), lr=1e-6)
@@ -510,8 +527,11 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "prompts_per_gpu": args.prompts, "group": args.group,
+                "scaling": "strong" if args.workload == "cfg5" else "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": WORKLOAD if args.workload == "cfg4" else WORKLOAD5,
+                           "prompts_per_gpu": len(make_prompts(args, rank, 0)), "group": args.group,
+                           "kv_pages": policy._num_blocks,
                            "new_tokens": args.new_tokens, "prompt_len": [args.prompt_min, args.prompt_max],
                            "layers": args.layers, "parallelism": f"dp{world}", "beta_kl": 0.04,
                            "rollout": "reference scheduler" if args.no_share_prefix else
@@ -1075,6 +1095,9 @@ def run_attn_only():
 
 def main():
     args = parse()
+    args.total_prompts = 512
+    if args.workload == "cfg5" and args.prompt_max == 512:
+        args.prompt_max = 1024
     if args.rollout_attn:
         run_rollout_attn()
     elif args.attn_only:

@@ -1147,6 +1147,16 @@ int attn_fwd_tc_launch(const void* q, int64_t q_stride, const void* k, const voi
                        int hq, int hkv, float scale, void* out, int64_t o_stride, float* lse, int64_t total_q, int* err,
                        cudaStream_t st);
 
+int attn_bwd_dkdv_tc_launch(const void* q, const void* k, const void* v, int64_t stride, const void* dout,
+                            int64_t o_stride, const float* lse, const float* delta, const int32_t* cu_seqlens,
+                            const int32_t* tile_info, int n_tiles, int hq, int hkv, float scale, int64_t total,
+                            void* dk, void* dv, int* err, cudaStream_t st);
+
+int attn_bwd_dq_tc_launch(const void* q, const void* k, const void* v, int64_t stride, const void* dout,
+                          int64_t o_stride, const float* lse, const float* delta, const int32_t* cu_seqlens,
+                          const int32_t* tile_info, int n_tiles, int hq, int hkv, float scale, int64_t total, void* dq,
+                          int* err, cudaStream_t st);
+
 extern "C" size_t qb_paged_decode_workspace_bytes(int batch, int hq, int Dh, int max_splits) {
   if (max_splits <= 1) return 0;
   return (size_t)batch * max_splits * hq * (Dh + 4) * sizeof(float);
@@ -1299,9 +1309,17 @@ extern "C" int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, i
     cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM);
     set = true;
   }
-  attn_bwd_dkdv_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), 128, DKDV_SMEM, (cudaStream_t)stream>>>(p);
-  st = qb_launch_status();
+  if (hq == 2 * hkv) {  // dK, dV on tcgen05
+    st = attn_bwd_dkdv_tc_launch(q, k, v, stride, dout, o_stride, lse, delta, cu_seqlens, tile_info, n_tiles, hq,
+                                 hkv, scale, total, dk, dv, err, (cudaStream_t)stream);
+  } else {
+    attn_bwd_dkdv_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), 128, DKDV_SMEM, (cudaStream_t)stream>>>(p);
+    st = qb_launch_status();
+  }
   if (st != QB_OK) return st;
+  if (hq == 2 * hkv)  // dQ on tcgen05
+    return attn_bwd_dq_tc_launch(q, k, v, stride, dout, o_stride, lse, delta, cu_seqlens, tile_info, n_tiles, hq, hkv,
+                                 scale, total, dq, err, (cudaStream_t)stream);
   attn_bwd_dq_kernel<<<dim3((unsigned)n_tiles, (unsigned)hq), 128, DQ_SMEM, (cudaStream_t)stream>>>(p);
   return qb_launch_status();
 }

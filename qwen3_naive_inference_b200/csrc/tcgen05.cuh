@@ -33,6 +33,19 @@ QB_DEVICE uint64_t sw128_mnmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// MN-major operand whose 64-wide MN atoms lie `lbo` bytes apart (each atom: K-rows of 128 B in
+// 1024-byte 8-row groups, 128-byte swizzled) -- e.g. a [rows x 128] tile kept as two [rows x 64]
+// halves, read with the rows as the K dimension.
+QB_DEVICE uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Descriptor of K-step j (16 elements) inside a 64-deep K block.
 template <bool MN_MAJOR>
 QB_DEVICE uint64_t operand_desc(uint32_t stage_addr, int j) {

@@ -86,16 +86,18 @@ class _Embedding(torch.autograd.Function):
                                      _p(err_flag()), stream_ptr()), "qb_embedding_fwd")
         ctx.save_for_backward(ids)
         ctx.shape = weight.shape
+        ctx.grad32 = grad32_target(weight)
         return out
 
     @staticmethod
     def backward(ctx, g):
         (ids,) = ctx.saved_tensors
         g = g.contiguous()
-        acc = torch.zeros(ctx.shape, dtype=torch.float32, device=g.device)
+        direct = ctx.grad32  # fp32 accumulator of the table's gradient (see grad32_target)
+        acc = direct if direct is not None else torch.zeros(ctx.shape, dtype=torch.float32, device=g.device)
         check(lib().qb_embedding_bwd(_p(ids), ids.numel(), _p(g), ctx.shape[0], ctx.shape[1], _p(acc),
                                      _p(err_flag()), stream_ptr()), "qb_embedding_bwd")
-        return None, _to_bf16(acc)
+        return None, (None if direct is not None else _to_bf16(acc))
 
 
 def embedding(ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
@@ -105,6 +107,13 @@ def embedding(ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     if ids.dtype != torch.long:
         ids = ids.long()
     return _Embedding.apply(ids.contiguous(), weight)
+
+
+def grad32_target(param):
+    """The fp32 buffer a parameter's gradient accumulates into during a fused training pass
+    (attached by qwen3_grpo_train.GradBuffer), or None: backward kernels then add their products
+    straight into it (GEMM mode 2) instead of returning a bf16 gradient to autograd."""
+    return getattr(param, "_qb_grad32", None)
 
 
 def _to_bf16(acc: torch.Tensor) -> torch.Tensor:
@@ -472,8 +481,9 @@ class _Linear(torch.autograd.Function):
     dW = g^T . x (A stored [tokens, out] = [K, M], B stored [tokens, in] = [K, N])."""
 
     @staticmethod
-    def forward(ctx, x2, w):
+    def forward(ctx, x2, w, grad32):
         ctx.save_for_backward(x2, w)
+        ctx.grad32 = grad32
         return gemm(x2, w)
 
     @staticmethod
@@ -481,8 +491,13 @@ class _Linear(torch.autograd.Function):
         x2, w = ctx.saved_tensors
         g = g.contiguous()
         dx = gemm_ex(g, False, w, True) if ctx.needs_input_grad[0] else None
-        dw = gemm_ex(g, True, x2, True) if ctx.needs_input_grad[1] else None
-        return dx, dw
+        dw = None
+        if ctx.needs_input_grad[1]:
+            if ctx.grad32 is not None:  # dW += g^T x straight into the fp32 accumulator
+                gemm_ex(g, True, x2, True, out=ctx.grad32, mode=2)
+            else:
+                dw = gemm_ex(g, True, x2, True)
+        return dx, dw, None
 
 
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -492,7 +507,7 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     x2 = _gemm_operand(x.reshape(-1, shape[-1]))
     w2 = _gemm_operand(w)
     if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
-        y = _Linear.apply(x2, w2)
+        y = _Linear.apply(x2, w2, grad32_target(w) if w.requires_grad else None)
     else:
         y = gemm(x2, w2)
     return y.view(*shape[:-1], w.shape[0])

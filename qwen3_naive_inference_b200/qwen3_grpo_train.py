@@ -192,8 +192,13 @@ def batch_log_probs(model: Qwen3ForCausalLM, batch: PackedBatch, microbatch_toke
 
 
 def policy_loss_backward(model: Qwen3ForCausalLM, batch: PackedBatch, *, ref_lp=None, beta=0.0,
-                         clip_epsilon=CLIP_EPSILON, mask_total=None, microbatch_tokens=32768, chunk_rows=4096):
+                         clip_epsilon=CLIP_EPSILON, mask_total=None, microbatch_tokens=32768, chunk_rows=4096,
+                         process_group=None):
     """Fused recompute + GRPO loss + backward over microbatches; grads land in ``.grad``.
+
+    Gradients accumulate in fp32 (the model's GradBuffer); with ``process_group`` (or an
+    initialised default group) they are summed over ranks in fp32 before the bf16 ``.grad``
+    tensors are written.
 
     For each chunk of rows the lm_head logits are produced once: log-softmax+gather
     (qb_logprob_fwd) -> fused loss and d loss/d logp for those rows (qb_grpo_loss,
@@ -210,9 +215,27 @@ def policy_loss_backward(model: Qwen3ForCausalLM, batch: PackedBatch, *, ref_lp=
     loss = torch.zeros(3, dtype=torch.float32, device=dev)
     W = model.lm_head.weight
     V = W.shape[0]
-    dW = torch.zeros(W.shape, dtype=torch.float32, device=dev)
     L = ops.lib()
     err = ops.err_flag(dev)
+    buf = grad_buffer(model)
+    buf.zero()
+    buf.fold()  # gradients already present (none after zero_grad) join the fp32 sum
+    buf.attach()
+    dW = ops.grad32_target(W)
+    try:
+        _policy_microbatches(model, batch, buf, new_lp, grad_new, loss, W, V, L, err, dW, ref_lp, beta, clip_epsilon,
+                             mask_total, microbatch_tokens, chunk_rows)
+    finally:
+        buf.detach()
+    if process_group is not None or (dist.is_available() and dist.is_initialized()):
+        buf.allreduce(process_group)
+    buf.to_grads()
+    return loss, new_lp
+
+
+def _policy_microbatches(model, batch, buf, new_lp, grad_new, loss, W, V, L, err, dW, ref_lp, beta, clip_epsilon,
+                         mask_total, microbatch_tokens, chunk_rows):
+    dev = batch.device
     for r0, r1 in batch.microbatches(microbatch_tokens):
         ids, pos, cu, tiles, sel, tgt, dest, row_tok = batch.rows_meta(r0, r1)
         h = model.model.forward_packed(ids, pos, cu, tiles)
@@ -222,23 +245,17 @@ def policy_loss_backward(model: Qwen3ForCausalLM, batch: PackedBatch, *, ref_lp=
         lse = torch.empty(hs.shape[0], dtype=torch.float32, device=dev)
         tok_off = np.concatenate([[0], np.cumsum(row_tok)])
         with torch.no_grad():
-            dW = _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, loss, dW, batch, ref_lp,
-                                 beta, clip_epsilon, mask_total, r0, row_tok, tok_off, chunk_rows)
+            _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, loss, dW, batch, ref_lp,
+                            beta, clip_epsilon, mask_total, r0, row_tok, tok_off, chunk_rows)
         hs_all.backward(dhs)
+        buf.fold()
         del h, hs_all
-    g = ops._to_bf16(dW)
-    if W.grad is None:
-        W.grad = g
-    else:
-        W.grad.add_(g)
-    return loss, new_lp
 
 
 def _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, loss, dW, batch, ref_lp, beta,
                     clip_epsilon, mask_total, r0, row_tok, tok_off, chunk_rows):
     """Per row chunk: logits once (GEMM with the log-softmax + gather in its epilogue) -> fused
-    loss/grad -> d logits in place -> dh, dW.
-    Returns the updated fp32 dW accumulator."""
+    loss/grad -> d logits in place -> dh, and dW added into the fp32 accumulator ``dW``."""
     for a, b in _row_chunks(row_tok, chunk_rows):
         t0, t1 = int(tok_off[a]), int(tok_off[b])
         if t1 == t0:
@@ -258,7 +275,6 @@ def _lm_head_chunks(L, err, W, V, hs, dhs, lse, tgt, dest, new_lp, grad_new, los
         ops.gemm_ex(logits, False, W, True, out=dhs[t0:t1])  # dh = dlogits . W
         ops.gemm_ex(logits, True, hc, True, out=dW, mode=2)   # dW += dlogits^T . h (fp32)
         del logits
-    return dW
 
 
 def grpo_train_step(model, optimizer, input_ids, old_log_probs, response_mask, rewards, prompt_ids, *,
@@ -369,24 +385,76 @@ def make_reference_copy(model: Qwen3ForCausalLM) -> Qwen3ForCausalLM:
     return ref
 
 
-def allreduce_grads(model, group=None, bucket_bytes=256 << 20):
-    """Sum bf16 gradients over ranks in flat buckets (NCCL over NVLink)."""
+class GradBuffer:
+    """One flat fp32 buffer holding the gradient of every trainable parameter of a model.
+
+    During a fused training pass (:func:`policy_loss_backward`) each parameter carries a view of
+    it as ``_qb_grad32``: the projection, lm_head and embedding backward kernels add their
+    products straight into that view (GEMM mode 2, fp32), so microbatches accumulate in fp32;
+    the few small gradients autograd still returns in bf16 (norm weights) are folded in after each
+    microbatch.  For data parallelism the buffer is all-reduced in place, in flat buckets, in fp32
+    (no per-hop bf16 rounding, no concatenation or copy-back), and only then converted to the bf16
+    ``.grad`` tensors the optimizer reads.  The tied lm_head and embedding are two Parameters with
+    two gradients (the reference steps both, qwen3_naive.py:830-831), so both are reduced."""
+
+    def __init__(self, model):
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        n = sum(p.numel() for p in self.params)
+        self.flat = torch.zeros(n, dtype=torch.float32, device=self.params[0].device)
+        self.views, off = [], 0
+        for p in self.params:
+            self.views.append(self.flat[off:off + p.numel()].view(p.shape))
+            off += p.numel()
+
+    def zero(self):
+        self.flat.zero_()
+
+    def attach(self):
+        for p, v in zip(self.params, self.views):
+            p._qb_grad32 = v
+
+    def detach(self):
+        for p in self.params:
+            if hasattr(p, "_qb_grad32"):
+                del p._qb_grad32
+
+    def fold(self):
+        """Adds gradients autograd returned in bf16 into the fp32 views and clears them."""
+        for p, v in zip(self.params, self.views):
+            if p.grad is not None:
+                v.add_(p.grad)
+                p.grad = None
+
+    def allreduce(self, group=None, bucket_bytes=512 << 20):
+        """Sums the buffer over the ranks of ``group`` in place, bucket by bucket."""
+        step = max(1, bucket_bytes // 4)
+        for a in range(0, self.flat.numel(), step):
+            dist.all_reduce(self.flat[a:a + step], group=group)
+
+    def to_grads(self):
+        """bf16 ``.grad`` of every parameter from its fp32 view (the optimizer's input)."""
+        for p, v in zip(self.params, self.views):
+            p.grad = ops._to_bf16(v) if v.is_cuda else v.to(p.dtype)
+
+
+def grad_buffer(model) -> GradBuffer:
+    buf = getattr(model, "_qb_grad_buffer", None)
+    if buf is None:
+        buf = GradBuffer(model)
+        model._qb_grad_buffer = buf
+    return buf
+
+
+def allreduce_grads(model, group=None, bucket_bytes=512 << 20):
+    """Sums every parameter's ``.grad`` over ranks through the model's fp32 GradBuffer (for callers
+    that ran their own backward; :func:`grpo_step` reduces the fp32 accumulators directly)."""
     if group is None and not (dist.is_available() and dist.is_initialized()):
         return
-    grads = [p.grad for p in model.parameters() if p.grad is not None]
-    bucket, size = [], 0
-    for g in grads + [None]:
-        if g is not None:
-            bucket.append(g)
-            size += g.numel() * g.element_size()
-        if bucket and (g is None or size >= bucket_bytes):
-            flat = torch.cat([b.reshape(-1) for b in bucket])
-            dist.all_reduce(flat, group=group)
-            off = 0
-            for b in bucket:
-                b.copy_(flat[off:off + b.numel()].view_as(b))
-                off += b.numel()
-            bucket, size = [], 0
+    buf = grad_buffer(model)
+    buf.zero()
+    buf.fold()
+    buf.allreduce(group, bucket_bytes)
+    buf.to_grads()
 
 
 def grpo_step(policy: Qwen3ForCausalLM, optimizer, prompts, *, ref_model=None, group_size=8, max_new_tokens=512,
@@ -430,9 +498,8 @@ def grpo_step(policy: Qwen3ForCausalLM, optimizer, prompts, *, ref_model=None, g
     optimizer.zero_grad(set_to_none=True)
     loss, _ = policy_loss_backward(policy, batch, ref_lp=ref_lp, beta=beta if ref_lp is not None else 0.0,
                                    clip_epsilon=clip_epsilon, mask_total=mask_total,
-                                   microbatch_tokens=microbatch_tokens, chunk_rows=chunk_rows)
-    if use_dist:
-        allreduce_grads(policy, process_group)
+                                   microbatch_tokens=microbatch_tokens, chunk_rows=chunk_rows,
+                                   process_group=process_group)
     optimizer.step()
     loss_host = loss.cpu()  # the step's one device->host read of the result
     t_end = time.perf_counter()
