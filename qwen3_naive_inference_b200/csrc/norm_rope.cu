@@ -292,6 +292,91 @@ __global__ void qk_norm_rope_fwd_kernel(QkNormRopeParams p) {
   if (!is_q && slot >= 0) store4(p.k_cache + (slot * p.hkv + (head - p.hq)) * HD + lane * 4, o);
 }
 
+// One token per 128-thread block; every half-warp (16 lanes x 8 elements, 16-byte accesses)
+// owns one 128-wide head at a time and the block's eight half-warps cover heads h, h+8, ...
+// All of a half-warp's head rows are loaded before any is processed, so each lane has up to
+// four 16-byte loads in flight; the token's cos/sin row and the two norm weights are loaded once
+// per lane.  RoPE partners (j, j+64) sit 8 lanes apart.  Same rounding points as the warp kernel.
+constexpr int QK8_MAXH = 4;  // heads per half-warp held in registers at once (32 heads per pass)
+
+QB_DEVICE float half_warp_sum(float v) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(128)
+qk_norm_rope_fwd8_kernel(QkNormRopeParams p) {
+  const int64_t t = blockIdx.x;
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const int nheads = p.hq + 2 * p.hkv;
+  int64_t pos = p.positions[t];
+  if (pos < 0 || pos >= p.max_pos) {
+    if (threadIdx.x == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
+    pos = 0;
+  }
+  const int jj = (l & 7) * 8;  // rotation-table column of this lane's first element
+  const float4* cs4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + jj);
+  const float4* sn4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + HD / 2 + jj);
+  const float4 c0 = cs4[0], c1 = cs4[1], s0 = sn4[0], s1 = sn4[1];
+  const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  float qw[8], kw[8];
+  load8(p.qw + l * 8, qw);
+  load8(p.kw + l * 8, kw);
+  int64_t slot = -1;
+  if (p.k_cache != nullptr) {
+    slot = p.slots[t];
+    if (slot >= p.num_slots || slot < -1) {
+      if (threadIdx.x == 0) qb_set_err(p.err, QB_DEVERR_SLOT);
+      slot = -1;
+    }
+  }
+  const bf16* src = p.qkv + t * p.ld_in + l * 8;
+  for (int hc = 0; hc < nheads; hc += 8 * QK8_MAXH) {
+    float v[QK8_MAXH][8];
+#pragma unroll
+    for (int k = 0; k < QK8_MAXH; ++k) {
+      const int h = hc + hw + 8 * k;
+      if (h < nheads) load8(src + h * HD, v[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < QK8_MAXH; ++k) {
+      const int h = hc + hw + 8 * k;
+      const bool live = h < nheads;
+      const bool is_q = h < p.hq, is_v = h >= p.hq + p.hkv;
+      // RMSNorm over the head (every lane of the warp takes part in the shuffles)
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += live ? v[k][i] * v[k][i] : 0.f;
+      ss = half_warp_sum(ss);
+      const float rstd = rsqrtf(ss / (float)HD + p.eps);
+      float xn[8], o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xn[i] = live ? round_bf16((v[k][i] * rstd) * (is_q ? qw[i] : kw[i])) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float partner = __shfl_xor_sync(0xffffffffu, xn[i], 8);
+        o[i] = l < 8 ? xn[i] * cv[i] - partner * sv[i]   // x1*c - x2*s
+                     : xn[i] * cv[i] + partner * sv[i];  // x2*c + x1*s
+      }
+      if (!live) continue;
+      if (is_v) {  // v: copy (and store into the cache)
+        if (p.out) store8(p.out + t * p.ld_out + h * HD + l * 8, v[k]);
+        if (slot >= 0) store8(p.v_cache + (slot * p.hkv + (h - p.hq - p.hkv)) * HD + l * 8, v[k]);
+        continue;
+      }
+      if (l == 0) {
+        if (is_q && p.q_rstd) p.q_rstd[t * p.hq + h] = rstd;
+        if (!is_q && p.k_rstd) p.k_rstd[t * p.hkv + (h - p.hq)] = rstd;
+      }
+      if (p.out) store8(p.out + t * p.ld_out + h * HD + l * 8, o);
+      if (is_q && p.q_out) store8(p.q_out + (t * p.hq + h) * HD + l * 8, o);
+      if (!is_q && slot >= 0) store8(p.k_cache + (slot * p.hkv + (h - p.hq)) * HD + l * 8, o);
+    }
+  }
+}
+
 struct QkNormRopeBwdParams {
   const bf16* dout;
   const bf16* qkv;
@@ -379,6 +464,108 @@ __global__ void qk_norm_rope_bwd_kernel(QkNormRopeBwdParams p) {
     for (int i = 0; i < 4; ++i) {
       atomicAdd(&dqw_s[lane * 4 + i], dq_acc[i]);
       atomicAdd(&dkw_s[lane * 4 + i], dk_acc[i]);
+    }
+  }
+  __syncthreads();
+  if (p.rope_grad) {
+    for (int c = threadIdx.x; c < HD; c += blockDim.x) {
+      atomicAdd(p.dqw + c, dqw_s[c]);
+      atomicAdd(p.dkw + c, dkw_s[c]);
+    }
+  }
+}
+
+// The backward with 16-byte accesses: QKB_TOK tokens per 256-thread block, each half-warp owning
+// one (token, head) item at a time (16 lanes x 8 elements); norm-weight gradients are folded per
+// lane, then in shared memory, then one global atomic per column per block.  Same arithmetic as
+// qk_norm_rope_bwd_kernel.
+__global__ void __launch_bounds__(256)
+qk_norm_rope_bwd8_kernel(QkNormRopeBwdParams p) {
+  __shared__ float dqw_s[HD], dkw_s[HD];
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, nhw = blockDim.x >> 4;
+  for (int c = threadIdx.x; c < HD; c += blockDim.x) {
+    dqw_s[c] = 0.f;
+    dkw_s[c] = 0.f;
+  }
+  __syncthreads();
+  const int nheads = p.hq + 2 * p.hkv;
+  float dq_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, dk_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float qw[8], kw[8];
+  load8(p.qw + l * 8, qw);
+  load8(p.kw + l * 8, kw);
+  const int jj = (l & 7) * 8;
+  const int64_t t0 = (int64_t)blockIdx.x * QKB_TOK;
+  const int n_items = QKB_TOK * nheads;
+  // every lane of a warp runs the same number of iterations (shuffles below)
+  for (int base = 0; base < n_items; base += nhw) {
+    const int item = base + hw;
+    const int64_t t = t0 + item / nheads;
+    const int head = item % nheads;
+    const bool live = item < n_items && t < p.T;
+    const int64_t off = (live ? t : 0) * p.ld + head * HD + l * 8;
+    float g[8];
+    if (live) load8(p.dout + off, g);
+    else
+      for (int i = 0; i < 8; ++i) g[i] = 0.f;
+    const bool is_v = head >= p.hq + p.hkv, is_q = head < p.hq;
+    int64_t pos = live ? p.positions[t] : 0;
+    if (pos < 0 || pos >= p.max_pos) {
+      if (l == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
+      pos = 0;
+    }
+    const float4* cs4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + jj);
+    const float4* sn4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + HD / 2 + jj);
+    const float4 c0 = cs4[0], c1 = cs4[1], s0 = sn4[0], s1 = sn4[1];
+    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    // inverse rotation: dx1 = dy1*c + dy2*s, dx2 = dy2*c - dy1*s
+    float dxn[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float partner = __shfl_xor_sync(0xffffffffu, g[i], 8);
+      dxn[i] = l < 8 ? g[i] * cv[i] + partner * sv[i] : g[i] * cv[i] - partner * sv[i];
+    }
+    const bool norm = live && !is_v && p.rope_grad;
+    float x[8], xh[8], gx[8];
+    float rs = 0.f;
+    if (norm) {
+      load8(p.qkv + off, x);
+      rs = is_q ? p.q_rstd[t * p.hq + head] : p.k_rstd[t * p.hkv + (head - p.hq)];
+    } else {
+      for (int i = 0; i < 8; ++i) x[i] = 0.f;
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xh[i] = x[i] * rs;
+      gx[i] = dxn[i] * (is_q ? qw[i] : kw[i]);
+      dot += gx[i] * xh[i];
+    }
+    dot = half_warp_sum(dot) / (float)HD;
+    if (!live) continue;
+    if (is_v) {  // v passes through
+      store8(p.dqkv + off, g);
+      continue;
+    }
+    if (!p.rope_grad) {  // the reference's RoPE is invisible to autograd: q/k get no gradient
+      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      store8(p.dqkv + off, z);
+      continue;
+    }
+    float dx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (is_q) dq_acc[i] += dxn[i] * xh[i];
+      else dk_acc[i] += dxn[i] * xh[i];
+      dx[i] = rs * (gx[i] - xh[i] * dot);
+    }
+    store8(p.dqkv + off, dx);
+  }
+  if (p.rope_grad) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      atomicAdd(&dqw_s[l * 8 + i], dq_acc[i]);
+      atomicAdd(&dkw_s[l * 8 + i], dk_acc[i]);
     }
   }
   __syncthreads();
@@ -563,6 +750,13 @@ extern "C" int qb_qk_norm_rope_fwd(const void* qkv, int64_t T, int64_t ld_in, in
                      (const bf16*)q_norm_w, (const bf16*)k_norm_w, eps, (bf16*)out, ld_out,
                      (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, slot_mapping, num_slots,
                      q_rstd, k_rstd, err};
+  const bool vec16 = aligned16(qkv) && ld_in % 8 == 0 && (out == nullptr || (aligned16(out) && ld_out % 8 == 0)) &&
+                     (q_out == nullptr || aligned16(q_out)) && (k_cache == nullptr || (aligned16(k_cache) &&
+                     aligned16(v_cache))) && aligned16(q_norm_w) && aligned16(k_norm_w) && aligned16(cos_sin);
+  if (vec16) {  // 16-byte accesses, one token per block
+    qk_norm_rope_fwd8_kernel<<<(unsigned)T, 128, 0, (cudaStream_t)stream>>>(p);
+    return qb_launch_status();
+  }
   const int wpb = 8;
   dim3 grid((unsigned)T, (unsigned)((hq + 2 * hkv + wpb - 1) / wpb));
   qk_norm_rope_fwd_kernel<<<grid, wpb * 32, 0, (cudaStream_t)stream>>>(p);
@@ -585,6 +779,12 @@ extern "C" int qb_qk_norm_rope_bwd(const void* dout, const void* qkv, int64_t T,
                         max_pos, (const bf16*)q_norm_w, (const bf16*)k_norm_w, q_rstd, k_rstd,
                         rope_grad, (bf16*)dqkv, dq_norm_w, dk_norm_w, err};
   const unsigned grid = (unsigned)((T + QKB_TOK - 1) / QKB_TOK);
+  const bool vec16 = aligned16(dout) && aligned16(qkv) && aligned16(dqkv) && ld % 8 == 0 && aligned16(cos_sin) &&
+                     (!rope_grad || (aligned16(q_norm_w) && aligned16(k_norm_w)));
+  if (vec16 && q_norm_w && k_norm_w) {
+    qk_norm_rope_bwd8_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+    return qb_launch_status();
+  }
   qk_norm_rope_bwd_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return qb_launch_status();
 }
