@@ -207,11 +207,11 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int x = j & 1;
-      if (!mbar_wait(s_full(x), (uint32_t)(j >> 1) & 1u, abort_flag, p.err)) {
+      // tcgen05.ld/st below are warp-collective: every decision that leads to them is warp-uniform
+      if (__any_sync(0xffffffffu, !mbar_wait(s_full(x), (uint32_t)(j >> 1) & 1u, abort_flag, p.err))) {
         ok = false;
         break;
       }
-      __syncwarp();
       tc_fence_after();
       uint32_t v[64];
       tmem_ld32_nowait(t_lane + x * AT_KEYS, v);
@@ -232,25 +232,28 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(v[i]));
       float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       mt *= p.scale_log2;
-      if (mt > m_ref + AT_RESCALE || (m_ref == -INFINITY && mt > -INFINITY)) {
-        const float alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
+      const bool need = mt > m_ref + AT_RESCALE || (m_ref == -INFINITY && mt > -INFINITY);
+      float alpha = 1.f;
+      if (need) {
+        alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
         m_ref = mt;
         l *= alpha;
-        if (j > 0) {  // O holds P_0..P_{j-1} V: wait for the last of them, then rescale this row
-          if (!mbar_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag, p.err)) {
-            ok = false;
-            break;
-          }
-          __syncwarp();
-          tc_fence_after();
+      }
+      // O holds P_0..P_{j-1} V: when any row of the warp moved its max, the warp waits for the last
+      // of those products and rescales its 32 rows in TMEM together (the others by 1)
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (__any_sync(0xffffffffu, !mbar_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag, p.err))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 128; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(t_lane + AT_O_COL + c, o);
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(t_lane + AT_O_COL + c, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_lane + AT_O_COL + c, o);
-          }
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_lane + AT_O_COL + c, o);
         }
       }
       // P = exp2(S - max) as bf16 pairs over the first 32 columns of this S buffer
@@ -273,8 +276,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
       mbar_arrive(p_ready(x));
     }
     // epilogue: O / l -> bf16, and the row's log-sum-exp
-    if (ok && mbar_wait(o_last, 0, abort_flag, p.err)) {
-      __syncwarp();
+    if (ok && __all_sync(0xffffffffu, mbar_wait(o_last, 0, abort_flag, p.err))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       bf16* orow = p.out + (int64_t)(s0 + pos) * p.o_stride + (h0 + hh) * 128;
@@ -594,8 +596,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
       mbar_arrive(pd_ready);
     }
     // epilogue: dK (x scale) and dV of this key row
-    if (ok && mbar_wait(done_bar, 0, abort_flag, p.err)) {
-      __syncwarp();
+    if (ok && __all_sync(0xffffffffu, mbar_wait(done_bar, 0, abort_flag, p.err))) {
       tc_fence_after();
       const bool live = kpos < L;
       bf16* dkrow = p.dk + (int64_t)(s0 + kpos) * p.stride + kvh * 128;
@@ -818,11 +819,11 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
     const int lim = live ? pos : -1;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(s_full, (uint32_t)j & 1u, abort_flag, p.err)) {
+      // tcgen05.ld/st below are warp-collective: the warp leaves together
+      if (__any_sync(0xffffffffu, !mbar_wait(s_full, (uint32_t)j & 1u, abort_flag, p.err))) {
         ok = false;
         break;
       }
-      __syncwarp();
       tc_fence_after();
       const int k0 = j * BT_KEYS;
 #pragma unroll 1
@@ -844,8 +845,7 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
       tc_fence_before();
       mbar_arrive(ds_ready);
     }
-    if (ok && mbar_wait(done_bar, 0, abort_flag, p.err)) {
-      __syncwarp();
+    if (ok && __all_sync(0xffffffffu, mbar_wait(done_bar, 0, abort_flag, p.err))) {
       tc_fence_after();
       bf16* qrow = dq + (int64_t)(s0 + pos) * p.stride + (h0 + hh) * 128;
 #pragma unroll 1

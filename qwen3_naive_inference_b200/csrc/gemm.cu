@@ -267,8 +267,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
       const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
-      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag, p.err)) break;
-      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin
+      // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
+      if (__any_sync(0xffffffffu, !mbar_wait(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
@@ -486,8 +486,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     uint32_t acc_phase = 0;
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
       const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * 256;
-      if (!mbar_wait_cluster(tfull_bar(acc), acc_phase, abort_flag, p.err)) break;
-      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin
+      // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
+      if (__any_sync(0xffffffffu, !mbar_wait_cluster(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
@@ -667,8 +667,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     const int owner = quarter / (4 / S);            // CTA that finishes these 32 rows
     const int slice_row = (quarter % (4 / S)) * 32 + lane;  // row within the owner's slice
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-    if (mbar_wait(tfull_bar, 0, abort_flag, p.err)) {
-      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the spin
+    if (__all_sync(0xffffffffu, mbar_wait(tfull_bar, 0, abort_flag, p.err))) {  // warp-uniform (tcgen05.ld)
       tc_fence_after();
       if (owner != rank) {
         const int slot = (rank - owner - 1 + S) % S;  // this CTA's slot in the owner's buffer
@@ -683,8 +682,7 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
           for (int v = 0; v < 8; ++v)
             st_async_v4(dst + (uint32_t)(c + 4 * v) * 4, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3], rbar);
         }
-      } else if (recv_wait(recv_bar, abort_flag, p.err)) {
-        __syncwarp();
+      } else if (__all_sync(0xffffffffu, recv_wait(recv_bar, abort_flag, p.err))) {
         const int row = m0 + quarter * 32 + lane;
         const bool row_ok = row < p.M;
         const float* slots = reinterpret_cast<const float*>(gbase + S_STAGES * S_STAGE_BYTES) + slice_row * S_ROW;

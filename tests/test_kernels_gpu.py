@@ -208,15 +208,21 @@ def test_paged_prefill(cuda, qk):
         close_bf16(out, ref, 2e-2)
 
 
-@pytest.mark.parametrize("lens", [[1, 63, 64, 65, 200], [513], [1100, 40, 129]])
-def test_attention_packed_fwd_bwd(cuda, lens):
-    """Packed causal attention (the training path: tcgen05 forward, 64 query positions x 2 heads
-    per tile, 128-key tiles) against fp32 autograd; the forward per element within 2^-7 of
-    sum_j p_j |v_j| plus one bf16 ulp (P and the output are rounded to bf16)."""
+@pytest.mark.parametrize("lens,qscale", [([1, 63, 64, 65, 200], 1.0), ([513], 1.0), ([1100, 40, 129], 1.0),
+                                         ([700, 300], 6.0)])
+def test_attention_packed_fwd_bwd(cuda, lens, qscale):
+    """Packed causal attention (the training path on tcgen05: forward with 64 query positions x
+    2 heads per tile and 64-key tiles, dK/dV on 128-key tiles, dQ) against fp32 autograd; the
+    forward per element within 2^-7 of sum_j p_j |v_j| plus one bf16 ulp (P and the output are
+    rounded to bf16).  qscale 6 makes the scores wide enough that a row's running max jumps by
+    more than 2^8 between key tiles for some rows of a warp and not others, the case in which
+    the forward rescales O in TMEM."""
     hq, hkv = 16, 8
     T = sum(lens)
     g = gen(T)
-    qkv = torch.randn(T, (hq + 2 * hkv) * 128, generator=g).to(BF)
+    qkv = torch.randn(T, (hq + 2 * hkv) * 128, generator=g)
+    qkv[:, :hq * 128] *= qscale
+    qkv = qkv.to(BF)
     dout = torch.randn(T, hq * 128, generator=g).to(BF)
     cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
     tiles = torch.from_numpy(ops.build_tiles(lens))
