@@ -292,11 +292,12 @@ __global__ void qk_norm_rope_fwd_kernel(QkNormRopeParams p) {
   if (!is_q && slot >= 0) store4(p.k_cache + (slot * p.hkv + (head - p.hq)) * HD + lane * 4, o);
 }
 
-// One token per 128-thread block; every half-warp (16 lanes x 8 elements, 16-byte accesses)
-// owns one 128-wide head at a time and the block's eight half-warps cover heads h, h+8, ...
-// All of a half-warp's head rows are loaded before any is processed, so each lane has up to
-// four 16-byte loads in flight; the token's cos/sin row and the two norm weights are loaded once
-// per lane.  RoPE partners (j, j+64) sit 8 lanes apart.  Same rounding points as the warp kernel.
+// One token per 128-thread block, up to eight blocks per SM: every half-warp (16 lanes x 8
+// elements, 16-byte accesses) owns heads h, h+8, h+16, h+24 of the token.  The head rows are
+// loaded as packed bf16 before anything that depends on the token's position, so a block has its
+// whole row in flight at once and the position / slot loads overlap it; at 64 registers a thread
+// eight blocks (eight rows) stay resident per SM.  RoPE partners (j, j+64) sit 8 lanes apart.
+// Same rounding points as the warp kernel.
 constexpr int QK8_MAXH = 4;  // heads per half-warp held in registers at once (32 heads per pass)
 
 QB_DEVICE float half_warp_sum(float v) {
@@ -304,56 +305,70 @@ QB_DEVICE float half_warp_sum(float v) {
   for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+QB_DEVICE bf16x8 ld_row8(const bf16* p) { return *reinterpret_cast<const bf16x8*>(p); }
+QB_DEVICE void st_row8(bf16* p, const bf16x8& r) { *reinterpret_cast<bf16x8*>(p) = r; }
+QB_DEVICE void unpack8(const bf16x8& r, float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(r.u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+// cos and sin of the eight rotation-table columns jj..jj+7 of one position
+QB_DEVICE void load_rot8(const float* cos_sin, int64_t pos, int jj, float (&cv)[8], float (&sv)[8]) {
+  const float4* cs4 = reinterpret_cast<const float4*>(cos_sin + pos * HD + jj);
+  const float4* sn4 = reinterpret_cast<const float4*>(cos_sin + pos * HD + HD / 2 + jj);
+  const float4 c0 = cs4[0], c1 = cs4[1], s0 = sn4[0], s1 = sn4[1];
+  cv[0] = c0.x; cv[1] = c0.y; cv[2] = c0.z; cv[3] = c0.w; cv[4] = c1.x; cv[5] = c1.y; cv[6] = c1.z; cv[7] = c1.w;
+  sv[0] = s0.x; sv[1] = s0.y; sv[2] = s0.z; sv[3] = s0.w; sv[4] = s1.x; sv[5] = s1.y; sv[6] = s1.z; sv[7] = s1.w;
+}
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 8)
 qk_norm_rope_fwd8_kernel(QkNormRopeParams p) {
   const int64_t t = blockIdx.x;
   const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int nheads = p.hq + 2 * p.hkv;
-  int64_t pos = p.positions[t];
-  if (pos < 0 || pos >= p.max_pos) {
-    if (threadIdx.x == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
-    pos = 0;
-  }
-  const int jj = (l & 7) * 8;  // rotation-table column of this lane's first element
-  const float4* cs4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + jj);
-  const float4* sn4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + HD / 2 + jj);
-  const float4 c0 = cs4[0], c1 = cs4[1], s0 = sn4[0], s1 = sn4[1];
-  const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-  const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-  float qw[8], kw[8];
-  load8(p.qw + l * 8, qw);
-  load8(p.kw + l * 8, kw);
-  int64_t slot = -1;
-  if (p.k_cache != nullptr) {
-    slot = p.slots[t];
-    if (slot >= p.num_slots || slot < -1) {
-      if (threadIdx.x == 0) qb_set_err(p.err, QB_DEVERR_SLOT);
-      slot = -1;
-    }
-  }
   const bf16* src = p.qkv + t * p.ld_in + l * 8;
+  const int64_t pos_in = p.positions[t];
+  const int64_t slot_in = p.k_cache != nullptr ? (int64_t)p.slots[t] : -1;
   for (int hc = 0; hc < nheads; hc += 8 * QK8_MAXH) {
-    float v[QK8_MAXH][8];
+    bf16x8 raw[QK8_MAXH];
 #pragma unroll
     for (int k = 0; k < QK8_MAXH; ++k) {
       const int h = hc + hw + 8 * k;
-      if (h < nheads) load8(src + h * HD, v[k]);
+      raw[k] = h < nheads ? ld_row8(src + h * HD) : bf16x8{};
     }
+    int64_t pos = pos_in;
+    if (pos < 0 || pos >= p.max_pos) {
+      if (threadIdx.x == 0 && hc == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
+      pos = 0;
+    }
+    int64_t slot = slot_in;
+    if (slot >= p.num_slots || slot < -1) {
+      if (threadIdx.x == 0 && hc == 0) qb_set_err(p.err, QB_DEVERR_SLOT);
+      slot = -1;
+    }
+    float cv[8], sv[8];
+    load_rot8(p.cos_sin, pos, (l & 7) * 8, cv, sv);
+    const bf16x8 qwr = ld_row8(p.qw + l * 8), kwr = ld_row8(p.kw + l * 8);
 #pragma unroll
     for (int k = 0; k < QK8_MAXH; ++k) {
       const int h = hc + hw + 8 * k;
       const bool live = h < nheads;
       const bool is_q = h < p.hq, is_v = h >= p.hq + p.hkv;
-      // RMSNorm over the head (every lane of the warp takes part in the shuffles)
+      float v[8], w[8];
+      unpack8(raw[k], v);
+      unpack8(is_q ? qwr : kwr, w);
+      // RMSNorm over the head (every lane of the warp takes part in the shuffles; dead rows are 0)
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += live ? v[k][i] * v[k][i] : 0.f;
+      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
       ss = half_warp_sum(ss);
       const float rstd = rsqrtf(ss / (float)HD + p.eps);
       float xn[8], o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) xn[i] = live ? round_bf16((v[k][i] * rstd) * (is_q ? qw[i] : kw[i])) : 0.f;
+      for (int i = 0; i < 8; ++i) xn[i] = round_bf16((v[i] * rstd) * w[i]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float partner = __shfl_xor_sync(0xffffffffu, xn[i], 8);
@@ -361,9 +376,9 @@ qk_norm_rope_fwd8_kernel(QkNormRopeParams p) {
                      : xn[i] * cv[i] + partner * sv[i];  // x2*c + x1*s
       }
       if (!live) continue;
-      if (is_v) {  // v: copy (and store into the cache)
-        if (p.out) store8(p.out + t * p.ld_out + h * HD + l * 8, v[k]);
-        if (slot >= 0) store8(p.v_cache + (slot * p.hkv + (h - p.hq - p.hkv)) * HD + l * 8, v[k]);
+      if (is_v) {  // v: copied bit for bit (and stored into the cache)
+        if (p.out) st_row8(p.out + t * p.ld_out + h * HD + l * 8, raw[k]);
+        if (slot >= 0) st_row8(p.v_cache + (slot * p.hkv + (h - p.hq - p.hkv)) * HD + l * 8, raw[k]);
         continue;
       }
       if (l == 0) {
@@ -475,97 +490,104 @@ __global__ void qk_norm_rope_bwd_kernel(QkNormRopeBwdParams p) {
   }
 }
 
-// The backward with 16-byte accesses: QKB_TOK tokens per 256-thread block, each half-warp owning
-// one (token, head) item at a time (16 lanes x 8 elements); norm-weight gradients are folded per
-// lane, then in shared memory, then one global atomic per column per block.  Same arithmetic as
+// The backward with 16-byte accesses: a grid-stride loop over tokens, 128 threads a block and up
+// to four blocks per SM, every half-warp owning heads h, h+8, h+16, h+24 of the current token.
+// All of a token's loads (incoming gradients, raw q/k rows, their saved rstd) are issued before
+// the rotation table that depends on its position, so each block keeps a whole token in flight.
+// Norm-weight gradients are folded per lane across the block's tokens, then over the block in
+// shared memory, then one global atomic per column.  When dqkv == dout the v columns, whose
+// gradient passes through unchanged, are left in place.  Same arithmetic as
 // qk_norm_rope_bwd_kernel.
-__global__ void __launch_bounds__(256)
+constexpr int QKB8_BLOCKS_PER_SM = 4;
+__global__ void __launch_bounds__(128, QKB8_BLOCKS_PER_SM)
 qk_norm_rope_bwd8_kernel(QkNormRopeBwdParams p) {
   __shared__ float dqw_s[HD], dkw_s[HD];
-  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15, nhw = blockDim.x >> 4;
+  const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   for (int c = threadIdx.x; c < HD; c += blockDim.x) {
     dqw_s[c] = 0.f;
     dkw_s[c] = 0.f;
   }
   __syncthreads();
   const int nheads = p.hq + 2 * p.hkv;
+  const bool in_place = p.dqkv == p.dout;
   float dq_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}, dk_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  float qw[8], kw[8];
-  load8(p.qw + l * 8, qw);
-  load8(p.kw + l * 8, kw);
-  const int jj = (l & 7) * 8;
-  const int64_t t0 = (int64_t)blockIdx.x * QKB_TOK;
-  const int n_items = QKB_TOK * nheads;
-  // every lane of a warp runs the same number of iterations (shuffles below)
-  for (int base = 0; base < n_items; base += nhw) {
-    const int item = base + hw;
-    const int64_t t = t0 + item / nheads;
-    const int head = item % nheads;
-    const bool live = item < n_items && t < p.T;
-    const int64_t off = (live ? t : 0) * p.ld + head * HD + l * 8;
-    float g[8];
-    if (live) load8(p.dout + off, g);
-    else
-      for (int i = 0; i < 8; ++i) g[i] = 0.f;
-    const bool is_v = head >= p.hq + p.hkv, is_q = head < p.hq;
-    int64_t pos = live ? p.positions[t] : 0;
-    if (pos < 0 || pos >= p.max_pos) {
-      if (l == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
-      pos = 0;
-    }
-    const float4* cs4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + jj);
-    const float4* sn4 = reinterpret_cast<const float4*>(p.cos_sin + pos * HD + HD / 2 + jj);
-    const float4 c0 = cs4[0], c1 = cs4[1], s0 = sn4[0], s1 = sn4[1];
-    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    // inverse rotation: dx1 = dy1*c + dy2*s, dx2 = dy2*c - dy1*s
-    float dxn[8];
+  const bf16x8 qwr = ld_row8(p.qw + l * 8), kwr = ld_row8(p.kw + l * 8);
+  for (int64_t t = blockIdx.x; t < p.T; t += gridDim.x) {
+    const int64_t row = t * p.ld + l * 8;
+    const int64_t pos_in = p.positions[t];
+    for (int hc = 0; hc < nheads; hc += 8 * QK8_MAXH) {
+      bf16x8 g[QK8_MAXH], x[QK8_MAXH];
+      float rs[QK8_MAXH];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float partner = __shfl_xor_sync(0xffffffffu, g[i], 8);
-      dxn[i] = l < 8 ? g[i] * cv[i] + partner * sv[i] : g[i] * cv[i] - partner * sv[i];
-    }
-    const bool norm = live && !is_v && p.rope_grad;
-    float x[8], xh[8], gx[8];
-    float rs = 0.f;
-    if (norm) {
-      load8(p.qkv + off, x);
-      rs = is_q ? p.q_rstd[t * p.hq + head] : p.k_rstd[t * p.hkv + (head - p.hq)];
-    } else {
-      for (int i = 0; i < 8; ++i) x[i] = 0.f;
-    }
-    float dot = 0.f;
+      for (int k = 0; k < QK8_MAXH; ++k) {
+        const int h = hc + hw + 8 * k;
+        const bool live = h < nheads, is_q = h < p.hq;
+        const bool norm = live && h < p.hq + p.hkv && p.rope_grad;
+        g[k] = live ? ld_row8(p.dout + row + h * HD) : bf16x8{};
+        x[k] = norm ? ld_row8(p.qkv + row + h * HD) : bf16x8{};
+        rs[k] = norm ? (is_q ? p.q_rstd[t * p.hq + h] : p.k_rstd[t * p.hkv + (h - p.hq)]) : 0.f;
+      }
+      int64_t pos = pos_in;
+      if (pos < 0 || pos >= p.max_pos) {
+        if (l == 0) qb_set_err(p.err, QB_DEVERR_SHAPE);
+        pos = 0;
+      }
+      float cv[8], sv[8];
+      load_rot8(p.cos_sin, pos, (l & 7) * 8, cv, sv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      xh[i] = x[i] * rs;
-      gx[i] = dxn[i] * (is_q ? qw[i] : kw[i]);
-      dot += gx[i] * xh[i];
-    }
-    dot = half_warp_sum(dot) / (float)HD;
-    if (!live) continue;
-    if (is_v) {  // v passes through
-      store8(p.dqkv + off, g);
-      continue;
-    }
-    if (!p.rope_grad) {  // the reference's RoPE is invisible to autograd: q/k get no gradient
-      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      store8(p.dqkv + off, z);
-      continue;
-    }
-    float dx[8];
+      for (int k = 0; k < QK8_MAXH; ++k) {
+        const int h = hc + hw + 8 * k;
+        const bool live = h < nheads;
+        const bool is_v = h >= p.hq + p.hkv, is_q = h < p.hq;
+        float gv[8], xv[8], w[8];
+        unpack8(g[k], gv);
+        unpack8(x[k], xv);
+        unpack8(is_q ? qwr : kwr, w);
+        // inverse rotation: dx1 = dy1*c + dy2*s, dx2 = dy2*c - dy1*s
+        float dxn[8], xh[8], gx[8];
+        float dot = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (is_q) dq_acc[i] += dxn[i] * xh[i];
-      else dk_acc[i] += dxn[i] * xh[i];
-      dx[i] = rs * (gx[i] - xh[i] * dot);
+        for (int i = 0; i < 8; ++i) {
+          const float partner = __shfl_xor_sync(0xffffffffu, gv[i], 8);
+          dxn[i] = l < 8 ? gv[i] * cv[i] + partner * sv[i] : gv[i] * cv[i] - partner * sv[i];
+          xh[i] = xv[i] * rs[k];
+          gx[i] = dxn[i] * w[i];
+          dot += gx[i] * xh[i];
+        }
+        dot = half_warp_sum(dot) / (float)HD;
+        if (!live) continue;
+        if (is_v) {  // v passes through
+          if (!in_place) st_row8(p.dqkv + row + h * HD, g[k]);
+          continue;
+        }
+        if (!p.rope_grad) {  // the reference's RoPE is invisible to autograd: q/k get no gradient
+          st_row8(p.dqkv + row + h * HD, bf16x8{});
+          continue;
+        }
+        float dx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (is_q) dq_acc[i] += dxn[i] * xh[i];
+          else dk_acc[i] += dxn[i] * xh[i];
+          dx[i] = rs[k] * (gx[i] - xh[i] * dot);
+        }
+        store8(p.dqkv + row + h * HD, dx);
+      }
     }
-    store8(p.dqkv + off, dx);
   }
   if (p.rope_grad) {
+    // lanes l and l + 16 of a warp hold the same columns
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      atomicAdd(&dqw_s[l * 8 + i], dq_acc[i]);
-      atomicAdd(&dkw_s[l * 8 + i], dk_acc[i]);
+      dq_acc[i] += __shfl_xor_sync(0xffffffffu, dq_acc[i], 16);
+      dk_acc[i] += __shfl_xor_sync(0xffffffffu, dk_acc[i], 16);
+    }
+    if ((threadIdx.x & 16) == 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        atomicAdd(&dqw_s[l * 8 + i], dq_acc[i]);
+        atomicAdd(&dkw_s[l * 8 + i], dk_acc[i]);
+      }
     }
   }
   __syncthreads();
@@ -580,39 +602,73 @@ qk_norm_rope_bwd8_kernel(QkNormRopeBwdParams p) {
 // ---------------------------------------------------------------- SwiGLU / adds
 QB_DEVICE float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-__global__ void silu_mul_fwd_kernel(const bf16* __restrict__ gu, int64_t T, int64_t I,
-                                    bf16* __restrict__ out) {
-  const int64_t nvec = T * (I / 8);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / (I / 8), c = (i % (I / 8)) * 8;
-    float g[8], u[8], o[8];
-    load8(gu + row * 2 * I + c, g);
-    load8(gu + row * 2 * I + I + c, u);
+// One row per 128-thread block; a thread's (up to SILU_MAXV) 16-byte vectors of the row are all
+// loaded before any is used.  Rows are the block index, so no per-element index division.
+constexpr int SILU_MAXV = 3;
+__global__ void __launch_bounds__(128, 8)
+silu_mul_fwd_kernel(const bf16* __restrict__ gu, int64_t T, int64_t I, bf16* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  const bf16* g_row = gu + row * 2 * I;
+  const bf16* u_row = g_row + I;
+  for (int64_t c0 = threadIdx.x * 8; c0 < I; c0 += 128 * 8 * SILU_MAXV) {
+    bf16x8 gr[SILU_MAXV], ur[SILU_MAXV];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = silu_f(g[k]) * u[k];
-    store8(out + row * I + c, o);
+    for (int k = 0; k < SILU_MAXV; ++k) {
+      const int64_t c = c0 + k * 128 * 8;
+      if (c < I) {
+        gr[k] = *reinterpret_cast<const bf16x8*>(g_row + c);
+        ur[k] = *reinterpret_cast<const bf16x8*>(u_row + c);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < SILU_MAXV; ++k) {
+      const int64_t c = c0 + k * 128 * 8;
+      if (c >= I) break;
+      bf16x8 o;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 g = unpack_bf16x2(gr[k].u[i]), u = unpack_bf16x2(ur[k].u[i]);
+        o.u[i] = pack_bf16x2(silu_f(g.x) * u.x, silu_f(g.y) * u.y);
+      }
+      *reinterpret_cast<bf16x8*>(out + row * I + c) = o;
+    }
   }
 }
 
-__global__ void silu_mul_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ gu,
-                                    int64_t T, int64_t I, bf16* __restrict__ dgu) {
-  const int64_t nvec = T * (I / 8);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / (I / 8), c = (i % (I / 8)) * 8;
-    float g[8], u[8], d[8], dg[8], du[8];
-    load8(gu + row * 2 * I + c, g);
-    load8(gu + row * 2 * I + I + c, u);
-    load8(dout + row * I + c, d);
+__global__ void __launch_bounds__(128, 5)
+silu_mul_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ gu, int64_t T, int64_t I,
+                    bf16* __restrict__ dgu) {
+  const int64_t row = blockIdx.x;
+  const bf16* g_row = gu + row * 2 * I;
+  const bf16* u_row = g_row + I;
+  for (int64_t c0 = threadIdx.x * 8; c0 < I; c0 += 128 * 8 * SILU_MAXV) {
+    bf16x8 gr[SILU_MAXV], ur[SILU_MAXV], dr[SILU_MAXV];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float sg = 1.0f / (1.0f + expf(-g[k]));
-      du[k] = d[k] * (g[k] * sg);
-      dg[k] = d[k] * u[k] * sg * (1.0f + g[k] * (1.0f - sg));
+    for (int k = 0; k < SILU_MAXV; ++k) {
+      const int64_t c = c0 + k * 128 * 8;
+      if (c < I) {
+        gr[k] = *reinterpret_cast<const bf16x8*>(g_row + c);
+        ur[k] = *reinterpret_cast<const bf16x8*>(u_row + c);
+        dr[k] = *reinterpret_cast<const bf16x8*>(dout + row * I + c);
+      }
     }
-    store8(dgu + row * 2 * I + c, dg);
-    store8(dgu + row * 2 * I + I + c, du);
+#pragma unroll
+    for (int k = 0; k < SILU_MAXV; ++k) {
+      const int64_t c = c0 + k * 128 * 8;
+      if (c >= I) break;
+      float g[8], u[8], d[8], dg[8], du[8];
+      unpack8(gr[k], g);
+      unpack8(ur[k], u);
+      unpack8(dr[k], d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float sg = 1.0f / (1.0f + expf(-g[j]));
+        du[j] = d[j] * (g[j] * sg);
+        dg[j] = d[j] * u[j] * sg * (1.0f + g[j] * (1.0f - sg));
+      }
+      store8(dgu + row * 2 * I + c, dg);
+      store8(dgu + row * 2 * I + I + c, du);
+    }
   }
 }
 
@@ -782,30 +838,33 @@ extern "C" int qb_qk_norm_rope_bwd(const void* dout, const void* qkv, int64_t T,
   const bool vec16 = aligned16(dout) && aligned16(qkv) && aligned16(dqkv) && ld % 8 == 0 && aligned16(cos_sin) &&
                      (!rope_grad || (aligned16(q_norm_w) && aligned16(k_norm_w)));
   if (vec16 && q_norm_w && k_norm_w) {
-    qk_norm_rope_bwd8_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
+    const int64_t cap = 148 * QKB8_BLOCKS_PER_SM;  // one wave of resident blocks; the kernel strides over tokens
+    const int64_t g8 = T < cap ? T : cap;
+    qk_norm_rope_bwd8_kernel<<<(unsigned)g8, 128, 0, (cudaStream_t)stream>>>(p);
     return qb_launch_status();
   }
+  QB_CHECK_ARG(dout != dqkv);  // the warp kernel does not handle aliasing
   qk_norm_rope_bwd_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
   return qb_launch_status();
 }
 
 extern "C" int qb_silu_mul_fwd(const void* gate_up, int64_t T, int64_t I, void* out,
                                qb_stream_t stream) {
-  QB_CHECK_ARG(T >= 0 && I > 0 && I % 8 == 0);
+  QB_CHECK_ARG(T >= 0 && T < (int64_t)1 << 31 && I > 0 && I % 8 == 0);
   if (T == 0) return QB_OK;
   QB_CHECK_ARG(gate_up && out && aligned16(gate_up) && aligned16(out));
-  silu_mul_fwd_kernel<<<grid_for(T * I / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+  silu_mul_fwd_kernel<<<(unsigned)T, 128, 0, (cudaStream_t)stream>>>(
       (const bf16*)gate_up, T, I, (bf16*)out);
   return qb_launch_status();
 }
 
 extern "C" int qb_silu_mul_bwd(const void* dout, const void* gate_up, int64_t T, int64_t I,
                                void* dgate_up, qb_stream_t stream) {
-  QB_CHECK_ARG(T >= 0 && I > 0 && I % 8 == 0);
+  QB_CHECK_ARG(T >= 0 && T < (int64_t)1 << 31 && I > 0 && I % 8 == 0);
   if (T == 0) return QB_OK;
   QB_CHECK_ARG(dout && gate_up && dgate_up && aligned16(dout) && aligned16(gate_up) &&
                aligned16(dgate_up));
-  silu_mul_bwd_kernel<<<grid_for(T * I / 8, 256), 256, 0, (cudaStream_t)stream>>>(
+  silu_mul_bwd_kernel<<<(unsigned)T, 128, 0, (cudaStream_t)stream>>>(
       (const bf16*)dout, (const bf16*)gate_up, T, I, (bf16*)dgate_up);
   return qb_launch_status();
 }

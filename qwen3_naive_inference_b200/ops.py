@@ -22,7 +22,7 @@ from ._lib import NativeError, check
 
 __all__ = [
     "NativeError", "lib", "stream_ptr", "err_flag", "check_device_errors", "embedding", "rmsnorm",
-    "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "attention_packed", "attention_paged_prefill",
+    "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "qk_norm_rope_attention", "attention_packed", "attention_paged_prefill",
     "paged_decode_attention", "silu_mul", "add", "linear", "logprob", "sample", "grpo_advantage",
     "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan", "lm_head_logprob",
     "grpo_logit_loss",
@@ -170,17 +170,39 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: f
 
 
 # ---------------------------------------------------------------- QK-Norm + RoPE
+def _qk_norm_rope_fwd(qkv, positions, cos_sin, qw, kw, eps, hq, hkv, save=True):
+    """Rotated copy of ``qkv`` plus (with ``save``) the per-head rstd the backward needs."""
+    T, ld = qkv.shape
+    out = torch.empty_like(qkv)
+    q_rstd = torch.empty(T, hq, dtype=torch.float32, device=qkv.device) if save else None
+    k_rstd = torch.empty(T, hkv, dtype=torch.float32, device=qkv.device) if save else None
+    check(lib().qb_qk_norm_rope_fwd(_p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin),
+                                    cos_sin.shape[0], _p(qw), _p(kw), eps, _p(out), ld, 0, 0, 0, 0, 0,
+                                    _p(q_rstd) if save else 0, _p(k_rstd) if save else 0, _p(err_flag()),
+                                    stream_ptr()),
+          "qb_qk_norm_rope_fwd")
+    return out, q_rstd, k_rstd
+
+
+def _qk_norm_rope_bwd(dout, dqkv, qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd, hq, hkv, rope_grad):
+    """Writes the projection gradient into ``dqkv`` (which may be ``dout`` itself: the v columns
+    then stay in place) and returns the norm-weight gradients (None without rope_grad)."""
+    T, ld = qkv.shape
+    dqw = torch.zeros(128, dtype=torch.float32, device=qkv.device)
+    dkw = torch.zeros(128, dtype=torch.float32, device=qkv.device)
+    check(lib().qb_qk_norm_rope_bwd(_p(dout), _p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin),
+                                    cos_sin.shape[0], _p(qw), _p(kw), _p(q_rstd), _p(k_rstd),
+                                    1 if rope_grad else 0, _p(dqkv), _p(dqw), _p(dkw), _p(err_flag()),
+                                    stream_ptr()), "qb_qk_norm_rope_bwd")
+    if not rope_grad:  # the reference's Triton RoPE leaves q_norm/k_norm without a grad
+        return None, None
+    return _to_bf16(dqw).to(qw.dtype), _to_bf16(dkw).to(kw.dtype)
+
+
 class _QKNormRope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, positions, cos_sin, qw, kw, eps, hq, hkv, rope_grad):
-        T, ld = qkv.shape
-        out = torch.empty_like(qkv)
-        q_rstd = torch.empty(T, hq, dtype=torch.float32, device=qkv.device)
-        k_rstd = torch.empty(T, hkv, dtype=torch.float32, device=qkv.device)
-        check(lib().qb_qk_norm_rope_fwd(_p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin),
-                                        cos_sin.shape[0], _p(qw), _p(kw), eps, _p(out), ld, 0, 0, 0, 0, 0,
-                                        _p(q_rstd), _p(k_rstd), _p(err_flag()), stream_ptr()),
-              "qb_qk_norm_rope_fwd")
+        out, q_rstd, k_rstd = _qk_norm_rope_fwd(qkv, positions, cos_sin, qw, kw, eps, hq, hkv)
         ctx.save_for_backward(qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd)
         ctx.cfg = (hq, hkv, rope_grad)
         return out
@@ -190,17 +212,10 @@ class _QKNormRope(torch.autograd.Function):
         qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd = ctx.saved_tensors
         hq, hkv, rope_grad = ctx.cfg
         dout = dout.contiguous()
-        T, ld = qkv.shape
-        dqkv = torch.empty_like(qkv)
-        dqw = torch.zeros(128, dtype=torch.float32, device=qkv.device)
-        dkw = torch.zeros(128, dtype=torch.float32, device=qkv.device)
-        check(lib().qb_qk_norm_rope_bwd(_p(dout), _p(qkv), T, ld, hq, hkv, 128, _p(positions), _p(cos_sin),
-                                        cos_sin.shape[0], _p(qw), _p(kw), _p(q_rstd), _p(k_rstd),
-                                        1 if rope_grad else 0, _p(dqkv), _p(dqw), _p(dkw), _p(err_flag()),
-                                        stream_ptr()), "qb_qk_norm_rope_bwd")
-        if not rope_grad:  # the reference's Triton RoPE leaves q_norm/k_norm without a grad
-            return dqkv, None, None, None, None, None, None, None, None
-        return dqkv, None, None, _to_bf16(dqw).to(qw.dtype), _to_bf16(dkw).to(kw.dtype), None, None, None, None
+        dqkv = torch.empty_like(qkv)  # the incoming gradient may be the caller's tensor: not in place
+        dqw, dkw = _qk_norm_rope_bwd(dout, dqkv, qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd, hq, hkv,
+                                     rope_grad)
+        return dqkv, None, None, dqw, dkw, None, None, None, None
 
 
 def qk_norm_rope(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, rope_grad=True):
@@ -241,20 +256,38 @@ def build_tiles(lengths, block: int = 64) -> np.ndarray:
     return np.stack([seq, start.astype(np.int32)], axis=1).astype(np.int32).reshape(-1)
 
 
+def _attn_packed_fwd(qkv, cu, tiles, hq, hkv, scale):
+    T, ld = qkv.shape
+    out = torch.empty(T, hq * 128, dtype=qkv.dtype, device=qkv.device)
+    lse = torch.empty(hq, T, dtype=torch.float32, device=qkv.device)
+    base = qkv.data_ptr()
+    k_ptr = base + hq * 128 * 2
+    v_ptr = base + (hq + hkv) * 128 * 2
+    check(lib().qb_attn_varlen_fwd(base, ld, k_ptr, v_ptr, ld, 0, 0, 0, 256, _p(cu), _p(cu), cu.numel() - 1,
+                                   _p(tiles), tiles.numel() // 2, 0, hq, hkv, 128, scale, _p(out), hq * 128,
+                                   _p(lse), T, _p(err_flag()), stream_ptr()), "qb_attn_varlen_fwd")
+    return out, lse
+
+
+def _attn_packed_bwd(dout, qkv, cu, tiles, out, lse, hq, hkv, scale):
+    """Fresh [T, ld] gradient w.r.t. the packed (rotated) q | k | v columns."""
+    T, ld = qkv.shape
+    dqkv = torch.empty_like(qkv)
+    delta = torch.empty(hq, T, dtype=torch.float32, device=qkv.device)
+    b = qkv.data_ptr()
+    db = dqkv.data_ptr()
+    koff, voff = hq * 128 * 2, (hq + hkv) * 128 * 2
+    check(lib().qb_attn_varlen_bwd(b, b + koff, b + voff, ld, _p(out), _p(dout), hq * 128, _p(lse), _p(cu),
+                                   cu.numel() - 1, _p(tiles), tiles.numel() // 2, hq, hkv, 128, scale, T,
+                                   _p(delta), db, db + koff, db + voff, _p(err_flag()), stream_ptr()),
+          "qb_attn_varlen_bwd")
+    return dqkv
+
+
 class _AttnPacked(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, cu, tiles, hq, hkv, scale):
-        T, ld = qkv.shape
-        out = torch.empty(T, hq * 128, dtype=qkv.dtype, device=qkv.device)
-        lse = torch.empty(hq, T, dtype=torch.float32, device=qkv.device)
-        batch = cu.numel() - 1
-        n_tiles = tiles.numel() // 2
-        base = qkv.data_ptr()
-        k_ptr = base + hq * 128 * 2
-        v_ptr = base + (hq + hkv) * 128 * 2
-        check(lib().qb_attn_varlen_fwd(base, ld, k_ptr, v_ptr, ld, 0, 0, 0, 256, _p(cu), _p(cu), batch,
-                                       _p(tiles), n_tiles, 0, hq, hkv, 128, scale, _p(out), hq * 128, _p(lse), T,
-                                       _p(err_flag()), stream_ptr()), "qb_attn_varlen_fwd")
+        out, lse = _attn_packed_fwd(qkv, cu, tiles, hq, hkv, scale)
         ctx.save_for_backward(qkv, cu, tiles, out, lse)
         ctx.cfg = (hq, hkv, scale)
         return out
@@ -263,18 +296,42 @@ class _AttnPacked(torch.autograd.Function):
     def backward(ctx, dout):
         qkv, cu, tiles, out, lse = ctx.saved_tensors
         hq, hkv, scale = ctx.cfg
-        dout = dout.contiguous()
-        T, ld = qkv.shape
-        dqkv = torch.empty_like(qkv)
-        delta = torch.empty(hq, T, dtype=torch.float32, device=qkv.device)
-        b = qkv.data_ptr()
-        db = dqkv.data_ptr()
-        koff, voff = hq * 128 * 2, (hq + hkv) * 128 * 2
-        check(lib().qb_attn_varlen_bwd(b, b + koff, b + voff, ld, _p(out), _p(dout), hq * 128, _p(lse), _p(cu),
-                                       cu.numel() - 1, _p(tiles), tiles.numel() // 2, hq, hkv, 128, scale, T,
-                                       _p(delta), db, db + koff, db + voff, _p(err_flag()), stream_ptr()),
-              "qb_attn_varlen_bwd")
-        return dqkv, None, None, None, None, None
+        return _attn_packed_bwd(dout.contiguous(), qkv, cu, tiles, out, lse, hq, hkv, scale), \
+            None, None, None, None, None
+
+
+class _QKNormRopeAttn(torch.autograd.Function):
+    """QK-norm + RoPE followed by packed causal attention as one autograd node, so the attention
+    backward's fresh gradient buffer takes the QK-norm backward in place (its v columns are
+    already final and are not copied)."""
+
+    @staticmethod
+    def forward(ctx, qkv, positions, cos_sin, qw, kw, eps, hq, hkv, rope_grad, cu, tiles, scale):
+        rot, q_rstd, k_rstd = _qk_norm_rope_fwd(qkv, positions, cos_sin, qw, kw, eps, hq, hkv)
+        out, lse = _attn_packed_fwd(rot, cu, tiles, hq, hkv, scale)
+        ctx.save_for_backward(qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd, rot, cu, tiles, out, lse)
+        ctx.cfg = (hq, hkv, rope_grad, scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd, rot, cu, tiles, out, lse = ctx.saved_tensors
+        hq, hkv, rope_grad, scale = ctx.cfg
+        d = _attn_packed_bwd(dout.contiguous(), rot, cu, tiles, out, lse, hq, hkv, scale)
+        dqw, dkw = _qk_norm_rope_bwd(d, d, qkv, positions, cos_sin, qw, kw, q_rstd, k_rstd, hq, hkv, rope_grad)
+        return d, None, None, dqw, dkw, None, None, None, None, None, None, None
+
+
+def qk_norm_rope_attention(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, cu_seqlens, tiles, hq, hkv, scale,
+                           rope_grad=True):
+    """``attention_packed(qk_norm_rope(qkv, ...), ...)`` with one fused backward (training path)."""
+    _cuda(qkv, positions, cos_sin, cu_seqlens, tiles)
+    qkv = qkv.contiguous()
+    if torch.is_grad_enabled() and (qkv.requires_grad or q_norm_w.requires_grad):
+        return _QKNormRopeAttn.apply(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, rope_grad,
+                                     cu_seqlens, tiles, scale)
+    rot, _, _ = _qk_norm_rope_fwd(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, save=False)
+    return _attn_packed_fwd(rot, cu_seqlens, tiles, hq, hkv, scale)[0]
 
 
 def attention_packed(qkv_rot, cu_seqlens, tiles, hq, hkv, scale):

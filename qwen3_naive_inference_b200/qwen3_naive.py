@@ -295,10 +295,9 @@ class Qwen3Attention(nn.Module):
     def forward_packed(self, x, positions, cu_seqlens, tiles):
         """Training/recompute path over packed sequences (each attends only to itself)."""
         qkv = ops.linear(x, self.qkv_proj.weight)
-        qkv_rot = ops.qk_norm_rope(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
-                                   self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads,
-                                   rope_grad=self.rope_grad)
-        o = ops.attention_packed(qkv_rot, cu_seqlens, tiles, self.num_heads, self.num_kv_heads, self.scale)
+        o = ops.qk_norm_rope_attention(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
+                                       self.k_norm.weight, self.eps, cu_seqlens, tiles, self.num_heads,
+                                       self.num_kv_heads, self.scale, rope_grad=self.rope_grad)
         return ops.linear(o, self.o_proj.weight)
 
     def forward(self, x):

@@ -137,6 +137,50 @@ def test_qk_norm_rope_backward(cuda, rope_grad):
         assert xd.grad[:, :(hq + hkv) * 128].abs().max().item() == 0.0
 
 
+@pytest.mark.parametrize("rope_grad", [True, False])
+def test_qk_norm_rope_attention_fused_backward(cuda, rope_grad):
+    """The fused node (QK-norm backward in place in the attention backward's buffer) against the
+    two-node composition: same projection gradient bit for bit, same norm-weight gradients up to
+    the order of the fp32 atomics.  1500 tokens: more than one wave of the backward's grid, so
+    blocks walk several tokens."""
+    hq, hkv = 16, 8
+    lens = [700, 300, 500]
+    T = sum(lens)
+    qkv, pos, qw, kw = _qkv_case(T, 21)
+    pos = torch.cat([torch.arange(n) for n in lens])
+    cs = R.rope_cache(128, 4096, 1e6).to(cuda)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=cuda)
+    tiles = torch.from_numpy(ops.build_tiles(lens)).to(cuda)
+    dout = torch.randn(T, hq * 128, generator=gen(22)).to(BF).to(cuda)
+    scale = 128 ** -0.5
+    grads = []
+    for fused in (False, True):
+        x = qkv.to(cuda).requires_grad_(True)
+        qwd, kwd = qw.to(cuda).requires_grad_(True), kw.to(cuda).requires_grad_(True)
+        if fused:
+            o = ops.qk_norm_rope_attention(x, pos.to(cuda), cs, qwd, kwd, 1e-6, cu, tiles, hq, hkv, scale,
+                                           rope_grad=rope_grad)
+        else:
+            rot = ops.qk_norm_rope(x, pos.to(cuda), cs, qwd, kwd, 1e-6, hq, hkv, rope_grad=rope_grad)
+            o = ops.attention_packed(rot, cu, tiles, hq, hkv, scale)
+        o.backward(dout)
+        grads.append((o.detach(), x.grad, qwd.grad, kwd.grad))
+    ops.check_device_errors()
+    (o0, dx0, dq0, dk0), (o1, dx1, dq1, dk1) = grads
+    assert torch.equal(o0, o1)
+    assert torch.equal(dx0, dx1)
+    if rope_grad:
+        torch.testing.assert_close(dq1.float(), dq0.float(), rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(dk1.float(), dk0.float(), rtol=1e-2, atol=1e-2)
+    else:
+        assert dq1 is None and dk1 is None
+        assert dx1[:, :(hq + hkv) * 128].abs().max().item() == 0.0
+    with torch.no_grad():
+        o2 = ops.qk_norm_rope_attention(qkv.to(cuda), pos.to(cuda), cs, qw.to(cuda), kw.to(cuda), 1e-6, cu, tiles,
+                                        hq, hkv, scale)
+    assert torch.equal(o2, o0)
+
+
 def test_silu_mul(cuda):
     g = gen(11)
     gu = torch.randn(19, 2 * 3072, generator=g).to(BF)
