@@ -331,6 +331,11 @@ int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
                     int b_mn_major, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int mode,
                     int* err, qb_stream_t stream);
+/* The tile layout qb_gemm_bf16 / qb_gemm_bf16_ex choose for an M x N x K product (B MN-major or
+ * not): *pair = 1 for 256-row tiles on a CTA pair, *tile_n = the tile's width (N), *split = the
+ * number of CTAs a 128 x 128 tile's K range is split over (1: none).  Needs the current device
+ * (the split layouts are sized by cluster occupancy).  For tests and tuning. */
+int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int* pair, int* tile_n, int* split);
 
 /* ---------------------------------------------------------------- optimizer helpers
  * dst (bf16) = bf16(src fp32); used to hand fp32-accumulated gradients to the

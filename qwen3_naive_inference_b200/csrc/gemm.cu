@@ -299,26 +299,34 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 }
 
 // ---------------------------------------------------------------- CTA-pair kernel (cta_group::2)
-// A cluster of two CTAs on two SMs computes a 256 x 256 tile.  Per 64-deep K block each CTA
-// loads its own 128 rows of A and its own 128-row half of B (N) -- 32 KB -- into its ring,
+// A cluster of two CTAs on two SMs computes a 256 x PBN tile (PBN = 256, 192 or 128).  Per 64-deep
+// K block each CTA loads its own 128 rows of A and its own PBN/2-row half of B (N) into its ring,
 // signalling the stage barrier of the even CTA (the leader), whose one thread issues
-// tcgen05.mma.cta_group::2 (M = 256, N = 256) reading both CTAs' stages; each CTA's TMEM receives
-// its 128 rows of the accumulator (double-buffered, 2 x 256 columns).  Each SM pulls 32 KB per
-// 0.5 us of MMA work instead of the 48 KB of a 128 x 256 tile, and 6 stages fit, so the ring
-// covers the operands' latency.  The leader's commits release both CTAs' stages and
-// accumulators (one commit per CTA's barrier); each CTA's epilogue drains its own TMEM rows and
-// tells the leader through a remote arrive.  Every wait is bounded; each CTA loads from this
-// GPU's memory only.
-constexpr int P_STAGES = 6;
-constexpr int P_HALF_BYTES = 128 * BK * 2;             // 16 KB: 128 rows x 64 K of A, or of B
-constexpr int P_STAGE_BYTES = 2 * P_HALF_BYTES;        // this CTA's A rows + B half
-constexpr int P_TMEM_COLS = 512;                       // 2 accumulators x 256 columns
-constexpr int P_SMEM = P_STAGES * P_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// tcgen05.mma.cta_group::2 (M = 256, N = PBN) reading both CTAs' stages; each CTA's TMEM receives
+// its 128 rows of the accumulator (double-buffered).  Each SM pulls (128 + PBN/2) rows of operands
+// per K block for a 128 x PBN share of the product, against (128 + PBN) rows for the same share
+// on one CTA: 256-wide tiles for products that fill every SM pair, 192 / 128-wide ones for the
+// decode step's skinny products (M = 512), whose time is the operands' trip from L2.  The
+// leader's commits release both CTAs' stages and accumulators (one commit per CTA's barrier);
+// each CTA's epilogue drains its own TMEM rows and tells the leader through a remote arrive.
+// Every wait is bounded; each CTA loads from this GPU's memory only.
+constexpr int P_HALF_BYTES = 128 * BK * 2;  // 16 KB: 128 rows x 64 K of A (this CTA's rows)
 
-template <bool A_MN, bool B_MN>
+template <int PBN>
+struct PairShape {
+  static constexpr int B_ROWS = PBN / 2;                       // this CTA's rows of B
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static constexpr int STAGE_BYTES = P_HALF_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;  // 6 / 7 / 8 stages
+  static constexpr int ACC_STRIDE = PBN <= 128 ? PBN : 256;   // TMEM columns between the accumulators
+  static constexpr int TMEM_COLS = 2 * ACC_STRIDE;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <bool A_MN, bool B_MN, int PBN>
 struct PairCfg {
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
-                                    ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(256 >> 3) << 17) |
+                                    ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(PBN >> 3) << 17) |
                                     ((uint32_t)(256 >> 4) << 24);
 };
 
@@ -355,11 +363,13 @@ QB_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, in
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
       : "memory");
 }
-template <bool MN_MAJOR>
+// ROWS rows (M or N) x 64 K of one operand: one K-major box, or ROWS/64 MN-major 64-wide atoms.
+template <bool MN_MAJOR, int ROWS>
 QB_DEVICE void load_half(uint32_t dst, const CUtensorMap* map, int k0, int mn0, uint32_t bar) {
-  if (MN_MAJOR) {
-    tma_load_2d_pair(dst, map, mn0, k0, bar);
-    tma_load_2d_pair(dst + 64 * 128, map, mn0 + 64, k0, bar);
+  if constexpr (MN_MAJOR) {
+    static_assert(ROWS % 64 == 0, "MN-major operands load whole 64-wide atoms");
+#pragma unroll
+    for (int a = 0; a < ROWS / 64; ++a) tma_load_2d_pair(dst + a * 64 * 128, map, mn0 + a * 64, k0, bar);
   } else {
     tma_load_2d_pair(dst, map, k0, mn0, bar);
   }
@@ -376,10 +386,14 @@ QB_DEVICE void umma_commit_pair(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-template <int MODE, bool A_MN, bool B_MN>
+template <int MODE, bool A_MN, bool B_MN, int PBN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  GemmParams p) {
+  using Sh = PairShape<PBN>;
+  constexpr int P_STAGES = Sh::STAGES;
+  constexpr int P_STAGE_BYTES = Sh::STAGE_BYTES;
+  constexpr int P_TMEM_COLS = Sh::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023) & ~1023u;  // the same offset in both CTAs of the pair
@@ -399,7 +413,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   const uint32_t rank = cluster_rank(), peer = rank ^ 1;
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-  const int tiles_m = (p.M + 255) / 256, tiles_n = (p.N + 255) / 256;
+  const int tiles_m = (p.M + 255) / 256, tiles_n = (p.N + PBN - 1) / PBN;
   const int n_tiles = tiles_m * tiles_n;
   const int kblocks = (p.K + BK - 1) / BK;
 
@@ -433,14 +447,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     int stage = 0;
     uint32_t phase = 0;
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
-      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * 256 + (int)rank * 128;
+      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * PBN + (int)rank * Sh::B_ROWS;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
         const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
         const uint32_t lf = cluster_addr(full_bar(stage), 0);
         mbar_expect_tx_remote(lf, P_STAGE_BYTES);
-        load_half<A_MN>(sa, &tmap_a, kb * BK, m0, lf);
-        load_half<B_MN>(sb, &tmap_b, kb * BK, n0, lf);
+        load_half<A_MN, 128>(sa, &tmap_a, kb * BK, m0, lf);
+        load_half<B_MN, Sh::B_ROWS>(sb, &tmap_b, kb * BK, n0, lf);
         if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
       }
     }
@@ -453,7 +467,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
       if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1, abort_flag, p.err)) break;
       tc_fence_after();
-      const uint32_t d = tmem + acc * 256;
+      const uint32_t d = tmem + acc * Sh::ACC_STRIDE;
       bool ok = true;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait_cluster(full_bar(stage), phase, abort_flag, p.err)) { ok = false; break; }
@@ -461,7 +475,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
 #pragma unroll
         for (int j = 0; j < BK / 16; ++j)
-          umma_pair(d, operand_desc<A_MN>(sa, j), operand_desc<B_MN>(sb, j), PairCfg<A_MN, B_MN>::IDESC,
+          umma_pair(d, operand_desc<A_MN>(sa, j), operand_desc<B_MN>(sb, j), PairCfg<A_MN, B_MN, PBN>::IDESC,
                     (kb | j) != 0);
         umma_commit_pair(empty_bar(stage));  // both CTAs' stage is free once these MMAs read it
         umma_commit_pair(cluster_addr(empty_bar(stage), peer));
@@ -485,19 +499,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
-      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * 256;
+      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * PBN;
       // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
       if (__any_sync(0xffffffffu, !mbar_wait_cluster(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
       if constexpr (MODE == 3) {
-        lse_tile<256>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * 256, row, row_ok, n0, t / tiles_m);
+        lse_tile<PBN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE, row, row_ok, n0,
+                      t / tiles_m);
       } else {
 #pragma unroll 1
-        for (int c = 0; c < 256; c += 32) {
+        for (int c = 0; c < PBN; c += 32) {
           uint32_t r[32];
-          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * 256 + c, r);
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE + c, r);
           const int col = n0 + c;
           if (!row_ok || col >= p.N) continue;
           store_row32<MODE>(p, row, col, r);
@@ -767,21 +782,22 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStrea
   return qb_launch_status();
 }
 
-template <int MODE, bool A_MN, bool B_MN>
+template <int MODE, bool A_MN, bool B_MN, int PBN>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
-  auto kern = gemm_pair_kernel<MODE, A_MN, B_MN>;
+  auto kern = gemm_pair_kernel<MODE, A_MN, B_MN, PBN>;
+  constexpr int SMEM = PairShape<PBN>::SMEM;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess)
       return qb_launch_status();
     attr = true;
   }
-  const int tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
+  const int tiles = ((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
   const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = P_SMEM;
+  cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attrs[1];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
@@ -863,11 +879,21 @@ int split_clusters(int S) {
   return n;
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int PBN>
 int launch_pair_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStream_t st) {
-  if (mode == 0) return launch_pair<0, A_MN, B_MN>(ta, tb, p, st);
-  if (mode == 1) return launch_pair<1, A_MN, B_MN>(ta, tb, p, st);
-  return launch_pair<2, A_MN, B_MN>(ta, tb, p, st);
+  if (mode == 0) return launch_pair<0, A_MN, B_MN, PBN>(ta, tb, p, st);
+  if (mode == 1) return launch_pair<1, A_MN, B_MN, PBN>(ta, tb, p, st);
+  return launch_pair<2, A_MN, B_MN, PBN>(ta, tb, p, st);
+}
+
+template <bool A_MN, bool B_MN>
+int launch_pair_pbn(int pbn, int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p,
+                    cudaStream_t st) {
+  if (pbn == 128) return launch_pair_mode<A_MN, B_MN, 128>(mode, ta, tb, p, st);
+  if constexpr (!B_MN) {  // an MN-major B loads whole 64-wide atoms: 96 rows a CTA do not split
+    if (pbn == 192) return launch_pair_mode<A_MN, B_MN, 192>(mode, ta, tb, p, st);
+  }
+  return launch_pair_mode<A_MN, B_MN, 256>(mode, ta, tb, p, st);
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
@@ -886,6 +912,46 @@ int launch_layout(int bn, int mode, const CUtensorMap& ta, const CUtensorMap& tb
 
 inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; }
 
+// The layout of one product.  256x256 tiles on CTA pairs when they fill every SM pair at least
+// once; 128 x 256 single-CTA tiles when they cover every SM at least once.  Otherwise every
+// candidate is costed by the operand bytes its busiest SM pulls through L2 (the bound of these
+// one-wave products): 128 x {128, 192} single-CTA tiles in waves over the SMs, 256 x {128, 192}
+// tiles on CTA pairs in waves over the SM pairs, or 128 x 128 tiles split along K over a cluster
+// of 2 or 4 CTAs (one wave, plus the partials' exchange, costed as two K blocks).
+struct GemmPlan {
+  bool pair;
+  int bn;     // tile width (N): of the pair's 256-row tile, or of the single CTA's 128-row tile
+  int split;  // CTAs a 128 x 128 tile's K range is split over (1: none)
+};
+
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
+  const int sms = sm_count();
+  const int64_t tm = (M + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
+  if (N >= 256 && M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2) return {true, 256, 1};
+  if (N >= 256 && tm * ((N + 255) / 256) >= sms) return {false, 256, 1};
+  const int64_t t128 = tm * ((N + 127) / 128), t192 = tm * ((N + 191) / 192);
+  GemmPlan best_plan{false, 128, 1};
+  const int64_t kb_bytes = (int64_t)(BM + 128) * BK * 2;
+  int64_t best = (t128 + sms - 1) / sms * kblocks * kb_bytes;
+  const int64_t c192 = (t192 + sms - 1) / sms * kblocks * (int64_t)(BM + 192) * BK * 2;
+  if (N > 128 && c192 < best) { best = c192; best_plan = {false, 192, 1}; }
+  if (M > 128) {
+    for (int cand = 128; cand <= 192; cand += 64) {
+      if (cand == 192 && (b_mn || N <= 128)) continue;  // an MN-major B splits into 64-wide atoms only
+      const int64_t pairs = ((M + 255) / 256) * ((N + cand - 1) / cand);
+      const int64_t c = (pairs + sms / 2 - 1) / (sms / 2) * kblocks * (int64_t)(128 + cand / 2) * BK * 2;
+      if (c < best) { best = c; best_plan = {true, cand, 1}; }
+    }
+  }
+  for (int S = 2; S <= 4; S *= 2) {
+    if (kblocks < 2 * S || t128 > split_clusters(S)) continue;
+    const int64_t c = (kblocks + S - 1) / S * kb_bytes + 2 * kb_bytes;
+    if (c < best) { best = c; best_plan = {false, 128, S}; }
+  }
+  return best_plan;
+}
+
+
 int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, bool b_mn, void* C,
                   int64_t ldc, int64_t M, int64_t N, int64_t K, int mode, int* err, cudaStream_t st) {
   QB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && mode >= 0 && mode <= 2);
@@ -897,38 +963,19 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
   const int64_t elem = mode == 0 ? 2 : 4;
   const int vec_ok = al16(C) && (ldc * elem) % 16 == 0;
-  const int sms = sm_count();
-  const int64_t tm = (M + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
-  // 256x256 tiles on CTA pairs when they fill every SM pair at least once
-  const bool pair = N >= 256 && M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2;
+  const GemmPlan pl = plan_gemm(M, N, K, b_mn);
+  const int64_t tm = (M + BM - 1) / BM;
+  const int pbn = pl.pair ? pl.bn : 0, bn = pl.bn, split = pl.split;
   CUtensorMap ta, tb;
-  if (pair) {
+  if (pbn) {
     if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
-    if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128)) return QB_ERR_INVALID;
+    if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)(pbn / 2)))
+      return QB_ERR_INVALID;
     GemmParams pp{C, ldc, (int)M, (int)N, (int)K, 0, 0, vec_ok, err};
-    if (!a_mn && !b_mn) return launch_pair_mode<false, false>(mode, ta, tb, pp, st);
-    if (!a_mn && b_mn) return launch_pair_mode<false, true>(mode, ta, tb, pp, st);
-    if (a_mn && !b_mn) return launch_pair_mode<true, false>(mode, ta, tb, pp, st);
-    return launch_pair_mode<true, true>(mode, ta, tb, pp, st);
-  }
-  // Single-CTA tiles.  128x256 when they cover every SM at least once; otherwise the layout whose
-  // busiest SM pulls the fewest operand bytes: 128x128 or 128x192 tiles (in waves over the SMs),
-  // or 128x128 tiles split along K over a cluster of 2 or 4 CTAs (one wave, plus the partials'
-  // exchange, costed as two K blocks).
-  const int64_t t128 = tm * ((N + 127) / 128), t192 = tm * ((N + 191) / 192);
-  int bn = 128, split = 1;
-  if (N >= 256 && tm * ((N + 255) / 256) >= sms) {
-    bn = 256;
-  } else {
-    const int64_t kb_bytes = (int64_t)(BM + 128) * BK * 2;
-    int64_t best = (t128 + sms - 1) / sms * kblocks * kb_bytes;
-    const int64_t c192 = (t192 + sms - 1) / sms * kblocks * (int64_t)(BM + 192) * BK * 2;
-    if (N > 128 && c192 < best) { best = c192; bn = 192; }
-    for (int S = 2; S <= 4; S *= 2) {
-      if (kblocks < 2 * S || t128 > split_clusters(S)) continue;
-      const int64_t c = (kblocks + S - 1) / S * kb_bytes + 2 * kb_bytes;
-      if (c < best) { best = c; bn = 128; split = S; }
-    }
+    if (!a_mn && !b_mn) return launch_pair_pbn<false, false>(pbn, mode, ta, tb, pp, st);
+    if (!a_mn && b_mn) return launch_pair_pbn<false, true>(pbn, mode, ta, tb, pp, st);
+    if (a_mn && !b_mn) return launch_pair_pbn<true, false>(pbn, mode, ta, tb, pp, st);
+    return launch_pair_pbn<true, true>(pbn, mode, ta, tb, pp, st);
   }
   if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
   if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)bn)) return QB_ERR_INVALID;
@@ -1006,7 +1053,7 @@ int lm_head_logprob(const void* h, int64_t ldh, const void* W, int64_t ldw, int6
   if (!operand_tmap(&ta, h, false, (uint64_t)n, (uint64_t)K, (uint64_t)ldh, BM)) return QB_ERR_INVALID;
   if (!operand_tmap(&tb, W, false, (uint64_t)V, (uint64_t)K, (uint64_t)ldw, pair ? 128 : (uint32_t)bn))
     return QB_ERR_INVALID;
-  int status = pair ? launch_pair<3, false, false>(ta, tb, p, st)
+  int status = pair ? launch_pair<3, false, false, 256>(ta, tb, p, st)
                     : (bn == 256 ? launch<256, 4, 3, false, false>(ta, tb, p, st)
                                  : launch<128, 6, 3, false, false>(ta, tb, p, st));
   if (status != QB_OK) return status;
@@ -1034,6 +1081,15 @@ extern "C" int qb_lm_head_logprob(const void* h, int64_t ldh, const void* W, int
                                   void* logits, int64_t ld_logits, void* workspace, int* err, qb_stream_t stream) {
   return lm_head_logprob(h, ldh, W, ldw, n, V, K, targets, dest, logp, lse, logits, ld_logits, workspace, err,
                          (cudaStream_t)stream);
+}
+
+extern "C" int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int* pair, int* tile_n, int* split) {
+  QB_CHECK_ARG(M > 0 && N > 0 && K > 0 && pair && tile_n && split);
+  const GemmPlan pl = plan_gemm(M, N, K, b_mn_major != 0);
+  *pair = pl.pair ? 1 : 0;
+  *tile_n = pl.bn;
+  *split = pl.split;
+  return QB_OK;
 }
 
 extern "C" size_t qb_lm_head_logprob_workspace_bytes(int64_t n, int64_t V) {

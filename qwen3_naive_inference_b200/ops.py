@@ -506,6 +506,15 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode
     return out
 
 
+def gemm_plan(M: int, N: int, K: int, b_mn: bool = False) -> tuple[str, int, int]:
+    """The layout the GEMM picks for an M x N x K product: ("pair" | "single", tile width, split)."""
+    import ctypes
+    pair, tile_n, split = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check(lib().qb_gemm_plan(M, N, K, 1 if b_mn else 0, ctypes.addressof(pair), ctypes.addressof(tile_n),
+                             ctypes.addressof(split)), "qb_gemm_plan")
+    return ("pair" if pair.value else "single", tile_n.value, split.value)
+
+
 def gemm_ex(a: torch.Tensor, a_mn: bool, b: torch.Tensor, b_mn: bool, out: torch.Tensor | None = None,
             mode: int = 0) -> torch.Tensor:
     """C = op(a) @ op(b).T on the tcgen05 GEMM.  ``a`` is [M, K] (a_mn False) or stored [K, M]

@@ -24,7 +24,10 @@ def ref(a, b):
                                    (512, 1024, 2048), (512, 1024, 3072), (300, 1000, 1024), (4, 256, 512),
                                    (809, 256, 512),
                                    # 128x192 tiles (one wave where 128x128 would need two), N and K tails
-                                   (512, 6144, 1024), (500, 5000, 1000)])
+                                   (512, 6144, 1024), (500, 5000, 1000),
+                                   # 256 x 128 / 256 x 192 tiles on CTA pairs (decode-step qkv / gate_up),
+                                   # M, N and K tails
+                                   (480, 4096, 1024), (300, 4000, 1000), (257, 6100, 1000)])
 def test_gemm_bf16_out(cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M * 7 + N)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -37,7 +40,8 @@ def test_gemm_bf16_out(cuda, M, N, K):
 
 
 @pytest.mark.parametrize("mode", [1, 2])
-@pytest.mark.parametrize("M,N,K", [(200, 384, 512), (2000, 2600, 648), (513, 1024, 3072), (500, 5000, 1000)])
+@pytest.mark.parametrize("M,N,K", [(200, 384, 512), (2000, 2600, 648), (513, 1024, 3072), (500, 5000, 1000),
+                                   (512, 4096, 1024)])
 def test_gemm_fp32_out_and_accumulate(cuda, mode, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(mode)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -83,7 +87,8 @@ def test_gemm_repeated_calls_stable(cuda):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 1024, 776), (1000, 384, 4096), (64, 151936, 200),
-                                   (2048, 2560, 512), (2000, 2600, 648), (400, 6000, 200)])
+                                   (2048, 2560, 512), (2000, 2600, 648), (400, 6000, 200), (512, 4096, 1024),
+                                   (300, 4000, 520)])
 def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
     """Backward layouts: A stored [K, M] and/or B stored [K, N]; K need not be a multiple of 64
     (row pitches stay multiples of 8 elements, the TMA rule)."""
@@ -100,6 +105,21 @@ def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
     out = acc.clone()
     ops.gemm_ex(a_st, a_mn, b_st, b_mn, out=out, mode=2)
     assert torch.allclose(out, acc + r, rtol=1e-3, atol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K,b_mn,want", [
+    (8192, 6144, 1024, False, ("pair", 256, 1)),   # training shapes: 256 x 256 tiles fill the SM pairs
+    (512, 4096, 1024, False, ("pair", 128, 1)),    # decode qkv_proj
+    (512, 4096, 1024, True, ("pair", 128, 1)),
+    (512, 6144, 1024, False, ("pair", 192, 1)),    # decode gate_up_proj
+    (512, 6144, 1024, True, ("single", 192, 1)),   # an MN-major B cannot split 96-row halves
+    (512, 1024, 2048, False, ("single", 128, 4)),  # decode o_proj: split-K over 4-CTA clusters
+    (512, 1024, 3072, False, ("single", 128, 4)),  # decode down_proj
+    (7, 300, 128, False, ("single", 128, 1)),
+])
+def test_gemm_plan(cuda, M, N, K, b_mn, want):
+    """The layouts the cases above rely on are the ones the dispatcher picks."""
+    assert ops.gemm_plan(M, N, K, b_mn) == want
 
 
 def test_gemm_k_tail_k_major(cuda):
