@@ -85,6 +85,8 @@ def parse():
                     help="skip the extra untimed step under CUPTI that measures the dominant kernel inside the step")
     ap.add_argument("--no-share-prefix", action="store_true",
                     help="roll out with the reference's scheduler (every completion prefilled and stored)")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch every kernel with plain stream ordering (no programmatic dependent launch)")
     return ap.parse_args()
 
 
@@ -537,6 +539,7 @@ def run_ours(args):
                            "rollout": "reference scheduler" if args.no_share_prefix else
                            "grouped: prompt prefilled once per group, shared KV pages, shared-prefix decode attention",
                            "l2": "inputs far larger than L2 (weights + 60+ GB KV cache per step)",
+                           "launch": "plain stream order" if args.no_pdl else "programmatic dependent launch",
                            "tokens_per_step": tokens // max(1, args.steps)},
                 "phases_s": {"rollout": last["t_rollout"], "ref_logprob": last["t_ref"], "train": last["t_train"],
                              "rollout_detail": last.get("rollout_stats")},
@@ -1095,6 +1098,9 @@ def run_attn_only():
 
 def main():
     args = parse()
+    if args.no_pdl and args.impl == "ours":
+        from qwen3_naive_inference_b200._lib import load
+        load().qb_set_pdl(0)
     args.total_prompts = 512
     if args.workload == "cfg5" and args.prompt_max == 512:
         args.prompt_max = 1024

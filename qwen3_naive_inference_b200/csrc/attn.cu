@@ -303,6 +303,8 @@ QB_DEVICE void decode_own_tile(const DecodeParams& p, uint8_t* smem, int split, 
 
 __global__ void __launch_bounds__(DEC_WARPS * 32)
 paged_decode_kernel(DecodeParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   decode_own_tile<DEC_STAGES>(p, smem, blockIdx.x, blockIdx.y, blockIdx.z);
 }
@@ -312,6 +314,8 @@ paged_decode_kernel(DecodeParams p) {
 // outputs are accumulated four slots per step so their loads overlap.  Empty slots (LSE = -inf)
 // were never written: their outputs are not read.
 __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (item >= batch * p.hq) return;
   const int lane = threadIdx.x & 31;
@@ -579,6 +583,8 @@ constexpr int GRP_SMEM = GRP_STAGES * DEC_STAGE_BYTES;
 
 __global__ void __launch_bounds__(DEC_WARPS * 32)
 paged_decode_grouped_kernel(DecodeParams p, GroupParams gp) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   int i = blockIdx.x;
   if (i < gp.n_shared_ctas) {
@@ -626,6 +632,8 @@ struct FwdParams {
 template <bool PAGED>
 __global__ void __launch_bounds__(FA_WARPS * 32)
 attn_fwd_kernel(FwdParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const int tile = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -836,6 +844,8 @@ struct BwdParams {
 
 // delta[h, row] = sum_d dO[row,h,d] * O[row,h,d]; one warp per (row, head).
 __global__ void attn_bwd_delta_kernel(BwdParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (item >= p.total * p.hq) return;
   const int lane = threadIdx.x & 31;
@@ -873,6 +883,8 @@ constexpr int DQ_SMEM = 6 * 64 * ROWB;
 
 __global__ void __launch_bounds__(128)
 attn_bwd_dkdv_kernel(BwdParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const int tile = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1016,6 +1028,8 @@ attn_bwd_dkdv_kernel(BwdParams p) {
 // CTA = (64-query tile, q head), 4 warps x 16 queries; loops over key tiles <= the query tile.
 __global__ void __launch_bounds__(128)
 attn_bwd_dq_kernel(BwdParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   const int tile = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1185,13 +1199,10 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
     attr_set = true;
   }
   dim3 grid((unsigned)max_splits, (unsigned)hkv, (unsigned)batch);
-  paged_decode_kernel<<<grid, DEC_WARPS * 32, DEC_SMEM, (cudaStream_t)stream>>>(p);
-  int st = qb_launch_status();
+  int st = qb_launch(paged_decode_kernel, dim3(grid), dim3(DEC_WARPS * 32), DEC_SMEM, (cudaStream_t)stream, 1, p);
   if (st != QB_OK || max_splits == 1) return st;
   const int wpb = 8;
-  paged_decode_combine_kernel<<<(unsigned)((batch * hq + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
-      p, batch);
-  return qb_launch_status();
+  return qb_launch(paged_decode_combine_kernel, dim3((unsigned)((batch * hq + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, p, batch);
 }
 
 extern "C" size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int Dh, int n_slots) {
@@ -1229,13 +1240,10 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
     cudaFuncSetAttribute(paged_decode_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GRP_SMEM);
     attr_set = true;
   }
-  paged_decode_grouped_kernel<<<(unsigned)n_ctas, DEC_WARPS * 32, GRP_SMEM, (cudaStream_t)stream>>>(d, gp);
-  int st = qb_launch_status();
+  int st = qb_launch(paged_decode_grouped_kernel, dim3((unsigned)n_ctas), dim3(DEC_WARPS * 32), GRP_SMEM, (cudaStream_t)stream, 1, d, gp);
   if (st != QB_OK) return st;
   const int wpb = 8;
-  paged_decode_combine_kernel<<<(unsigned)((batch * hq + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
-      d, batch);
-  return qb_launch_status();
+  return qb_launch(paged_decode_combine_kernel, dim3((unsigned)((batch * hq + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, d, batch);
 }
 
 extern "C" int qb_attn_varlen_fwd(const void* q, int64_t q_stride, const void* k, const void* v,
@@ -1272,16 +1280,16 @@ extern "C" int qb_attn_varlen_fwd(const void* q, int64_t q_stride, const void* k
       cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
       set = true;
     }
-    attn_fwd_kernel<true><<<grid, FA_WARPS * 32, FA_SMEM, (cudaStream_t)stream>>>(p);
+    return qb_launch(attn_fwd_kernel<true>, dim3(grid), dim3(FA_WARPS * 32), FA_SMEM, (cudaStream_t)stream, 1, p);
   } else {
     static bool set = false;
     if (!set) {
       cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
       set = true;
     }
-    attn_fwd_kernel<false><<<grid, FA_WARPS * 32, FA_SMEM, (cudaStream_t)stream>>>(p);
+    return qb_launch(attn_fwd_kernel<false>, dim3(grid), dim3(FA_WARPS * 32), FA_SMEM, (cudaStream_t)stream, 1,
+                     p);
   }
-  return qb_launch_status();
 }
 
 extern "C" int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, int64_t stride,
@@ -1300,8 +1308,7 @@ extern "C" int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, i
               o_stride, lse, cu_seqlens, tile_info, hq, hkv, scale, scale * LOG2E, total, delta,
               (bf16*)dq, (bf16*)dk, (bf16*)dv, err};
   const int wpb = 8;
-  attn_bwd_delta_kernel<<<(unsigned)((total * hq + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(p);
-  int st = qb_launch_status();
+  int st = qb_launch(attn_bwd_delta_kernel, dim3((unsigned)((total * hq + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, p);
   if (st != QB_OK) return st;
   static bool set = false;
   if (!set) {
@@ -1313,13 +1320,11 @@ extern "C" int qb_attn_varlen_bwd(const void* q, const void* k, const void* v, i
     st = attn_bwd_dkdv_tc_launch(q, k, v, stride, dout, o_stride, lse, delta, cu_seqlens, tile_info, n_tiles, hq,
                                  hkv, scale, total, dk, dv, err, (cudaStream_t)stream);
   } else {
-    attn_bwd_dkdv_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), 128, DKDV_SMEM, (cudaStream_t)stream>>>(p);
-    st = qb_launch_status();
+    st = qb_launch(attn_bwd_dkdv_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(128), DKDV_SMEM, (cudaStream_t)stream, 1, p);
   }
   if (st != QB_OK) return st;
   if (hq == 2 * hkv)  // dQ on tcgen05
     return attn_bwd_dq_tc_launch(q, k, v, stride, dout, o_stride, lse, delta, cu_seqlens, tile_info, n_tiles, hq, hkv,
                                  scale, total, dq, err, (cudaStream_t)stream);
-  attn_bwd_dq_kernel<<<dim3((unsigned)n_tiles, (unsigned)hq), 128, DQ_SMEM, (cudaStream_t)stream>>>(p);
-  return qb_launch_status();
+  return qb_launch(attn_bwd_dq_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hq)), dim3(128), DQ_SMEM, (cudaStream_t)stream, 1, p);
 }

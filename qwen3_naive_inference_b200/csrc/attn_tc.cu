@@ -63,6 +63,7 @@ struct AttnTcParams {
 __global__ void __launch_bounds__(AT_THREADS, 2)
 attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                    const __grid_constant__ CUtensorMap tv, AttnTcParams p) {
+  qb_pdl_wait();  // metadata and operands may come from the kernel before; also before any exit
   extern __shared__ uint8_t smem_raw[];
   const int tile = blockIdx.x, kvh = blockIdx.y;
   const int b = p.tiles ? p.tiles[2 * tile] : tile / p.tiles_per_seq;
@@ -123,6 +124,7 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
 
   if (warp == 0 && lane < 2) {
     // ------------------------------------------------------------ TMA producers
@@ -349,8 +351,7 @@ int attn_fwd_tc_launch(const void* q, int64_t q_stride, const void* k, const voi
   AttnTcParams p{cu_seqlens, tile_info, tiles_per_seq, hq, hkv, scale * 1.4426950408889634f,
                  (bf16*)out, o_stride, lse, total_q, err};
   (void)batch;
-  attn_fwd_tc_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), AT_THREADS, AT_SMEM, st>>>(tq, tk, tv, p);
-  return qb_launch_status();
+  return qb_launch(attn_fwd_tc_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(AT_THREADS), AT_SMEM, st, 1, tq, tk, tv, p);
 }
 
 namespace {
@@ -407,6 +408,7 @@ __global__ void __launch_bounds__(BT_THREADS, 1)
 attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                         AttnBwdTcParams p) {
+  qb_pdl_wait();  // metadata and operands may come from the kernel before; also before any exit
   extern __shared__ uint8_t smem_raw[];
   const int tile = blockIdx.x, kvh = blockIdx.y;
   const int b = p.tiles[2 * tile], k_start = p.tiles[2 * tile + 1];
@@ -455,6 +457,7 @@ attn_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -661,8 +664,7 @@ int attn_bwd_dkdv_tc_launch(const void* q, const void* k, const void* v, int64_t
   }
   AttnBwdTcParams p{cu_seqlens, tile_info, hq, hkv, scale, scale * 1.4426950408889634f, lse, delta, total,
                     (bf16*)dk, (bf16*)dv, stride, err};
-  attn_bwd_dkdv_tc_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), BT_THREADS, BT_SMEM, st>>>(tq, tk, tv, tdo, p);
-  return qb_launch_status();
+  return qb_launch(attn_bwd_dkdv_tc_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(BT_THREADS), BT_SMEM, st, 1, tq, tk, tv, tdo, p);
 }
 
 namespace {
@@ -684,6 +686,7 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
 attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                       AttnBwdTcParams p, bf16* dq) {
+  qb_pdl_wait();  // metadata and operands may come from the kernel before; also before any exit
   extern __shared__ uint8_t smem_raw[];
   const int tile = blockIdx.x, kvh = blockIdx.y;
   const int b = p.tiles[2 * tile], q_start = p.tiles[2 * tile + 1];
@@ -735,6 +738,7 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
 
   if (warp == 0 && lane < 2) {
     // ------------------------------------------------------------ TMA producers: lane 0 Q, dO and K; lane 1 V
@@ -900,7 +904,6 @@ int attn_bwd_dq_tc_launch(const void* q, const void* k, const void* v, int64_t s
   }
   AttnBwdTcParams p{cu_seqlens, tile_info, hq, hkv, scale, scale * 1.4426950408889634f, lse, delta, total,
                     nullptr, nullptr, stride, err};
-  attn_bwd_dq_tc_kernel<<<dim3((unsigned)n_tiles, (unsigned)hkv), DQ_THREADS, DQ_SMEM_TC, st>>>(tq, tk, tv, tdo, p,
-                                                                                               (bf16*)dq);
-  return qb_launch_status();
+  return qb_launch(attn_bwd_dq_tc_kernel, dim3((unsigned)n_tiles, (unsigned)hkv), dim3(DQ_THREADS), DQ_SMEM_TC, st, 1,
+                   tq, tk, tv, tdo, p, (bf16*)dq);
 }

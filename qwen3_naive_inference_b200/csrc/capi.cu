@@ -1,5 +1,20 @@
-// Library-wide entry points of the C ABI: version and status strings.
+// Library-wide entry points of the C ABI: version and status strings, the launch switch.
+#include <atomic>
+
 #include "common.cuh"
+
+namespace {
+std::atomic<int> g_pdl{1};
+}  // namespace
+
+bool qb_pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
+extern "C" int qb_set_pdl(int on) {
+  g_pdl.store(on ? 1 : 0, std::memory_order_relaxed);
+  return QB_OK;
+}
+
+extern "C" int qb_get_pdl(void) { return g_pdl.load(std::memory_order_relaxed); }
 
 extern "C" int qb_abi_version(void) { return 2; }
 

@@ -24,6 +24,55 @@ static inline int qb_launch_status() {
   return e == cudaSuccess ? QB_OK : (QB_ERR_CUDA_BASE + (int)e);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialization (when the library-wide switch is on):
+// a kernel may be scheduled as soon as every CTA of the kernel before it in the stream has passed
+// qb_pdl_trigger(), so its launch and prologue (barrier init, TMEM allocation, tensor-map
+// prefetch) overlap that kernel's tail; qb_pdl_wait() then blocks until the kernel before has
+// completed and its writes are visible.  Both are no-ops in a kernel launched without the
+// attribute.  Rules every kernel launched through qb_launch follows:
+//   * every thread calls qb_pdl_wait() before its first global access that depends on earlier
+//     work (any read of an input another kernel may have written, and every global write), and
+//     before it exits -- a kernel that could complete without waiting would let the kernel after
+//     it pass its own wait while the kernel before is still running;
+//   * a kernel that allocates TMEM calls qb_pdl_trigger() only after its allocation succeeded,
+//     so the next kernel never holds TMEM this one still needs.
+QB_DEVICE void qb_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QB_DEVICE void qb_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Library-wide switch (qb_set_pdl in the C ABI); on by default.
+bool qb_pdl_enabled();
+
+// Launch `kern` on `st` with a cluster of `cluster_x` CTAs (1: none) and, when the switch is on,
+// programmatic stream serialization.  Returns the launch status like qb_launch_status().
+template <typename... KArgs, typename... Args>
+static inline int qb_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  unsigned n = 0;
+  if (cluster_x > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = (unsigned)cluster_x;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (qb_pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  (void)cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  return qb_launch_status();  // the launch's own error (consumed here: callers return this value)
+}
+
 #define QB_CHECK_ARG(cond)            \
   do {                                \
     if (!(cond)) return QB_ERR_INVALID; \

@@ -209,6 +209,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
+  qb_pdl_wait();     // operands and C may come from the kernel before
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -305,11 +307,12 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 // tcgen05.mma.cta_group::2 (M = 256, N = PBN) reading both CTAs' stages; each CTA's TMEM receives
 // its 128 rows of the accumulator (double-buffered).  Each SM pulls (128 + PBN/2) rows of operands
 // per K block for a 128 x PBN share of the product, against (128 + PBN) rows for the same share
-// on one CTA: 256-wide tiles for products that fill every SM pair, 192 / 128-wide ones for the
-// decode step's skinny products (M = 512), whose time is the operands' trip from L2.  The
-// leader's commits release both CTAs' stages and accumulators (one commit per CTA's barrier);
-// each CTA's epilogue drains its own TMEM rows and tells the leader through a remote arrive.
-// Every wait is bounded; each CTA loads from this GPU's memory only.
+// on one CTA.  The dispatcher uses PBN = 256, for products that fill every SM pair; the narrower
+// tiles pull fewer bytes per SM but measured slower on the decode step's M = 512 products, whose
+// time is latency rather than operand traffic.  The leader's commits release both CTAs' stages
+// and accumulators (one commit per CTA's barrier); each CTA's epilogue drains its own TMEM rows
+// and tells the leader through a remote arrive.  Every wait is bounded; each CTA loads from this
+// GPU's memory only.
 constexpr int P_HALF_BYTES = 128 * BK * 2;  // 16 KB: 128 rows x 64 K of A (this CTA's rows)
 
 template <int PBN>
@@ -441,6 +444,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   cluster_sync();  // barriers and TMEM of both CTAs exist before either uses the other's
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
+  qb_pdl_wait();     // operands and C may come from the kernel before
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer (each CTA)
@@ -640,6 +645,8 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   cluster_sync();  // every CTA's receive barrier exists before any CTA pushes into it
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
+  qb_pdl_wait();     // operands and C may come from the kernel before
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -778,8 +785,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStrea
   }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, THREADS, Cfg::SMEM, st>>>(ta, tb, p);
-  return qb_launch_status();
+  return qb_launch(kern, dim3(grid), dim3(THREADS), Cfg::SMEM, st, 1, ta, tb, p);
 }
 
 template <int MODE, bool A_MN, bool B_MN, int PBN>
@@ -794,20 +800,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cuda
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
   const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * pairs));
-  cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = SMEM;
-  cfg.stream = st;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeClusterDimension;
-  attrs[0].val.clusterDim.x = 2;
-  attrs[0].val.clusterDim.y = 1;
-  attrs[0].val.clusterDim.z = 1;
-  cfg.attrs = attrs;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return qb_launch_status();
-  return qb_launch_status();
+  return qb_launch(kern, dim3((unsigned)(2 * pairs)), dim3(THREADS), SMEM, st, 2, ta, tb, p);
 }
 
 template <int S, int MODE, bool A_MN, bool B_MN>
@@ -819,20 +812,8 @@ int launch_split(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cud
       return qb_launch_status();
     attr = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.tiles_m * p.tiles_n * S));
-  cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = SplitCfg<S>::SMEM;
-  cfg.stream = st;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeClusterDimension;
-  attrs[0].val.clusterDim.x = S;
-  attrs[0].val.clusterDim.y = 1;
-  attrs[0].val.clusterDim.z = 1;
-  cfg.attrs = attrs;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return qb_launch_status();
-  return qb_launch_status();
+  return qb_launch(kern, dim3((unsigned)(p.tiles_m * p.tiles_n * S)), dim3(THREADS), SplitCfg<S>::SMEM, st, S, ta,
+                   tb, p);
 }
 
 template <int S, bool A_MN, bool B_MN>
@@ -889,10 +870,7 @@ int launch_pair_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, Gem
 template <bool A_MN, bool B_MN>
 int launch_pair_pbn(int pbn, int mode, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p,
                     cudaStream_t st) {
-  if (pbn == 128) return launch_pair_mode<A_MN, B_MN, 128>(mode, ta, tb, p, st);
-  if constexpr (!B_MN) {  // an MN-major B loads whole 64-wide atoms: 96 rows a CTA do not split
-    if (pbn == 192) return launch_pair_mode<A_MN, B_MN, 192>(mode, ta, tb, p, st);
-  }
+  (void)pbn;  // plan_gemm only picks 256-wide pair tiles
   return launch_pair_mode<A_MN, B_MN, 256>(mode, ta, tb, p, st);
 }
 
@@ -914,10 +892,9 @@ inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) =
 
 // The layout of one product.  256x256 tiles on CTA pairs when they fill every SM pair at least
 // once; 128 x 256 single-CTA tiles when they cover every SM at least once.  Otherwise every
-// candidate is costed by the operand bytes its busiest SM pulls through L2 (the bound of these
-// one-wave products): 128 x {128, 192} single-CTA tiles in waves over the SMs, 256 x {128, 192}
-// tiles on CTA pairs in waves over the SM pairs, or 128 x 128 tiles split along K over a cluster
-// of 2 or 4 CTAs (one wave, plus the partials' exchange, costed as two K blocks).
+// candidate is costed by the operand bytes its busiest SM pulls: 128 x {128, 192} single-CTA
+// tiles in waves over the SMs, or 128 x 128 tiles split along K over a cluster of 2 or 4 CTAs
+// (one wave, plus the partials' exchange, costed as two K blocks).
 struct GemmPlan {
   bool pair;
   int bn;     // tile width (N): of the pair's 256-row tile, or of the single CTA's 128-row tile
@@ -935,14 +912,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
   int64_t best = (t128 + sms - 1) / sms * kblocks * kb_bytes;
   const int64_t c192 = (t192 + sms - 1) / sms * kblocks * (int64_t)(BM + 192) * BK * 2;
   if (N > 128 && c192 < best) { best = c192; best_plan = {false, 192, 1}; }
-  if (M > 128) {
-    for (int cand = 128; cand <= 192; cand += 64) {
-      if (cand == 192 && (b_mn || N <= 128)) continue;  // an MN-major B splits into 64-wide atoms only
-      const int64_t pairs = ((M + 255) / 256) * ((N + cand - 1) / cand);
-      const int64_t c = (pairs + sms / 2 - 1) / (sms / 2) * kblocks * (int64_t)(128 + cand / 2) * BK * 2;
-      if (c < best) { best = c; best_plan = {true, cand, 1}; }
-    }
-  }
+  (void)b_mn;  // 256 x {128, 192} pair tiles pull fewer bytes per SM but measured slower at M = 512
   for (int S = 2; S <= 4; S *= 2) {
     if (kblocks < 2 * S || t128 > split_clusters(S)) continue;
     const int64_t c = (kblocks + S - 1) / S * kb_bytes + 2 * kb_bytes;
@@ -999,6 +969,8 @@ __global__ void __launch_bounds__(128)
 lse_combine_kernel(const float2* __restrict__ part, int n_part, const float* __restrict__ tgt_logit,
                    const int64_t* __restrict__ targets, const int64_t* __restrict__ dest, int64_t n, int64_t V,
                    float* __restrict__ logp, float* __restrict__ lse, int* err) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   constexpr float LN2 = 0.6931471805599453f;
   const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -1057,9 +1029,8 @@ int lm_head_logprob(const void* h, int64_t ldh, const void* W, int64_t ldw, int6
                     : (bn == 256 ? launch<256, 4, 3, false, false>(ta, tb, p, st)
                                  : launch<128, 6, 3, false, false>(ta, tb, p, st));
   if (status != QB_OK) return status;
-  lse_combine_kernel<<<(unsigned)((n + 3) / 4), 128, 0, st>>>(part, n_part, tgt, targets, dest, n, V, logp, lse,
-                                                              err);
-  return qb_launch_status();
+  return qb_launch(lse_combine_kernel, dim3((unsigned)((n + 3) / 4)), dim3(128), 0, st, 1, part, n_part, tgt, targets,
+                   dest, n, V, logp, lse, err);
 }
 
 }  // namespace

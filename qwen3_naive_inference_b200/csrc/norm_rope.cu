@@ -24,6 +24,14 @@ QB_DEVICE void load8(const bf16* p, float (&v)[8]) {
     v[2 * i + 1] = f.y;
   }
 }
+QB_DEVICE void unpack8(const bf16x8& r, float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16x2(r.u[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
 QB_DEVICE void store8(bf16* p, const float (&v)[8]) {
   bf16x8 r;
 #pragma unroll
@@ -35,6 +43,8 @@ QB_DEVICE void store8(bf16* p, const float (&v)[8]) {
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, int64_t n,
                                      const bf16* __restrict__ table, int64_t vocab,
                                      int64_t hidden, bf16* __restrict__ out, int* err) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= n) return;
   const int lane = threadIdx.x & 31;
@@ -53,6 +63,8 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, int64_t n,
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, int64_t n,
                                      const bf16* __restrict__ dout, int64_t vocab, int64_t hidden,
                                      float* __restrict__ dtable, int* err) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= n) return;
   const int lane = threadIdx.x & 31;
@@ -77,6 +89,8 @@ template <int NV>
 __global__ void rmsnorm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                    bf16* __restrict__ y, float* __restrict__ rstd_out,
                                    int64_t rows, float eps) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   constexpr int COLS = NV * 256;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -106,6 +120,8 @@ template <int NV>
 __global__ void add_rmsnorm_fwd_kernel(const bf16* __restrict__ x, bf16* __restrict__ res,
                                        const bf16* __restrict__ w, bf16* __restrict__ y,
                                        int64_t rows, float eps) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   constexpr int COLS = NV * 256;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -138,57 +154,82 @@ __global__ void add_rmsnorm_fwd_kernel(const bf16* __restrict__ x, bf16* __restr
 }
 
 // dx = rstd * (dy*w - xhat * mean(dy*w*xhat)),  dw += sum_rows(dy * xhat).
-// Grid-strided over rows; each warp keeps its dw partial in registers, the
-// block folds warps in shared memory and issues one atomicAdd per column.
+// Grid-strided over rows, one warp a row, 128-thread blocks, four blocks per SM: the weight row
+// and each warp's dw partial sit in shared memory (a lane owns its columns, so no atomics there)
+// and a row's x and dy stay packed bf16 until used.  The block folds its warps' partials and
+// issues one 16-byte atomic add per four columns.
+constexpr int RMSB_WARPS = 4;
 template <int NV>
-__global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
-                                   const bf16* __restrict__ w, const float* __restrict__ rstd,
-                                   bf16* __restrict__ dx, float* __restrict__ dw, int64_t rows) {
+__global__ void __launch_bounds__(RMSB_WARPS * 32, 3)
+rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
+                   const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw, int64_t rows) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   constexpr int COLS = NV * 256;
-  extern __shared__ float dw_smem[];  // [COLS]
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int c = threadIdx.x; c < COLS; c += blockDim.x) dw_smem[c] = 0.f;
-  float wv[NV][8];
-  float dwp[NV][8];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    load8(w + j * 256 + lane * 8, wv[j]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) dwp[j][i] = 0.f;
-  }
+  extern __shared__ float rms_smem[];  // w [COLS] then one dw partial [COLS] per warp
+  float* w_s = rms_smem;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* dw_w = rms_smem + COLS * (1 + wid);
+  for (int c = threadIdx.x; c < COLS; c += blockDim.x) w_s[c] = bf2f(w[c]);
+  for (int c = lane; c < COLS; c += 32) dw_w[c] = 0.f;
   __syncthreads();
-  for (int64_t row = (int64_t)blockIdx.x * nw + wid; row < rows; row += (int64_t)gridDim.x * nw) {
-    const float rs = rstd[row];
-    float xh[NV][8], g[NV][8];
-    float dot = 0.f;
+  for (int64_t row = (int64_t)blockIdx.x * RMSB_WARPS + wid; row < rows; row += (int64_t)gridDim.x * RMSB_WARPS) {
+    bf16x8 xr[NV], gr[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int64_t off = row * COLS + j * 256 + lane * 8;
-      load8(x + off, xh[j]);
-      load8(dy + off, g[j]);
+      xr[j] = *reinterpret_cast<const bf16x8*>(x + off);
+      gr[j] = *reinterpret_cast<const bf16x8*>(dy + off);
+    }
+    const float rs = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      float xv[8], g[8];
+      unpack8(xr[j], xv);
+      unpack8(gr[j], g);
+      float4* dp = reinterpret_cast<float4*>(dw_w + j * 256 + lane * 8);
+      const float4* wp = reinterpret_cast<const float4*>(w_s + j * 256 + lane * 8);
+      float4 d0 = dp[0], d1 = dp[1];
+      const float4 w0 = wp[0], w1 = wp[1];
+      float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        xh[j][i] *= rs;
-        dwp[j][i] += g[j][i] * xh[j][i];
-        g[j][i] *= wv[j][i];
-        dot += g[j][i] * xh[j][i];
+        const float xh = xv[i] * rs;
+        dv[i] += g[i] * xh;
+        dot += (g[i] * wv[i]) * xh;
       }
+      dp[0] = make_float4(dv[0], dv[1], dv[2], dv[3]);
+      dp[1] = make_float4(dv[4], dv[5], dv[6], dv[7]);
     }
     dot = warp_sum(dot) / (float)COLS;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      float o[8];
+      float xv[8], g[8], o[8];
+      unpack8(xr[j], xv);
+      unpack8(gr[j], g);
+      const float4* wp = reinterpret_cast<const float4*>(w_s + j * 256 + lane * 8);
+      const float4 w0 = wp[0], w1 = wp[1];
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = rs * (g[j][i] - xh[j][i] * dot);
+      for (int i = 0; i < 8; ++i) o[i] = rs * (g[i] * wv[i] - (xv[i] * rs) * dot);
       store8(dx + row * COLS + j * 256 + lane * 8, o);
     }
   }
-#pragma unroll
-  for (int j = 0; j < NV; ++j)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) atomicAdd(&dw_smem[j * 256 + lane * 8 + i], dwp[j][i]);
   __syncthreads();
-  for (int c = threadIdx.x; c < COLS; c += blockDim.x) atomicAdd(dw + c, dw_smem[c]);
+  for (int c = threadIdx.x * 4; c < COLS; c += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < RMSB_WARPS; ++k) {
+      const float4 v = *reinterpret_cast<const float4*>(rms_smem + COLS * (1 + k) + c);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    atomicAdd(reinterpret_cast<float4*>(dw + c), acc);
+  }
 }
 
 // ---------------------------------------------------------------- QK-Norm + RoPE
@@ -233,6 +274,8 @@ struct QkNormRopeParams {
 // Grid: (T, ceil((hq + 2*hkv) / warps_per_block)).  Heads [0,hq) are q, [hq, hq+hkv)
 // k, [hq+hkv, hq+2hkv) v.
 __global__ void qk_norm_rope_fwd_kernel(QkNormRopeParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t t = blockIdx.x;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -307,14 +350,6 @@ QB_DEVICE float half_warp_sum(float v) {
 }
 QB_DEVICE bf16x8 ld_row8(const bf16* p) { return *reinterpret_cast<const bf16x8*>(p); }
 QB_DEVICE void st_row8(bf16* p, const bf16x8& r) { *reinterpret_cast<bf16x8*>(p) = r; }
-QB_DEVICE void unpack8(const bf16x8& r, float (&v)[8]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = unpack_bf16x2(r.u[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
 // cos and sin of the eight rotation-table columns jj..jj+7 of one position
 QB_DEVICE void load_rot8(const float* cos_sin, int64_t pos, int jj, float (&cv)[8], float (&sv)[8]) {
   const float4* cs4 = reinterpret_cast<const float4*>(cos_sin + pos * HD + jj);
@@ -326,6 +361,8 @@ QB_DEVICE void load_rot8(const float* cos_sin, int64_t pos, int jj, float (&cv)[
 
 __global__ void __launch_bounds__(128, 8)
 qk_norm_rope_fwd8_kernel(QkNormRopeParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t t = blockIdx.x;
   const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int nheads = p.hq + 2 * p.hkv;
@@ -416,6 +453,8 @@ struct QkNormRopeBwdParams {
 // pairs; norm-weight grads are folded in shared memory, one atomic per column per block.
 constexpr int QKB_TOK = 16;
 __global__ void qk_norm_rope_bwd_kernel(QkNormRopeBwdParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ float dqw_s[HD], dkw_s[HD];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int c = threadIdx.x; c < HD; c += blockDim.x) { dqw_s[c] = 0.f; dkw_s[c] = 0.f; }
@@ -501,6 +540,8 @@ __global__ void qk_norm_rope_bwd_kernel(QkNormRopeBwdParams p) {
 constexpr int QKB8_BLOCKS_PER_SM = 4;
 __global__ void __launch_bounds__(128, QKB8_BLOCKS_PER_SM)
 qk_norm_rope_bwd8_kernel(QkNormRopeBwdParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ float dqw_s[HD], dkw_s[HD];
   const int hw = threadIdx.x >> 4, l = threadIdx.x & 15;
   for (int c = threadIdx.x; c < HD; c += blockDim.x) {
@@ -607,6 +648,8 @@ QB_DEVICE float silu_f(float g) { return g / (1.0f + expf(-g)); }
 constexpr int SILU_MAXV = 3;
 __global__ void __launch_bounds__(128, 8)
 silu_mul_fwd_kernel(const bf16* __restrict__ gu, int64_t T, int64_t I, bf16* __restrict__ out) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t row = blockIdx.x;
   const bf16* g_row = gu + row * 2 * I;
   const bf16* u_row = g_row + I;
@@ -638,6 +681,8 @@ silu_mul_fwd_kernel(const bf16* __restrict__ gu, int64_t T, int64_t I, bf16* __r
 __global__ void __launch_bounds__(128, 5)
 silu_mul_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ gu, int64_t T, int64_t I,
                     bf16* __restrict__ dgu) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t row = blockIdx.x;
   const bf16* g_row = gu + row * 2 * I;
   const bf16* u_row = g_row + I;
@@ -674,6 +719,8 @@ silu_mul_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ gu, 
 
 __global__ void add_bf16_kernel(const bf16* __restrict__ a, const bf16* __restrict__ b,
                                 bf16* __restrict__ out, int64_t n) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t nvec = n / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -692,11 +739,15 @@ __global__ void add_bf16_kernel(const bf16* __restrict__ a, const bf16* __restri
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restrict__ dst, int64_t n) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     dst[i] = f2bf(src[i]);
 }
 __global__ void accumulate_bf16_kernel(const bf16* __restrict__ src, float* __restrict__ acc, int64_t n) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     acc[i] += bf2f(src[i]);
@@ -721,9 +772,7 @@ extern "C" int qb_embedding_fwd(const int64_t* ids, int64_t n, const void* table
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(ids && table && out && aligned16(table) && aligned16(out));
   const int wpb = 8;
-  embedding_fwd_kernel<<<(unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
-      ids, n, (const bf16*)table, vocab, hidden, (bf16*)out, err);
-  return qb_launch_status();
+  return qb_launch(embedding_fwd_kernel, dim3((unsigned)((n + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, ids, n, (const bf16*)table, vocab, hidden, (bf16*)out, err);
 }
 
 extern "C" int qb_embedding_bwd(const int64_t* ids, int64_t n, const void* dout, int64_t vocab,
@@ -732,9 +781,7 @@ extern "C" int qb_embedding_bwd(const int64_t* ids, int64_t n, const void* dout,
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(ids && dout && dtable && aligned16(dout));
   const int wpb = 8;
-  embedding_bwd_kernel<<<(unsigned)((n + wpb - 1) / wpb), wpb * 32, 0, (cudaStream_t)stream>>>(
-      ids, n, (const bf16*)dout, vocab, hidden, dtable, err);
-  return qb_launch_status();
+  return qb_launch(embedding_bwd_kernel, dim3((unsigned)((n + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, ids, n, (const bf16*)dout, vocab, hidden, dtable, err);
 }
 
 #define QB_NV_DISPATCH(cols, KERNEL_CALL)  \
@@ -753,9 +800,9 @@ extern "C" int qb_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd
   QB_CHECK_ARG(x && w && y && aligned16(x) && aligned16(w) && aligned16(y));
   const int wpb = 8;
   const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
-  QB_NV_DISPATCH(cols, (rmsnorm_fwd_kernel<NV><<<grid, wpb * 32, 0, (cudaStream_t)stream>>>(
-                           (const bf16*)x, (const bf16*)w, (bf16*)y, rstd, rows, eps)));
-  return qb_launch_status();
+  int st = QB_OK;
+  QB_NV_DISPATCH(cols, (st = qb_launch(rmsnorm_fwd_kernel<NV>, dim3(grid), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, (const bf16*)x, (const bf16*)w, (bf16*)y, rstd, rows, eps)));
+  return st;
 }
 
 extern "C" int qb_add_rmsnorm_fwd(const void* x, void* residual, const void* w, void* y,
@@ -766,9 +813,9 @@ extern "C" int qb_add_rmsnorm_fwd(const void* x, void* residual, const void* w, 
                aligned16(y));
   const int wpb = 8;
   const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
-  QB_NV_DISPATCH(cols, (add_rmsnorm_fwd_kernel<NV><<<grid, wpb * 32, 0, (cudaStream_t)stream>>>(
-                           (const bf16*)x, (bf16*)residual, (const bf16*)w, (bf16*)y, rows, eps)));
-  return qb_launch_status();
+  int st = QB_OK;
+  QB_NV_DISPATCH(cols, (st = qb_launch(add_rmsnorm_fwd_kernel<NV>, dim3(grid), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, (const bf16*)x, (bf16*)residual, (const bf16*)w, (bf16*)y, rows, eps)));
+  return st;
 }
 
 extern "C" int qb_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd,
@@ -777,14 +824,14 @@ extern "C" int qb_rmsnorm_bwd(const void* dy, const void* x, const void* w, cons
   if (rows == 0) return QB_OK;
   QB_CHECK_ARG(dy && x && w && rstd && dx && dw && aligned16(dy) && aligned16(x) &&
                aligned16(w) && aligned16(dx));
-  const int wpb = 8;
-  int64_t g = (rows + wpb - 1) / wpb;
-  if (g > 148 * 4) g = 148 * 4;
-  const size_t smem = (size_t)cols * sizeof(float);
-  QB_NV_DISPATCH(cols, (rmsnorm_bwd_kernel<NV><<<(unsigned)g, wpb * 32, smem, (cudaStream_t)stream>>>(
-                           (const bf16*)dy, (const bf16*)x, (const bf16*)w, rstd, (bf16*)dx, dw,
+  QB_CHECK_ARG((reinterpret_cast<uintptr_t>(dw) & 15) == 0);  // 16-byte atomic adds
+  int64_t g = (rows + RMSB_WARPS - 1) / RMSB_WARPS;
+  if (g > 148 * 3) g = 148 * 3;  // one wave of resident blocks; warps stride over the rows
+  const size_t smem = (1 + RMSB_WARPS) * (size_t)cols * sizeof(float);
+  int st = QB_OK;
+  QB_NV_DISPATCH(cols, (st = qb_launch(rmsnorm_bwd_kernel<NV>, dim3((unsigned)g), dim3(RMSB_WARPS * 32), smem, (cudaStream_t)stream, 1, (const bf16*)dy, (const bf16*)x, (const bf16*)w, rstd, (bf16*)dx, dw,
                            rows)));
-  return qb_launch_status();
+  return st;
 }
 
 extern "C" int qb_qk_norm_rope_fwd(const void* qkv, int64_t T, int64_t ld_in, int hq, int hkv,
@@ -810,13 +857,11 @@ extern "C" int qb_qk_norm_rope_fwd(const void* qkv, int64_t T, int64_t ld_in, in
                      (q_out == nullptr || aligned16(q_out)) && (k_cache == nullptr || (aligned16(k_cache) &&
                      aligned16(v_cache))) && aligned16(q_norm_w) && aligned16(k_norm_w) && aligned16(cos_sin);
   if (vec16) {  // 16-byte accesses, one token per block
-    qk_norm_rope_fwd8_kernel<<<(unsigned)T, 128, 0, (cudaStream_t)stream>>>(p);
-    return qb_launch_status();
+    return qb_launch(qk_norm_rope_fwd8_kernel, dim3((unsigned)T), dim3(128), 0, (cudaStream_t)stream, 1, p);
   }
   const int wpb = 8;
   dim3 grid((unsigned)T, (unsigned)((hq + 2 * hkv + wpb - 1) / wpb));
-  qk_norm_rope_fwd_kernel<<<grid, wpb * 32, 0, (cudaStream_t)stream>>>(p);
-  return qb_launch_status();
+  return qb_launch(qk_norm_rope_fwd_kernel, dim3(grid), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, p);
 }
 
 extern "C" int qb_qk_norm_rope_bwd(const void* dout, const void* qkv, int64_t T, int64_t ld,
@@ -840,12 +885,10 @@ extern "C" int qb_qk_norm_rope_bwd(const void* dout, const void* qkv, int64_t T,
   if (vec16 && q_norm_w && k_norm_w) {
     const int64_t cap = 148 * QKB8_BLOCKS_PER_SM;  // one wave of resident blocks; the kernel strides over tokens
     const int64_t g8 = T < cap ? T : cap;
-    qk_norm_rope_bwd8_kernel<<<(unsigned)g8, 128, 0, (cudaStream_t)stream>>>(p);
-    return qb_launch_status();
+    return qb_launch(qk_norm_rope_bwd8_kernel, dim3((unsigned)g8), dim3(128), 0, (cudaStream_t)stream, 1, p);
   }
   QB_CHECK_ARG(dout != dqkv);  // the warp kernel does not handle aliasing
-  qk_norm_rope_bwd_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(p);
-  return qb_launch_status();
+  return qb_launch(qk_norm_rope_bwd_kernel, dim3(grid), dim3(256), 0, (cudaStream_t)stream, 1, p);
 }
 
 extern "C" int qb_silu_mul_fwd(const void* gate_up, int64_t T, int64_t I, void* out,
@@ -853,9 +896,7 @@ extern "C" int qb_silu_mul_fwd(const void* gate_up, int64_t T, int64_t I, void* 
   QB_CHECK_ARG(T >= 0 && T < (int64_t)1 << 31 && I > 0 && I % 8 == 0);
   if (T == 0) return QB_OK;
   QB_CHECK_ARG(gate_up && out && aligned16(gate_up) && aligned16(out));
-  silu_mul_fwd_kernel<<<(unsigned)T, 128, 0, (cudaStream_t)stream>>>(
-      (const bf16*)gate_up, T, I, (bf16*)out);
-  return qb_launch_status();
+  return qb_launch(silu_mul_fwd_kernel, dim3((unsigned)T), dim3(128), 0, (cudaStream_t)stream, 1, (const bf16*)gate_up, T, I, (bf16*)out);
 }
 
 extern "C" int qb_silu_mul_bwd(const void* dout, const void* gate_up, int64_t T, int64_t I,
@@ -864,32 +905,26 @@ extern "C" int qb_silu_mul_bwd(const void* dout, const void* gate_up, int64_t T,
   if (T == 0) return QB_OK;
   QB_CHECK_ARG(dout && gate_up && dgate_up && aligned16(dout) && aligned16(gate_up) &&
                aligned16(dgate_up));
-  silu_mul_bwd_kernel<<<(unsigned)T, 128, 0, (cudaStream_t)stream>>>(
-      (const bf16*)dout, (const bf16*)gate_up, T, I, (bf16*)dgate_up);
-  return qb_launch_status();
+  return qb_launch(silu_mul_bwd_kernel, dim3((unsigned)T), dim3(128), 0, (cudaStream_t)stream, 1, (const bf16*)dout, (const bf16*)gate_up, T, I, (bf16*)dgate_up);
 }
 
 extern "C" int qb_add_bf16(const void* a, const void* b, void* out, int64_t n, qb_stream_t stream) {
   QB_CHECK_ARG(n >= 0);
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(a && b && out && aligned16(a) && aligned16(b) && aligned16(out));
-  add_bf16_kernel<<<grid_for(n / 8 + 1, 256), 256, 0, (cudaStream_t)stream>>>(
-      (const bf16*)a, (const bf16*)b, (bf16*)out, n);
-  return qb_launch_status();
+  return qb_launch(add_bf16_kernel, dim3(grid_for(n / 8 + 1, 256)), dim3(256), 0, (cudaStream_t)stream, 1, (const bf16*)a, (const bf16*)b, (bf16*)out, n);
 }
 
 extern "C" int qb_f32_to_bf16(const float* src, void* dst, int64_t n, qb_stream_t stream) {
   QB_CHECK_ARG(n >= 0);
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(src && dst);
-  f32_to_bf16_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(src, (bf16*)dst, n);
-  return qb_launch_status();
+  return qb_launch(f32_to_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, (cudaStream_t)stream, 1, src, (bf16*)dst, n);
 }
 
 extern "C" int qb_accumulate_bf16(const void* src, float* acc, int64_t n, qb_stream_t stream) {
   QB_CHECK_ARG(n >= 0);
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(src && acc);
-  accumulate_bf16_kernel<<<grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>((const bf16*)src, acc, n);
-  return qb_launch_status();
+  return qb_launch(accumulate_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, (cudaStream_t)stream, 1, (const bf16*)src, acc, n);
 }

@@ -250,6 +250,8 @@ struct SampleParams {
 };
 
 __global__ void __launch_bounds__(SNT, 4) sample_kernel(SampleParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ MS sh_ms[32];
   __shared__ AM sh_am[32];
   __shared__ int hist[256];
@@ -473,6 +475,8 @@ constexpr int LNT = 256;
 __global__ void __launch_bounds__(LNT)
 logprob_fwd_kernel(const bf16* __restrict__ logits, int64_t V, int64_t ld, const int64_t* __restrict__ targets,
                    const int64_t* __restrict__ dest, float* __restrict__ logp, float* __restrict__ lse, int* err) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ MS sh[32];
   const int64_t row = blockIdx.x;
   const bf16* lrow = logits + row * ld;
@@ -510,6 +514,8 @@ logprob_fwd_kernel(const bf16* __restrict__ logits, int64_t V, int64_t ld, const
 __global__ void __launch_bounds__(LNT)
 logprob_bwd_kernel(bf16* __restrict__ logits, int64_t V, int64_t ld, const int64_t* __restrict__ targets,
                    const int64_t* __restrict__ dest, const float* __restrict__ lse, const float* __restrict__ gl) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   const int64_t row = blockIdx.x;
   bf16* lrow = logits + row * ld;
   const int64_t d = dest ? dest[row] : row;
@@ -541,6 +547,8 @@ constexpr int MS_BLOCKS = 256;
 
 __global__ void mask_sum_kernel(const float* __restrict__ mask, int64_t n, float* __restrict__ out,
                                 uint32_t* __restrict__ ws) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ float red[32];
   __shared__ bool last;
   float s = 0.f;
@@ -588,6 +596,8 @@ QB_DEVICE float group_advantage(const float* rewards, const int64_t* gids, int64
 
 __global__ void advantage_kernel(const float* __restrict__ rewards, const int64_t* __restrict__ gids, int64_t n,
                                  float* __restrict__ adv) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
   const float a = group_advantage(rewards, gids, n, r, red);
@@ -650,6 +660,8 @@ struct LossParams {
 // to ppo_clipped_loss (:184-199).
 template <bool FROM_REWARDS>
 __global__ void grpo_loss_kernel(LossParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ float red[32];
   __shared__ bool last;
   const int64_t r = p.row_begin + blockIdx.x;
@@ -737,6 +749,8 @@ QB_DEVICE void ll_merge(float& m2, float& s, float om2, float os) {
 
 __global__ void __launch_bounds__(LL_THREADS)
 logit_loss_kernel(LogitLossParams p) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   constexpr float L2E = 1.4426950408889634f, LN2 = 0.6931471805599453f;
   extern __shared__ __align__(128) uint8_t ll_smem[];
   __shared__ float red[2][LL_THREADS / 32];
@@ -881,6 +895,8 @@ logit_loss_kernel(LogitLossParams p) {
 // loss_out (+=) from the per-token terms, summed in a fixed order.
 __global__ void logit_loss_reduce_kernel(const float* __restrict__ row_part, int64_t n_rows,
                                          const float* __restrict__ mask_total, float beta, float* loss_out) {
+  qb_pdl_trigger();
+  qb_pdl_wait();
   __shared__ float red[32];
   float su = 0.f, kl = 0.f;
   for (int64_t i = threadIdx.x; i < n_rows; i += blockDim.x) {
@@ -910,8 +926,7 @@ extern "C" int qb_sample(const void* logits, int64_t n, int64_t V, int64_t ld, f
   QB_CHECK_ARG(logits && tokens && logp && al16(logits) && ld % 8 == 0);
   if (V % 8 != 0) return QB_ERR_UNSUPPORTED;
   SampleParams p{(const bf16*)logits, V, ld, temperature, top_k, seed, offset, tokens, logp, err};
-  sample_kernel<<<(unsigned)n, SNT, 0, (cudaStream_t)stream>>>(p);
-  return qb_launch_status();
+  return qb_launch(sample_kernel, dim3((unsigned)n), dim3(SNT), 0, (cudaStream_t)stream, 1, p);
 }
 
 extern "C" int qb_logprob_fwd(const void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
@@ -920,9 +935,8 @@ extern "C" int qb_logprob_fwd(const void* logits, int64_t n, int64_t V, int64_t 
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(logits && targets && logp && lse && al16(logits) && ld % 8 == 0);
   if (V % 8 != 0) return QB_ERR_UNSUPPORTED;
-  logprob_fwd_kernel<<<(unsigned)n, LNT, 0, (cudaStream_t)stream>>>((const bf16*)logits, V, ld, targets, dest,
+  return qb_launch(logprob_fwd_kernel, dim3((unsigned)n), dim3(LNT), 0, (cudaStream_t)stream, 1, (const bf16*)logits, V, ld, targets, dest,
                                                                     logp, lse, err);
-  return qb_launch_status();
 }
 
 extern "C" int qb_logprob_bwd(void* logits, int64_t n, int64_t V, int64_t ld, const int64_t* targets,
@@ -933,9 +947,8 @@ extern "C" int qb_logprob_bwd(void* logits, int64_t n, int64_t V, int64_t ld, co
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(logits && targets && lse && grad_logp && al16(logits) && ld % 8 == 0);
   if (V % 8 != 0) return QB_ERR_UNSUPPORTED;
-  logprob_bwd_kernel<<<(unsigned)n, LNT, 0, (cudaStream_t)stream>>>((bf16*)logits, V, ld, targets, dest, lse,
+  return qb_launch(logprob_bwd_kernel, dim3((unsigned)n), dim3(LNT), 0, (cudaStream_t)stream, 1, (bf16*)logits, V, ld, targets, dest, lse,
                                                                     grad_logp);
-  return qb_launch_status();
 }
 
 extern "C" int qb_grpo_advantage(const float* rewards, const int64_t* group_ids, int64_t n, float* adv,
@@ -943,8 +956,7 @@ extern "C" int qb_grpo_advantage(const float* rewards, const int64_t* group_ids,
   QB_CHECK_ARG(n >= 0 && n <= 65536);
   if (n == 0) return QB_OK;
   QB_CHECK_ARG(rewards && group_ids && adv);
-  advantage_kernel<<<(unsigned)n, 256, 0, (cudaStream_t)stream>>>(rewards, group_ids, n, adv);
-  return qb_launch_status();
+  return qb_launch(advantage_kernel, dim3((unsigned)n), dim3(256), 0, (cudaStream_t)stream, 1, rewards, group_ids, n, adv);
 }
 
 extern "C" size_t qb_grpo_workspace_bytes(int64_t n_rows) {
@@ -958,8 +970,7 @@ extern "C" int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void
   int64_t blocks = (n + 255) / 256;
   if (blocks > MS_BLOCKS) blocks = MS_BLOCKS;
   if (blocks < 1) blocks = 1;
-  mask_sum_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(mask, n, mask_total, (uint32_t*)workspace);
-  return qb_launch_status();
+  return qb_launch(mask_sum_kernel, dim3((unsigned)blocks), dim3(256), 0, (cudaStream_t)stream, 1, mask, n, mask_total, (uint32_t*)workspace);
 }
 
 extern "C" int qb_grpo_loss(const float* rewards, const int64_t* group_ids, int64_t n_rows, int64_t S,
@@ -982,8 +993,7 @@ extern "C" int qb_grpo_loss(const float* rewards, const int64_t* group_ids, int6
   LossParams p{rewards, group_ids, nullptr, n_rows, S, row_begin, new_lp, old_lp, ref_lp, mask, denom,
                (float)(1.0 - (double)clip_eps), (float)(1.0 + (double)clip_eps), beta, grad_scale, grad_new,
                loss_out, adv_out, ws};
-  grpo_loss_kernel<true><<<(unsigned)(row_end - row_begin), 256, 0, (cudaStream_t)stream>>>(p);
-  return qb_launch_status();
+  return qb_launch(grpo_loss_kernel<true>, dim3((unsigned)(row_end - row_begin)), dim3(256), 0, (cudaStream_t)stream, 1, p);
 }
 
 extern "C" int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, const float* token_adv,
@@ -1004,8 +1014,7 @@ extern "C" int qb_ppo_clipped_loss(const float* old_lp, const float* new_lp, con
   LossParams p{nullptr, nullptr, token_adv, n_rows, S, 0, new_lp, old_lp, ref_lp, mask, denom,
                (float)(1.0 - (double)clip_eps), (float)(1.0 + (double)clip_eps), beta, grad_scale, grad_new,
                loss_out, nullptr, ws};
-  grpo_loss_kernel<false><<<(unsigned)n_rows, 256, 0, (cudaStream_t)stream>>>(p);
-  return qb_launch_status();
+  return qb_launch(grpo_loss_kernel<false>, dim3((unsigned)n_rows), dim3(256), 0, (cudaStream_t)stream, 1, p);
 }
 
 // ================================================================ allocation-free GRPO loss
@@ -1132,7 +1141,9 @@ extern "C" int qb_grpo_logit_loss(void* logits, int64_t ld, int64_t V, const int
     if (e != QB_OK) return e;
     denom = slot;
   }
-  advantage_kernel<<<(unsigned)n_seqs, 256, 0, st>>>(rewards, group_ids, n_seqs, adv);
+  const int st_adv = qb_launch(advantage_kernel, dim3((unsigned)n_seqs), dim3(256), 0, st, 1, rewards, group_ids,
+                               n_seqs, adv);
+  if (st_adv != QB_OK) return st_adv;
   if (adv_out && cudaMemcpyAsync(adv_out, adv, n_seqs * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return qb_launch_status();
   const int chunk = (int)(((V + LL_CTAS - 1) / LL_CTAS + 7) / 8 * 8);
@@ -1147,19 +1158,8 @@ extern "C" int qb_grpo_logit_loss(void* logits, int64_t ld, int64_t V, const int
   LogitLossParams p{(bf16*)logits, ld, V, n_rows, S, targets, adv, old_lp, ref_lp, mask, denom,
                     (float)(1.0 - (double)clip_eps), (float)(1.0 + (double)clip_eps), beta, new_lp, grad_new, part,
                     chunk, err};
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(n_rows * LL_CTAS));
-  cfg.blockDim = dim3(LL_THREADS);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeClusterDimension;
-  attrs[0].val.clusterDim.x = LL_CTAS;
-  attrs[0].val.clusterDim.y = 1;
-  attrs[0].val.clusterDim.z = 1;
-  cfg.attrs = attrs;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, logit_loss_kernel, p) != cudaSuccess) return qb_launch_status();
-  logit_loss_reduce_kernel<<<1, 1024, 0, st>>>(part, n_rows, denom, beta, loss_out);
-  return qb_launch_status();
+  const int st_ll = qb_launch(logit_loss_kernel, dim3((unsigned)(n_rows * LL_CTAS)), dim3(LL_THREADS), (size_t)smem,
+                              st, LL_CTAS, p);
+  if (st_ll != QB_OK) return st_ll;
+  return qb_launch(logit_loss_reduce_kernel, dim3(1), dim3(1024), 0, st, 1, part, n_rows, denom, beta, loss_out);
 }

@@ -37,6 +37,16 @@ def test_version_and_status_strings():
     assert b"unsupported" in lib.qb_status_string(2)
 
 
+def test_pdl_switch():
+    """The library-wide launch switch (programmatic dependent launch) needs no GPU to set."""
+    lib = _lib.load()
+    old = lib.qb_get_pdl()
+    assert old == 1  # on by default
+    assert lib.qb_set_pdl(0) == 0 and lib.qb_get_pdl() == 0
+    assert lib.qb_set_pdl(7) == 0 and lib.qb_get_pdl() == 1
+    lib.qb_set_pdl(old)
+
+
 def test_workspace_size_queries():
     lib = _lib.load()
     assert lib.qb_paged_decode_workspace_bytes(256, 16, 128, 1) == 0

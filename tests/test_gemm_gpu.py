@@ -25,8 +25,7 @@ def ref(a, b):
                                    (809, 256, 512),
                                    # 128x192 tiles (one wave where 128x128 would need two), N and K tails
                                    (512, 6144, 1024), (500, 5000, 1000),
-                                   # 256 x 128 / 256 x 192 tiles on CTA pairs (decode-step qkv / gate_up),
-                                   # M, N and K tails
+                                   # decode-like shapes with M, N and K tails
                                    (480, 4096, 1024), (300, 4000, 1000), (257, 6100, 1000)])
 def test_gemm_bf16_out(cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M * 7 + N)
@@ -88,7 +87,7 @@ def test_gemm_repeated_calls_stable(cuda):
 @pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (296, 1024, 776), (1000, 384, 4096), (64, 151936, 200),
                                    (2048, 2560, 512), (2000, 2600, 648), (400, 6000, 200), (512, 4096, 1024),
-                                   (300, 4000, 520)])
+                                   (304, 4000, 520)])
 def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
     """Backward layouts: A stored [K, M] and/or B stored [K, N]; K need not be a multiple of 64
     (row pitches stay multiples of 8 elements, the TMA rule)."""
@@ -109,10 +108,8 @@ def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
 
 @pytest.mark.parametrize("M,N,K,b_mn,want", [
     (8192, 6144, 1024, False, ("pair", 256, 1)),   # training shapes: 256 x 256 tiles fill the SM pairs
-    (512, 4096, 1024, False, ("pair", 128, 1)),    # decode qkv_proj
-    (512, 4096, 1024, True, ("pair", 128, 1)),
-    (512, 6144, 1024, False, ("pair", 192, 1)),    # decode gate_up_proj
-    (512, 6144, 1024, True, ("single", 192, 1)),   # an MN-major B cannot split 96-row halves
+    (512, 4096, 1024, False, ("single", 128, 1)),  # decode qkv_proj: one wave of 128 x 128 tiles
+    (512, 6144, 1024, False, ("single", 192, 1)),  # decode gate_up_proj: one wave of 128 x 192
     (512, 1024, 2048, False, ("single", 128, 4)),  # decode o_proj: split-K over 4-CTA clusters
     (512, 1024, 3072, False, ("single", 128, 4)),  # decode down_proj
     (7, 300, 128, False, ("single", 128, 1)),
