@@ -26,6 +26,7 @@ one extra untimed step under CUPTI (--no-inner-profile skips it).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -308,6 +309,26 @@ def step_roofline(prompt_lens, group, new, layers, step_s, peaks):
             "basis": "sum over phases of max(FLOP/peak, bytes/peak); decode steps HBM-bound, the rest tensor-bound"}
 
 
+def progress(msg):
+    """Phase marker on stderr (the JSON line alone goes to stdout)."""
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
+@contextlib.contextmanager
+def plain_launches():
+    """Steps run under torch.profiler (CUPTI activity records) launch every kernel with plain
+    stream order: CUPTI tracing and programmatic dependent launches are kept apart.  The decode
+    graphs record the launch mode, so they are recaptured for the profiled step."""
+    from qwen3_naive_inference_b200._lib import load
+    lib = load()
+    old = lib.qb_get_pdl()
+    lib.qb_set_pdl(0)
+    try:
+        yield
+    finally:
+        lib.qb_set_pdl(old)
+
+
 def in_step_kernel_profile(torch, run_step):
     """Device time per kernel name over one GRPO step (CUPTI records via torch.profiler, graph
     replays included).  Returns ({name: (launches, total_us)}, step outputs)."""
@@ -315,7 +336,7 @@ def in_step_kernel_profile(torch, run_step):
 
     from torch.profiler import ProfilerActivity, profile
     torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    with plain_launches(), profile(activities=[ProfilerActivity.CUDA]) as prof:
         out = run_step()
         torch.cuda.synchronize()
     agg = defaultdict(lambda: [0, 0.0])
@@ -453,8 +474,10 @@ def run_ours(args):
 
     sampler = ClockSampler(local)
     sampler.start()
+    progress("warm-up done")
     ms, tokens, wall, launches, _, _, last = timed(args.steps, host_inputs=False)
     clocks = sampler.stop()
+    progress("timed steps done")
     peaks = {}
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -468,6 +491,12 @@ def run_ours(args):
                                args.layers, ms / 1000.0 / args.steps, peaks)
     whole_step["frac"] = roof_s / (ms / 1000.0)
     whole_step["total_s_all_timed_steps"] = roof_s
+    e2e = None
+    if not args.no_e2e:
+        ems, etok, _, _, h2d, d2h, _ = timed(args.steps, host_inputs=True)
+        e2e = {"value": etok / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.steps),
+               "d2h_bytes_per_step": d2h // max(1, args.steps)}
+    progress("e2e steps done")
     # the dominant kernel inside the step: one more (untimed) step under CUPTI; every rank runs it
     in_step = None
     if not args.no_inner_profile:
@@ -487,12 +516,8 @@ def run_ours(args):
                        "source": "CUPTI kernel records of one untimed bench step (all decode steps, all layers)"}
     if args.kernel_profile and rank == 0:
         kernel_profile(args, torch, lambda: step(0, make_prompts(args, rank, 200, dev)), args.kernel_profile)
+    progress("profiles done")
     value = tokens / (ms / 1000.0)
-    e2e = None
-    if not args.no_e2e:
-        ems, etok, _, _, h2d, d2h, _ = timed(args.steps, host_inputs=True)
-        e2e = {"value": etok / (ems / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d // max(1, args.steps),
-               "d2h_bytes_per_step": d2h // max(1, args.steps)}
     # roofline of the dominant kernel: the grouped (shared-prefix) decode attention, on the
     # mid-rollout case, launches back to back between events on its stream; the timed call is the
     # tile kernel plus its small split-K combine
@@ -649,7 +674,7 @@ def kernel_profile(args, torch, run_step, path):
     from collections import Counter
     from torch.profiler import ProfilerActivity, profile
     torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    with plain_launches(), profile(activities=[ProfilerActivity.CUDA]) as prof:
         out = run_step()
         torch.cuda.synchronize()
     tot, cnt = Counter(), Counter()

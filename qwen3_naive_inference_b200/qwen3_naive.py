@@ -33,6 +33,12 @@ import torch.nn as nn
 from . import _lib, ops
 
 
+def _pdl_mode() -> int:
+    """The library's launch mode (programmatic dependent launch on/off): captured decode graphs
+    record it, so a change recaptures them."""
+    return int(_lib.load().qb_get_pdl())
+
+
 # ============================================================================ config
 @dataclass
 class Qwen3Config:
@@ -742,7 +748,7 @@ class Qwen3ForCausalLM(nn.Module):
 
     def _capture_decode_graphs(self, temperature=1.0, top_k=None, grouped=False):
         """Capture decode+lm_head+sampling graphs for every bucket (largest first, one shared pool)."""
-        self._graph_key = (float(temperature), top_k, bool(grouped))
+        self._graph_key = (float(temperature), top_k, bool(grouped), _pdl_mode())
         self._graphs = {}
         self._graph_pool = None
         self._gin_dev.zero_()
@@ -951,7 +957,7 @@ class Qwen3ForCausalLM(nn.Module):
         dev = self.lm_head.weight.device
         self.allocate_global_kv_cache()
         seed = int(torch.randint(0, 2**62, (1,)).item())
-        key = (float(temperature), top_k, True)
+        key = (float(temperature), top_k, True, _pdl_mode())
         if not self.use_cuda_graphs:
             self._has_cuda_graphs = False
         elif (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx or getattr(self, "_graph_key", None) != key
@@ -1101,7 +1107,7 @@ class Qwen3ForCausalLM(nn.Module):
         if not self.use_cuda_graphs:
             self._has_cuda_graphs = False
         elif (not self._has_cuda_graphs or self._graph_max_ctx < max_ctx
-                or getattr(self, "_graph_key", None) != (float(temperature), top_k, False)):
+                or getattr(self, "_graph_key", None) != (float(temperature), top_k, False, _pdl_mode())):
             if not self._has_cuda_graphs or self._graph_max_ctx < max_ctx:
                 self._init_cuda_graphs(max_bs=512, max_ctx=max(max_ctx, 1024))
             self._capture_decode_graphs(temperature, top_k)
