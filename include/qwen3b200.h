@@ -46,11 +46,12 @@ typedef void* qb_stream_t;
 int qb_abi_version(void);
 /* Static description of a status code. */
 const char* qb_status_string(int status);
-/* Programmatic dependent launch (library-wide, on by default): each kernel of this library may be
- * scheduled while the kernel before it in the stream finishes, overlapping its launch and
- * prologue with that kernel's tail; it waits on the device for that kernel's completion before
- * touching memory.  Works inside CUDA graph capture.  qb_set_pdl(0) launches every kernel with
- * plain stream ordering; qb_get_pdl reports the setting. */
+/* Programmatic dependent launch (library-wide, on by default): the tcgen05 GEMM and attention
+ * kernels may be scheduled while the kernel before them in the stream is still running, so their
+ * launch and prologue (barrier init, TMEM allocation) overlap it; they wait on the device for that
+ * kernel's completion before touching memory.  Short kernels launch in plain stream order.  Works
+ * inside CUDA graph capture.  qb_set_pdl(0) launches every kernel with plain stream ordering;
+ * qb_get_pdl reports the setting. */
 int qb_set_pdl(int on);
 int qb_get_pdl(void);
 

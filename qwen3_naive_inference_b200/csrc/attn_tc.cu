@@ -351,7 +351,7 @@ int attn_fwd_tc_launch(const void* q, int64_t q_stride, const void* k, const voi
   AttnTcParams p{cu_seqlens, tile_info, tiles_per_seq, hq, hkv, scale * 1.4426950408889634f,
                  (bf16*)out, o_stride, lse, total_q, err};
   (void)batch;
-  return qb_launch(attn_fwd_tc_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(AT_THREADS), AT_SMEM, st, 1, tq, tk, tv, p);
+  return qb_launch_ex(attn_fwd_tc_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(AT_THREADS), AT_SMEM, st, 1, true, tq, tk, tv, p);
 }
 
 namespace {
@@ -664,7 +664,7 @@ int attn_bwd_dkdv_tc_launch(const void* q, const void* k, const void* v, int64_t
   }
   AttnBwdTcParams p{cu_seqlens, tile_info, hq, hkv, scale, scale * 1.4426950408889634f, lse, delta, total,
                     (bf16*)dk, (bf16*)dv, stride, err};
-  return qb_launch(attn_bwd_dkdv_tc_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(BT_THREADS), BT_SMEM, st, 1, tq, tk, tv, tdo, p);
+  return qb_launch_ex(attn_bwd_dkdv_tc_kernel, dim3(dim3((unsigned)n_tiles, (unsigned)hkv)), dim3(BT_THREADS), BT_SMEM, st, 1, true, tq, tk, tv, tdo, p);
 }
 
 namespace {
@@ -904,6 +904,6 @@ int attn_bwd_dq_tc_launch(const void* q, const void* k, const void* v, int64_t s
   }
   AttnBwdTcParams p{cu_seqlens, tile_info, hq, hkv, scale, scale * 1.4426950408889634f, lse, delta, total,
                     nullptr, nullptr, stride, err};
-  return qb_launch(attn_bwd_dq_tc_kernel, dim3((unsigned)n_tiles, (unsigned)hkv), dim3(DQ_THREADS), DQ_SMEM_TC, st, 1,
-                   tq, tk, tv, tdo, p, (bf16*)dq);
+  return qb_launch_ex(attn_bwd_dq_tc_kernel, dim3((unsigned)n_tiles, (unsigned)hkv), dim3(DQ_THREADS), DQ_SMEM_TC,
+                      st, 1, true, tq, tk, tv, tdo, p, (bf16*)dq);
 }

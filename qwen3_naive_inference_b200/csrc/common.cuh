@@ -25,12 +25,15 @@ static inline int qb_launch_status() {
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch
-// Kernels are launched with programmatic stream serialization (when the library-wide switch is on):
-// a kernel may be scheduled as soon as every CTA of the kernel before it in the stream has passed
-// qb_pdl_trigger(), so its launch and prologue (barrier init, TMEM allocation, tensor-map
-// prefetch) overlap that kernel's tail; qb_pdl_wait() then blocks until the kernel before has
-// completed and its writes are visible.  Both are no-ops in a kernel launched without the
-// attribute.  Rules every kernel launched through qb_launch follows:
+// The tcgen05 kernels (GEMMs, training attention), whose prologue is long (barrier init, TMEM
+// allocation, tensor-map prefetch), are launched with programmatic stream serialization when the
+// library-wide switch is on: such a kernel may be scheduled as soon as every CTA of the kernel
+// before it in the stream has passed qb_pdl_trigger(), so its launch and prologue overlap that
+// kernel's run; qb_pdl_wait() then blocks until the kernel before has completed and its writes
+// are visible.  Short kernels are launched with plain stream order (measured: the early launch
+// costs them more than it hides) but still trigger at their start, so a GEMM after them starts
+// early.  Both calls are no-ops in a kernel launched without the attribute.  Rules every kernel
+// of the library follows:
 //   * every thread calls qb_pdl_wait() before its first global access that depends on earlier
 //     work (any read of an input another kernel may have written, and every global write), and
 //     before it exits -- a kernel that could complete without waiting would let the kernel after
@@ -43,11 +46,12 @@ QB_DEVICE void qb_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents
 // Library-wide switch (qb_set_pdl in the C ABI); on by default.
 bool qb_pdl_enabled();
 
-// Launch `kern` on `st` with a cluster of `cluster_x` CTAs (1: none) and, when the switch is on,
-// programmatic stream serialization.  Returns the launch status like qb_launch_status().
+// Launch `kern` on `st` with a cluster of `cluster_x` CTAs (1: none) and, when `early` and the
+// switch is on, programmatic stream serialization.  Returns the launch status like
+// qb_launch_status().
 template <typename... KArgs, typename... Args>
-static inline int qb_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                            int cluster_x, Args&&... args) {
+static inline int qb_launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               int cluster_x, bool early, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -62,7 +66,7 @@ static inline int qb_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
     attrs[n].val.clusterDim.z = 1;
     ++n;
   }
-  if (qb_pdl_enabled()) {
+  if (early && qb_pdl_enabled()) {
     attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
@@ -71,6 +75,12 @@ static inline int qb_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_
   cfg.numAttrs = n;
   (void)cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
   return qb_launch_status();  // the launch's own error (consumed here: callers return this value)
+}
+// Plain stream order (short kernels).
+template <typename... KArgs, typename... Args>
+static inline int qb_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            int cluster_x, Args&&... args) {
+  return qb_launch_ex(kern, grid, block, smem, st, cluster_x, false, static_cast<Args&&>(args)...);
 }
 
 #define QB_CHECK_ARG(cond)            \

@@ -785,7 +785,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cudaStrea
   }
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  return qb_launch(kern, dim3(grid), dim3(THREADS), Cfg::SMEM, st, 1, ta, tb, p);
+  return qb_launch_ex(kern, dim3(grid), dim3(THREADS), Cfg::SMEM, st, 1, true, ta, tb, p);
 }
 
 template <int MODE, bool A_MN, bool B_MN, int PBN>
@@ -800,7 +800,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cuda
   }
   const int tiles = ((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
   const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
-  return qb_launch(kern, dim3((unsigned)(2 * pairs)), dim3(THREADS), SMEM, st, 2, ta, tb, p);
+  return qb_launch_ex(kern, dim3((unsigned)(2 * pairs)), dim3(THREADS), SMEM, st, 2, true, ta, tb, p);
 }
 
 template <int S, int MODE, bool A_MN, bool B_MN>
@@ -812,7 +812,7 @@ int launch_split(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cud
       return qb_launch_status();
     attr = true;
   }
-  return qb_launch(kern, dim3((unsigned)(p.tiles_m * p.tiles_n * S)), dim3(THREADS), SplitCfg<S>::SMEM, st, S, ta,
+  return qb_launch_ex(kern, dim3((unsigned)(p.tiles_m * p.tiles_n * S)), dim3(THREADS), SplitCfg<S>::SMEM, st, S, true, ta,
                    tb, p);
 }
 
