@@ -331,6 +331,10 @@ int qb_mask_sum(const float* mask, int64_t n, float* mask_total, void* workspace
  * zero-filled); A and B 16-byte aligned with lda, ldb % 8 == 0 (TMA operands); any ldc >= N. */
 int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                  int64_t M, int64_t N, int64_t K, int mode, int* err, qb_stream_t stream);
+/* Flag ORed into the mode of qb_gemm_bf16 / qb_gemm_bf16_ex: B is written by no kernel that may
+ * still be running on the stream when the GEMM is launched (weights during inference), so the
+ * kernel may start fetching B before the kernel before it has finished. */
+#define QB_GEMM_B_STATIC 0x100
 /* The same product with either operand stored MN-major, for the backward of the projections
  * (the reference's autograd of nn.Linear / lm_head):
  *   a_mn_major = 0: A is [M, K] (K contiguous);  1: A is stored [K, M] (M contiguous, lda >= M)

@@ -36,6 +36,7 @@ struct GemmParams {
   float2* lse_part;        // [M, n_part]: per N tile, (max, sum of exp) of the row in the log2 domain
   float* tgt_logit;        // [M] fp32 logit at the target column
   int n_part;              // row pitch of lse_part (= number of N tiles of the launch)
+  int b_static;            // B is written by no kernel still in flight: it may be read before the PDL wait
 };
 
 // One epilogue thread's 32 consecutive fp32 accumulator columns of output row `row`, starting
@@ -210,21 +211,38 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
-  qb_pdl_wait();     // operands and C may come from the kernel before
+  // With a static B (weights no kernel in flight writes), the producer requests the B halves of
+  // its first tile's first ring stages before waiting for the kernel before: their DRAM trip
+  // overlaps that kernel's tail.  Each such stage expects its full bytes, so it completes only
+  // once the A half, requested after the wait, has landed too.
+  int pre = 0;
+  uint32_t issued = 0;  // producer: per-stage bit, a load is in flight
+  if (warp == 0 && lane == 0 && p.b_static && (int)blockIdx.x < n_tiles) {
+    const int n0 = ((int)blockIdx.x / p.tiles_m) * BN;
+    pre = kblocks < STAGES ? kblocks : STAGES;
+    for (int s = 0; s < pre; ++s) {
+      mbar_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
+      load_operand<B_MN, BN>(base + s * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmap_b, s * BK, n0, full_bar(s));
+      issued |= 1u << s;
+    }
+  }
+  qb_pdl_wait();  // A, and C in MODE 2, may come from the kernel before
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t issued = 0, last_parity = 0;  // per-stage bit: a load is in flight; its phase parity
+    uint32_t last_parity = 0;  // per-stage bit: the phase parity of its load in flight
     for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
       const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
       for (int kb = 0; kb < kblocks; ++kb) {
-        if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
+        // the first `pre` stages of the first tile: fresh barriers, B already requested
+        const bool pre_b = t == (int)blockIdx.x && kb < pre;
+        if (!pre_b && !mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
         const uint32_t sa = base + stage * Cfg::STAGE_BYTES, sb = sa + Cfg::A_BYTES;
-        mbar_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
+        if (!pre_b) mbar_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
         load_operand<A_MN, BM>(sa, &tmap_a, kb * BK, m0, full_bar(stage));
-        load_operand<B_MN, BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
+        if (!pre_b) load_operand<B_MN, BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
         issued |= 1u << stage;
         last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -646,19 +664,32 @@ gemm_split_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   qb_pdl_trigger();  // after the TMEM allocation: the next kernel cannot take it from this CTA
-  qb_pdl_wait();     // operands and C may come from the kernel before
+  // A static B's first ring stages are requested before the wait for the kernel before (as in
+  // gemm_tcgen05_kernel); each such stage completes once its A half, requested after, lands too.
+  int pre = 0;
+  uint32_t issued = 0;  // producer: per-stage bit, a load is in flight
+  if (warp == 0 && lane == 0 && p.b_static) {
+    pre = kb1 - kb0 < S_STAGES ? kb1 - kb0 : S_STAGES;
+    for (int s = 0; s < pre; ++s) {
+      mbar_expect_tx(full_bar(s), S_STAGE_BYTES);
+      load_operand<B_MN, S_BN>(base + s * S_STAGE_BYTES + BM * BK * 2, &tmap_b, (kb0 + s) * BK, n0, full_bar(s));
+      issued |= 1u << s;
+    }
+  }
+  qb_pdl_wait();  // A, and C in MODE 2, may come from the kernel before
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     int stage = 0;
     uint32_t phase = 0;
-    uint32_t issued = 0, last_parity = 0;
+    uint32_t last_parity = 0;
     for (int kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
-      if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
+      const bool pre_b = kb - kb0 < pre;  // fresh barrier, B already requested
+      if (!pre_b && !mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
       const uint32_t sa = base + stage * S_STAGE_BYTES, sb = sa + BM * BK * 2;
-      mbar_expect_tx(full_bar(stage), S_STAGE_BYTES);
+      if (!pre_b) mbar_expect_tx(full_bar(stage), S_STAGE_BYTES);
       load_operand<A_MN, BM>(sa, &tmap_a, kb * BK, m0, full_bar(stage));
-      load_operand<B_MN, S_BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
+      if (!pre_b) load_operand<B_MN, S_BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
       issued |= 1u << stage;
       last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
       if (++stage == S_STAGES) { stage = 0; phase ^= 1; }
@@ -924,6 +955,8 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
 
 int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, bool b_mn, void* C,
                   int64_t ldc, int64_t M, int64_t N, int64_t K, int mode, int* err, cudaStream_t st) {
+  const int b_static = (mode & QB_GEMM_B_STATIC) ? 1 : 0;
+  mode &= ~QB_GEMM_B_STATIC;
   QB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && mode >= 0 && mode <= 2);
   if (M == 0 || N == 0) return QB_OK;
   if (K == 0) return QB_ERR_UNSUPPORTED;
@@ -950,6 +983,7 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
   if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)bn)) return QB_ERR_INVALID;
   GemmParams p{C, ldc, (int)M, (int)N, (int)K, (int)tm, (int)((N + bn - 1) / bn), vec_ok, err};
+  p.b_static = b_static;
   if (split > 1) {
     if (!a_mn && !b_mn) return launch_split_s<false, false>(split, mode, ta, tb, p, st);
     if (!a_mn && b_mn) return launch_split_s<false, true>(split, mode, ta, tb, p, st);

@@ -490,10 +490,16 @@ def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode: int = 0) -> torch.Tensor:
+QB_GEMM_B_STATIC = 0x100  # include/qwen3b200.h
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode: int = 0,
+         b_static: bool = False) -> torch.Tensor:
     """tcgen05 GEMM: ``a @ b.T`` for bf16 a [M, K], b [N, K] (unit stride along K).
 
-    mode 0 -> bf16 result, 1 -> fp32 result, 2 -> ``out += a @ b.T`` in fp32."""
+    mode 0 -> bf16 result, 1 -> fp32 result, 2 -> ``out += a @ b.T`` in fp32.  ``b_static``: no
+    kernel still running on the stream writes ``b`` (weights), so the GEMM may fetch it before
+    the kernel before it has finished."""
     _cuda(a, b)
     if a.dtype != BF16 or b.dtype != BF16 or a.stride(-1) != 1 or b.stride(-1) != 1:
         raise NativeError("gemm needs bf16 operands with unit stride along K")
@@ -501,8 +507,9 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode
     N = b.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=BF16 if mode == 0 else torch.float32, device=a.device)
-    check(lib().qb_gemm_bf16(_p(a), a.stride(0), _p(b), b.stride(0), _p(out), out.stride(0), M, N, K, mode,
-                             _p(err_flag()), stream_ptr()), "qb_gemm_bf16")
+    flags = QB_GEMM_B_STATIC if b_static else 0
+    check(lib().qb_gemm_bf16(_p(a), a.stride(0), _p(b), b.stride(0), _p(out), out.stride(0), M, N, K,
+                             mode | flags, _p(err_flag()), stream_ptr()), "qb_gemm_bf16")
     return out
 
 
@@ -575,7 +582,8 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
         y = _Linear.apply(x2, w2, grad32_target(w) if w.requires_grad else None)
     else:
-        y = gemm(x2, w2)
+        # a Parameter is written only by the optimizer's kernels, finished before any forward
+        y = gemm(x2, w2, b_static=isinstance(w, torch.nn.Parameter))
     return y.view(*shape[:-1], w.shape[0])
 
 
