@@ -712,12 +712,15 @@ def kernel_profile(args, torch, run_step, path):
         lines.append(f"| {k[:90]} | {cnt[k]} | {v / 1e3:.2f} | {100 * v / T:.1f}% |")
     recs.sort()
     gaps = {"rollout": [0.0, 0], "ref log-probs + train": [0.0, 0]}
-    for (t0, n0, d0), (t1, _, _) in zip(recs, recs[1:]):
+    long_gaps = {"rollout": [], "ref log-probs + train": []}
+    for (t0, n0, d0), (t1, n1, _) in zip(recs, recs[1:]):
         g = t1 - (t0 + d0)
         ph = "rollout" if t1 <= split else "ref log-probs + train"
         if 0 < g < 100:  # idle time between back-to-back launches (longer gaps are host waits)
             gaps[ph][0] += g
             gaps[ph][1] += 1
+        elif g >= 100:
+            long_gaps[ph].append((g, n0, n1))
     for ph in phase_tot:
         PT = sum(phase_tot[ph].values()) or 1.0
         lines += ["", f"## {ph}: {PT / 1e3:.1f} ms of kernel time; {gaps[ph][0] / 1e3:.1f} ms idle in "
@@ -726,6 +729,19 @@ def kernel_profile(args, torch, run_step, path):
         for k, v in phase_tot[ph].most_common(20):
             c = phase_cnt[ph][k]
             lines.append(f"| {k[:90]} | {c} | {v / 1e3:.2f} | {v / c:.2f} | {100 * v / PT:.1f}% |")
+        lg = sorted(long_gaps[ph], reverse=True)
+        lines += ["", f"{len(lg)} gaps of 100 us or more (the device idle while the host works): "
+                  f"{sum(g for g, _, _ in lg) / 1e3:.1f} ms in total; the longest:", "",
+                  "| gap us | after kernel | before kernel |", "|---|---|---|"]
+        for g, a, b in lg[:15]:
+            lines.append(f"| {g:.0f} | {a[:60]} | {b[:60]} |")
+        pairs = Counter()
+        for g, a, b in lg:
+            pairs[(a[:50], b[:50])] += g
+        lines += ["", "Long gaps summed by the kernels on either side:", "", "| ms | after | before |",
+                  "|---|---|---|"]
+        for (a, b), g in pairs.most_common(10):
+            lines.append(f"| {g / 1e3:.1f} | {a} | {b} |")
     Path(path).parent.mkdir(parents=True, exist_ok=True)
     Path(path).write_text("\n".join(lines) + "\n")
 
