@@ -701,16 +701,22 @@ class Qwen3ForCausalLM(nn.Module):
         self._graph_bs = [b for b in self.GRAPH_BATCH_SIZES if b <= max_bs]
         mb = self._graph_bs[-1]
         W = self._graph_max_blocks
-        # packed inputs: i64 ids[mb] pos[mb] rng[2] | i32 ctx[mb] slots[mb] bt[mb*W] members[mb*8]
-        #                shared_len[mb] kv_start[mb]
-        n64 = 2 * mb + 2
+        # packed inputs: i64 ids[mb] pos[mb] rng[2] feed_src[mb] | i32 ctx[mb] slots[mb] bt[mb*W]
+        #                members[mb*8] shared_len[mb] kv_start[mb]
+        # (feed_src: per row, the row of the previous step whose sample is its input token, or -1;
+        # read by the gather that runs before a step submitted ahead of its predecessor's read-back)
+        n64 = 3 * mb + 2
         n32 = 2 * mb + mb * W + 8 * mb + 2 * mb
-        self._gin_host = torch.zeros(n64 * 8 + n32 * 4, dtype=torch.uint8, pin_memory=True)
-        self._gin_dev = torch.zeros_like(self._gin_host, device=dev)
+        # two pinned copies, alternated per step: a step is filled while the one before may still
+        # wait for its upload
+        self._gin_hosts = [torch.zeros(n64 * 8 + n32 * 4, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        self._gin_turn = 0
+        self._gin_dev = torch.zeros_like(self._gin_hosts[0], device=dev)
 
         def views(i64, i32):
             o = 2 * mb + mb * W
             return {"input_ids": i64[:mb], "positions": i64[mb:2 * mb], "rng_state": i64[2 * mb:2 * mb + 2],
+                    "feed_src": i64[2 * mb + 2:3 * mb + 2],
                     "context_lens": i32[:mb], "slot_mapping": i32[mb:2 * mb],
                     "block_tables": i32[2 * mb:o].reshape(mb, W), "members": i32[o:o + 8 * mb].reshape(mb, 8),
                     "shared_len": i32[o + 8 * mb:o + 9 * mb], "kv_start": i32[o + 9 * mb:o + 10 * mb]}
@@ -718,8 +724,8 @@ class Qwen3ForCausalLM(nn.Module):
         self._graph_bufs = views(self._gin_dev[:n64 * 8].view(torch.int64), self._gin_dev[n64 * 8:].view(torch.int32))
         self._graph_bufs["tokens"] = torch.zeros(mb, dtype=torch.int64, device=dev)
         self._graph_bufs["logp"] = torch.zeros(mb, dtype=torch.float32, device=dev)
-        self._graph_host = views(self._gin_host[:n64 * 8].numpy().view(np.int64),
-                                 self._gin_host[n64 * 8:].numpy().view(np.int32))
+        self._graph_hosts = [views(h[:n64 * 8].numpy().view(np.int64), h[n64 * 8:].numpy().view(np.int32))
+                             for h in self._gin_hosts]
         self._graphs = {}
         self._graph_pool = None
         self._has_cuda_graphs = False
@@ -777,16 +783,27 @@ class Qwen3ForCausalLM(nn.Module):
         torch.cuda.synchronize()
         self._has_cuda_graphs = True
 
-    def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None, arrays=None):
+    def _graph_fits(self, bs, arrays=None):
+        """A captured decode graph covers ``bs`` rows (and the block-table width of ``arrays``)."""
+        if not self._has_cuda_graphs or _round_bs(bs, self._graph_bs) is None:
+            return False
+        return arrays is None or arrays[3].shape[1] <= self._graph_max_blocks
+
+    def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None, arrays=None, feed=None):
         """Fill the static inputs with one H2D copy, replay, return (tokens, logp) device views.
 
         ``groups`` (grouped graphs): list of (member row indices, shared key count, first own key).
-        ``arrays``: (ids, positions, context_lens, block_tables, slots) already built for ``seqs``."""
+        ``arrays``: (ids, positions, context_lens, block_tables, slots) already built for ``seqs``.
+        ``feed``: (src, prev_tokens) -- row i's input token is prev_tokens[src[i]] (the previous
+        step's sample, still on the device) where src[i] >= 0, else ids[i]; gathered on the device
+        after the upload, so this step can be enqueued before the previous one is read back."""
         bs = len(seqs)
         gbs = _round_bs(bs, self._graph_bs)
         if gbs is None or (arrays is not None and arrays[3].shape[1] > self._graph_max_blocks):
             return None
-        hb = self._graph_host
+        turn = self._gin_turn
+        self._gin_turn ^= 1
+        hb = self._graph_hosts[turn]
         if arrays is None:
             ids, pos, ctx, bt, slots = self._decode_arrays(seqs, width=self._graph_max_blocks)
         else:
@@ -814,7 +831,14 @@ class Qwen3ForCausalLM(nn.Module):
                 g_i += 1
         hb["rng_state"][0] = rng_counter
         hb["rng_state"][1] = rng_seed
-        self._gin_dev.copy_(self._gin_host, non_blocking=True)
+        if feed is not None:
+            hb["feed_src"][:bs] = feed[0]
+        self._gin_dev.copy_(self._gin_hosts[turn], non_blocking=True)
+        if feed is not None:
+            b = self._graph_bufs
+            ids, src = b["input_ids"][:bs], b["feed_src"][:bs]
+            fed = feed[1].index_select(0, src.clamp(min=0))
+            ids.copy_(torch.where(src >= 0, fed, ids))
         g, _, n_kernels = self._graphs[gbs]
         g.replay()
         _lib.LAUNCHES[0] += n_kernels
@@ -967,11 +991,14 @@ class Qwen3ForCausalLM(nn.Module):
             self._init_cuda_graphs(max_bs=512, max_ctx=ctx_cap, max_shared=ctx_cap)
             self._capture_decode_graphs(temperature, top_k, grouped=True)
         cap = 2 * self.MAX_TOKENS_PER_STEP + 512 * 8
-        return {"dev": dev, "seed": seed, "temperature": temperature, "top_k": top_k,
-                "rng": torch.tensor([0, seed], dtype=torch.int64, device=dev),
-                "tok_host": torch.empty(cap, dtype=torch.int64, pin_memory=True),
-                "lp_host": torch.empty(cap, dtype=torch.float32, pin_memory=True),
-                "err_host": torch.zeros(1, dtype=torch.int32, pin_memory=True), "err": ops.err_flag(dev)}
+        ctx = {"dev": dev, "seed": seed, "temperature": temperature, "top_k": top_k,
+               "rng": torch.tensor([0, seed], dtype=torch.int64, device=dev),
+               "rb": [(torch.empty(cap, dtype=torch.int64, pin_memory=True),
+                       torch.empty(cap, dtype=torch.float32, pin_memory=True),
+                       torch.zeros(1, dtype=torch.int32, pin_memory=True)) for _ in range(2)],
+               "rb_turn": 0, "err": ops.err_flag(dev)}
+        ctx["tok_host"], ctx["lp_host"], ctx["err_host"] = ctx["rb"][0]  # the synchronous steps' slot
+        return ctx
 
     def _grouped_launch(self, ctx, prefill, done, decode_rows, groups_rows, step, G, n_samples):
         """Enqueues one grouped-rollout step: a grouped-decode graph when only decode
@@ -1048,24 +1075,35 @@ class Qwen3ForCausalLM(nn.Module):
                             count=n)
         return pos, cl, self._block_table_array(rows), slots
 
-    def _decode_submit(self, ctx, rows, groups_rows, step, ids, arrays):
+    def _decode_submit(self, ctx, rows, groups_rows, step, ids, arrays, feed=None):
         """Enqueue one decode step over ``rows`` (input token ``ids``, metadata ``arrays`` from
-        _decode_step_arrays) and the read-back of its samples; returns a handle for _decode_collect."""
+        _decode_step_arrays) and the read-back of its samples; returns a handle for _decode_collect.
+
+        ``feed`` = (src, handle of the step before, not yet read back): the inputs of rows with
+        src >= 0 are that step's samples, gathered on the device (graph replays only: the caller
+        checks _graph_fits).  Read-backs alternate between two pinned slots, so a step can be
+        collected while the next one is already queued."""
         pos, cl, bt, slots = arrays
         full = (ids, pos, cl, bt, slots)
         r = None
         if self._has_cuda_graphs:
-            r = self._run_decode_graph(rows, step, ctx["seed"], groups=groups_rows, arrays=full)
+            fd = None if feed is None else (feed[0], feed[1]["tokens"])
+            r = self._run_decode_graph(rows, step, ctx["seed"], groups=groups_rows, arrays=full, feed=fd)
         if r is None:
+            if feed is not None:
+                raise RuntimeError("a device-fed decode step needs a captured graph")
             r = self._grouped_decode_eager(ctx, full, groups_rows, step)
         n = len(rows)
         toks_dev, logp_dev = r
-        ctx["tok_host"][:n].copy_(toks_dev, non_blocking=True)
-        ctx["lp_host"][:n].copy_(logp_dev, non_blocking=True)
-        ctx["err_host"].copy_(ctx["err"], non_blocking=True)
+        slot = ctx["rb_turn"]
+        ctx["rb_turn"] ^= 1
+        tok_h, lp_h, err_h = ctx["rb"][slot]
+        tok_h[:n].copy_(toks_dev, non_blocking=True)
+        lp_h[:n].copy_(logp_dev, non_blocking=True)
+        err_h.copy_(ctx["err"], non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
-        return {"n": n, "event": ev}
+        return {"n": n, "event": ev, "slot": slot, "tokens": toks_dev}
 
     def _decode_collect(self, ctx, handle):
         """Waits for a submitted step; returns its (tokens, log-probs) as numpy arrays."""
@@ -1074,10 +1112,11 @@ class Qwen3ForCausalLM(nn.Module):
         st = self.rollout_stats
         st["gpu_wait_s"] = st.get("gpu_wait_s", 0.0) + time.perf_counter() - t0
         st["steps"] = st.get("steps", 0) + 1
-        if int(ctx["err_host"][0]):
+        tok_h, lp_h, err_h = ctx["rb"][handle["slot"]]
+        if int(err_h[0]):
             ops.check_device_errors(ctx["dev"])
         n = handle["n"]
-        return ctx["tok_host"][:n].numpy().copy(), ctx["lp_host"][:n].numpy().copy()
+        return tok_h[:n].numpy().copy(), lp_h[:n].numpy().copy()
 
     @torch.no_grad()
     def generate_grouped_with_logprobs(self, prompt_ids_list, group_size, max_new_tokens=256, temperature=0.6,
@@ -1402,12 +1441,16 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
 
     # ---- pipelined decode: with no group waiting and every running group decoding, the rows of
     # step k+1 are known before step k's tokens are (a member leaves only by EOS, found after
-    # the fact, or by its token budget, known ahead).  Step k+1 is planned while step k runs,
-    # submitted right after step k's read-back with step k's tokens as its inputs, and step k's
-    # bookkeeping runs while step k+1 is on the GPU.  A member that sampled EOS at step k has
-    # already been submitted for step k+1: that sample is discarded.  The rows' random draws
-    # are independent, so the others are unaffected; pages it still writes at step k+1 are
-    # freed on the host first but reused only by steps that run after it on the stream.
+    # the fact, or by its token budget, known ahead).  Step k+1 is planned while step k runs and
+    # queued behind it before step k is read back: its input tokens are step k's samples,
+    # gathered on the device from the decode graph's output, so the GPU goes from step k to
+    # step k+1 without waiting for the host.  Step k's read-back and bookkeeping, and step
+    # k+2's planning, then overlap step k+1.  (Without a captured graph for step k+1 it is
+    # submitted after step k's read-back with the tokens from the host.)  A member that sampled
+    # EOS at step k has already been submitted for step k+1: that sample is discarded.  The
+    # rows' random draws are independent, so the others are unaffected; pages it still writes at
+    # step k+1 are freed on the host first but reused only by steps that run after it on the
+    # stream.
     def plan_step(prev_rows=None):
         """Rows, groups, metadata and, per row, its index in ``prev_rows`` (the step in flight,
         whose samples are this step's inputs) of the next decode step; None when no row is left
@@ -1427,12 +1470,12 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
             src = np.fromiter((pos_of.get(id(m), -1) for m in rows), dtype=np.int64, count=len(rows))
         return rows, groups_of(rows), model._decode_step_arrays(rows), src
 
-    def submit(plan, ids):
+    def submit(plan, ids, feed=None):
         nonlocal step
         rows, grows, arrays, _ = plan
         step += 1
         model.rollout_stats["decode_steps"] = model.rollout_stats.get("decode_steps", 0) + 1
-        h = model._decode_submit(ctx, rows, grows, step, ids, arrays)
+        h = model._decode_submit(ctx, rows, grows, step, ids, arrays, feed=feed)
         for m in rows:
             m.kv_len += 1
             m.inflight += 1
@@ -1446,9 +1489,16 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
         h = submit(plan, np.fromiter((m.last_token for m in rows), dtype=np.int64, count=len(rows)))
         while True:
             nplan = plan_step(rows)  # overlaps the step in flight
-            toks, lps = model._decode_collect(ctx, h)
             h_nxt = None
-            if nplan is not None:
+            if nplan is not None and model._graph_fits(len(nplan[0]), nplan[2]):
+                # step k+1 is queued behind step k before k is read back: its input tokens are
+                # step k's samples, gathered on the device (a row new to k+1 brings its own)
+                src = nplan[3]
+                own = np.fromiter((0 if j >= 0 else m.last_token for j, m in zip(src, nplan[0])), dtype=np.int64,
+                                  count=len(src))
+                h_nxt = submit(nplan, own, feed=(src, h))
+            toks, lps = model._decode_collect(ctx, h)
+            if nplan is not None and h_nxt is None:
                 src = nplan[3]
                 if (src >= 0).all():
                     ids = toks[src]

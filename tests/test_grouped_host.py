@@ -28,6 +28,8 @@ class HostGrouped(Qwen3ForCausalLM):
         self.checks = 0
         self.resets = 0
         self.pipelined = 0
+        self.fed = 0
+        self.feed_on_device = True  # steps queued ahead take their inputs from the step before
 
     def _grouped_setup(self, max_ctx, max_shared, temperature, top_k):
         return {}
@@ -43,13 +45,23 @@ class HostGrouped(Qwen3ForCausalLM):
         ctx["toks"] = toks
         assert len(toks) == n_samples
 
+    def _graph_fits(self, bs, arrays=None):
+        return self.feed_on_device
+
     # pipelined decode steps: the input token of a row comes from the host (the previous step's
-    # read-back), its position from the step's metadata
-    def _decode_submit(self, ctx, rows, groups_rows, step, ids, arrays):
+    # read-back) or, for a step queued before that read-back, from the previous step's samples
+    # (the device gather: row i takes sample src[i] where src[i] >= 0); its position from the
+    # step's metadata
+    def _decode_submit(self, ctx, rows, groups_rows, step, ids, arrays, feed=None):
         pos, cl, bt, slots = arrays
         assert list(cl) == [m.kv_len for m in rows]
         self._check(rows, groups_rows)
         self.pipelined += 1
+        if feed is not None:
+            src, prev = feed
+            assert len(src) == len(rows)
+            ids = [prev[j] if j >= 0 else t for j, t in zip(src, ids)]
+            self.fed += 1
         return [nxt(int(t), int(p)) for t, p in zip(ids, pos)]
 
     def _decode_collect(self, ctx, handle):
@@ -133,15 +145,19 @@ def test_grouped_rollout_host_logic(num_blocks, lens, G, new, eos):
 
 @pytest.mark.parametrize("eos", [None, EOS])
 def test_pipelined_decode_matches_synchronous(eos):
-    """Submitting step k+1 before step k's bookkeeping (speculating on EOS) gives exactly the
-    synchronous scheduler's completions and leaves no page referenced."""
+    """Submitting step k+1 before step k's bookkeeping (speculating on EOS) -- with its inputs
+    from the host after step k's read-back, or gathered from step k's samples before it -- gives
+    exactly the synchronous scheduler's completions and leaves no page referenced."""
     rng = np.random.default_rng(1)
     prompts = [rng.integers(0, V, int(L)).tolist() for L in rng.integers(64, 513, 16)]
     outs = []
-    for pipe in (False, True):
+    for pipe, fed in ((False, False), (True, False), (True, True)):
         m = HostGrouped(400)
         m.pipeline_decode = pipe
+        m.feed_on_device = fed
         outs.append(m.generate_grouped_with_logprobs([torch.tensor([p]) for p in prompts], 8, max_new_tokens=300,
                                                      temperature=1.0, top_k=None, eos_token_ids=eos))
         assert (m.pipelined > 0) == pipe
-    assert outs[0][0] == outs[1][0] and outs[0][1] == outs[1][1]
+        assert (m.fed > 0) == fed
+    for o in outs[1:]:
+        assert outs[0][0] == o[0] and outs[0][1] == o[1]
