@@ -783,11 +783,11 @@ class Qwen3ForCausalLM(nn.Module):
         torch.cuda.synchronize()
         self._has_cuda_graphs = True
 
-    def _graph_fits(self, bs, arrays=None):
-        """A captured decode graph covers ``bs`` rows (and the block-table width of ``arrays``)."""
+    def _graph_fits(self, bs, width=0):
+        """A captured decode graph covers ``bs`` rows with block tables ``width`` pages wide."""
         if not self._has_cuda_graphs or _round_bs(bs, self._graph_bs) is None:
             return False
-        return arrays is None or arrays[3].shape[1] <= self._graph_max_blocks
+        return width <= self._graph_max_blocks
 
     def _run_decode_graph(self, seqs, rng_counter, rng_seed, groups=None, arrays=None, feed=None):
         """Fill the static inputs with one H2D copy, replay, return (tokens, logp) device views.
@@ -1490,7 +1490,7 @@ def _generate_grouped(model, prompts, G, max_new_tokens, temperature, top_k, eos
         while True:
             nplan = plan_step(rows)  # overlaps the step in flight
             h_nxt = None
-            if nplan is not None and model._graph_fits(len(nplan[0]), nplan[2]):
+            if nplan is not None and model._graph_fits(len(nplan[0]), nplan[2][2].shape[1]):
                 # step k+1 is queued behind step k before k is read back: its input tokens are
                 # step k's samples, gathered on the device (a row new to k+1 brings its own)
                 src = nplan[3]

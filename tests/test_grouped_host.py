@@ -45,7 +45,7 @@ class HostGrouped(Qwen3ForCausalLM):
         ctx["toks"] = toks
         assert len(toks) == n_samples
 
-    def _graph_fits(self, bs, arrays=None):
+    def _graph_fits(self, bs, width=0):
         return self.feed_on_device
 
     # pipelined decode steps: the input token of a row comes from the host (the previous step's
