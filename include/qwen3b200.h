@@ -343,6 +343,15 @@ int qb_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
                     int b_mn_major, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int mode,
                     int* err, qb_stream_t stream);
+/* gate_up projection fused with SwiGLU (Qwen3MLP.forward's gate_up_proj then silu(gate) * up,
+ * qwen3_naive.py:692-701) in one GEMM:
+ *   H[M, I] = bf16( silu(g) * u ),  g = bf16(A . W[0:I]^T), u = bf16(A . W[I:2I]^T)
+ * with W the [2I, K] gate_up weight (gate rows first, ldw >= K) -- the same bits as qb_gemm_bf16
+ * into [M, 2I] followed by qb_silu_mul_fwd.  GU (nullable, [M, ldgu >= 2I]) also receives the bf16
+ * gate_up product (what the backward, qb_silu_mul_bwd, reads).  flags: 0 or QB_GEMM_B_STATIC.
+ * A, W 16-byte aligned, lda, ldw % 8 == 0; any ldh >= I. */
+int qb_gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t ldw, void* H, int64_t ldh, void* GU,
+                   int64_t ldgu, int64_t M, int64_t I, int64_t K, int flags, int* err, qb_stream_t stream);
 /* The tile layout qb_gemm_bf16 / qb_gemm_bf16_ex choose for an M x N x K product (B MN-major or
  * not): *pair = 1 for 256-row tiles on a CTA pair, *tile_n = the tile's width (N), *split = the
  * number of CTAs a 128 x 128 tile's K range is split over (1: none).  Needs the current device

@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "qb_gemm_bf16_ex": (I, [P, L, I, P, L, I, P, L, L, L, L, I, P, P]),
     "qb_set_pdl": (I, [I]),
     "qb_get_pdl": (I, []),
+    "qb_gemm_swiglu": (I, [P, L, P, L, P, L, P, L, L, L, L, I, P, P]),
     "qb_gemm_plan": (I, [L, L, L, I, P, P, P]),
     "qb_f32_to_bf16": (I, [P, P, L, P]),
     "qb_accumulate_bf16": (I, [P, P, L, P]),

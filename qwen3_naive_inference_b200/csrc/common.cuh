@@ -113,6 +113,10 @@ QB_DEVICE float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
+// SiLU as the SwiGLU kernels and the GEMM's SwiGLU epilogue compute it (one definition, so the
+// fused and unfused paths give the same bits): fp32, IEEE divide, CUDA's expf.
+QB_DEVICE float qb_silu(float g) { return g / (1.0f + expf(-g)); }
+
 QB_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -37,6 +37,12 @@ struct GemmParams {
   float* tgt_logit;        // [M] fp32 logit at the target column
   int n_part;              // row pitch of lse_part (= number of N tiles of the launch)
   int b_static;            // B is written by no kernel still in flight: it may be read before the PDL wait
+  // MODE 4 (gate_up projection -> SwiGLU): B is the [2*half, K] gate_up weight (gate rows, then up
+  // rows); an N tile of width BN holds BN/2 gate columns and the same BN/2 up columns; C receives
+  // silu(gate) * up [M, N = half], C2 (nullable) the bf16 gate_up itself [M, 2*half] for a backward.
+  void* C2;
+  int64_t ld2;
+  int half;
 };
 
 // One epilogue thread's 32 consecutive fp32 accumulator columns of output row `row`, starting
@@ -136,6 +142,55 @@ QB_DEVICE void lse_tile(const GemmParams& p, uint32_t taddr, int row, bool row_o
   }
 }
 
+// MODE 4: this thread's row of a tile whose TMEM columns [0, BN/2) hold gate and [BN/2, BN) the
+// matching up columns.  Both are rounded to bf16 first -- the values the unfused path stores and
+// its SwiGLU kernel reads -- so the result has the same bits as gate_up GEMM + SwiGLU kernel.
+template <int BN>
+QB_DEVICE void swiglu_tile(const GemmParams& p, uint32_t taddr, int row, bool row_ok, int n0) {
+  constexpr int H = BN / 2;
+#pragma unroll 1
+  for (int c = 0; c < H; c += 32) {
+    uint32_t g[32], u[32];
+    tmem_ld32(taddr + c, g);  // warp-collective: every lane loads before any lane skips
+    tmem_ld32(taddr + H + c, u);
+    const int col = n0 + c;
+    if (!row_ok || col >= p.N) continue;
+    const bool full = col + 32 <= p.N && p.vec_ok;
+    bf16* dst = reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col;
+    bf16* gdst = p.C2 ? reinterpret_cast<bf16*>(p.C2) + (int64_t)row * p.ld2 + col : nullptr;
+    uint32_t gp[16], up[16], hp[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      gp[i] = pack_bf16x2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
+      up[i] = pack_bf16x2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+      const float2 gf = unpack_bf16x2(gp[i]), uf = unpack_bf16x2(up[i]);
+      hp[i] = pack_bf16x2(qb_silu(gf.x) * uf.x, qb_silu(gf.y) * uf.y);
+    }
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        reinterpret_cast<uint4*>(dst)[q] = make_uint4(hp[4 * q], hp[4 * q + 1], hp[4 * q + 2], hp[4 * q + 3]);
+        if (gdst) {
+          reinterpret_cast<uint4*>(gdst)[q] = make_uint4(gp[4 * q], gp[4 * q + 1], gp[4 * q + 2], gp[4 * q + 3]);
+          reinterpret_cast<uint4*>(gdst + p.half)[q] =
+              make_uint4(up[4 * q], up[4 * q + 1], up[4 * q + 2], up[4 * q + 3]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (col + i >= p.N) break;
+        const uint32_t w = i & 1 ? 16 : 0;
+        dst[i] = __ushort_as_bfloat16((unsigned short)(hp[i >> 1] >> w));
+        if (gdst) {
+          gdst[i] = __ushort_as_bfloat16((unsigned short)(gp[i >> 1] >> w));
+          gdst[p.half + i] = __ushort_as_bfloat16((unsigned short)(up[i >> 1] >> w));
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES, int MODE, bool A_MN, bool B_MN>
 struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -160,6 +215,19 @@ QB_DEVICE void load_operand(uint32_t dst, const CUtensorMap* map, int k0, int mn
     for (int a = 0; a < ROWS / 64; ++a) tma_load_2d(dst + a * 64 * 128, map, mn0 + a * 64, k0, bar);
   } else {
     tma_load_2d(dst, map, k0, mn0, bar);
+  }
+}
+
+// The B rows of N tile `tile_n` (BN rows x 64 K): one box, or in MODE 4 the tile's BN/2 gate rows
+// and the same BN/2 up rows (`half` rows further) as two boxes of BN/2 rows.
+template <int MODE, bool B_MN, int BN>
+QB_DEVICE void load_b(uint32_t sb, const CUtensorMap* map, int k0, int tile_n, int half, uint32_t bar) {
+  if constexpr (MODE == 4) {
+    static_assert(!B_MN, "the SwiGLU epilogue reads K-major weights");
+    load_operand<B_MN, BN / 2>(sb, map, k0, tile_n * (BN / 2), bar);
+    load_operand<B_MN, BN / 2>(sb + (BN / 2) * BK * 2, map, k0, half + tile_n * (BN / 2), bar);
+  } else {
+    load_operand<B_MN, BN>(sb, map, k0, tile_n * BN, bar);
   }
 }
 
@@ -218,11 +286,11 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
   int pre = 0;
   uint32_t issued = 0;  // producer: per-stage bit, a load is in flight
   if (warp == 0 && lane == 0 && p.b_static && (int)blockIdx.x < n_tiles) {
-    const int n0 = ((int)blockIdx.x / p.tiles_m) * BN;
+    const int tile_n = (int)blockIdx.x / p.tiles_m;
     pre = kblocks < STAGES ? kblocks : STAGES;
     for (int s = 0; s < pre; ++s) {
       mbar_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
-      load_operand<B_MN, BN>(base + s * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmap_b, s * BK, n0, full_bar(s));
+      load_b<MODE, B_MN, BN>(base + s * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmap_b, s * BK, tile_n, p.half, full_bar(s));
       issued |= 1u << s;
     }
   }
@@ -234,7 +302,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     uint32_t phase = 0;
     uint32_t last_parity = 0;  // per-stage bit: the phase parity of its load in flight
     for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
-      const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
+      const int m0 = (t % p.tiles_m) * BM, tile_n = t / p.tiles_m;
       for (int kb = 0; kb < kblocks; ++kb) {
         // the first `pre` stages of the first tile: fresh barriers, B already requested
         const bool pre_b = t == (int)blockIdx.x && kb < pre;
@@ -242,7 +310,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         const uint32_t sa = base + stage * Cfg::STAGE_BYTES, sb = sa + Cfg::A_BYTES;
         if (!pre_b) mbar_expect_tx(full_bar(stage), Cfg::STAGE_BYTES);
         load_operand<A_MN, BM>(sa, &tmap_a, kb * BK, m0, full_bar(stage));
-        if (!pre_b) load_operand<B_MN, BN>(sb, &tmap_b, kb * BK, n0, full_bar(stage));
+        if (!pre_b) load_b<MODE, B_MN, BN>(sb, &tmap_b, kb * BK, tile_n, p.half, full_bar(stage));
         issued |= 1u << stage;
         last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -286,7 +354,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
-      const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * BN;
+      const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * (MODE == 4 ? BN / 2 : BN);
       // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
       if (__any_sync(0xffffffffu, !mbar_wait(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
@@ -295,6 +363,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
       if constexpr (MODE == 3) {
         lse_tile<BN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE, row, row_ok, n0,
                      t / p.tiles_m);
+      } else if constexpr (MODE == 4) {
+        swiglu_tile<BN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE, row, row_ok, n0);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -434,7 +504,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   const uint32_t rank = cluster_rank(), peer = rank ^ 1;
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-  const int tiles_m = (p.M + 255) / 256, tiles_n = (p.N + PBN - 1) / PBN;
+  constexpr int TN = MODE == 4 ? PBN / 2 : PBN;  // output columns of an N tile
+  static_assert(MODE != 4 || !B_MN, "the SwiGLU epilogue reads K-major weights");
+  const int tiles_m = (p.M + 255) / 256, tiles_n = (p.N + TN - 1) / TN;
   const int n_tiles = tiles_m * tiles_n;
   const int kblocks = (p.K + BK - 1) / BK;
 
@@ -470,7 +542,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     int stage = 0;
     uint32_t phase = 0;
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
-      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * PBN + (int)rank * Sh::B_ROWS;
+      // this CTA's half of B: rows [rank * PBN/2, ...) of the tile; in MODE 4 the even CTA takes the
+      // tile's gate rows and the odd CTA the same rows of up
+      const int m0 = (t % tiles_m) * 256 + (int)rank * 128,
+                n0 = MODE == 4 ? (rank ? p.half : 0) + (t / tiles_m) * TN : (t / tiles_m) * PBN + (int)rank * Sh::B_ROWS;
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
         const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
@@ -522,7 +597,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
-      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * PBN;
+      const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * TN;
       // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
       if (__any_sync(0xffffffffu, !mbar_wait_cluster(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
@@ -531,6 +606,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       if constexpr (MODE == 3) {
         lse_tile<PBN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE, row, row_ok, n0,
                       t / tiles_m);
+      } else if constexpr (MODE == 4) {
+        swiglu_tile<PBN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE, row, row_ok, n0);
       } else {
 #pragma unroll 1
         for (int c = 0; c < PBN; c += 32) {
@@ -829,7 +906,8 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cuda
       return qb_launch_status();
     attr = true;
   }
-  const int tiles = ((p.M + 255) / 256) * ((p.N + PBN - 1) / PBN);
+  constexpr int TN = MODE == 4 ? PBN / 2 : PBN;
+  const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN);
   const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
   return qb_launch_ex(kern, dim3((unsigned)(2 * pairs)), dim3(THREADS), SMEM, st, 2, true, ta, tb, p);
 }
@@ -996,6 +1074,45 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   return launch_layout<true, true>(bn, mode, ta, tb, p, st);
 }
 
+// ---------------------------------------------------------------- gate_up projection -> SwiGLU
+// H[M, I] = silu(A W_gate^T) * (A W_up^T) with W = [W_gate; W_up] the [2I, K] gate_up weight, in one
+// GEMM whose N tiles pair each gate column block with the same up block (MODE 4); GU (nullable)
+// also receives the bf16 gate_up product for a backward.  256-row tiles on CTA pairs (128 gate +
+// 128 up columns) when they fill every SM pair, else single-CTA tiles of 96 + 96 or 128 + 128
+// columns by the busiest SM's operand bytes.
+int gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t ldw, void* H, int64_t ldh, void* GU, int64_t ldgu,
+                int64_t M, int64_t I, int64_t K, int flags, int* err, cudaStream_t st) {
+  QB_CHECK_ARG(M >= 0 && I > 0 && K > 0 && (flags & ~QB_GEMM_B_STATIC) == 0);
+  if (M == 0) return QB_OK;
+  QB_CHECK_ARG(A && W && H && al16(A) && al16(W) && lda % 8 == 0 && ldw % 8 == 0 && lda >= K && ldw >= K);
+  QB_CHECK_ARG(ldh >= I && (GU == nullptr || ldgu >= 2 * I));
+  QB_CHECK_ARG(M < (1ll << 31) && I < (1ll << 30) && K < (1ll << 31));
+  const int vec_ok = al16(H) && ldh % 8 == 0 && (GU == nullptr || (al16(GU) && ldgu % 8 == 0 && I % 8 == 0));
+  const int sms = sm_count();
+  const int64_t tm = (M + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
+  const bool pair = M >= 256 && ((M + 255) / 256) * ((I + 127) / 128) >= sms / 2;
+  int bn = 256;
+  if (!pair) {
+    int64_t best = -1;
+    for (int cand = 192; cand <= 256; cand += 64) {
+      const int64_t tiles = tm * ((I + cand / 2 - 1) / (cand / 2));
+      const int64_t c = (tiles + sms - 1) / sms * kblocks * (int64_t)(BM + cand) * BK * 2;
+      if (best < 0 || c < best) { best = c; bn = cand; }
+    }
+  }
+  CUtensorMap ta, tb;
+  if (!operand_tmap(&ta, A, false, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
+  if (!operand_tmap(&tb, W, false, (uint64_t)(2 * I), (uint64_t)K, (uint64_t)ldw, (uint32_t)(pair ? 128 : bn / 2)))
+    return QB_ERR_INVALID;
+  GemmParams p{H, ldh, (int)M, (int)I, (int)K, (int)tm, (int)((I + bn / 2 - 1) / (bn / 2)), vec_ok, err};
+  p.b_static = (flags & QB_GEMM_B_STATIC) ? 1 : 0;
+  p.C2 = GU;
+  p.ld2 = ldgu;
+  p.half = (int)I;
+  if (pair) return launch_pair<4, false, false, 256>(ta, tb, p, st);
+  return bn == 256 ? launch<256, 4, 4, false, false>(ta, tb, p, st) : launch<192, 5, 4, false, false>(ta, tb, p, st);
+}
+
 // ---------------------------------------------------------------- lm_head -> log-softmax -> gather
 // The per-tile (max, sum of exp) pairs of a row are merged into the row's log-sum-exp, and the
 // target's log-prob is its fp32 logit minus that.  One warp per row.
@@ -1086,6 +1203,12 @@ extern "C" int qb_lm_head_logprob(const void* h, int64_t ldh, const void* W, int
                                   void* logits, int64_t ld_logits, void* workspace, int* err, qb_stream_t stream) {
   return lm_head_logprob(h, ldh, W, ldw, n, V, K, targets, dest, logp, lse, logits, ld_logits, workspace, err,
                          (cudaStream_t)stream);
+}
+
+extern "C" int qb_gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t ldw, void* H, int64_t ldh, void* GU,
+                              int64_t ldgu, int64_t M, int64_t I, int64_t K, int flags, int* err,
+                              qb_stream_t stream) {
+  return gemm_swiglu(A, lda, W, ldw, H, ldh, GU, ldgu, M, I, K, flags, err, (cudaStream_t)stream);
 }
 
 extern "C" int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int* pair, int* tile_n, int* split) {

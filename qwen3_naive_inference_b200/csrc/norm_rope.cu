@@ -641,7 +641,7 @@ qk_norm_rope_bwd8_kernel(QkNormRopeBwdParams p) {
 }
 
 // ---------------------------------------------------------------- SwiGLU / adds
-QB_DEVICE float silu_f(float g) { return g / (1.0f + expf(-g)); }
+QB_DEVICE float silu_f(float g) { return qb_silu(g); }
 
 // One row per 128-thread block; a thread's (up to SILU_MAXV) 16-byte vectors of the row are all
 // loaded before any is used.  Rows are the block index, so no per-element index division.

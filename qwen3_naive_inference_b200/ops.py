@@ -23,7 +23,7 @@ from ._lib import NativeError, check
 __all__ = [
     "NativeError", "lib", "stream_ptr", "err_flag", "check_device_errors", "embedding", "rmsnorm",
     "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "qk_norm_rope_attention", "attention_packed", "attention_paged_prefill",
-    "paged_decode_attention", "silu_mul", "add", "linear", "logprob", "sample", "grpo_advantage",
+    "paged_decode_attention", "silu_mul", "add", "linear", "swiglu_linear", "logprob", "sample", "grpo_advantage",
     "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan", "lm_head_logprob",
     "grpo_logit_loss",
 ]
@@ -585,6 +585,60 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         # a Parameter is written only by the optimizer's kernels, finished before any forward
         y = gemm(x2, w2, b_static=isinstance(w, torch.nn.Parameter))
     return y.view(*shape[:-1], w.shape[0])
+
+
+def _gemm_swiglu(x2, w, with_gu, b_static):
+    M, K = x2.shape
+    I = w.shape[0] // 2
+    h = torch.empty(M, I, dtype=BF16, device=x2.device)
+    gu = torch.empty(M, 2 * I, dtype=BF16, device=x2.device) if with_gu else None
+    check(lib().qb_gemm_swiglu(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(h), I, _p(gu) if with_gu else 0,
+                               2 * I, M, I, K, QB_GEMM_B_STATIC if b_static else 0, _p(err_flag()),
+                               stream_ptr()), "qb_gemm_swiglu")
+    return h, gu
+
+
+class _SwigluLinear(torch.autograd.Function):
+    """h = silu(x W_gate^T) * (x W_up^T) in one GEMM (SwiGLU in its epilogue); the bf16 gate_up
+    product is kept for the backward, which is the unfused one: SwiGLU backward, then dX and dW of
+    the gate_up projection."""
+
+    @staticmethod
+    def forward(ctx, x2, w, grad32):
+        h, gu = _gemm_swiglu(x2, w, True, False)
+        ctx.save_for_backward(x2, w, gu)
+        ctx.grad32 = grad32
+        return h
+
+    @staticmethod
+    def backward(ctx, d):
+        x2, w, gu = ctx.saved_tensors
+        d = d.contiguous()
+        dgu = torch.empty_like(gu)
+        check(lib().qb_silu_mul_bwd(_p(d), _p(gu), gu.shape[0], gu.shape[1] // 2, _p(dgu), stream_ptr()),
+              "qb_silu_mul_bwd")
+        dx = gemm_ex(dgu, False, w, True) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            if ctx.grad32 is not None:
+                gemm_ex(dgu, True, x2, True, out=ctx.grad32, mode=2)
+            else:
+                dw = gemm_ex(dgu, True, x2, True)
+        return dx, dw, None
+
+
+def swiglu_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``silu_mul(linear(x, w))`` for the [2I, in] gate_up weight (gate rows first) in one fused
+    GEMM: the same bits as the two-kernel path."""
+    _cuda(x, w)
+    shape = x.shape
+    x2 = _gemm_operand(x.reshape(-1, shape[-1]))
+    w2 = _gemm_operand(w)
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
+        h = _SwigluLinear.apply(x2, w2, grad32_target(w) if w.requires_grad else None)
+    else:
+        h, _ = _gemm_swiglu(x2, w2, False, isinstance(w, torch.nn.Parameter))
+    return h.view(*shape[:-1], w.shape[0] // 2)
 
 
 # ---------------------------------------------------------------- log-prob / sampling

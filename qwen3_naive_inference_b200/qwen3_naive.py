@@ -377,7 +377,7 @@ class Qwen3MLP(nn.Module):
     def forward(self, x):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1])
-        h = ops.silu_mul(ops.linear(x2, self.gate_up_proj.weight))
+        h = ops.swiglu_linear(x2, self.gate_up_proj.weight)  # gate_up GEMM with SwiGLU in its epilogue
         return ops.linear(h, self.down_proj.weight).view(*shape[:-1], -1)
 
 

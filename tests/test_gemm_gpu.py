@@ -126,3 +126,43 @@ def test_gemm_k_tail_k_major(cuda):
     c = ops.gemm_ex(a.contiguous(), False, b.contiguous(), False)
     r = ref(a, b)
     assert (c.float() - r).abs().max().item() <= 1e-2 * r.abs().max().item()
+
+
+@pytest.mark.parametrize("M,I,K", [
+    (512, 3072, 1024),   # decode step: single-CTA tiles of 96 gate + 96 up columns, one wave
+    (300, 3000, 1000),   # M, I (not a multiple of the half tile) and K tails
+    (2048, 3072, 1024),  # 256-row tiles on CTA pairs (128 gate + 128 up columns)
+    (1000, 3072, 520),   # pairs with an M tail and a K tail
+    (7, 200, 64),
+])
+def test_gemm_swiglu_matches_unfused(cuda, M, I, K):
+    """The gate_up GEMM with SwiGLU in its epilogue gives the bits of the gate_up GEMM followed by
+    the SwiGLU kernel, and its optional gate_up output the bits of the plain GEMM."""
+    g = torch.Generator(device=cuda).manual_seed(M + I + K)
+    x = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * I, K, device=cuda, generator=g) * K ** -0.5).to(torch.bfloat16)
+    gu_ref = ops.gemm(x, w)
+    h_ref = ops.silu_mul(gu_ref)
+    h, gu = ops._gemm_swiglu(x, w, True, False)
+    assert torch.equal(gu, gu_ref)
+    assert torch.equal(h, h_ref)
+    h2, none = ops._gemm_swiglu(x, w, False, True)
+    assert none is None and torch.equal(h2, h_ref)
+    ops.check_device_errors()
+
+
+def test_swiglu_linear_autograd(cuda):
+    """Forward and gradients of the fused op equal those of linear + silu_mul."""
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x0 = torch.randn(600, 1024, device=cuda, generator=g).to(torch.bfloat16)
+    w0 = (torch.randn(2 * 3072, 1024, device=cuda, generator=g) * 0.03).to(torch.bfloat16)
+    d = torch.randn(600, 3072, device=cuda, generator=g).to(torch.bfloat16)
+    outs = []
+    for fused in (False, True):
+        x = x0.clone().requires_grad_(True)
+        w = w0.clone().requires_grad_(True)
+        h = ops.swiglu_linear(x, w) if fused else ops.silu_mul(ops.linear(x, w))
+        h.backward(d)
+        outs.append((h.detach(), x.grad, w.grad))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
