@@ -352,6 +352,21 @@ int qb_gemm_bf16_ex(const void* A, int64_t lda, int a_mn_major, const void* B, i
  * A, W 16-byte aligned, lda, ldw % 8 == 0; any ldh >= I. */
 int qb_gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t ldw, void* H, int64_t ldh, void* GU,
                    int64_t ldgu, int64_t M, int64_t I, int64_t K, int flags, int* err, qb_stream_t stream);
+/* qkv projection fused with QK-norm + RoPE and the paged K/V store (Qwen3Attention: qkv_proj,
+ * q_norm / k_norm, the Triton RoPE and store_kvcache, qwen3_naive.py:608-627, :664-669) in one GEMM:
+ * the projection A . W^T ([M, N = (hq + 2 hkv) * 128], W [N, K]) is rounded to bf16 per element and
+ * each 128-wide head is then normed and rotated exactly as qb_qk_norm_rope_fwd does -- the same bits.
+ * Outputs, each nullable: out [M, ld_out] (rotated q, k and the v columns), raw [M, ld_raw] (the
+ * bf16 projection, for a backward), q_out [M, hq, 128], k_cache / v_cache [num_slots, hkv, 128]
+ * (row slot_mapping[r] <- rotated k / v of row r; -1 skips), q_rstd [M, hq] / k_rstd [M, hkv].
+ * cos_sin [max_pos, 128] fp32, 8-byte aligned; norm weights 4-byte aligned; every bf16 output
+ * 16-byte aligned with a leading dimension % 8 == 0.  flags: 0 or QB_GEMM_B_STATIC. */
+int qb_gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, int64_t ldw, int64_t M, int hq, int hkv,
+                         int64_t K, const int64_t* positions, const float* cos_sin, int64_t max_pos,
+                         const void* q_norm_w, const void* k_norm_w, float eps, void* out, int64_t ld_out,
+                         void* raw, int64_t ld_raw, void* q_out, void* k_cache, void* v_cache,
+                         const int32_t* slot_mapping, int64_t num_slots, float* q_rstd, float* k_rstd, int flags,
+                         int* err, qb_stream_t stream);
 /* The tile layout qb_gemm_bf16 / qb_gemm_bf16_ex choose for an M x N x K product (B MN-major or
  * not): *pair = 1 for 256-row tiles on a CTA pair, *tile_n = the tile's width (N), *split = the
  * number of CTAs a 128 x 128 tile's K range is split over (1: none).  Needs the current device

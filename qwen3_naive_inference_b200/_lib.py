@@ -61,6 +61,8 @@ SIGNATURES: dict[str, tuple] = {
     "qb_set_pdl": (I, [I]),
     "qb_get_pdl": (I, []),
     "qb_gemm_swiglu": (I, [P, L, P, L, P, L, P, L, L, L, L, I, P, P]),
+    "qb_gemm_qk_norm_rope": (I, [P, L, P, L, L, I, I, L, P, P, L, P, P, F, P, L, P, L, P, P, P, P, L, P, P, I, P,
+                                 P]),
     "qb_gemm_plan": (I, [L, L, L, I, P, P, P]),
     "qb_f32_to_bf16": (I, [P, P, L, P]),
     "qb_accumulate_bf16": (I, [P, P, L, P]),

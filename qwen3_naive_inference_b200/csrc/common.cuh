@@ -117,6 +117,29 @@ QB_DEVICE float2 unpack_bf16x2(uint32_t u) {
 // fused and unfused paths give the same bits): fp32, IEEE divide, CUDA's expf.
 QB_DEVICE float qb_silu(float g) { return g / (1.0f + expf(-g)); }
 
+// QK-norm + RoPE arithmetic shared by the standalone kernel and the qkv GEMM's epilogue, with the
+// fused multiply-adds written out so both give the same bits (a 128-wide head; RoPE pairs (j, j+64)).
+// Sum of squares of eight consecutive elements of a head, in order.
+QB_DEVICE float qk_sumsq8(const float (&v)[8]) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = fmaf(v[i], v[i], s);
+  return s;
+}
+// The head's sum of squares from its sixteen 8-element partial sums p[g] (elements 8g..8g+7),
+// combined in the order of a half-warp butterfly over offsets 8, 4, 2, 1.
+QB_DEVICE float qk_sumsq_tree(const float (&p)[16]) {
+  float t[8], u[4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t[i] = p[i] + p[i + 8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) u[i] = t[i] + t[i + 4];
+  return (u[0] + u[2]) + (u[1] + u[3]);
+}
+QB_DEVICE float qk_rstd(float ss, float eps) { return rsqrtf(ss / 128.0f + eps); }
+QB_DEVICE float qk_rope_lo(float x1, float x2, float c, float s) { return fmaf(x1, c, -(x2 * s)); }  // x1*c - x2*s
+QB_DEVICE float qk_rope_hi(float x2, float x1, float c, float s) { return fmaf(x2, c, x1 * s); }     // x2*c + x1*s
+
 QB_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -43,6 +43,25 @@ struct GemmParams {
   void* C2;
   int64_t ld2;
   int half;
+  // MODE 5 (qkv projection -> QK-norm + RoPE, + paged KV store): the output columns are 128-wide
+  // heads, q heads [0, hq), k heads [hq, hq+hkv), then v; C (nullable) receives the rotated q/k and
+  // the v columns, C2 (nullable) the bf16 projection itself.
+  struct QkEpilogue {
+    const int64_t* positions;  // [M]
+    const float* cos_sin;      // [max_pos, 128]: cos | sin
+    int64_t max_pos;
+    const bf16* qw;            // q_norm / k_norm weights [128]
+    const bf16* kw;
+    float eps;
+    int hq, hkv;
+    bf16* q_out;               // nullable [M, hq, 128] rotated q
+    bf16* k_cache;             // nullable [num_slots, hkv, 128]: rotated k of row r at slots[r]
+    bf16* v_cache;             //                                   raw v
+    const int32_t* slots;      // [M], -1 skips the store
+    int64_t num_slots;
+    float* q_rstd;             // nullable [M, hq] / [M, hkv] for a backward
+    float* k_rstd;
+  } qk;
 };
 
 // One epilogue thread's 32 consecutive fp32 accumulator columns of output row `row`, starting
@@ -188,6 +207,90 @@ QB_DEVICE void swiglu_tile(const GemmParams& p, uint32_t taddr, int row, bool ro
         }
       }
     }
+  }
+}
+
+// MODE 5: this thread's row of a tile of whole 128-wide heads.  The projection is rounded to bf16
+// (the value the unfused path stores), then QK-norm and RoPE follow the standalone kernel's
+// arithmetic step for step (its half-warp reduction order included), so the bits are the same.
+QB_DEVICE void st_head(bf16* dst, const uint32_t (&x)[64]) {
+#pragma unroll
+  for (int q = 0; q < 16; ++q)
+    reinterpret_cast<uint4*>(dst)[q] = make_uint4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+}
+
+template <int BN>
+QB_DEVICE void qknorm_tile(const GemmParams& p, uint32_t taddr, int row, bool row_ok, int n0) {
+  static_assert(BN % 128 == 0, "whole heads per tile");
+  const GemmParams::QkEpilogue& e = p.qk;
+#pragma unroll 1
+  for (int hh = 0; hh < BN / 128; ++hh) {
+    uint32_t x[64];  // the head's 128 values as bf16 pairs
+#pragma unroll
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + hh * 128 + c, r);  // warp-collective: every lane loads before any lane skips
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[c / 2 + i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    }
+    const int col = n0 + hh * 128;
+    if (!row_ok || col >= p.N) continue;
+    const int head = col / 128;
+    const bool is_q = head < e.hq, is_v = head >= e.hq + e.hkv;
+    if (p.C2) st_head(reinterpret_cast<bf16*>(p.C2) + (int64_t)row * p.ld2 + col, x);
+    int64_t slot = -1;
+    if (e.k_cache) {
+      slot = e.slots[row];
+      if (slot >= e.num_slots || slot < -1) {
+        qb_set_err(p.err, QB_DEVERR_SLOT);
+        slot = -1;
+      }
+    }
+    bf16* out = p.C ? reinterpret_cast<bf16*>(p.C) + (int64_t)row * p.ldc + col : nullptr;
+    if (is_v) {  // v: the projection itself (and into the cache)
+      if (out) st_head(out, x);
+      if (slot >= 0) st_head(e.v_cache + (slot * e.hkv + (head - e.hq - e.hkv)) * 128, x);
+      continue;
+    }
+    int64_t pos = e.positions[row];
+    if (pos < 0 || pos >= e.max_pos) {
+      qb_set_err(p.err, QB_DEVERR_SHAPE);
+      pos = 0;
+    }
+    float part[16];
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+      float v8[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(x[4 * g + i]);
+        v8[2 * i] = f.x;
+        v8[2 * i + 1] = f.y;
+      }
+      part[g] = qk_sumsq8(v8);
+    }
+    const float rstd = qk_rstd(qk_sumsq_tree(part), e.eps);
+    const bf16* w = is_q ? e.qw : e.kw;
+    const float* cs = e.cos_sin + pos * 128;
+#pragma unroll
+    for (int j = 0; j < 64; j += 2) {  // RoPE pairs (j, j+64) and (j+1, j+65)
+      const float2 lo = unpack_bf16x2(x[j / 2]), hi = unpack_bf16x2(x[32 + j / 2]);
+      const float2 wl = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + j));
+      const float2 wh = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + 64 + j));
+      const float2 c = *reinterpret_cast<const float2*>(cs + j), sn = *reinterpret_cast<const float2*>(cs + 64 + j);
+      const float xl0 = round_bf16((lo.x * rstd) * wl.x), xl1 = round_bf16((lo.y * rstd) * wl.y);
+      const float xh0 = round_bf16((hi.x * rstd) * wh.x), xh1 = round_bf16((hi.y * rstd) * wh.y);
+      x[j / 2] = pack_bf16x2(qk_rope_lo(xl0, xh0, c.x, sn.x), qk_rope_lo(xl1, xh1, c.y, sn.y));
+      x[32 + j / 2] = pack_bf16x2(qk_rope_hi(xh0, xl0, c.x, sn.x), qk_rope_hi(xh1, xl1, c.y, sn.y));
+    }
+    if (is_q) {
+      if (e.q_rstd) e.q_rstd[(int64_t)row * e.hq + head] = rstd;
+      if (e.q_out) st_head(e.q_out + ((int64_t)row * e.hq + head) * 128, x);
+    } else {
+      if (e.k_rstd) e.k_rstd[(int64_t)row * e.hkv + (head - e.hq)] = rstd;
+      if (slot >= 0) st_head(e.k_cache + (slot * e.hkv + (head - e.hq)) * 128, x);
+    }
+    if (out) st_head(out, x);
   }
 }
 
@@ -365,6 +468,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                      t / p.tiles_m);
       } else if constexpr (MODE == 4) {
         swiglu_tile<BN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE, row, row_ok, n0);
+      } else if constexpr (MODE == 5) {
+        qknorm_tile<BN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Cfg::ACC_STRIDE, row, row_ok, n0);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -608,6 +713,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
                       t / tiles_m);
       } else if constexpr (MODE == 4) {
         swiglu_tile<PBN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE, row, row_ok, n0);
+      } else if constexpr (MODE == 5) {
+        qknorm_tile<PBN>(p, tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE, row, row_ok, n0);
       } else {
 #pragma unroll 1
         for (int c = 0; c < PBN; c += 32) {
@@ -1113,6 +1220,53 @@ int gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t ldw, void* H,
   return bn == 256 ? launch<256, 4, 4, false, false>(ta, tb, p, st) : launch<192, 5, 4, false, false>(ta, tb, p, st);
 }
 
+// ---------------------------------------------------------------- qkv projection -> QK-norm + RoPE
+// The qkv projection (N = (hq + 2 hkv) * 128) with QK-norm, RoPE and the paged K/V store in its
+// epilogue (MODE 5): whole heads per tile, 256-row tiles on CTA pairs when they fill every SM pair,
+// else single-CTA tiles of one or two heads by the busiest SM's operand bytes.
+int gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, int64_t ldw, int64_t M, int hq, int hkv, int64_t K,
+                      const GemmParams::QkEpilogue& qk, void* out, int64_t ld_out, void* raw, int64_t ld_raw,
+                      int flags, int* err, cudaStream_t st) {
+  QB_CHECK_ARG(M >= 0 && hq > 0 && hkv > 0 && K > 0 && (flags & ~QB_GEMM_B_STATIC) == 0);
+  if (M == 0) return QB_OK;
+  const int64_t N = (int64_t)(hq + 2 * hkv) * 128;
+  QB_CHECK_ARG(A && W && al16(A) && al16(W) && lda % 8 == 0 && ldw % 8 == 0 && lda >= K && ldw >= K);
+  QB_CHECK_ARG(qk.positions && qk.cos_sin && qk.max_pos > 0 && qk.qw && qk.kw);
+  QB_CHECK_ARG((reinterpret_cast<uintptr_t>(qk.cos_sin) & 7) == 0 && (reinterpret_cast<uintptr_t>(qk.qw) & 3) == 0 &&
+               (reinterpret_cast<uintptr_t>(qk.kw) & 3) == 0);
+  QB_CHECK_ARG(out == nullptr || (al16(out) && ld_out >= N && ld_out % 8 == 0));
+  QB_CHECK_ARG(raw == nullptr || (al16(raw) && ld_raw >= N && ld_raw % 8 == 0));
+  QB_CHECK_ARG(qk.q_out == nullptr || al16(qk.q_out));
+  QB_CHECK_ARG((qk.k_cache == nullptr) == (qk.v_cache == nullptr));
+  QB_CHECK_ARG(qk.k_cache == nullptr || (al16(qk.k_cache) && al16(qk.v_cache) && qk.slots && qk.num_slots > 0));
+  QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
+  const int sms = sm_count();
+  const int64_t tm = (M + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
+  const bool pair = M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2;
+  int bn = 256;
+  if (!pair) {
+    int64_t best = -1;
+    for (int cand = 128; cand <= 256; cand += 128) {
+      const int64_t tiles = tm * ((N + cand - 1) / cand);
+      const int64_t c = (tiles + sms - 1) / sms * kblocks * (int64_t)(BM + cand) * BK * 2;
+      if (best < 0 || c < best) { best = c; bn = cand; }
+    }
+  }
+  CUtensorMap ta, tb;
+  if (!operand_tmap(&ta, A, false, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
+  if (!operand_tmap(&tb, W, false, (uint64_t)N, (uint64_t)K, (uint64_t)ldw, (uint32_t)(pair ? 128 : bn)))
+    return QB_ERR_INVALID;
+  GemmParams p{out, ld_out, (int)M, (int)N, (int)K, (int)tm, (int)((N + bn - 1) / bn), 1, err};
+  p.b_static = (flags & QB_GEMM_B_STATIC) ? 1 : 0;
+  p.C2 = raw;
+  p.ld2 = ld_raw;
+  p.qk = qk;
+  p.qk.hq = hq;
+  p.qk.hkv = hkv;
+  if (pair) return launch_pair<5, false, false, 256>(ta, tb, p, st);
+  return bn == 256 ? launch<256, 4, 5, false, false>(ta, tb, p, st) : launch<128, 6, 5, false, false>(ta, tb, p, st);
+}
+
 // ---------------------------------------------------------------- lm_head -> log-softmax -> gather
 // The per-tile (max, sum of exp) pairs of a row are merged into the row's log-sum-exp, and the
 // target's log-prob is its fp32 logit minus that.  One warp per row.
@@ -1209,6 +1363,18 @@ extern "C" int qb_gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t
                               int64_t ldgu, int64_t M, int64_t I, int64_t K, int flags, int* err,
                               qb_stream_t stream) {
   return gemm_swiglu(A, lda, W, ldw, H, ldh, GU, ldgu, M, I, K, flags, err, (cudaStream_t)stream);
+}
+
+extern "C" int qb_gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, int64_t ldw, int64_t M, int hq, int hkv,
+                                    int64_t K, const int64_t* positions, const float* cos_sin, int64_t max_pos,
+                                    const void* q_norm_w, const void* k_norm_w, float eps, void* out, int64_t ld_out,
+                                    void* raw, int64_t ld_raw, void* q_out, void* k_cache, void* v_cache,
+                                    const int32_t* slot_mapping, int64_t num_slots, float* q_rstd, float* k_rstd,
+                                    int flags, int* err, qb_stream_t stream) {
+  GemmParams::QkEpilogue qk{positions, cos_sin, max_pos, (const bf16*)q_norm_w, (const bf16*)k_norm_w, eps, hq, hkv,
+                            (bf16*)q_out, (bf16*)k_cache, (bf16*)v_cache, slot_mapping, num_slots, q_rstd, k_rstd};
+  return gemm_qk_norm_rope(A, lda, W, ldw, M, hq, hkv, K, qk, out, ld_out, raw, ld_raw, flags, err,
+                           (cudaStream_t)stream);
 }
 
 extern "C" int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int* pair, int* tile_n, int* split) {

@@ -398,19 +398,15 @@ qk_norm_rope_fwd8_kernel(QkNormRopeParams p) {
       unpack8(raw[k], v);
       unpack8(is_q ? qwr : kwr, w);
       // RMSNorm over the head (every lane of the warp takes part in the shuffles; dead rows are 0)
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
-      ss = half_warp_sum(ss);
-      const float rstd = rsqrtf(ss / (float)HD + p.eps);
+      const float ss = half_warp_sum(qk_sumsq8(v));
+      const float rstd = qk_rstd(ss, p.eps);
       float xn[8], o[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) xn[i] = round_bf16((v[i] * rstd) * w[i]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float partner = __shfl_xor_sync(0xffffffffu, xn[i], 8);
-        o[i] = l < 8 ? xn[i] * cv[i] - partner * sv[i]   // x1*c - x2*s
-                     : xn[i] * cv[i] + partner * sv[i];  // x2*c + x1*s
+        o[i] = l < 8 ? qk_rope_lo(xn[i], partner, cv[i], sv[i]) : qk_rope_hi(xn[i], partner, cv[i], sv[i]);
       }
       if (!live) continue;
       if (is_v) {  // v: copied bit for bit (and stored into the cache)

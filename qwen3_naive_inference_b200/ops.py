@@ -22,7 +22,8 @@ from ._lib import NativeError, check
 
 __all__ = [
     "NativeError", "lib", "stream_ptr", "err_flag", "check_device_errors", "embedding", "rmsnorm",
-    "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "qk_norm_rope_attention", "attention_packed", "attention_paged_prefill",
+    "add_rmsnorm", "qk_norm_rope", "qk_norm_rope_store", "qk_norm_rope_attention", "qkv_norm_rope_store",
+    "gemm_qk_norm_rope", "qkv_attention", "attention_packed", "attention_paged_prefill",
     "paged_decode_attention", "silu_mul", "add", "linear", "swiglu_linear", "logprob", "sample", "grpo_advantage",
     "grpo_loss", "mask_sum", "build_tiles", "decode_split_plan", "lm_head_logprob",
     "grpo_logit_loss",
@@ -246,6 +247,35 @@ def qk_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv
     return q
 
 
+def gemm_qk_norm_rope(x, w, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, *, out=None, raw=None,
+                      q_out=None, k_cache=None, v_cache=None, slot_mapping=None, q_rstd=None, k_rstd=None,
+                      b_static=False):
+    """``qb_gemm_qk_norm_rope``: the qkv projection x [T, K] . w^T with QK-norm, RoPE and the paged
+    K/V store in the GEMM's epilogue (same bits as linear + qk_norm_rope[_store]).  Writes the given
+    outputs; returns nothing."""
+    _cuda(x, w, positions, cos_sin)
+    x2, w2 = _gemm_operand(x), _gemm_operand(w)
+    T, K = x2.shape
+    num_slots = 0 if k_cache is None else k_cache.numel() // (hkv * 128)
+    opt = lambda t: 0 if t is None else _p(t)  # noqa: E731
+    check(lib().qb_gemm_qk_norm_rope(_p(x2), x2.stride(0), _p(w2), w2.stride(0), T, hq, hkv, K, _p(positions),
+                                     _p(cos_sin), cos_sin.shape[0], _p(q_norm_w), _p(k_norm_w), eps, opt(out),
+                                     0 if out is None else out.stride(0), opt(raw), 0 if raw is None else raw.stride(0),
+                                     opt(q_out), opt(k_cache), opt(v_cache), opt(slot_mapping), num_slots, opt(q_rstd),
+                                     opt(k_rstd), QB_GEMM_B_STATIC if b_static else 0, _p(err_flag()), stream_ptr()),
+          "qb_gemm_qk_norm_rope")
+
+
+def qkv_norm_rope_store(x, w, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, k_cache, v_cache,
+                        slot_mapping):
+    """Paged path in one GEMM: ``qk_norm_rope_store(linear(x, w), ...)`` -- returns rotated q
+    [T, hq, 128]; rotated k and v go to the cache rows slot_mapping (inference only)."""
+    q = torch.empty(x.shape[0], hq, 128, dtype=BF16, device=x.device)
+    gemm_qk_norm_rope(x, w, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, q_out=q, k_cache=k_cache,
+                      v_cache=v_cache, slot_mapping=slot_mapping, b_static=isinstance(w, torch.nn.Parameter))
+    return q
+
+
 # ---------------------------------------------------------------- attention
 def build_tiles(lengths, block: int = 64) -> np.ndarray:
     """Host list of (sequence, first row) pairs covering each sequence in 64-row tiles."""
@@ -331,6 +361,60 @@ def qk_norm_rope_attention(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, cu_
         return _QKNormRopeAttn.apply(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, rope_grad,
                                      cu_seqlens, tiles, scale)
     rot, _, _ = _qk_norm_rope_fwd(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, save=False)
+    return _attn_packed_fwd(rot, cu_seqlens, tiles, hq, hkv, scale)[0]
+
+
+class _QkvNormRopeAttn(torch.autograd.Function):
+    """qkv projection -> QK-norm + RoPE -> packed causal attention as one autograd node: the
+    forward is one GEMM with QK-norm and RoPE in its epilogue (which also keeps the bf16 projection
+    and the rstd for the backward) and the attention kernel; the backward is the attention
+    backward, the QK-norm backward in place in its gradient buffer, then dX and dW of the
+    projection."""
+
+    @staticmethod
+    def forward(ctx, x2, w, grad32, positions, cos_sin, qw, kw, eps, hq, hkv, rope_grad, cu, tiles, scale):
+        T = x2.shape[0]
+        N = (hq + 2 * hkv) * 128
+        raw = torch.empty(T, N, dtype=BF16, device=x2.device)
+        rot = torch.empty(T, N, dtype=BF16, device=x2.device)
+        q_rstd = torch.empty(T, hq, dtype=torch.float32, device=x2.device)
+        k_rstd = torch.empty(T, hkv, dtype=torch.float32, device=x2.device)
+        gemm_qk_norm_rope(x2, w, positions, cos_sin, qw, kw, eps, hq, hkv, out=rot, raw=raw, q_rstd=q_rstd,
+                          k_rstd=k_rstd)
+        out, lse = _attn_packed_fwd(rot, cu, tiles, hq, hkv, scale)
+        ctx.save_for_backward(x2, w, raw, positions, cos_sin, qw, kw, q_rstd, k_rstd, rot, cu, tiles, out, lse)
+        ctx.cfg = (hq, hkv, rope_grad, scale)
+        ctx.grad32 = grad32
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2, w, raw, positions, cos_sin, qw, kw, q_rstd, k_rstd, rot, cu, tiles, out, lse = ctx.saved_tensors
+        hq, hkv, rope_grad, scale = ctx.cfg
+        d = _attn_packed_bwd(dout.contiguous(), rot, cu, tiles, out, lse, hq, hkv, scale)
+        dqw, dkw = _qk_norm_rope_bwd(d, d, raw, positions, cos_sin, qw, kw, q_rstd, k_rstd, hq, hkv, rope_grad)
+        dx = gemm_ex(d, False, w, True) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            if ctx.grad32 is not None:
+                gemm_ex(d, True, x2, True, out=ctx.grad32, mode=2)
+            else:
+                dw = gemm_ex(d, True, x2, True)
+        return dx, dw, None, None, None, dqw, dkw, None, None, None, None, None, None, None
+
+
+def qkv_attention(x, w, positions, cos_sin, q_norm_w, k_norm_w, eps, cu_seqlens, tiles, hq, hkv, scale,
+                  rope_grad=True):
+    """``attention_packed(qk_norm_rope(linear(x, w), ...), ...)`` with the projection, QK-norm and
+    RoPE in one GEMM (training / recompute path); returns [T, hq * 128]."""
+    _cuda(x, w, positions, cos_sin, cu_seqlens, tiles)
+    x2, w2 = _gemm_operand(x), _gemm_operand(w)
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad or q_norm_w.requires_grad):
+        return _QkvNormRopeAttn.apply(x2, w2, grad32_target(w) if w.requires_grad else None, positions, cos_sin,
+                                      q_norm_w, k_norm_w, eps, hq, hkv, rope_grad, cu_seqlens, tiles, scale)
+    rot = torch.empty(x2.shape[0], (hq + 2 * hkv) * 128, dtype=BF16, device=x2.device)
+    gemm_qk_norm_rope(x2, w2, positions, cos_sin, q_norm_w, k_norm_w, eps, hq, hkv, out=rot,
+                      b_static=isinstance(w, torch.nn.Parameter))
     return _attn_packed_fwd(rot, cu_seqlens, tiles, hq, hkv, scale)[0]
 
 

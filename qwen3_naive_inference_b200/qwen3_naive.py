@@ -300,10 +300,10 @@ class Qwen3Attention(nn.Module):
 
     def forward_packed(self, x, positions, cu_seqlens, tiles):
         """Training/recompute path over packed sequences (each attends only to itself)."""
-        qkv = ops.linear(x, self.qkv_proj.weight)
-        o = ops.qk_norm_rope_attention(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
-                                       self.k_norm.weight, self.eps, cu_seqlens, tiles, self.num_heads,
-                                       self.num_kv_heads, self.scale, rope_grad=self.rope_grad)
+        # one GEMM for the projection, QK-norm and RoPE, then the attention kernel
+        o = ops.qkv_attention(x, self.qkv_proj.weight, positions, self._cos_sin(x.device), self.q_norm.weight,
+                              self.k_norm.weight, self.eps, cu_seqlens, tiles, self.num_heads, self.num_kv_heads,
+                              self.scale, rope_grad=self.rope_grad)
         return ops.linear(o, self.o_proj.weight)
 
     def forward(self, x):
@@ -320,10 +320,10 @@ class Qwen3Attention(nn.Module):
         ``decode_tail`` = (n_prefill_rows, context_lens, block_tables, decode_plan): the rows from
         n_prefill_rows on are single decode tokens whose attention runs on the decode kernel of
         ``decode_plan`` (cu_seqlens and ``block_tables`` then describe the prefill rows only)."""
-        qkv = ops.linear(x, self.qkv_proj.weight)
-        q = ops.qk_norm_rope_store(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
-                                   self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads,
-                                   self.k_cache, self.v_cache, block_mapping)
+        # qkv projection with QK-norm, RoPE and the K/V store in the GEMM's epilogue
+        q = ops.qkv_norm_rope_store(x, self.qkv_proj.weight, positions, self._cos_sin(x.device), self.q_norm.weight,
+                                    self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads, self.k_cache,
+                                    self.v_cache, block_mapping)
         if block_tables is None:
             raise ValueError("the paged prefill kernel reads K/V through block_tables")
         if decode_tail is None:
@@ -358,10 +358,11 @@ class Qwen3Attention(nn.Module):
 
     def forward_decode(self, x, positions, context_lens, block_tables, slot_mapping=None, *, decode_plan=None):
         """One new token per sequence (qwen3_naive.py:642-683); attends to context_lens + 1 keys."""
-        qkv = ops.linear(x, self.qkv_proj.weight)
-        q = ops.qk_norm_rope_store(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
-                                   self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads,
-                                   self.k_cache, self.v_cache, slot_mapping)
+        if slot_mapping is None:
+            raise ValueError("the decode step stores the new token's K/V through slot_mapping")
+        q = ops.qkv_norm_rope_store(x, self.qkv_proj.weight, positions, self._cos_sin(x.device), self.q_norm.weight,
+                                    self.k_norm.weight, self.eps, self.num_heads, self.num_kv_heads, self.k_cache,
+                                    self.v_cache, slot_mapping)
         o = self._decode_attention(q, context_lens, block_tables, decode_plan)
         return ops.linear(o.view(x.shape[0], -1), self.o_proj.weight)
 

@@ -181,6 +181,82 @@ def test_qk_norm_rope_attention_fused_backward(cuda, rope_grad):
     assert torch.equal(o2, o0)
 
 
+@pytest.mark.parametrize("T", [512, 45, 2048])  # decode step (one head per tile), tails, CTA pairs
+def test_gemm_qk_norm_rope_matches_unfused(cuda, T):
+    """The qkv GEMM with QK-norm + RoPE (+ K/V store) in its epilogue gives the bits of the
+    projection followed by the standalone QK-norm + RoPE kernel."""
+    hq, hkv, K = 16, 8, 1024
+    N = (hq + 2 * hkv) * 128
+    g = torch.Generator(device=cuda).manual_seed(T)
+    x = torch.randn(T, K, device=cuda, generator=g).to(BF)
+    w = (torch.randn(N, K, device=cuda, generator=g) * K ** -0.5).to(BF)
+    pos = torch.randint(0, 4000, (T,), device=cuda, generator=g)
+    cs = R.rope_cache(128, 4096, 1e6).to(cuda)
+    qw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(BF)
+    kw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(BF)
+    qkv = ops.gemm(x, w)
+    # training layout: rotated copy, raw projection, rstd
+    ref_out, ref_qr, ref_kr = ops._qk_norm_rope_fwd(qkv, pos, cs, qw, kw, 1e-6, hq, hkv)
+    out, raw = torch.empty_like(qkv), torch.empty_like(qkv)
+    qr, kr = torch.empty_like(ref_qr), torch.empty_like(ref_kr)
+    ops.gemm_qk_norm_rope(x, w, pos, cs, qw, kw, 1e-6, hq, hkv, out=out, raw=raw, q_rstd=qr, k_rstd=kr)
+    assert torch.equal(raw, qkv)
+    assert torch.equal(out, ref_out)
+    assert torch.equal(qr, ref_qr) and torch.equal(kr, ref_kr)
+    # paged layout: rotated q, k/v rows into the cache (slot -1 skips the store)
+    nslots = 3 * 4096
+    slots = torch.randperm(nslots, device=cuda, generator=g)[:T].to(torch.int32)
+    slots[T // 2] = -1
+    kc0 = torch.zeros(nslots, hkv, 128, dtype=BF, device=cuda)
+    kc, vc, kc_r, vc_r = kc0.clone(), kc0.clone(), kc0.clone(), kc0.clone()
+    q_ref = ops.qk_norm_rope_store(qkv, pos, cs, qw, kw, 1e-6, hq, hkv, kc_r, vc_r, slots)
+    q = ops.qkv_norm_rope_store(x, w, pos, cs, qw, kw, 1e-6, hq, hkv, kc, vc, slots)
+    assert torch.equal(q, q_ref)
+    assert torch.equal(kc, kc_r) and torch.equal(vc, vc_r)
+    ops.check_device_errors()
+
+
+@pytest.mark.parametrize("rope_grad", [True, False])
+def test_qkv_attention_fused_matches_unfused(cuda, rope_grad):
+    """Projection + QK-norm + RoPE + attention as one node: same output and gradients as
+    linear followed by the QK-norm + attention node (norm-weight grads up to atomics order)."""
+    hq, hkv, K = 16, 8, 1024
+    lens = [700, 300, 500]
+    T = sum(lens)
+    g = torch.Generator().manual_seed(31)
+    x0 = torch.randn(T, K, generator=g).to(BF).to(cuda)
+    w0 = (torch.randn((hq + 2 * hkv) * 128, K, generator=g) * K ** -0.5).to(BF).to(cuda)
+    qw0 = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    kw0 = (1 + 0.1 * torch.randn(128, generator=g)).to(BF).to(cuda)
+    pos = torch.cat([torch.arange(n) for n in lens]).to(cuda)
+    cs = R.rope_cache(128, 4096, 1e6).to(cuda)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=cuda)
+    tiles = torch.from_numpy(ops.build_tiles(lens)).to(cuda)
+    dout = torch.randn(T, hq * 128, generator=g).to(BF).to(cuda)
+    res = []
+    for fused in (False, True):
+        x, w = x0.clone().requires_grad_(True), w0.clone().requires_grad_(True)
+        qw, kw = qw0.clone().requires_grad_(True), kw0.clone().requires_grad_(True)
+        if fused:
+            o = ops.qkv_attention(x, w, pos, cs, qw, kw, 1e-6, cu, tiles, hq, hkv, 128 ** -0.5, rope_grad=rope_grad)
+        else:
+            o = ops.qk_norm_rope_attention(ops.linear(x, w), pos, cs, qw, kw, 1e-6, cu, tiles, hq, hkv, 128 ** -0.5,
+                                           rope_grad=rope_grad)
+        o.backward(dout)
+        res.append((o.detach(), x.grad, w.grad, qw.grad, kw.grad))
+    ops.check_device_errors()
+    (o0, dx0, dw0, dq0, dk0), (o1, dx1, dw1, dq1, dk1) = res
+    assert torch.equal(o0, o1) and torch.equal(dx0, dx1) and torch.equal(dw0, dw1)
+    if rope_grad:
+        torch.testing.assert_close(dq1.float(), dq0.float(), rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(dk1.float(), dk0.float(), rtol=1e-2, atol=1e-2)
+    else:
+        assert dq1 is None and dk1 is None and dq0 is None and dk0 is None
+    with torch.no_grad():
+        o2 = ops.qkv_attention(x0, w0, pos, cs, qw0, kw0, 1e-6, cu, tiles, hq, hkv, 128 ** -0.5)
+    assert torch.equal(o2, o0)
+
+
 def test_silu_mul(cuda):
     g = gen(11)
     gu = torch.randn(19, 2 * 3072, generator=g).to(BF)
