@@ -194,13 +194,20 @@ def test_gemm_qk_norm_rope_matches_unfused(cuda, T):
     cs = R.rope_cache(128, 4096, 1e6).to(cuda)
     qw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(BF)
     kw = (1 + 0.1 * torch.randn(128, device=cuda, generator=g)).to(BF)
-    qkv = ops.gemm(x, w)
+    plain = ops.gemm(x, w)
     # training layout: rotated copy, raw projection, rstd
-    ref_out, ref_qr, ref_kr = ops._qk_norm_rope_fwd(qkv, pos, cs, qw, kw, 1e-6, hq, hkv)
-    out, raw = torch.empty_like(qkv), torch.empty_like(qkv)
-    qr, kr = torch.empty_like(ref_qr), torch.empty_like(ref_kr)
+    out, raw = torch.empty_like(plain), torch.empty_like(plain)
+    qr = torch.empty(T, hq, dtype=torch.float32, device=cuda)
+    kr = torch.empty(T, hkv, dtype=torch.float32, device=cuda)
     ops.gemm_qk_norm_rope(x, w, pos, cs, qw, kw, 1e-6, hq, hkv, out=out, raw=raw, q_rstd=qr, k_rstd=kr)
-    assert torch.equal(raw, qkv)
+    # the projection: the plain GEMM's bits where it picks the same (non split-K) layout, else
+    # within its output rounding
+    if ops.gemm_plan(T, N, K)[2] == 1:
+        assert torch.equal(raw, plain)
+    else:
+        assert (raw.float() - plain.float()).abs().max().item() <= 1e-2 * plain.float().abs().max().item()
+    qkv = raw
+    ref_out, ref_qr, ref_kr = ops._qk_norm_rope_fwd(qkv, pos, cs, qw, kw, 1e-6, hq, hkv)
     assert torch.equal(out, ref_out)
     assert torch.equal(qr, ref_qr) and torch.equal(kr, ref_kr)
     # paged layout: rotated q, k/v rows into the cache (slot -1 skips the store)
