@@ -1059,16 +1059,23 @@ def run_gemm_only(shape=None):
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak = peaks.get("bf16_tflops", 1590.0)
     out = {}
+    # a custom shape "M,N,K[,1]": the optional 1 stores B [K, N] (MN-major, as the backward reads a weight)
     shapes = GEMM_SHAPES if shape is None else {"custom": tuple(int(x) for x in shape.split(","))}
-    for name, (M, N, K) in shapes.items():
+    for name, dims in shapes.items():
+        M, N, K = dims[:3]
+        b_mn = len(dims) > 3 and dims[3] == 1
         g = torch.Generator(device=dev).manual_seed(0)
         a = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         b = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        if b_mn:
+            b = b.t().contiguous()
         copies = max(1, min(64, -(-2 * 126 * 2**20 // (N * K * 2))))
         bs = [b] + [b.clone() for _ in range(copies - 1)]
         c = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         res = {}
-        for impl, fn in [("tcgen05", lambda w: ops.gemm(a, w, out=c)), ("cublas", lambda w: torch.mm(a, w.t(), out=c))]:
+        ours = (lambda w: ops.gemm_ex(a, False, w, True, out=c)) if b_mn else (lambda w: ops.gemm(a, w, out=c))
+        theirs = (lambda w: torch.mm(a, w, out=c)) if b_mn else (lambda w: torch.mm(a, w.t(), out=c))
+        for impl, fn in [("tcgen05", ours), ("cublas", theirs)]:
             for w in bs[:3]:
                 fn(w)
             torch.cuda.synchronize()
@@ -1095,8 +1102,8 @@ def run_gemm_only(shape=None):
                             if str(getattr(e, "device_type", "")).endswith("CUDA")})
             res[impl] = {"ms": ms, "tflops": 2 * M * N * K / (ms / 1000) / 1e12, "kernels": names}
             del graph
-        ref = (a.float() @ b.float().t())
-        ops.gemm(a, b, out=c)
+        ref = (a.float() @ (b.float() if b_mn else b.float().t()))
+        ours(b)
         res["max_rel_err"] = ((c.float() - ref).abs().max() / ref.abs().max()).item()
         res["frac_of_peak"] = res["tcgen05"]["tflops"] / peak
         res["weight_copies"] = len(bs)
