@@ -1109,8 +1109,9 @@ inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) =
 // The layout of one product.  256x256 tiles on CTA pairs when they fill every SM pair at least
 // once; 128 x 256 single-CTA tiles when they cover every SM at least once.  Otherwise every
 // candidate is costed by the operand bytes its busiest SM pulls: 128 x {128, 192} single-CTA
-// tiles in waves over the SMs, or 128 x 128 tiles split along K over a cluster of 2 or 4 CTAs
-// (one wave, plus the partials' exchange, costed as two K blocks).
+// tiles in waves over the SMs, 256 x 256 pair tiles in waves over the SM pairs, or 128 x 128
+// tiles split along K over a cluster of 2 or 4 CTAs (one wave, plus the partials' exchange,
+// costed as two K blocks).
 struct GemmPlan {
   bool pair;
   int bn;     // tile width (N): of the pair's 256-row tile, or of the single CTA's 128-row tile
@@ -1128,7 +1129,16 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
   int64_t best = (t128 + sms - 1) / sms * kblocks * kb_bytes;
   const int64_t c192 = (t192 + sms - 1) / sms * kblocks * (int64_t)(BM + 192) * BK * 2;
   if (N > 128 && c192 < best) { best = c192; best_plan = {false, 192, 1}; }
-  (void)b_mn;  // 256 x {128, 192} pair tiles pull fewer bytes per SM but measured slower at M = 512
+  (void)b_mn;
+  // 256 x 256 tiles on CTA pairs that do not fill every SM pair: each SM pulls (128 + 128) rows per K
+  // block for twice a 128 x 128 tile's MMA work, which long-K products need (a 128 x 128 tile's
+  // operands alone would ask ~35 TB/s of L2 at the MMA rate).  Ties go to single-CTA tiles (the
+  // decode step's M = 512 products measured slower on pairs).
+  if (M > 128 && N > 128) {
+    const int64_t pairs = ((M + 255) / 256) * ((N + 255) / 256);
+    const int64_t c = (pairs + sms / 2 - 1) / (sms / 2) * kblocks * (int64_t)(128 + 128) * BK * 2;
+    if (c < best) { best = c; best_plan = {true, 256, 1}; }
+  }
   for (int S = 2; S <= 4; S *= 2) {
     if (kblocks < 2 * S || t128 > split_clusters(S)) continue;
     const int64_t c = (kblocks + S - 1) / S * kb_bytes + 2 * kb_bytes;

@@ -26,7 +26,9 @@ def ref(a, b):
                                    # 128x192 tiles (one wave where 128x128 would need two), N and K tails
                                    (512, 6144, 1024), (500, 5000, 1000),
                                    # decode-like shapes with M, N and K tails
-                                   (480, 4096, 1024), (300, 4000, 1000), (257, 6100, 1000)])
+                                   (480, 4096, 1024), (300, 4000, 1000), (257, 6100, 1000),
+                                   # pairs below one tile per SM pair (long K), with tails
+                                   (1000, 1000, 20000), (4096, 1024, 30000)])
 def test_gemm_bf16_out(cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M * 7 + N)
     a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
@@ -113,6 +115,10 @@ def test_gemm_mn_major_operands(cuda, a_mn, b_mn, M, N, K):
     (512, 1024, 2048, False, ("single", 128, 4)),  # decode o_proj: split-K over 4-CTA clusters
     (512, 1024, 3072, False, ("single", 128, 4)),  # decode down_proj
     (7, 300, 128, False, ("single", 128, 1)),
+    # long K, too few 256 x 256 tiles to fill the SM pairs: pairs anyway (half the operand bytes
+    # per MMA cycle): the lm_head backward dh = dlogits . W and a layer's weight gradient
+    (4096, 1024, 151936, True, ("pair", 256, 1)),
+    (4096, 1024, 32768, True, ("pair", 256, 1)),
 ])
 def test_gemm_plan(cuda, M, N, K, b_mn, want):
     """The layouts the cases above rely on are the ones the dispatcher picks."""
