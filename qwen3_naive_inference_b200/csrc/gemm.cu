@@ -1132,9 +1132,9 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
   (void)b_mn;
   // 256 x 256 tiles on CTA pairs that do not fill every SM pair: each SM pulls (128 + 128) rows per K
   // block for twice a 128 x 128 tile's MMA work, which long-K products need (a 128 x 128 tile's
-  // operands alone would ask ~35 TB/s of L2 at the MMA rate).  Ties go to single-CTA tiles (the
-  // decode step's M = 512 products measured slower on pairs).
-  if (M > 128 && N > 128) {
+  // operands alone would ask ~35 TB/s of L2 at the MMA rate).  Long K only (64+ K blocks), ties to
+  // single-CTA tiles: the decode step's M = 512, K = 1024 products measured slower on pairs.
+  if (M > 128 && N > 128 && kblocks >= 64) {
     const int64_t pairs = ((M + 255) / 256) * ((N + 255) / 256);
     const int64_t c = (pairs + sms / 2 - 1) / (sms / 2) * kblocks * (int64_t)(128 + 128) * BK * 2;
     if (c < best) { best = c; best_plan = {true, 256, 1}; }
