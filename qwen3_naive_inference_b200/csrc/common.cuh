@@ -113,9 +113,13 @@ QB_DEVICE float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(v);
 }
 
-// SiLU as the SwiGLU kernels and the GEMM's SwiGLU epilogue compute it (one definition, so the
-// fused and unfused paths give the same bits): fp32, IEEE divide, CUDA's expf.
-QB_DEVICE float qb_silu(float g) { return g / (1.0f + expf(-g)); }
+// SiLU as the SwiGLU kernel and the GEMM's SwiGLU epilogue compute it (one definition, so the fused
+// and unfused paths give the same bits): fp32 with the fast exponential and divide intrinsics (a
+// few ulp of fp32, far below the bf16 rounding that follows; 1 + e^-g overflowing to inf gives 0).
+QB_DEVICE float qb_silu(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+// Requests the 128-byte line holding p into L1 (no register written).
+QB_DEVICE void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
 
 // QK-norm + RoPE arithmetic shared by the standalone kernel and the qkv GEMM's epilogue, with the
 // fused multiply-adds written out so both give the same bits (a 128-wide head; RoPE pairs (j, j+64)).

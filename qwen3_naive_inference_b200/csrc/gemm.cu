@@ -219,6 +219,17 @@ QB_DEVICE void st_head(bf16* dst, const uint32_t (&x)[64]) {
     reinterpret_cast<uint4*>(dst)[q] = make_uint4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
 }
 
+// MODE 5, before this thread's accumulator row is ready: its token's rotation-table row (512 B)
+// into L1, so the epilogue's table reads do not wait on L2.
+QB_DEVICE void qknorm_prefetch(const GemmParams& p, int row) {
+  if (row >= p.M) return;
+  int64_t pos = p.qk.positions[row];
+  if (pos < 0 || pos >= p.qk.max_pos) pos = 0;
+  const float* cs = p.qk.cos_sin + pos * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) prefetch_l1(cs + q * 32);
+}
+
 template <int BN>
 QB_DEVICE void qknorm_tile(const GemmParams& p, uint32_t taddr, int row, bool row_ok, int n0) {
   static_assert(BN % 128 == 0, "whole heads per tile");
@@ -458,6 +469,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < n_tiles && !*abort_flag; t += gridDim.x) {
       const int m0 = (t % p.tiles_m) * BM, n0 = (t / p.tiles_m) * (MODE == 4 ? BN / 2 : BN);
+      if constexpr (MODE == 5) qknorm_prefetch(p, m0 + row_in_tile);
       // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
       if (__any_sync(0xffffffffu, !mbar_wait(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
@@ -703,6 +715,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     uint32_t acc_phase = 0;
     for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
       const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * TN;
+      if constexpr (MODE == 5) qknorm_prefetch(p, m0 + row_in_tile);
       // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
       if (__any_sync(0xffffffffu, !mbar_wait_cluster(tfull_bar(acc), acc_phase, abort_flag, p.err))) break;
       tc_fence_after();
