@@ -182,12 +182,11 @@ size_t qb_paged_decode_workspace_bytes(int batch, int hq, int D, int max_splits)
  * multiple of 64.  Keys in [shared_len, kv_start) are never read, so a member's own tokens
  * may start on a fresh page after a partially filled shared prompt page; with kv_start ==
  * shared_len the result equals qb_paged_decode_attn.  The shared keys are read once per group
- * for all members' query heads and each member's own keys separately, in one launch; the CTA
- * that writes the last of a (sequence, kv head)'s split-K partials (shared_splits + own_splits
- * slots) merges them into the output.  workspace: qb_paged_decode_grouped_workspace_bytes(batch,
- * hq, D, shared_splits + own_splits) bytes: the partials, then batch * hq/2 arrival counters that
- * must be zero before the first call (every call leaves them zero); calls sharing one must not
- * overlap. */
+ * for all members' query heads and each member's own keys separately (one launch), then a
+ * second kernel merges the split-K partials (shared_splits + own_splits slots per sequence
+ * and head).  workspace: qb_paged_decode_grouped_workspace_bytes(batch, hq, D,
+ * shared_splits + own_splits) bytes, any contents (every call rewrites the partials it reads);
+ * calls sharing one must not overlap. */
 int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
                                  int64_t num_blocks, int page_size, const int32_t* block_tables,
                                  int64_t bt_stride, const int32_t* seqlens, int seqlen_add,

@@ -61,9 +61,6 @@ struct DecodeParams {
   // prefix handled elsewhere).
   int n_slots, slot_off;
   const int32_t* kv_start;
-  // nullable [batch, hkv] arrival counters (grouped decode): the CTA that writes the last of the
-  // n_slots partials of (sequence, kv head) merges them into the output and zeroes its counter
-  int* done;
 };
 
 // Marks the partial of (b, slot, h) empty (log2-domain LSE = -inf) so the merge ignores it.
@@ -349,63 +346,6 @@ __global__ void paged_decode_combine_kernel(DecodeParams p, int batch) {
   *reinterpret_cast<uint2*>(orow) = r;
 }
 
-// The split-K merge of sequence b, head h over dims [d0, d0 + ND) (ND = 2: d0 even; ND = 16: d0 a
-// multiple of 16, so every vector access is aligned): paged_decode_combine_kernel's arithmetic, in
-// slot order, so the bits are the same.  The partials were written by other CTAs: read through L2
-// (ld.global.cg), after the arrival that made this CTA the last.
-template <int ND>
-QB_DEVICE void merge_partials(const DecodeParams& p, int b, int h, int d0) {
-  static_assert(ND == 2 || ND == 16, "merge width");
-  const float* base = p.ws + ((int64_t)b * p.n_slots * p.hq + h) * WS_ROW;
-  const int64_t sstride = (int64_t)p.hq * WS_ROW;
-  float M = NEG_INF;
-  for (int s = 0; s < p.n_slots; ++s) M = fmaxf(M, __ldcg(base + s * sstride + D));
-  float W = 0.f;
-  float acc[ND];
-#pragma unroll
-  for (int i = 0; i < ND; ++i) acc[i] = 0.f;
-  for (int s = 0; s < p.n_slots; ++s) {
-    const float ls = __ldcg(base + s * sstride + D);
-    if (ls == NEG_INF) continue;  // never written
-    const float w = exp2f(ls - M);
-    W += w;
-    const float* row = base + s * sstride + d0;
-    if constexpr (ND == 2) {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(row));
-      acc[0] += w * v.x;
-      acc[1] += w * v.y;
-    } else {
-#pragma unroll
-      for (int i = 0; i < ND; i += 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(row + i));
-        acc[i] += w * v.x;
-        acc[i + 1] += w * v.y;
-        acc[i + 2] += w * v.z;
-        acc[i + 3] += w * v.w;
-      }
-    }
-  }
-  const float inv = (W > 0.f) ? 1.f / W : 0.f;
-  bf16* orow = p.out + ((int64_t)b * p.hq + h) * D + d0;
-#pragma unroll
-  for (int i = 0; i < ND; i += 2)
-    *reinterpret_cast<uint32_t*>(orow + i) = pack_bf16x2(acc[i] * inv, acc[i + 1] * inv);
-}
-
-// Arrival of an own-key CTA (sequence b, kv head kvh) after its partials: the last of the n_slots
-// writers merges both heads (thread: head tid/64, two dims) and zeroes the counter.
-QB_DEVICE void own_arrive(const DecodeParams& p, int b, int kvh, int tid) {
-  __shared__ int last;
-  __threadfence();  // this thread's partial stores, before the arrival below
-  __syncthreads();
-  if (tid == 0) last = atomicAdd(&p.done[b * p.hkv + kvh], 1) == p.n_slots - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  merge_partials<2>(p, b, kvh * 2 + (tid >> 6), (tid & 63) * 2);
-  if (tid == 0) p.done[b * p.hkv + kvh] = 0;
-}
-
 // ============================================================================
 // Shared-prefix decode attention (GRPO groups)
 // ============================================================================
@@ -636,29 +576,6 @@ QB_DEVICE void decode_shared_tile(const DecodeParams& p, const GroupParams& gp, 
   }
 }
 
-// Arrival of a shared-prefix CTA (group grp, kv head kvh) after its partials: one per member; a
-// member whose last partial this was gets merged here (thread: row tid/8 = member, head; 16 dims).
-QB_DEVICE void shared_arrive(const DecodeParams& p, const GroupParams& gp, int grp, int kvh, int tid) {
-  __shared__ int last_mask;
-  __shared__ int mems[GMAX];
-  __threadfence();
-  if (tid == 0) last_mask = 0;
-  __syncthreads();
-  if (tid < GMAX) {
-    int m = gp.members[grp * GMAX + tid];
-    if (m >= gp.batch || m < 0) m = -1;  // bad ids were reported by the tile
-    mems[tid] = m;
-    if (m >= 0 && atomicAdd(&p.done[m * p.hkv + kvh], 1) == p.n_slots - 1) atomicOr(&last_mask, 1 << tid);
-  }
-  __syncthreads();
-  const int mask = last_mask;
-  if (mask == 0) return;
-  __threadfence();
-  const int r = tid >> 3, j = r >> 1;
-  if ((mask >> j) & 1) merge_partials<16>(p, mems[j], kvh * 2 + (r & 1), (tid & 7) * 16);
-  if (tid < GMAX && ((mask >> tid) & 1)) p.done[mems[tid] * p.hkv + kvh] = 0;
-}
-
 // Two stage buffers (64 KB): three CTAs per SM overlap one another's start-up latency, which
 // dominates the short own-key items of a decode step.
 constexpr int GRP_STAGES = 2;
@@ -674,13 +591,11 @@ paged_decode_grouped_kernel(DecodeParams p, GroupParams gp) {
     const int split = i % gp.shared_splits;
     i /= gp.shared_splits;
     decode_shared_tile<GRP_STAGES>(p, gp, smem, split, i % p.hkv, i / p.hkv);
-    if (p.done) shared_arrive(p, gp, i / p.hkv, i % p.hkv, threadIdx.x);
   } else {
     i -= gp.n_shared_ctas;
     const int split = i % gp.own_splits;
     i /= gp.own_splits;
     decode_own_tile<GRP_STAGES>(p, smem, split, i % p.hkv, i / p.hkv);
-    if (p.done) own_arrive(p, i / p.hkv, i % p.hkv, threadIdx.x);
   }
 }
 
@@ -1291,10 +1206,8 @@ extern "C" int qb_paged_decode_attn(const void* q, const void* k_cache, const vo
 }
 
 extern "C" size_t qb_paged_decode_grouped_workspace_bytes(int batch, int hq, int Dh, int n_slots) {
-  // split-K partials: n_slots per (sequence, head), then the arrival counters (one per sequence and
-  // kv head, hq / 2 of them)
-  const size_t partials = (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float);
-  return partials + ((size_t)batch * (hq / 2) * sizeof(int) + 15) / 16 * 16;
+  // split-K partials: n_slots per (sequence, head)
+  return (size_t)batch * n_slots * hq * (Dh + 4) * sizeof(float);
 }
 
 extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, const void* v_cache,
@@ -1317,20 +1230,20 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
   const int64_t n_ctas = n_shared + (int64_t)own_splits * hkv * batch;
   QB_CHECK_ARG(n_ctas < (1ll << 31));
   // shared splits fill slots [0, shared_splits), own splits the rest; n_slots >= 2, so every CTA
-  // writes a partial, and the CTA that writes the last one of a (sequence, kv head) merges them
-  int* done = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) +
-                                     (size_t)batch * n_slots * hq * (D + 4) * sizeof(float));
+  // writes a partial and the combine kernel produces the output
   DecodeParams d{(const bf16*)q, (const bf16*)k_cache, (const bf16*)v_cache, num_blocks, block_tables, bt_stride,
                  seqlens, seqlen_add, hq, hkv, scale * LOG2E, split_tokens, n_slots, workspace, (bf16*)out, err,
-                 n_slots, shared_splits, kv_start, done};
+                 n_slots, shared_splits, kv_start};
   GroupParams gp{group_members, shared_len, batch, shared_splits, own_splits, (int)n_shared};
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(paged_decode_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GRP_SMEM);
     attr_set = true;
   }
-  return qb_launch(paged_decode_grouped_kernel, dim3((unsigned)n_ctas), dim3(DEC_WARPS * 32), GRP_SMEM,
-                   (cudaStream_t)stream, 1, d, gp);
+  int st = qb_launch(paged_decode_grouped_kernel, dim3((unsigned)n_ctas), dim3(DEC_WARPS * 32), GRP_SMEM, (cudaStream_t)stream, 1, d, gp);
+  if (st != QB_OK) return st;
+  const int wpb = 8;
+  return qb_launch(paged_decode_combine_kernel, dim3((unsigned)((batch * hq + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, d, batch);
 }
 
 extern "C" int qb_attn_varlen_fwd(const void* q, int64_t q_stride, const void* k, const void* v,

@@ -493,8 +493,7 @@ def grouped_decode_plan(batch, hkv, max_shared, max_own, sm_count=148):
 def grouped_workspace(batch, hq, D, plan, device):
     """Workspace of :func:`paged_decode_attention_grouped` (split-K partials)."""
     nbytes = lib().qb_paged_decode_grouped_workspace_bytes(batch, hq, D, plan[1] + plan[2])
-    # zeros: the tail holds arrival counters that start at zero (every call leaves them zero)
-    return torch.zeros(nbytes // 4, dtype=torch.float32, device=device)
+    return torch.empty(nbytes // 4, dtype=torch.float32, device=device)
 
 
 def paged_decode_attention_grouped(q, k_cache, v_cache, block_tables, seqlens, scale, group_members, shared_len,

@@ -53,8 +53,7 @@ def test_workspace_size_queries():
     assert lib.qb_paged_decode_workspace_bytes(256, 16, 128, 4) == 256 * 4 * 16 * 132 * 4
     assert lib.qb_grpo_workspace_bytes(4096) >= 16 + 8 * 4096
     # grouped decode: split-K partials only (shared + own slots per sequence and head)
-    # split-K partials, then one arrival counter per (sequence, kv head)
-    assert lib.qb_paged_decode_grouped_workspace_bytes(512, 16, 128, 2) == 512 * 2 * 16 * 132 * 4 + 512 * 8 * 4
+    assert lib.qb_paged_decode_grouped_workspace_bytes(512, 16, 128, 2) == 512 * 2 * 16 * 132 * 4
 
 
 def test_host_side_argument_validation():
