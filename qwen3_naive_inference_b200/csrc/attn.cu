@@ -1243,7 +1243,9 @@ extern "C" int qb_paged_decode_attn_grouped(const void* q, const void* k_cache, 
   int st = qb_launch(paged_decode_grouped_kernel, dim3((unsigned)n_ctas), dim3(DEC_WARPS * 32), GRP_SMEM, (cudaStream_t)stream, 1, d, gp);
   if (st != QB_OK) return st;
   const int wpb = 8;
-  return qb_launch(paged_decode_combine_kernel, dim3((unsigned)((batch * hq + wpb - 1) / wpb)), dim3(wpb * 32), 0, (cudaStream_t)stream, 1, d, batch);
+  // launched early: resident while the tile kernel finishes, it starts the moment that completes
+  return qb_launch_ex(paged_decode_combine_kernel, dim3((unsigned)((batch * hq + wpb - 1) / wpb)), dim3(wpb * 32), 0,
+                      (cudaStream_t)stream, 1, true, d, batch);
 }
 
 extern "C" int qb_attn_varlen_fwd(const void* q, int64_t q_stride, const void* k, const void* v,
