@@ -367,11 +367,14 @@ int qb_gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, int64_t ldw,
                          void* raw, int64_t ld_raw, void* q_out, void* k_cache, void* v_cache,
                          const int32_t* slot_mapping, int64_t num_slots, float* q_rstd, float* k_rstd, int flags,
                          int* err, qb_stream_t stream);
-/* The tile layout qb_gemm_bf16 / qb_gemm_bf16_ex choose for an M x N x K product (B MN-major or
- * not): *pair = 1 for 256-row tiles on a CTA pair, *tile_n = the tile's width (N), *split = the
- * number of CTAs a 128 x 128 tile's K range is split over (1: none).  Needs the current device
- * (the split layouts are sized by cluster occupancy).  For tests and tuning. */
-int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int* pair, int* tile_n, int* split);
+/* The tile layout qb_gemm_bf16 / qb_gemm_bf16_ex choose for an M x N x K product in `mode` (B
+ * MN-major or not): *pair = 1 for 256-row tiles on a CTA pair, *tile_n = the tile's width (N),
+ * *split = the number of CTAs a tile's K range is split over (1: none): the CTAs of a 128 x 128
+ * tile's cluster, or in mode 2 (C +=) several pairs whose partials are added to C atomically, so
+ * the sum's order varies from run to run.  Needs the current device (the split layouts are sized by
+ * cluster occupancy).  For tests and tuning. */
+int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int mode, int* pair, int* tile_n,
+                 int* split);
 
 /* ---------------------------------------------------------------- optimizer helpers
  * dst (bf16) = bf16(src fp32); used to hand fp32-accumulated gradients to the

@@ -63,7 +63,7 @@ SIGNATURES: dict[str, tuple] = {
     "qb_gemm_swiglu": (I, [P, L, P, L, P, L, P, L, L, L, L, I, P, P]),
     "qb_gemm_qk_norm_rope": (I, [P, L, P, L, L, I, I, L, P, P, L, P, P, F, P, L, P, L, P, P, P, P, L, P, P, I, P,
                                  P]),
-    "qb_gemm_plan": (I, [L, L, L, I, P, P, P]),
+    "qb_gemm_plan": (I, [L, L, L, I, I, P, P, P]),
     "qb_f32_to_bf16": (I, [P, P, L, P]),
     "qb_accumulate_bf16": (I, [P, P, L, P]),
 }

@@ -37,6 +37,7 @@ struct GemmParams {
   float* tgt_logit;        // [M] fp32 logit at the target column
   int n_part;              // row pitch of lse_part (= number of N tiles of the launch)
   int b_static;            // B is written by no kernel still in flight: it may be read before the PDL wait
+  int ksplit;              // pair kernel, MODE 2: K split over this many pairs per tile (atomic adds to C)
   // MODE 4 (gate_up projection -> SwiGLU): B is the [2*half, K] gate_up weight (gate rows, then up
   // rows); an N tile of width BN holds BN/2 gate columns and the same BN/2 up columns; C receives
   // silu(gate) * up [M, N = half], C2 (nullable) the bf16 gate_up itself [M, 2*half] for a backward.
@@ -105,6 +106,23 @@ QB_DEVICE void store_row32(const GemmParams& p, int row, int col, const uint32_t
           if (col + i < p.N) dst[i] = (MODE == 2 ? dst[i] : 0.f) + __uint_as_float(r[i]);
       }
     }
+}
+
+// MODE 2 with K split over several CTAs: this thread's 32 fp32 columns added to C atomically (16-byte
+// vector adds where the row is aligned), since the splits of a tile finish in any order.
+QB_DEVICE void red_row32(const GemmParams& p, int row, int col, const uint32_t (&r)[32]) {
+  float* dst = reinterpret_cast<float*>(p.C) + (int64_t)row * p.ldc + col;
+  if (col + 32 <= p.N && p.vec_ok) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      atomicAdd(reinterpret_cast<float4*>(dst) + q, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                                __uint_as_float(r[4 * q + 2]),
+                                                                __uint_as_float(r[4 * q + 3])));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col + i < p.N) atomicAdd(dst + i, __uint_as_float(r[i]));
+  }
 }
 
 // MODE 3 (lm_head -> log-softmax -> gather): the epilogue thread that holds row `row` of a tile
@@ -626,6 +644,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   const int tiles_m = (p.M + 255) / 256, tiles_n = (p.N + TN - 1) / TN;
   const int n_tiles = tiles_m * tiles_n;
   const int kblocks = (p.K + BK - 1) / BK;
+  // work units: (tile, K split), split-major; a unit covers K blocks [kb0, kb1) of its tile
+  const int ksplit = MODE == 2 && p.ksplit > 1 ? p.ksplit : 1;
+  const int n_units = n_tiles * ksplit;
+  auto unit_kb = [&](int u, int& kb0, int& kb1) {
+    const int sp = u / n_tiles;
+    kb0 = sp * kblocks / ksplit;
+    kb1 = (sp + 1) * kblocks / ksplit;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
@@ -658,12 +684,15 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     // ------------------------------------------------------------ producer (each CTA)
     int stage = 0;
     uint32_t phase = 0;
-    for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+    for (int u = pair; u < n_units && !*abort_flag; u += n_pairs) {
+      const int t = u % n_tiles;
+      int kb0, kb1;
+      unit_kb(u, kb0, kb1);
       // this CTA's half of B: rows [rank * PBN/2, ...) of the tile; in MODE 4 the even CTA takes the
       // tile's gate rows and the odd CTA the same rows of up
       const int m0 = (t % tiles_m) * 256 + (int)rank * 128,
                 n0 = MODE == 4 ? (rank ? p.half : 0) + (t / tiles_m) * TN : (t / tiles_m) * PBN + (int)rank * Sh::B_ROWS;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1, abort_flag, p.err)) break;
         const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
         const uint32_t lf = cluster_addr(full_bar(stage), 0);
@@ -679,19 +708,21 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     uint32_t phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+    for (int u = pair; u < n_units && !*abort_flag; u += n_pairs) {
       if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1, abort_flag, p.err)) break;
       tc_fence_after();
       const uint32_t d = tmem + acc * Sh::ACC_STRIDE;
+      int kb0, kb1;
+      unit_kb(u, kb0, kb1);
       bool ok = true;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_cluster(full_bar(stage), phase, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = base + stage * P_STAGE_BYTES, sb = sa + P_HALF_BYTES;
 #pragma unroll
         for (int j = 0; j < BK / 16; ++j)
           umma_pair(d, operand_desc<A_MN>(sa, j), operand_desc<B_MN>(sb, j), PairCfg<A_MN, B_MN, PBN>::IDESC,
-                    (kb | j) != 0);
+                    (kb != kb0 || j != 0));
         umma_commit_pair(empty_bar(stage));  // both CTAs' stage is free once these MMAs read it
         umma_commit_pair(cluster_addr(empty_bar(stage), peer));
         if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
@@ -713,7 +744,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     const uint32_t leader_tempty0 = cluster_addr(tempty_bar(0), 0), leader_tempty1 = cluster_addr(tempty_bar(1), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair; t < n_tiles && !*abort_flag; t += n_pairs) {
+    for (int u = pair; u < n_units && !*abort_flag; u += n_pairs) {
+      const int t = u % n_tiles;
       const int m0 = (t % tiles_m) * 256 + (int)rank * 128, n0 = (t / tiles_m) * TN;
       if constexpr (MODE == 5) qknorm_prefetch(p, m0 + row_in_tile);
       // tcgen05.ld is warp-collective: the warp leaves (or goes on) together
@@ -735,7 +767,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * Sh::ACC_STRIDE + c, r);
           const int col = n0 + c;
           if (!row_ok || col >= p.N) continue;
-          store_row32<MODE>(p, row, col, r);
+          if (MODE == 2 && ksplit > 1)
+            red_row32(p, row, col, r);
+          else
+            store_row32<MODE>(p, row, col, r);
         }
       }
       tc_fence_before();
@@ -1027,7 +1062,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams p, cuda
     attr = true;
   }
   constexpr int TN = MODE == 4 ? PBN / 2 : PBN;
-  const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN);
+  const int tiles = ((p.M + 255) / 256) * ((p.N + TN - 1) / TN) * (MODE == 2 && p.ksplit > 1 ? p.ksplit : 1);
   const int pairs = tiles < sm_count() / 2 ? tiles : sm_count() / 2;
   return qb_launch_ex(kern, dim3((unsigned)(2 * pairs)), dim3(THREADS), SMEM, st, 2, true, ta, tb, p);
 }
@@ -1128,13 +1163,33 @@ inline bool al16(const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) =
 struct GemmPlan {
   bool pair;
   int bn;     // tile width (N): of the pair's 256-row tile, or of the single CTA's 128-row tile
-  int split;  // CTAs a 128 x 128 tile's K range is split over (1: none)
+  int split;  // K split: over the CTAs of a 128 x 128 tile's cluster (single), or over pairs (MODE 2)
 };
 
-GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
-  const int sms = sm_count();
+// pair_split: the K range of a pair tile may be split over several pairs whose partials are added
+// to C atomically (MODE 2, C += A.B^T): weight gradients whose tiles leave pairs idle.
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn, bool pair_split) {
+  const int sms = sm_count(), P = sms / 2;
   const int64_t tm = (M + BM - 1) / BM, kblocks = (K + BK - 1) / BK;
-  if (N >= 256 && M >= 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sms / 2) return {true, 256, 1};
+  const int64_t pairs = ((M + 255) / 256) * ((N + 255) / 256);
+  // 256 x 256 pair tiles, K split S ways: waves of units over the pairs x K blocks per unit
+  // (a split must save 10%: its atomic adds to C are not in the cost)
+  auto pair_plan = [&](int64_t& cost) {
+    int S = 1;
+    cost = (pairs + P - 1) / P * kblocks * (int64_t)(128 + 128) * BK * 2;
+    const int64_t cost1 = cost;
+    for (int s = 2; pair_split && s <= 4; ++s) {
+      if (kblocks / s < 32) break;
+      const int64_t c = (pairs * s + P - 1) / P * ((kblocks + s - 1) / s) * (int64_t)(128 + 128) * BK * 2;
+      if (c < cost && 10 * c < 9 * cost1) { cost = c; S = s; }
+    }
+    return S;
+  };
+  if (N >= 256 && M >= 256 && pairs >= P) {
+    int64_t c;
+    const int S = pair_plan(c);
+    return {true, 256, S};
+  }
   if (N >= 256 && tm * ((N + 255) / 256) >= sms) return {false, 256, 1};
   const int64_t t128 = tm * ((N + 127) / 128), t192 = tm * ((N + 191) / 192);
   GemmPlan best_plan{false, 128, 1};
@@ -1148,9 +1203,9 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, bool b_mn) {
   // operands alone would ask ~35 TB/s of L2 at the MMA rate).  Long K only (64+ K blocks), ties to
   // single-CTA tiles: the decode step's M = 512, K = 1024 products measured slower on pairs.
   if (M > 128 && N > 128 && kblocks >= 64) {
-    const int64_t pairs = ((M + 255) / 256) * ((N + 255) / 256);
-    const int64_t c = (pairs + sms / 2 - 1) / (sms / 2) * kblocks * (int64_t)(128 + 128) * BK * 2;
-    if (c < best) { best = c; best_plan = {true, 256, 1}; }
+    int64_t c;
+    const int S = pair_plan(c);
+    if (c < best) { best = c; best_plan = {true, 256, S}; }
   }
   for (int S = 2; S <= 4; S *= 2) {
     if (kblocks < 2 * S || t128 > split_clusters(S)) continue;
@@ -1174,15 +1229,16 @@ int gemm_dispatch(const void* A, int64_t lda, bool a_mn, const void* B, int64_t 
   QB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31));
   const int64_t elem = mode == 0 ? 2 : 4;
   const int vec_ok = al16(C) && (ldc * elem) % 16 == 0;
-  const GemmPlan pl = plan_gemm(M, N, K, b_mn);
+  const GemmPlan pl = plan_gemm(M, N, K, b_mn, mode == 2);
   const int64_t tm = (M + BM - 1) / BM;
-  const int pbn = pl.pair ? pl.bn : 0, bn = pl.bn, split = pl.split;
+  const int pbn = pl.pair ? pl.bn : 0, bn = pl.bn, split = pl.pair ? 1 : pl.split;
   CUtensorMap ta, tb;
   if (pbn) {
     if (!operand_tmap(&ta, A, a_mn, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM)) return QB_ERR_INVALID;
     if (!operand_tmap(&tb, B, b_mn, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, (uint32_t)(pbn / 2)))
       return QB_ERR_INVALID;
     GemmParams pp{C, ldc, (int)M, (int)N, (int)K, 0, 0, vec_ok, err};
+    pp.ksplit = pl.split;  // > 1 only in MODE 2
     if (!a_mn && !b_mn) return launch_pair_pbn<false, false>(pbn, mode, ta, tb, pp, st);
     if (!a_mn && b_mn) return launch_pair_pbn<false, true>(pbn, mode, ta, tb, pp, st);
     if (a_mn && !b_mn) return launch_pair_pbn<true, false>(pbn, mode, ta, tb, pp, st);
@@ -1400,9 +1456,10 @@ extern "C" int qb_gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, i
                            (cudaStream_t)stream);
 }
 
-extern "C" int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int* pair, int* tile_n, int* split) {
-  QB_CHECK_ARG(M > 0 && N > 0 && K > 0 && pair && tile_n && split);
-  const GemmPlan pl = plan_gemm(M, N, K, b_mn_major != 0);
+extern "C" int qb_gemm_plan(int64_t M, int64_t N, int64_t K, int b_mn_major, int mode, int* pair, int* tile_n,
+                            int* split) {
+  QB_CHECK_ARG(M > 0 && N > 0 && K > 0 && mode >= 0 && mode <= 2 && pair && tile_n && split);
+  const GemmPlan pl = plan_gemm(M, N, K, b_mn_major != 0, mode == 2);
   *pair = pl.pair ? 1 : 0;
   *tile_n = pl.bn;
   *split = pl.split;

@@ -597,11 +597,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, mode
     return out
 
 
-def gemm_plan(M: int, N: int, K: int, b_mn: bool = False) -> tuple[str, int, int]:
+def gemm_plan(M: int, N: int, K: int, b_mn: bool = False, mode: int = 0) -> tuple[str, int, int]:
     """The layout the GEMM picks for an M x N x K product: ("pair" | "single", tile width, split)."""
     import ctypes
     pair, tile_n, split = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
-    check(lib().qb_gemm_plan(M, N, K, 1 if b_mn else 0, ctypes.addressof(pair), ctypes.addressof(tile_n),
+    check(lib().qb_gemm_plan(M, N, K, 1 if b_mn else 0, mode, ctypes.addressof(pair), ctypes.addressof(tile_n),
                              ctypes.addressof(split)), "qb_gemm_plan")
     return ("pair" if pair.value else "single", tile_n.value, split.value)
 

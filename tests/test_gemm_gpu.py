@@ -125,6 +125,34 @@ def test_gemm_plan(cuda, M, N, K, b_mn, want):
     assert ops.gemm_plan(M, N, K, b_mn) == want
 
 
+@pytest.mark.parametrize("M,N,K,want", [
+    (1024, 2048, 32768, ("pair", 256, 2)),  # o_proj weight gradient: 32 pair tiles, K split 2 ways
+    (6144, 1024, 32768, ("pair", 256, 3)),  # gate_up: 96 tiles would take two waves of 74 pairs
+    (1024, 3072, 32768, ("pair", 256, 3)),  # down_proj
+    (4096, 1024, 32768, ("pair", 256, 1)),  # qkv: 64 tiles, no split saves a wave
+    (151936, 1024, 4096, ("pair", 256, 1)),  # lm_head: a huge C, a 2% saving is not worth atomics
+])
+def test_gemm_plan_weight_gradients(cuda, M, N, K, want):
+    """Mode 2 (C +=) may split K over pairs; the plain modes never do."""
+    assert ops.gemm_plan(M, N, K, True, mode=2) == want
+    assert ops.gemm_plan(M, N, K, True, mode=0)[2] == 1
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 2048, 16384), (1000, 1000, 20000), (600, 3000, 9000)])
+def test_gemm_accumulate_split_over_pairs(cuda, M, N, K):
+    """C += A.B^T with K split over CTA pairs (atomic adds): backward layouts, M/N/K tails."""
+    g = torch.Generator(device=cuda).manual_seed(M + N)
+    a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(torch.bfloat16)
+    assert ops.gemm_plan(M, N, K, True, mode=2)[2] > 1
+    acc = torch.randn(M, N, device=cuda, generator=g)
+    out = acc.clone()
+    ops.gemm_ex(a.t().contiguous(), True, b.t().contiguous(), True, out=out, mode=2)
+    ref = acc + a.float() @ b.float().t()
+    assert torch.allclose(out, ref, rtol=1e-3, atol=2e-2)
+    ops.check_device_errors()
+
+
 def test_gemm_k_tail_k_major(cuda):
     g = torch.Generator(device=cuda).manual_seed(3)
     a = torch.randn(200, 100, device=cuda, generator=g).to(torch.bfloat16)[:, :72]
