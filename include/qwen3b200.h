@@ -359,7 +359,7 @@ int qb_gemm_swiglu(const void* A, int64_t lda, const void* W, int64_t ldw, void*
  * Outputs, each nullable: out [M, ld_out] (rotated q, k and the v columns), raw [M, ld_raw] (the
  * bf16 projection, for a backward), q_out [M, hq, 128], k_cache / v_cache [num_slots, hkv, 128]
  * (row slot_mapping[r] <- rotated k / v of row r; -1 skips), q_rstd [M, hq] / k_rstd [M, hkv].
- * cos_sin [max_pos, 128] fp32, 8-byte aligned; norm weights 4-byte aligned; every bf16 output
+ * cos_sin [max_pos, 128] fp32, 16-byte aligned; norm weights 8-byte aligned; every bf16 output
  * 16-byte aligned with a leading dimension % 8 == 0.  flags: 0 or QB_GEMM_B_STATIC. */
 int qb_gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, int64_t ldw, int64_t M, int hq, int hkv,
                          int64_t K, const int64_t* positions, const float* cos_sin, int64_t max_pos,

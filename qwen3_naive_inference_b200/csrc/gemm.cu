@@ -302,15 +302,20 @@ QB_DEVICE void qknorm_tile(const GemmParams& p, uint32_t taddr, int row, bool ro
     const bf16* w = is_q ? e.qw : e.kw;
     const float* cs = e.cos_sin + pos * 128;
 #pragma unroll
-    for (int j = 0; j < 64; j += 2) {  // RoPE pairs (j, j+64) and (j+1, j+65)
-      const float2 lo = unpack_bf16x2(x[j / 2]), hi = unpack_bf16x2(x[32 + j / 2]);
-      const float2 wl = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + j));
-      const float2 wh = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(w + 64 + j));
-      const float2 c = *reinterpret_cast<const float2*>(cs + j), sn = *reinterpret_cast<const float2*>(cs + 64 + j);
-      const float xl0 = round_bf16((lo.x * rstd) * wl.x), xl1 = round_bf16((lo.y * rstd) * wl.y);
-      const float xh0 = round_bf16((hi.x * rstd) * wh.x), xh1 = round_bf16((hi.y * rstd) * wh.y);
-      x[j / 2] = pack_bf16x2(qk_rope_lo(xl0, xh0, c.x, sn.x), qk_rope_lo(xl1, xh1, c.y, sn.y));
-      x[32 + j / 2] = pack_bf16x2(qk_rope_hi(xh0, xl0, c.x, sn.x), qk_rope_hi(xh1, xl1, c.y, sn.y));
+    for (int j = 0; j < 64; j += 4) {  // RoPE pairs (j+i, j+i+64), i < 4: 16-byte table loads
+      const float4 c = *reinterpret_cast<const float4*>(cs + j), sn = *reinterpret_cast<const float4*>(cs + 64 + j);
+      const uint2 wlr = *reinterpret_cast<const uint2*>(w + j), whr = *reinterpret_cast<const uint2*>(w + 64 + j);
+      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const float2 lo = unpack_bf16x2(x[j / 2 + h2]), hi = unpack_bf16x2(x[32 + j / 2 + h2]);
+        const float2 wl = unpack_bf16x2(h2 ? wlr.y : wlr.x), wh = unpack_bf16x2(h2 ? whr.y : whr.x);
+        const float c0 = cc[2 * h2], c1 = cc[2 * h2 + 1], s0 = ss[2 * h2], s1 = ss[2 * h2 + 1];
+        const float xl0 = round_bf16((lo.x * rstd) * wl.x), xl1 = round_bf16((lo.y * rstd) * wl.y);
+        const float xh0 = round_bf16((hi.x * rstd) * wh.x), xh1 = round_bf16((hi.y * rstd) * wh.y);
+        x[j / 2 + h2] = pack_bf16x2(qk_rope_lo(xl0, xh0, c0, s0), qk_rope_lo(xl1, xh1, c1, s1));
+        x[32 + j / 2 + h2] = pack_bf16x2(qk_rope_hi(xh0, xl0, c0, s0), qk_rope_hi(xh1, xl1, c1, s1));
+      }
     }
     if (is_q) {
       if (e.q_rstd) e.q_rstd[(int64_t)row * e.hq + head] = rstd;
@@ -1311,8 +1316,8 @@ int gemm_qk_norm_rope(const void* A, int64_t lda, const void* W, int64_t ldw, in
   const int64_t N = (int64_t)(hq + 2 * hkv) * 128;
   QB_CHECK_ARG(A && W && al16(A) && al16(W) && lda % 8 == 0 && ldw % 8 == 0 && lda >= K && ldw >= K);
   QB_CHECK_ARG(qk.positions && qk.cos_sin && qk.max_pos > 0 && qk.qw && qk.kw);
-  QB_CHECK_ARG((reinterpret_cast<uintptr_t>(qk.cos_sin) & 7) == 0 && (reinterpret_cast<uintptr_t>(qk.qw) & 3) == 0 &&
-               (reinterpret_cast<uintptr_t>(qk.kw) & 3) == 0);
+  QB_CHECK_ARG((reinterpret_cast<uintptr_t>(qk.cos_sin) & 15) == 0 && (reinterpret_cast<uintptr_t>(qk.qw) & 7) == 0 &&
+               (reinterpret_cast<uintptr_t>(qk.kw) & 7) == 0);
   QB_CHECK_ARG(out == nullptr || (al16(out) && ld_out >= N && ld_out % 8 == 0));
   QB_CHECK_ARG(raw == nullptr || (al16(raw) && ld_raw >= N && ld_raw % 8 == 0));
   QB_CHECK_ARG(qk.q_out == nullptr || al16(qk.q_out));

@@ -300,10 +300,12 @@ class Qwen3Attention(nn.Module):
 
     def forward_packed(self, x, positions, cu_seqlens, tiles):
         """Training/recompute path over packed sequences (each attends only to itself)."""
-        # one GEMM for the projection, QK-norm and RoPE, then the attention kernel
-        o = ops.qkv_attention(x, self.qkv_proj.weight, positions, self._cos_sin(x.device), self.q_norm.weight,
-                              self.k_norm.weight, self.eps, cu_seqlens, tiles, self.num_heads, self.num_kv_heads,
-                              self.scale, rope_grad=self.rope_grad)
+        # projection, then QK-norm + RoPE + attention as one node (the GEMM with QK-norm in its epilogue,
+        # ops.qkv_attention, is slower at training sizes: its row-per-thread epilogue throttles the LSU)
+        qkv = ops.linear(x, self.qkv_proj.weight)
+        o = ops.qk_norm_rope_attention(qkv, positions, self._cos_sin(x.device), self.q_norm.weight,
+                                       self.k_norm.weight, self.eps, cu_seqlens, tiles, self.num_heads,
+                                       self.num_kv_heads, self.scale, rope_grad=self.rope_grad)
         return ops.linear(o, self.o_proj.weight)
 
     def forward(self, x):
