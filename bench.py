@@ -75,6 +75,12 @@ def parse():
                     help="eager decode launches (for launch-list profiling; ncu and graph replays do not mix)")
     ap.add_argument("--attn-only", action="store_true",
                     help="training attention forward + backward on one microbatch of the bench's sequences")
+    ap.add_argument("--gemm-qk", action="store_true",
+                    help="qkv GEMM with the QK-norm + RoPE epilogue against GEMM + standalone kernel (decode "
+                         "step and training sizes)")
+    ap.add_argument("--elementwise", action="store_true",
+                    help="the row kernels (QK-norm/RoPE fwd+bwd, SwiGLU fwd+bwd, RMSNorm bwd) on a training "
+                         "microbatch")
     ap.add_argument("--loss-only", action="store_true",
                     help="config 1: fused log-prob -> GRPO loss -> logit gradient over 1024 rows of logits")
     ap.add_argument("--kernel-profile", default=None, metavar="PATH",
@@ -1112,6 +1118,113 @@ def run_gemm_only(shape=None):
     print(json.dumps({"gemm": out, "peak_tflops": peak}), flush=True)
 
 
+def _event_time(torch, fn, reps=20, warm=3):
+    """Mean ms per call of fn() over `reps` back-to-back calls, CUDA events on the current stream."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(reps):
+        fn()
+    b.record(st)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_gemm_qk():
+    """The qkv projection with QK-norm + RoPE in the GEMM epilogue against the plain GEMM followed
+    by the standalone QK-norm + RoPE kernel: T = 512 (decode step: rotated q out, K/V into the paged
+    cache) and T = 4096 (training layout: raw projection + rotated copy + rstd)."""
+    import torch
+
+    from oracle import ref_ops as R  # the rotation table only
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    bf = torch.bfloat16
+    hq, hkv, K = 16, 8, 1024
+    N = (hq + 2 * hkv) * 128
+    cs = R.rope_cache(128, 4096, 1e6).to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.03).to(bf)
+    qw = torch.ones(128, dtype=bf, device=dev)
+    kw = torch.ones(128, dtype=bf, device=dev)
+    res = {}
+    for T, train in ((512, False), (4096, True)):
+        x = torch.randn(T, K, device=dev, generator=g).to(bf)
+        pos = torch.randint(0, 4000, (T,), device=dev, generator=g)
+        out, raw = torch.empty(T, N, dtype=bf, device=dev), torch.empty(T, N, dtype=bf, device=dev)
+        qr, kr = torch.empty(T, hq, device=dev), torch.empty(T, hkv, device=dev)
+        kc = torch.zeros(4096, hkv, 128, dtype=bf, device=dev)
+        vc = torch.zeros_like(kc)
+        slots = torch.arange(T, dtype=torch.int32, device=dev)
+        if train:
+            fused = lambda: ops.gemm_qk_norm_rope(x, w, pos, cs, qw, kw, 1e-6, hq, hkv, out=out, raw=raw,  # noqa: E731
+                                                  q_rstd=qr, k_rstd=kr)
+            unfused = lambda: ops._qk_norm_rope_fwd(ops.gemm(x, w, out=raw), pos, cs, qw, kw, 1e-6, hq, hkv)  # noqa: E731
+        else:
+            fused = lambda: ops.qkv_norm_rope_store(x, w, pos, cs, qw, kw, 1e-6, hq, hkv, kc, vc, slots)  # noqa: E731
+            unfused = lambda: ops.qk_norm_rope_store(ops.gemm(x, w, out=raw), pos, cs, qw, kw, 1e-6, hq, hkv,  # noqa: E731
+                                                     kc, vc, slots)
+        res[f"T{T}"] = {"fused_ms": _event_time(torch, fused), "gemm_then_kernel_ms": _event_time(torch, unfused)}
+    ops.check_device_errors()
+    print(json.dumps({"gemm_qk_norm_rope": res}), flush=True)
+
+
+def run_elementwise():
+    """The HBM-bound row kernels on one training microbatch (T = 32768 tokens): mean time per call
+    (CUDA events) and algorithmic bytes / time."""
+    import torch
+
+    from oracle import ref_ops as R  # the rotation table only
+    from qwen3_naive_inference_b200 import ops
+    dev = torch.device("cuda", 0)
+    bf = torch.bfloat16
+    T, hq, hkv, H, I = 32768, 16, 8, 1024, 3072
+    N = (hq + 2 * hkv) * 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    cs = R.rope_cache(128, 4096, 1e6).to(dev)
+    qkv = torch.randn(T, N, device=dev, generator=g).to(bf)
+    pos = torch.randint(0, 4000, (T,), device=dev, generator=g)
+    qw = torch.ones(128, dtype=bf, device=dev)
+    kw = torch.ones(128, dtype=bf, device=dev)
+    rot, q_rstd, k_rstd = ops._qk_norm_rope_fwd(qkv, pos, cs, qw, kw, 1e-6, hq, hkv)
+    d = torch.randn(T, N, device=dev, generator=g).to(bf)
+    gu = torch.randn(T, 2 * I, device=dev, generator=g).to(bf)
+    dh = torch.randn(T, I, device=dev, generator=g).to(bf)
+    dgu = torch.empty_like(gu)
+    x = torch.randn(T, H, device=dev, generator=g).to(bf)
+    dy = torch.randn(T, H, device=dev, generator=g).to(bf)
+    nw = torch.ones(H, dtype=bf, device=dev)
+    rstd = torch.ones(T, device=dev)
+    dx = torch.empty_like(x)
+    dnw = torch.zeros(H, device=dev)
+    lib = ops.lib()
+    cases = {
+        # rotated q, k and the copied v: read + write of the row
+        "qk_norm_rope_fwd8": (lambda: ops._qk_norm_rope_fwd(qkv, pos, cs, qw, kw, 1e-6, hq, hkv), 2 * T * N * 2),
+        # in place in the attention gradient: read dq/dk and raw q/k, write dq/dk (v untouched)
+        "qk_norm_rope_bwd8": (lambda: ops._qk_norm_rope_bwd(d, d, qkv, pos, cs, qw, kw, q_rstd, k_rstd, hq, hkv,
+                                                            True), 3 * T * (hq + hkv) * 128 * 2),
+        "silu_mul_fwd": (lambda: ops.silu_mul(gu), T * 3 * I * 2),
+        "silu_mul_bwd": (lambda: ops.check(lib.qb_silu_mul_bwd(ops._p(dh), ops._p(gu), T, I, ops._p(dgu),
+                                                               ops.stream_ptr()), "qb_silu_mul_bwd"), T * 5 * I * 2),
+        "rmsnorm_bwd": (lambda: ops.check(lib.qb_rmsnorm_bwd(ops._p(dy), ops._p(x), ops._p(nw), ops._p(rstd), ops._p(dx),
+                                                             ops._p(dnw), T, H, ops.stream_ptr()), "qb_rmsnorm_bwd"),
+                        3 * T * H * 2),
+    }
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    res = {}
+    for name, (fn, nbytes) in cases.items():
+        ms = _event_time(torch, fn)
+        res[name] = {"ms": ms, "algorithmic_bytes": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                     "frac_of_measured_copy": nbytes / (ms * 1e-3) / 1e9 / hbm}
+    ops.check_device_errors()
+    print(json.dumps({"elementwise": res, "tokens": T}), flush=True)
+
+
 def run_attn_only():
     """Packed causal attention of the training step (16 q / 8 kv heads, d128) on one 32k-token
     microbatch of bench-shaped sequences (prompt U[64,512] + 512 completion tokens): forward and
@@ -1159,6 +1272,10 @@ def main():
         run_rollout_attn()
     elif args.attn_only:
         run_attn_only()
+    elif args.gemm_qk:
+        run_gemm_qk()
+    elif args.elementwise:
+        run_elementwise()
     elif args.gemm_only:
         run_gemm_only(args.gemm_shape)
     elif args.loss_only:
