@@ -421,7 +421,11 @@ def run_ours(args):
     # share (cfg5 on few GPUs) gets what fits in memory and the scheduler admits groups in waves
     need = len(make_prompts(args, rank, 0)) * args.group * math.ceil(max_ctx / 256) + 64
     free, _ = torch.cuda.mem_get_info(dev)
-    fit = int((free - (24 << 30)) // policy._block_bytes())  # keep 24 GB for activations and the step
+    # keep room for the training pass, which runs with the pool still allocated: ~48 KB of saved
+    # activations per token and layer for a microbatch, plus 16 GB for the optimizer state, the
+    # gradient buffer, the logits chunk and the backward's transient buffers
+    reserve = (16 << 30) + args.microbatch_tokens * args.layers * (48 << 10)
+    fit = int((free - reserve) // policy._block_bytes())
     policy._num_blocks = max(64, min(need, fit))
     policy.max_model_len = max_ctx
     policy.use_cuda_graphs = not args.no_graphs
